@@ -1,0 +1,143 @@
+// Device helpers shared by the two attention kernels: parameters, plan
+// access, fast exp2/log2, bf16 unpacking and the split-KV merge.
+#pragma once
+
+#include "common.cuh"
+
+namespace aspire {
+
+struct AttnParams {
+  const __nv_bfloat16* q;
+  int64_t q_stride_n, q_stride_h;
+  const __nv_bfloat16* kv;
+  int64_t num_pages_total;
+  const int32_t* kv_indices;
+  __nv_bfloat16* out;
+  int64_t o_stride_n, o_stride_h;
+  float* lse;                // optional
+  __half* dump;              // optional
+  int64_t dump_num_heads, dump_kv_stride;
+  float scale_log2;          // sm_scale * log2(e)
+  int32_t num_qo_heads, num_kv_heads, group;
+  const int32_t* plan;       // int workspace + kStatusBytes
+  uint32_t* status;          // int workspace (first word)
+  float* partial_o;          // float workspace
+};
+
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__device__ __forceinline__ float lg2(float x) {
+  float y;
+  asm("lg2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__device__ __forceinline__ void bf16x8_to_f32(const uint4 u, float* f) {
+  f[0] = __uint_as_float(u.x << 16);
+  f[1] = __uint_as_float(u.x & 0xffff0000u);
+  f[2] = __uint_as_float(u.y << 16);
+  f[3] = __uint_as_float(u.y & 0xffff0000u);
+  f[4] = __uint_as_float(u.z << 16);
+  f[5] = __uint_as_float(u.z & 0xffff0000u);
+  f[6] = __uint_as_float(u.w << 16);
+  f[7] = __uint_as_float(u.w & 0xffff0000u);
+}
+
+__device__ __forceinline__ WorkItem load_item(const int32_t* plan, int idx) {
+  const int4* src = reinterpret_cast<const int4*>(plan + plan[kHdrOffItems]) + idx * 4;
+  WorkItem it;
+  int4* dst = reinterpret_cast<int4*>(&it);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) dst[i] = src[i];
+  return it;
+}
+
+__device__ __forceinline__ float* partial_lse_ptr(const AttnParams& p) {
+  const int64_t off = (int64_t(uint32_t(p.plan[kHdrPartialLseLo]))) |
+                      (int64_t(p.plan[kHdrPartialLseHi]) << 32);
+  return p.partial_o + off;
+}
+
+__device__ __forceinline__ void record_status(uint32_t* status, uint32_t bits) {
+  if (status) atomicOr(status, bits);
+}
+
+// Location of packed query row `pq` of an item: token row and query head.
+__device__ __forceinline__ void packed_row(const AttnParams& p, const WorkItem& it, int pq,
+                                           int& q_idx, int& head) {
+  q_idx = pq / p.group;
+  head = it.kv_head * p.group + (pq - q_idx * p.group);
+}
+
+// Writes one finished (normalised) output row element and its LSE.
+__device__ __forceinline__ void store_final(const AttnParams& p, const WorkItem& it, int pq, int d,
+                                            float o, float lse) {
+  int q_idx, head;
+  packed_row(p, it, pq, q_idx, head);
+  const int64_t tok = int64_t(it.q_start) + q_idx;
+  p.out[tok * p.o_stride_n + int64_t(head) * p.o_stride_h + d] = __float2bfloat16_rn(o);
+  if (d == 0 && p.lse) p.lse[tok * p.num_qo_heads + head] = lse;
+}
+
+// Split-KV epilogue of one item, run by all `nthreads` threads of the CTA
+// after the normalised partial rows (o_rows[r][d], lse_rows[r]) of this chunk
+// are available through `get_o`/`get_lse`.  Items that own their whole KV
+// range write through; chunked items publish a partial, and the CTA that
+// completes a merge group combines all chunks in chunk order (deterministic).
+// No CTA ever waits for another: the last arriver does the merge.
+template <typename GetO, typename GetLse>
+__device__ __forceinline__ void finish_item(const AttnParams& p, const WorkItem& it, int tid,
+                                            int nthreads, int* smem_flag, GetO get_o,
+                                            GetLse get_lse) {
+  const int nrows = it.pq_end - it.pq_begin;
+  if (it.n_chunks <= 1) {
+    for (int e = tid; e < nrows * kHeadDim; e += nthreads) {
+      const int r = e / kHeadDim, d = e - r * kHeadDim;
+      store_final(p, it, it.pq_begin + r, d, get_o(r, d), get_lse(r));
+    }
+    return;
+  }
+  float* plse = partial_lse_ptr(p);
+  const int64_t base = int64_t(it.partial_base) + int64_t(it.chunk) * nrows;
+  for (int e = tid; e < nrows * kHeadDim; e += nthreads) {
+    const int r = e / kHeadDim, d = e - r * kHeadDim;
+    p.partial_o[(base + r) * kHeadDim + d] = get_o(r, d);
+    if (d == 0) plse[base + r] = get_lse(r);
+  }
+  __threadfence();
+  __syncthreads();
+  int32_t* counters = const_cast<int32_t*>(p.plan) + p.plan[kHdrOffCounters];
+  if (tid == 0) {
+    const int prev = atomicAdd(&counters[it.merge_id], 1);
+    *smem_flag = (prev == it.n_chunks - 1);
+  }
+  __syncthreads();
+  if (!*smem_flag) return;
+  __threadfence();
+  for (int e = tid; e < nrows * kHeadDim; e += nthreads) {
+    const int r = e / kHeadDim, d = e - r * kHeadDim;
+    float m = -INFINITY;
+    for (int c = 0; c < it.n_chunks; ++c)
+      m = fmaxf(m, __ldcg(plse + it.partial_base + int64_t(c) * nrows + r));
+    float acc = 0.f, wsum = 0.f;
+    if (m != -INFINITY) {
+      for (int c = 0; c < it.n_chunks; ++c) {
+        const int64_t prow = it.partial_base + int64_t(c) * nrows + r;
+        const float l = __ldcg(plse + prow);
+        const float w = ex2(l - m);
+        wsum += w;
+        acc += w * __ldcg(p.partial_o + prow * kHeadDim + d);
+      }
+    }
+    const float o = wsum > 0.f ? acc / wsum : 0.f;
+    const float lse = wsum > 0.f ? m + lg2(wsum) : -INFINITY;
+    store_final(p, it, it.pq_begin + r, d, o, lse);
+  }
+  if (tid == 0) counters[it.merge_id] = 0;
+}
+
+}  // namespace aspire

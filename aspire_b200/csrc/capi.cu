@@ -1,0 +1,298 @@
+// extern "C" entry points of libaspire_b200.so (declared in
+// include/aspire_b200.h): argument checking, launch configuration and
+// error reporting.  No entry point allocates memory or synchronises.
+#include <cmath>
+#include <cstdlib>
+#include <algorithm>
+#include <cstring>
+#include <string>
+
+#include "kernels.cuh"
+#include "errors.h"
+
+namespace aspire {
+
+// ---- error state ----------------------------------------------------------
+namespace {
+thread_local std::string g_last_error;
+}
+
+int set_error(int code, const std::string& msg) {
+  g_last_error = msg;
+  return code;
+}
+void clear_error() { g_last_error.clear(); }
+const char* last_error() { return g_last_error.c_str(); }
+int check_cuda(int st, const char* what) {
+  if (st == cudaSuccess) return ASPIRE_OK;
+  return set_error(ASPIRE_ERR_CUDA, std::string(what) + ": " +
+                                        cudaGetErrorString(static_cast<cudaError_t>(st)));
+}
+
+int plan_impl(const int32_t* qo_indptr, const int32_t* kv_indptr, const int32_t* kv_len,
+              int32_t batch_size, int32_t num_qo_heads, int32_t num_kv_heads, int32_t head_dim,
+              int32_t page_size, int32_t causal, int32_t num_sms, bool tc_enabled,
+              void* host_buf, size_t host_buf_bytes, size_t float_ws_bytes,
+              AspirePlanInfo* info);
+
+namespace {
+
+int current_sm_count(int* out) {
+  int dev = 0;
+  int rc = check_cuda(cudaGetDevice(&dev), "cudaGetDevice");
+  if (rc) return rc;
+  return check_cuda(cudaDeviceGetAttribute(out, cudaDevAttrMultiProcessorCount, dev),
+                    "cudaDeviceGetAttribute(SM count)");
+}
+
+// Opt-in to large dynamic shared memory once per (kernel, device, size).
+int ensure_smem(const void* func, size_t bytes, int* configured_bytes) {
+  if (int(bytes) <= *configured_bytes) return ASPIRE_OK;
+  int rc = check_cuda(cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           static_cast<int>(bytes)),
+                      "cudaFuncSetAttribute(max dynamic smem)");
+  if (rc == ASPIRE_OK) *configured_bytes = static_cast<int>(bytes);
+  return rc;
+}
+
+bool tc_env_enabled() {
+  const char* e = std::getenv("ASPIRE_B200_DISABLE_TC");
+  return !(e && e[0] == '1');
+}
+
+}  // namespace
+}  // namespace aspire
+
+using namespace aspire;
+
+extern "C" {
+
+int aspire_abi_version(void) { return ASPIRE_B200_ABI_VERSION; }
+
+const char* aspire_last_error(void) { return aspire::last_error(); }
+
+size_t aspire_status_offset(void) { return kStatusBytes; }
+
+const char* aspire_kernel_names(void) {
+  return "aspire_attn_gather_kernel\naspire_attn_tc_kernel\naspire_append_kv_kernel\n"
+         "aspire_select_pages_kernel\n";
+}
+
+int aspire_plan_host_only(const int32_t* qo_indptr, const int32_t* kv_indptr,
+                          const int32_t* kv_len, int32_t batch_size, int32_t num_qo_heads,
+                          int32_t num_kv_heads, int32_t head_dim, int32_t page_size,
+                          int32_t causal, int32_t num_ctas, void* host_buf,
+                          size_t host_buf_bytes, size_t float_ws_bytes, AspirePlanInfo* info) {
+  clear_error();
+  return plan_impl(qo_indptr, kv_indptr, kv_len, batch_size, num_qo_heads, num_kv_heads, head_dim,
+                   page_size, causal, num_ctas, tc_kernel_available() && tc_env_enabled(),
+                   host_buf, host_buf_bytes, float_ws_bytes, info);
+}
+
+int aspire_plan(const int32_t* qo_indptr, const int32_t* kv_indptr, const int32_t* kv_len,
+                int32_t batch_size, int32_t num_qo_heads, int32_t num_kv_heads, int32_t head_dim,
+                int32_t page_size, int32_t causal, int32_t num_ctas, void* host_buf,
+                size_t host_buf_bytes, void* dev_int_ws, size_t dev_int_ws_bytes,
+                size_t float_ws_bytes, void* stream, AspirePlanInfo* info) {
+  clear_error();
+  if (!dev_int_ws) return set_error(ASPIRE_ERR_INVALID, "aspire_plan: null device workspace");
+  if (num_ctas <= 0) {
+    int rc = current_sm_count(&num_ctas);
+    if (rc) return rc;
+  }
+  int rc = plan_impl(qo_indptr, kv_indptr, kv_len, batch_size, num_qo_heads, num_kv_heads, head_dim,
+                     page_size, causal, num_ctas, tc_kernel_available() && tc_env_enabled(),
+                     host_buf, host_buf_bytes, float_ws_bytes, info);
+  if (rc) return rc;
+  if (size_t(info->int_bytes) + kStatusBytes > dev_int_ws_bytes)
+    return set_error(ASPIRE_ERR_CAPACITY, "aspire_plan: plan needs " +
+                                              std::to_string(info->int_bytes + kStatusBytes) +
+                                              " bytes of device int workspace, have " +
+                                              std::to_string(dev_int_ws_bytes));
+  return check_cuda(cudaMemcpyAsync(static_cast<char*>(dev_int_ws) + kStatusBytes, host_buf,
+                                    size_t(info->int_bytes), cudaMemcpyHostToDevice,
+                                    static_cast<cudaStream_t>(stream)),
+                    "aspire_plan: cudaMemcpyAsync(plan upload)");
+}
+
+int aspire_mixed_attention(const AspireAttnArgs* a, const AspirePlanInfo* plan, void* stream) {
+  clear_error();
+  if (!a || !plan) return set_error(ASPIRE_ERR_INVALID, "aspire_mixed_attention: null argument");
+  if (a->head_dim != kHeadDim)
+    return set_error(ASPIRE_ERR_INVALID, "aspire_mixed_attention: head_dim must be 128");
+  if (a->page_size != kPageSize)
+    return set_error(ASPIRE_ERR_INVALID, "aspire_mixed_attention: page_size must be 16");
+  if (a->num_kv_heads <= 0 || a->num_qo_heads % a->num_kv_heads != 0)
+    return set_error(ASPIRE_ERR_INVALID, "aspire_mixed_attention: bad head counts");
+  if (a->num_qo_heads != plan->num_qo_heads || a->num_kv_heads != plan->num_kv_heads)
+    return set_error(ASPIRE_ERR_INVALID,
+                     "aspire_mixed_attention: head counts differ from the plan's");
+  if (!a->q || !a->kv_cache || !a->kv_indices || !a->out || !a->int_ws)
+    return set_error(ASPIRE_ERR_INVALID, "aspire_mixed_attention: null tensor pointer");
+  if ((reinterpret_cast<uintptr_t>(a->q) | reinterpret_cast<uintptr_t>(a->kv_cache)) & 15)
+    return set_error(ASPIRE_ERR_INVALID, "aspire_mixed_attention: q / kv_cache not 16-byte aligned");
+  if ((a->q_stride_n | a->q_stride_h) & 7)
+    return set_error(ASPIRE_ERR_INVALID,
+                     "aspire_mixed_attention: q strides must be multiples of 8 elements");
+  if (a->dump && (a->dump_num_heads < a->num_qo_heads || a->dump_kv_stride <= 0))
+    return set_error(ASPIRE_ERR_INVALID, "aspire_mixed_attention: bad dump geometry");
+  if (size_t(plan->int_bytes) + kStatusBytes > a->int_ws_bytes)
+    return set_error(ASPIRE_ERR_CAPACITY, "aspire_mixed_attention: int workspace smaller than plan");
+  if (size_t(plan->float_bytes) > a->float_ws_bytes)
+    return set_error(ASPIRE_ERR_CAPACITY, "aspire_mixed_attention: float workspace smaller than plan");
+  if (plan->num_merge > 0 && !a->float_ws)
+    return set_error(ASPIRE_ERR_INVALID, "aspire_mixed_attention: split-KV needs a float workspace");
+
+  AttnParams p;
+  p.q = static_cast<const __nv_bfloat16*>(a->q);
+  p.q_stride_n = a->q_stride_n;
+  p.q_stride_h = a->q_stride_h;
+  p.kv = static_cast<const __nv_bfloat16*>(a->kv_cache);
+  p.num_pages_total = a->num_pages_total;
+  p.kv_indices = a->kv_indices;
+  p.out = static_cast<__nv_bfloat16*>(a->out);
+  p.o_stride_n = a->o_stride_n;
+  p.o_stride_h = a->o_stride_h;
+  p.lse = a->lse;
+  p.dump = static_cast<__half*>(a->dump);
+  p.dump_num_heads = a->dump_num_heads;
+  p.dump_kv_stride = a->dump_kv_stride;
+  const float sm_scale = a->sm_scale > 0.f ? a->sm_scale : 1.0f / std::sqrt(float(kHeadDim));
+  p.scale_log2 = sm_scale * 1.44269504088896340736f;
+  p.num_qo_heads = a->num_qo_heads;
+  p.num_kv_heads = a->num_kv_heads;
+  p.group = a->num_qo_heads / a->num_kv_heads;
+  p.plan = reinterpret_cast<const int32_t*>(static_cast<const char*>(a->int_ws) + kStatusBytes);
+  p.status = static_cast<uint32_t*>(a->int_ws);
+  p.partial_o = static_cast<float*>(a->float_ws);
+
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int rc;
+  // Both kernel classes are launched on every call with plan-independent
+  // grids: items live in device memory, so a captured graph stays valid.
+  static thread_local int gather_smem_cfg = 48 * 1024;
+  {
+    const size_t smem = gather_smem_bytes();
+    rc = ensure_smem(reinterpret_cast<const void*>(&aspire_attn_gather_kernel), smem,
+                     &gather_smem_cfg);
+    if (rc) return rc;
+    aspire_attn_gather_kernel<<<plan->num_ctas * kGatherCtasPerSm, 128, smem, st>>>(p);
+    rc = check_cuda(cudaGetLastError(), "aspire_attn_gather_kernel launch");
+    if (rc) return rc;
+  }
+  if (plan->tc_enabled) {
+    static thread_local int tc_smem_cfg = 48 * 1024;
+    const size_t smem = tc_smem_bytes();
+    rc = ensure_smem(reinterpret_cast<const void*>(&aspire_attn_tc_kernel), smem, &tc_smem_cfg);
+    if (rc) return rc;
+    aspire_attn_tc_kernel<<<plan->num_ctas * kTcCtasPerSm, 192, smem, st>>>(p);
+    rc = check_cuda(cudaGetLastError(), "aspire_attn_tc_kernel launch");
+    if (rc) return rc;
+  }
+  return ASPIRE_OK;
+}
+
+int aspire_append_kv(const AspireAppendArgs* a, void* stream) {
+  clear_error();
+  if (!a) return set_error(ASPIRE_ERR_INVALID, "aspire_append_kv: null argument");
+  if (a->head_dim != kHeadDim || a->page_size != kPageSize)
+    return set_error(ASPIRE_ERR_INVALID, "aspire_append_kv: head_dim must be 128 and page_size 16");
+  if (a->num_tokens <= 0 || a->num_rows <= 0) return ASPIRE_OK;
+  if (!a->k || !a->v || !a->kv_cache || !a->append_indptr || !a->page_indices || !a->page_indptr ||
+      !a->last_page_len)
+    return set_error(ASPIRE_ERR_INVALID, "aspire_append_kv: null pointer");
+  if (((a->k_stride_n | a->k_stride_h | a->v_stride_n | a->v_stride_h) & 7) ||
+      ((reinterpret_cast<uintptr_t>(a->k) | reinterpret_cast<uintptr_t>(a->v) |
+        reinterpret_cast<uintptr_t>(a->kv_cache)) &
+       15))
+    return set_error(ASPIRE_ERR_INVALID,
+                     "aspire_append_kv: k/v/kv_cache must be 16-byte aligned with 8-element strides");
+  AppendParams p;
+  p.k = static_cast<const __nv_bfloat16*>(a->k);
+  p.v = static_cast<const __nv_bfloat16*>(a->v);
+  p.k_stride_n = a->k_stride_n;
+  p.k_stride_h = a->k_stride_h;
+  p.v_stride_n = a->v_stride_n;
+  p.v_stride_h = a->v_stride_h;
+  p.num_tokens = a->num_tokens;
+  p.append_indptr = a->append_indptr;
+  p.kv = static_cast<__nv_bfloat16*>(a->kv_cache);
+  p.num_pages_total = a->num_pages_total;
+  p.page_indices = a->page_indices;
+  p.page_indptr = a->page_indptr;
+  p.last_page_len = a->last_page_len;
+  p.num_rows = a->num_rows;
+  p.num_kv_heads = a->num_kv_heads;
+  p.status = a->status;
+  const int64_t warps = a->num_tokens * a->num_kv_heads;
+  const int64_t blocks = (warps * 32 + 255) / 256;
+  aspire_append_kv_kernel<<<static_cast<unsigned>(blocks), 256, 0,
+                            static_cast<cudaStream_t>(stream)>>>(p);
+  return check_cuda(cudaGetLastError(), "aspire_append_kv_kernel launch");
+}
+
+int aspire_select_pages(const AspireSelectArgs* a, void* stream) {
+  clear_error();
+  if (!a) return set_error(ASPIRE_ERR_INVALID, "aspire_select_pages: null argument");
+  if (a->batch <= 0) return ASPIRE_OK;
+  if (a->page_size != kPageSize)
+    return set_error(ASPIRE_ERR_INVALID, "aspire_select_pages: page_size must be 16");
+  if (!a->num_pages || !a->block_table || !a->table_out || !a->counts_out)
+    return set_error(ASPIRE_ERR_INVALID, "aspire_select_pages: null pointer");
+  if (!a->scores_in && (!a->dump || !a->lse || !a->qo_indptr))
+    return set_error(ASPIRE_ERR_INVALID,
+                     "aspire_select_pages: dump, lse and qo_indptr are required without scores_in");
+  if (a->num_heads <= 0 || a->num_heads > kMaxSelHeads)
+    return set_error(ASPIRE_ERR_INVALID, "aspire_select_pages: num_heads must be in [1, 128]");
+  if (a->pages_per_slot <= 0 || a->subset_cache_size <= 0 || a->L < 0)
+    return set_error(ASPIRE_ERR_INVALID, "aspire_select_pages: bad pages_per_slot / k / L");
+  if (a->subset_cache_size > a->pages_per_slot)
+    return set_error(ASPIRE_ERR_INVALID,
+                     "aspire_select_pages: subset_cache_size exceeds pages_per_slot (topk would fail)");
+  if (!a->scores_in && a->max_seq_len > a->kv_stride)
+    return set_error(ASPIRE_ERR_INVALID, "aspire_select_pages: max_seq_len exceeds kv_stride");
+  if (!a->scores_in && int64_t(a->pages_per_slot) * kPageSize < a->max_seq_len)
+    return set_error(ASPIRE_ERR_INVALID, "aspire_select_pages: pages_per_slot*16 < max_seq_len");
+  SelectParams p;
+  p.dump = reinterpret_cast<const __half*>(a->dump);
+  p.kv_stride = a->kv_stride;
+  p.max_seq_len = a->max_seq_len;
+  p.lse = a->lse;
+  p.lse_rows = a->lse_rows;
+  p.qo_indptr = a->qo_indptr;
+  p.row_ids = a->row_ids;
+  p.scores_in = a->scores_in;
+  p.num_pages = a->num_pages;
+  p.block_table = a->block_table;
+  p.block_table_stride = a->block_table_stride;
+  p.num_heads = a->num_heads;
+  p.pages_per_slot = a->pages_per_slot;
+  p.L = a->L;
+  p.subset_cache_size = a->subset_cache_size;
+  p.min_draft_pages = a->min_draft_pages;
+  p.draft_percent = a->draft_percent;
+  const int hd = a->head_dim > 0 ? a->head_dim : kHeadDim;
+  const double sm = a->sm_scale > 0.f ? double(a->sm_scale) : 1.0 / std::sqrt(double(hd));
+  // PageSelector keeps sm_scale * log2(e) as a Python float (double); the
+  // fp16 tensor multiply then uses it as an fp32 scalar.
+  p.scale_log2 = static_cast<float>(sm * 1.4426950408889634);
+  p.table_out = a->table_out;
+  p.table_stride = a->table_stride;
+  p.table_width = a->table_width;
+  p.counts_out = a->counts_out;
+  p.scores_out = a->scores_out;
+  p.status = a->status;
+  int cap = 1;
+  while (cap < std::min(a->pages_per_slot, a->subset_cache_size)) cap <<= 1;
+  p.sort_cap = cap;
+  const size_t smem = select_smem_bytes(a->pages_per_slot, cap);
+  if (smem > 200 * 1024)
+    return set_error(ASPIRE_ERR_CAPACITY, "aspire_select_pages: pages_per_slot too large");
+  static thread_local int sel_smem_cfg = 48 * 1024;
+  int rc = ensure_smem(reinterpret_cast<const void*>(&aspire_select_pages_kernel), smem, &sel_smem_cfg);
+  if (rc) return rc;
+  aspire_select_pages_kernel<<<a->batch, kSelThreads, smem, static_cast<cudaStream_t>(stream)>>>(p);
+  return check_cuda(cudaGetLastError(), "aspire_select_pages_kernel launch");
+}
+
+}  // extern "C"

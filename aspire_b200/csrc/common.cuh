@@ -1,0 +1,72 @@
+// Shared definitions of libaspire_b200: plan layout, work items, helpers.
+#pragma once
+
+#include <cstdint>
+#include <cstddef>
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include "../../include/aspire_b200.h"
+
+namespace aspire {
+
+constexpr int kHeadDim = 128;
+constexpr int kPageSize = 16;
+
+// The int workspace starts with a 256-byte control block (status word at
+// offset 0); the uploaded plan follows it.
+constexpr size_t kStatusBytes = 256;
+
+// Plan header (int32 words at the start of the plan).
+enum PlanHeader : int {
+  kHdrMagic = 0,
+  kHdrNumItems = 1,
+  kHdrNumGatherCtas = 2,     // grid of the gather kernel the list was built for
+  kHdrOffGatherIndptr = 3,   // int32 index of gather CTA indptr [num_ctas + 1]
+  kHdrOffTcIndptr = 4,       // int32 index of tcgen05 CTA indptr [num_ctas + 1]
+  kHdrOffItems = 5,          // int32 index of the item array
+  kHdrOffCounters = 6,       // int32 index of the merge counters [num_merge]
+  kHdrNumMerge = 7,
+  kHdrPartialLseLo = 8,      // float index of the partial LSE array (lo/hi words)
+  kHdrPartialLseHi = 9,
+  kHdrCausal = 10,
+  kHdrNumTcCtas = 11,        // grid of the tcgen05 kernel the list was built for
+  kHdrWords = 16,
+};
+constexpr int32_t kPlanMagic = 0x41535042;  // "ASPB"
+
+// One unit of work: a KV chunk of one (request row, KV head, packed-query tile).
+struct WorkItem {
+  int32_t row;           // request index (also the dump batch index)
+  int32_t kv_head;
+  int32_t q_start;       // first query token of the request
+  int32_t q_len;         // query tokens of the request
+  int32_t kv_page_base;  // offset of the request's page list in kv_indices
+  int32_t kv_len;        // KV tokens attended by the request
+  int32_t tok_begin;     // KV token range of this chunk
+  int32_t tok_end;
+  int32_t pq_begin;      // packed query rows [pq_begin, pq_end); packed = q_idx*group + g
+  int32_t pq_end;
+  int32_t chunk;         // chunk index within the merge group
+  int32_t n_chunks;
+  int32_t partial_base;  // partial row of chunk 0 of the merge group
+  int32_t merge_id;      // counter index, -1 when n_chunks == 1
+  int32_t kind;          // 0 = CUDA-core gather kernel, 1 = tcgen05 kernel
+  int32_t reserved;
+};
+static_assert(sizeof(WorkItem) == 64, "WorkItem must stay 64 bytes");
+
+constexpr int kItemWords = sizeof(WorkItem) / 4;
+
+// Resident CTAs per SM of each kernel class (sets the persistent grids).
+constexpr int kGatherCtasPerSm = 4;
+constexpr int kTcCtasPerSm = 1;
+
+// Packed query rows handled by one gather-kernel item.
+constexpr int kGatherQTile = 4;
+// Packed query rows handled by one tcgen05 item (N of the MMA after padding).
+constexpr int kTcQTile = 64;
+
+}  // namespace aspire

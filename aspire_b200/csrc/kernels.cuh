@@ -1,0 +1,60 @@
+// Parameter blocks and declarations of every kernel of libaspire_b200.
+#pragma once
+
+#include "attn_common.cuh"
+
+namespace aspire {
+
+struct AppendParams {
+  const __nv_bfloat16* k;
+  const __nv_bfloat16* v;
+  int64_t k_stride_n, k_stride_h, v_stride_n, v_stride_h;
+  int64_t num_tokens;
+  const int32_t* append_indptr;
+  __nv_bfloat16* kv;
+  int64_t num_pages_total;
+  const int32_t* page_indices;
+  const int32_t* page_indptr;
+  const int32_t* last_page_len;
+  int32_t num_rows;
+  int32_t num_kv_heads;
+  uint32_t* status;
+};
+
+struct SelectParams {
+  const __half* dump;
+  int64_t kv_stride, max_seq_len;
+  const float* lse;
+  int64_t lse_rows;
+  const int32_t* qo_indptr;
+  const int32_t* row_ids;
+  const float* scores_in;
+  const int32_t* num_pages;
+  const int32_t* block_table;
+  int64_t block_table_stride;
+  int32_t num_heads, pages_per_slot, L, subset_cache_size, min_draft_pages;
+  float draft_percent;
+  float scale_log2;
+  int32_t* table_out;
+  int64_t table_stride;
+  int32_t table_width;
+  int32_t* counts_out;
+  float* scores_out;
+  uint32_t* status;
+  int32_t sort_cap;  // power of two >= pages_per_slot
+};
+
+constexpr int kSelThreads = 512;
+constexpr int kMaxSelHeads = 128;
+
+__global__ void aspire_attn_gather_kernel(AttnParams p);
+__global__ void aspire_attn_tc_kernel(AttnParams p);
+__global__ void aspire_append_kv_kernel(AppendParams p);
+__global__ void aspire_select_pages_kernel(SelectParams p);
+
+size_t gather_smem_bytes();
+size_t tc_smem_bytes();
+bool tc_kernel_available();
+size_t select_smem_bytes(int pages_per_slot, int sort_cap);
+
+}  // namespace aspire

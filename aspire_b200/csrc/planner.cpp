@@ -1,0 +1,235 @@
+// Host work-list planner for the mixed paged attention.
+//
+// Stands in for FlashInfer's TwoStageHolisticPlan as called from
+// HolisticAttentionWrapper.plan / plan_host (aspire/attention/
+// holistic_wrapper.py:253-265, :323-335).  The planner is a different
+// design: every (request row, KV head, packed-query tile) is cut into
+// split-KV chunks of a common length chosen so that the persistent grid
+// gets several items per CTA, and items are placed on CTAs longest-first
+// onto the least-loaded CTA (LPT).  Rows whose packed query tile is wide
+// (verify rows) go to the tcgen05 kernel; narrow rows (draft / decode
+// rows) go to the CUDA-core gather kernel.
+#include <algorithm>
+#include <cstring>
+#include <numeric>
+#include <queue>
+#include <string>
+#include <vector>
+
+#include "common.cuh"
+#include "errors.h"
+
+namespace aspire {
+
+namespace {
+
+struct GroupDesc {
+  int32_t row, kv_head, q_start, q_len, kv_page_base, kv_len, pq_begin, pq_end, kind;
+};
+
+// Item cost in "tokens": the KV tokens streamed plus a fixed per-item
+// overhead covering setup, Q load and the epilogue.
+inline int64_t item_cost(const WorkItem& it) {
+  return int64_t(it.tok_end - it.tok_begin) + 96;
+}
+
+void assign_lpt(std::vector<WorkItem>& items, int num_ctas, std::vector<int32_t>& indptr,
+                std::vector<WorkItem>& ordered) {
+  indptr.assign(num_ctas + 1, 0);
+  ordered.clear();
+  if (items.empty()) return;
+  std::vector<int> order(items.size());
+  std::iota(order.begin(), order.end(), 0);
+  std::stable_sort(order.begin(), order.end(), [&](int a, int b) {
+    return item_cost(items[a]) > item_cost(items[b]);
+  });
+  using Load = std::pair<int64_t, int>;  // (load, cta)
+  std::priority_queue<Load, std::vector<Load>, std::greater<Load>> heap;
+  for (int c = 0; c < num_ctas; ++c) heap.push({0, c});
+  std::vector<std::vector<int>> per_cta(num_ctas);
+  for (int idx : order) {
+    Load top = heap.top();
+    heap.pop();
+    per_cta[top.second].push_back(idx);
+    top.first += item_cost(items[idx]);
+    heap.push(top);
+  }
+  ordered.reserve(items.size());
+  for (int c = 0; c < num_ctas; ++c) {
+    indptr[c] = static_cast<int32_t>(ordered.size());
+    for (int idx : per_cta[c]) ordered.push_back(items[idx]);
+  }
+  indptr[num_ctas] = static_cast<int32_t>(ordered.size());
+}
+
+}  // namespace
+
+int plan_impl(const int32_t* qo_indptr, const int32_t* kv_indptr, const int32_t* kv_len,
+              int32_t batch_size, int32_t num_qo_heads, int32_t num_kv_heads, int32_t head_dim,
+              int32_t page_size, int32_t causal, int32_t num_sms, bool tc_enabled,
+              void* host_buf, size_t host_buf_bytes, size_t float_ws_bytes,
+              AspirePlanInfo* info) {
+  if (!qo_indptr || !kv_indptr || !kv_len || !host_buf || !info)
+    return set_error(ASPIRE_ERR_INVALID, "aspire_plan: null pointer argument");
+  if (batch_size < 0) return set_error(ASPIRE_ERR_INVALID, "aspire_plan: batch_size < 0");
+  if (head_dim != kHeadDim)
+    return set_error(ASPIRE_ERR_INVALID, "aspire_plan: head_dim must be 128, got " +
+                                             std::to_string(head_dim));
+  if (page_size != kPageSize)
+    return set_error(ASPIRE_ERR_INVALID, "aspire_plan: page_size must be 16, got " +
+                                             std::to_string(page_size));
+  if (num_kv_heads <= 0 || num_qo_heads <= 0 || num_qo_heads % num_kv_heads != 0)
+    return set_error(ASPIRE_ERR_INVALID,
+                     "aspire_plan: num_qo_heads must be a positive multiple of num_kv_heads");
+  if (num_sms <= 0) return set_error(ASPIRE_ERR_INVALID, "aspire_plan: num_sms must be > 0");
+  const int gather_ctas = num_sms * kGatherCtasPerSm;
+  const int tc_ctas = num_sms * kTcCtasPerSm;
+  const int group = num_qo_heads / num_kv_heads;
+
+  // Rows -> (row, head, q-tile) groups.
+  std::vector<GroupDesc> groups;
+  int64_t total_tokens = 0;
+  int32_t max_q_len = 0;
+  for (int b = 0; b < batch_size; ++b) {
+    const int32_t q0 = qo_indptr[b], q1 = qo_indptr[b + 1];
+    const int32_t ql = q1 - q0;
+    if (ql < 0) return set_error(ASPIRE_ERR_INVALID, "aspire_plan: qo_indptr not monotonic");
+    if (ql == 0) continue;
+    const int32_t kl = kv_len[b];
+    if (kl < 0) return set_error(ASPIRE_ERR_INVALID, "aspire_plan: negative kv_len");
+    const int64_t pages_avail = int64_t(kv_indptr[b + 1]) - kv_indptr[b];
+    if (int64_t(kl) > pages_avail * kPageSize && kl > 0) {
+      // The page list must cover kv_len tokens.  (The dump program of the
+      // reference passes a constant-stride indptr that over-covers; that is
+      // fine.  Under-coverage would read foreign pages.)
+      return set_error(ASPIRE_ERR_INVALID,
+                       "aspire_plan: row " + std::to_string(b) + " kv_len " + std::to_string(kl) +
+                           " exceeds its page list (" + std::to_string(pages_avail) + " pages)");
+    }
+    max_q_len = std::max(max_q_len, ql);
+    const int32_t nq = ql * group;
+    const bool wide = tc_enabled && nq > kGatherQTile;
+    const int tile = wide ? kTcQTile : kGatherQTile;
+    for (int h = 0; h < num_kv_heads; ++h) {
+      for (int p0 = 0; p0 < nq; p0 += tile) {
+        GroupDesc g{b, h, q0, ql, kv_indptr[b], kl, p0, std::min(nq, p0 + tile), wide ? 1 : 0};
+        groups.push_back(g);
+        total_tokens += std::max<int32_t>(kl, 1);
+      }
+    }
+  }
+
+  // Common chunk length: several items per CTA, never below 512 tokens,
+  // a multiple of 128 tokens (one tcgen05 KV tile = 8 pages).
+  const int64_t target_items = int64_t(num_sms) * 4;
+  int64_t chunk = (total_tokens + target_items - 1) / std::max<int64_t>(target_items, 1);
+  chunk = std::max<int64_t>(chunk, 512);
+  chunk = (chunk + 127) / 128 * 128;
+
+  std::vector<WorkItem> gather_items, tc_items;
+  int32_t num_merge = 0;
+  int64_t partial_rows = 0;
+  for (const GroupDesc& g : groups) {
+    const int32_t n_chunks =
+        g.kv_len > 0 ? static_cast<int32_t>((g.kv_len + chunk - 1) / chunk) : 1;
+    const int32_t rows = g.pq_end - g.pq_begin;
+    int32_t merge_id = -1, partial_base = 0;
+    if (n_chunks > 1) {
+      merge_id = num_merge++;
+      if (partial_rows + int64_t(n_chunks) * rows > INT32_MAX)
+        return set_error(ASPIRE_ERR_CAPACITY, "aspire_plan: too many partial rows");
+      partial_base = static_cast<int32_t>(partial_rows);
+      partial_rows += int64_t(n_chunks) * rows;
+    }
+    for (int32_t c = 0; c < n_chunks; ++c) {
+      WorkItem it{};
+      it.row = g.row;
+      it.kv_head = g.kv_head;
+      it.q_start = g.q_start;
+      it.q_len = g.q_len;
+      it.kv_page_base = g.kv_page_base;
+      it.kv_len = g.kv_len;
+      it.tok_begin = static_cast<int32_t>(std::min<int64_t>(int64_t(c) * chunk, g.kv_len));
+      it.tok_end = static_cast<int32_t>(std::min<int64_t>(int64_t(c + 1) * chunk, g.kv_len));
+      it.pq_begin = g.pq_begin;
+      it.pq_end = g.pq_end;
+      it.chunk = c;
+      it.n_chunks = n_chunks;
+      it.partial_base = partial_base;
+      it.merge_id = merge_id;
+      it.kind = g.kind;
+      (g.kind ? tc_items : gather_items).push_back(it);
+    }
+  }
+
+  std::vector<int32_t> gather_indptr, tc_indptr;
+  std::vector<WorkItem> gather_ordered, tc_ordered;
+  assign_lpt(gather_items, gather_ctas, gather_indptr, gather_ordered);
+  assign_lpt(tc_items, tc_ctas, tc_indptr, tc_ordered);
+  // The tcgen05 list is stored after the gather list in one item array.
+  const int32_t n_gather = static_cast<int32_t>(gather_ordered.size());
+  for (auto& v : tc_indptr) v += n_gather;
+  const int32_t num_items = n_gather + static_cast<int32_t>(tc_ordered.size());
+
+  // Layout (int32 words): header | gather indptr | tc indptr | items | counters.
+  const int64_t off_gather = kHdrWords;
+  const int64_t off_tc = off_gather + gather_ctas + 1;
+  int64_t off_items = off_tc + tc_ctas + 1;
+  off_items = (off_items + 15) / 16 * 16;  // 64-byte aligned items
+  const int64_t off_counters = off_items + int64_t(num_items) * kItemWords;
+  const int64_t total_words = off_counters + num_merge;
+  const int64_t int_bytes = total_words * 4;
+  if (size_t(int_bytes) > host_buf_bytes)
+    return set_error(ASPIRE_ERR_CAPACITY, "aspire_plan: plan needs " + std::to_string(int_bytes) +
+                                              " bytes, host buffer has " +
+                                              std::to_string(host_buf_bytes));
+  const int64_t float_bytes = partial_rows * (kHeadDim + 1) * 4;
+  if (size_t(float_bytes) > float_ws_bytes)
+    return set_error(ASPIRE_ERR_CAPACITY,
+                     "aspire_plan: split-KV partials need " + std::to_string(float_bytes) +
+                         " bytes of float workspace, have " + std::to_string(float_ws_bytes));
+
+  int32_t* w = static_cast<int32_t*>(host_buf);
+  std::memset(w, 0, kHdrWords * 4);
+  w[kHdrMagic] = kPlanMagic;
+  w[kHdrNumItems] = num_items;
+  w[kHdrNumGatherCtas] = gather_ctas;
+  w[kHdrNumTcCtas] = tc_ctas;
+  w[kHdrCausal] = causal ? 1 : 0;
+  w[kHdrOffGatherIndptr] = static_cast<int32_t>(off_gather);
+  w[kHdrOffTcIndptr] = static_cast<int32_t>(off_tc);
+  w[kHdrOffItems] = static_cast<int32_t>(off_items);
+  w[kHdrOffCounters] = static_cast<int32_t>(off_counters);
+  w[kHdrNumMerge] = num_merge;
+  const int64_t lse_off = partial_rows * kHeadDim;
+  w[kHdrPartialLseLo] = static_cast<int32_t>(lse_off & 0xffffffff);
+  w[kHdrPartialLseHi] = static_cast<int32_t>(lse_off >> 32);
+  std::memcpy(w + off_gather, gather_indptr.data(), size_t(gather_ctas + 1) * 4);
+  std::memcpy(w + off_tc, tc_indptr.data(), size_t(tc_ctas + 1) * 4);
+  for (int64_t i = off_tc + tc_ctas + 1; i < off_items; ++i) w[i] = 0;
+  if (n_gather) std::memcpy(w + off_items, gather_ordered.data(), size_t(n_gather) * sizeof(WorkItem));
+  if (!tc_ordered.empty())
+    std::memcpy(w + off_items + int64_t(n_gather) * kItemWords, tc_ordered.data(),
+                tc_ordered.size() * sizeof(WorkItem));
+  std::memset(w + off_counters, 0, size_t(num_merge) * 4);
+
+  std::memset(info, 0, sizeof(*info));
+  info->num_items = num_items;
+  info->num_items_gather = n_gather;
+  info->num_items_tc = num_items - n_gather;
+  info->num_ctas = num_sms;
+  info->num_merge = num_merge;
+  info->chunk_tokens = static_cast<int32_t>(chunk);
+  info->partial_rows = partial_rows;
+  info->int_bytes = int_bytes;
+  info->float_bytes = float_bytes;
+  info->num_qo_heads = num_qo_heads;
+  info->num_kv_heads = num_kv_heads;
+  info->causal = causal ? 1 : 0;
+  info->batch_size = batch_size;
+  info->max_q_len = max_q_len;
+  info->tc_enabled = tc_enabled ? 1 : 0;
+  return ASPIRE_OK;
+}
+
+}  // namespace aspire

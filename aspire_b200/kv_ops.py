@@ -1,0 +1,94 @@
+"""Paged KV append: drop-in for ``mylib::update_kv_padded``.
+
+Same schema and error behaviour as ``aspire/attention/kv_ops.py:127-187``:
+``(Tensor k, Tensor v, Tensor kv_append_indptr, Tensor(a!) kv_cache,
+Tensor kv_page_indices, Tensor kv_page_indptr, Tensor kv_last_page_len,
+int page_size) -> ()``; non-contiguous k/v heads raise ``ValueError``.
+Registered as ``aspire_b200::update_kv_padded`` with a fake implementation
+so ``torch.compile(fullgraph=True)`` can trace it.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _capi
+
+
+def append_kv(
+    k: torch.Tensor,
+    v: torch.Tensor,
+    kv_append_indptr: torch.Tensor,
+    kv_cache: torch.Tensor,
+    kv_page_indices: torch.Tensor,
+    kv_page_indptr: torch.Tensor,
+    kv_last_page_len: torch.Tensor,
+    page_size: int,
+    status: torch.Tensor | None = None,
+) -> None:
+    """Writes the step's new K/V rows into their pages (C ABI ``aspire_append_kv``)."""
+    total_tokens = k.shape[0]
+    if total_tokens == 0:
+        return
+    head_dim = k.shape[2]
+    num_heads = k.shape[1]
+    if k.stride(-1) != 1 or v.stride(-1) != 1:
+        raise ValueError("update_kv_padded requires contiguous k/v head dimensions")
+    if k.stride(1) != head_dim or v.stride(1) != head_dim:
+        raise ValueError("update_kv_padded requires contiguous k/v heads")
+    if kv_cache.stride(-1) != 1:
+        raise ValueError("update_kv_padded requires a contiguous cache head dimension")
+    if not kv_cache.is_contiguous():
+        raise ValueError("aspire_b200 append requires a contiguous [pages, 2, page, heads, dim] cache")
+    if k.dtype != torch.bfloat16 or v.dtype != torch.bfloat16 or kv_cache.dtype != torch.bfloat16:
+        raise ValueError("aspire_b200 append requires bfloat16 k, v and kv_cache")
+    for name, t in (("kv_append_indptr", kv_append_indptr), ("kv_page_indices", kv_page_indices),
+                    ("kv_page_indptr", kv_page_indptr), ("kv_last_page_len", kv_last_page_len)):
+        if t.dtype != torch.int32 or not t.is_contiguous():
+            raise ValueError(f"{name} must be a contiguous int32 tensor")
+    num_rows = kv_last_page_len.shape[0]
+    if kv_append_indptr.shape[0] < num_rows + 1 or kv_page_indptr.shape[0] < num_rows + 1:
+        raise ValueError("kv_append_indptr / kv_page_indptr need len(kv_last_page_len) + 1 entries")
+    a = _capi.AspireAppendArgs()
+    a.k = k.data_ptr()
+    a.v = v.data_ptr()
+    a.k_stride_n, a.k_stride_h = k.stride(0), k.stride(1)
+    a.v_stride_n, a.v_stride_h = v.stride(0), v.stride(1)
+    a.num_tokens = total_tokens
+    a.append_indptr = kv_append_indptr.data_ptr()
+    a.kv_cache = kv_cache.data_ptr()
+    a.num_pages_total = kv_cache.shape[0]
+    a.page_indices = kv_page_indices.data_ptr()
+    a.page_indptr = kv_page_indptr.data_ptr()
+    a.last_page_len = kv_last_page_len.data_ptr()
+    a.num_rows = num_rows
+    a.num_kv_heads = num_heads
+    a.head_dim = head_dim
+    a.page_size = int(page_size)
+    a.status = status.data_ptr() if status is not None else None
+    stream = torch.cuda.current_stream(k.device).cuda_stream
+    rc = _capi.load_library().aspire_append_kv(ctypes.byref(a), ctypes.c_void_p(stream))
+    _capi.check(rc, "aspire_append_kv")
+
+
+torch.library.define(
+    "aspire_b200::update_kv_padded",
+    "(Tensor k, Tensor v, Tensor kv_append_indptr, Tensor(a!) kv_cache, "
+    "Tensor kv_page_indices, Tensor kv_page_indptr, Tensor kv_last_page_len, "
+    "int page_size) -> ()",
+)
+
+
+@torch.library.impl("aspire_b200::update_kv_padded", "cuda")
+def update_kv_padded(k, v, kv_append_indptr, kv_cache, kv_page_indices, kv_page_indptr,
+                     kv_last_page_len, page_size):
+    append_kv(k, v, kv_append_indptr, kv_cache, kv_page_indices, kv_page_indptr,
+              kv_last_page_len, page_size)
+
+
+@torch.library.register_fake("aspire_b200::update_kv_padded")
+def _update_kv_padded_fake(k, v, kv_append_indptr, kv_cache, kv_page_indices, kv_page_indptr,
+                           kv_last_page_len, page_size):
+    return None

@@ -1,0 +1,166 @@
+"""Page selection on the GPU: drop-in for ``PageSelectorFirstLastAvg``.
+
+Same constructor and ``compute_valid_counts`` / ``select`` /
+``select_subset`` / ``select_from_compact_first_last`` surface as
+``aspire/backends/page_selector.py:9-233``; scoring and top-k run as one
+fused kernel per call (``aspire_select_pages``) instead of ~20 torch ops.
+
+``select`` returns ``(selected[B, k] int32, valid_counts[B] int32)`` with the
+reference's layout: the valid prefix of each row holds the selected
+block-table ids in ascending order and the tail is zero.  ``select_into``
+writes the same rows straight into the caller's draft table and count
+buffer, fusing ``LMBackendBase._store_draft_rows`` (``base.py:1421-1471``)
+into the selection kernel, as ``_whole_batch_replan_impl`` (``base.py:648-667``)
+uses it.  Ties between equal page scores are broken by the lower page index.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import math
+from typing import Optional, Tuple
+
+import torch
+
+from . import _capi
+
+
+class PageSelectorFirstLastAvg:
+    """First/last verify-token page selector backed by libaspire_b200."""
+
+    def __init__(self, max_batch_size, pages_per_slot, subset_cache_size, L, n_heads, page_size,
+                 max_seq_length, device, bsz, dec_len, head_dim=128, kv_stride=None,
+                 draft_percent=None, min_draft_pages=None):
+        self._lib = _capi.load_library()
+        self.subset_cache_size = int(subset_cache_size)
+        self.L = int(L)
+        self._min_draft_pages = min_draft_pages
+        self.n_heads = int(n_heads)
+        self.page_size = int(page_size)
+        self.max_seq_length = int(max_seq_length)
+        self._kv_stride = int(kv_stride or max_seq_length)
+        self.pages_per_slot = int(pages_per_slot)
+        self.device = torch.device(device)
+        self._draft_percent = draft_percent
+        self._bsz = int(bsz)
+        self._dec_len = dec_len
+        self._head_dim = int(head_dim)
+        self._sm_scale = 1.0 / math.sqrt(head_dim)
+        self._max_batch = int(max_batch_size)
+        k = self.subset_cache_size
+        self._selected_buf = torch.zeros(max_batch_size, max(k, 1), dtype=torch.int32, device=self.device)
+        self._valid_counts_buf = torch.zeros(max_batch_size, dtype=torch.int32, device=self.device)
+        self._scores = torch.empty(max_batch_size, pages_per_slot, dtype=torch.float32, device=self.device)
+
+    # --------------------------------------------------------------- helpers
+    def compute_valid_counts(self, num_pages: torch.Tensor) -> torch.Tensor:
+        """Per-request draft page count (``page_selector.py:52-62``)."""
+        hi = num_pages.clamp(max=self.subset_cache_size).to(torch.int32)
+        if self._draft_percent is None:
+            if self._min_draft_pages is not None:
+                return num_pages.clamp(max=self._min_draft_pages).to(torch.int32)
+            return hi
+        floor = self._min_draft_pages if self._min_draft_pages is not None else self.L
+        lo = num_pages.clamp(max=floor).to(torch.int32)
+        target = (num_pages.float() * self._draft_percent / 100).ceil_().to(torch.int32)
+        return torch.clamp(target, lo, hi)
+
+    def _launch(self, *, dump, lse, qo_indptr, row_ids, scores_in, num_pages, block_table, batch,
+                table_out, table_width, counts_out, scores_out=None, status=None):
+        def ptr(t):
+            return t.data_ptr() if t is not None else None
+
+        for name, t in (("num_pages", num_pages), ("block_table", block_table), ("table_out", table_out),
+                        ("counts_out", counts_out), ("qo_indptr", qo_indptr), ("row_ids", row_ids)):
+            if t is not None and t.dtype != torch.int32:
+                raise ValueError(f"{name} must be int32, got {t.dtype}")
+        if block_table.stride(1) != 1 or table_out.stride(1) != 1:
+            raise ValueError("block_table and table rows must be contiguous")
+        a = _capi.AspireSelectArgs()
+        a.dump = ptr(dump)
+        a.kv_stride = self._kv_stride
+        a.max_seq_len = self.max_seq_length
+        a.lse = ptr(lse)
+        a.lse_rows = lse.shape[0] if lse is not None else 0
+        a.qo_indptr = ptr(qo_indptr)
+        a.row_ids = ptr(row_ids)
+        a.scores_in = ptr(scores_in)
+        a.num_pages = num_pages.data_ptr()
+        a.block_table = block_table.data_ptr()
+        a.block_table_stride = block_table.stride(0)
+        a.batch = int(batch)
+        a.num_heads = self.n_heads
+        a.page_size = self.page_size
+        a.pages_per_slot = self.pages_per_slot
+        a.L = self.L
+        a.subset_cache_size = self.subset_cache_size
+        a.min_draft_pages = -1 if self._min_draft_pages is None else int(self._min_draft_pages)
+        a.draft_percent = -1.0 if self._draft_percent is None else float(self._draft_percent)
+        a.sm_scale = self._sm_scale
+        a.head_dim = self._head_dim
+        a.table_out = table_out.data_ptr()
+        a.table_stride = table_out.stride(0)
+        a.table_width = int(table_width)
+        a.counts_out = counts_out.data_ptr()
+        a.scores_out = ptr(scores_out)
+        a.status = ptr(status)
+        stream = torch.cuda.current_stream(self.device).cuda_stream
+        _capi.check(self._lib.aspire_select_pages(ctypes.byref(a), ctypes.c_void_p(stream)),
+                    "aspire_select_pages")
+
+    def _contig_i32(self, t: torch.Tensor) -> torch.Tensor:
+        t = t.to(device=self.device, dtype=torch.int32)
+        return t if t.is_contiguous() else t.contiguous()
+
+    # ------------------------------------------------------------------ API
+    def select(self, attention_weights_buffer, lse_buffer, num_pages, block_table, qo_indptr,
+               scores_out: Optional[torch.Tensor] = None) -> Tuple[torch.Tensor, torch.Tensor]:
+        """Whole-batch selection (``page_selector.py:206-214``)."""
+        B = self._bsz
+        sel = self._selected_buf[:B]
+        counts = self._valid_counts_buf[:B]
+        self._launch(dump=attention_weights_buffer, lse=lse_buffer, qo_indptr=self._contig_i32(qo_indptr),
+                     row_ids=None, scores_in=None, num_pages=self._contig_i32(num_pages[:B]),
+                     block_table=self._contig_i32(block_table), batch=B, table_out=sel,
+                     table_width=self.subset_cache_size, counts_out=counts, scores_out=scores_out)
+        return sel, counts
+
+    def select_into(self, table, count_buffer, attention_weights_buffer, lse_buffer, num_pages,
+                    block_table, qo_indptr, batch: Optional[int] = None,
+                    scores_out: Optional[torch.Tensor] = None, status: Optional[torch.Tensor] = None):
+        """Selection written in place into ``table[:B]`` / ``count_buffer[:B]`` (zero tail)."""
+        B = self._bsz if batch is None else int(batch)
+        self._launch(dump=attention_weights_buffer, lse=lse_buffer, qo_indptr=self._contig_i32(qo_indptr),
+                     row_ids=None, scores_in=None, num_pages=self._contig_i32(num_pages[:B]),
+                     block_table=self._contig_i32(block_table), batch=B, table_out=table,
+                     table_width=table.shape[1], counts_out=count_buffer, scores_out=scores_out,
+                     status=status)
+
+    def select_subset(self, slot_ids, attention_weights_buffer, lse_buffer, num_pages, block_table,
+                      qo_indptr) -> Tuple[torch.Tensor, torch.Tensor]:
+        """Selection for a subset of slots (``page_selector.py:216-233``)."""
+        if slot_ids.numel() == 0:
+            empty = block_table.new_empty((0, self.subset_cache_size), dtype=torch.int32)
+            return empty, torch.zeros(0, dtype=torch.int32, device=self.device)
+        ids = slot_ids.to(device=self.device, dtype=torch.long)
+        n = ids.numel()
+        sel = torch.zeros(n, self.subset_cache_size, dtype=torch.int32, device=self.device)
+        counts = torch.zeros(n, dtype=torch.int32, device=self.device)
+        self._launch(dump=attention_weights_buffer, lse=lse_buffer, qo_indptr=self._contig_i32(qo_indptr),
+                     row_ids=self._contig_i32(ids), scores_in=None,
+                     num_pages=self._contig_i32(num_pages[ids]), block_table=self._contig_i32(block_table[ids]),
+                     batch=n, table_out=sel, table_width=self.subset_cache_size, counts_out=counts)
+        return sel, counts
+
+    def finalize_scores(self, scores: torch.Tensor, num_pages: torch.Tensor,
+                        block_table: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
+        """Top-k stage alone from raw fp32 page scores (``page_selector.py:79-108``)."""
+        n = scores.shape[0]
+        if scores.dtype != torch.float32 or not scores.is_contiguous() or scores.shape[1] != self.pages_per_slot:
+            raise ValueError("scores must be contiguous fp32 [batch, pages_per_slot]")
+        sel = torch.zeros(n, self.subset_cache_size, dtype=torch.int32, device=self.device)
+        counts = torch.zeros(n, dtype=torch.int32, device=self.device)
+        self._launch(dump=None, lse=None, qo_indptr=None, row_ids=None, scores_in=scores,
+                     num_pages=self._contig_i32(num_pages), block_table=self._contig_i32(block_table),
+                     batch=n, table_out=sel, table_width=self.subset_cache_size, counts_out=counts)
+        return sel, counts

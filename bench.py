@@ -1,0 +1,464 @@
+"""Benchmark of the unified mixed forward hot path on B200.
+
+One step = one decode step's hot path of a Qwen3-8B-shaped model (config 3 of
+the reference's benchmark list: 36 layers, 32 q / 8 KV heads, head_dim 128,
+batch 64, 32k context, sparse budget 128 pages, refresh layer -2):
+
+  * 35 ordinary layers: paged KV append + mixed draft/verify attention
+    (draft rows: 128 selected pages, q_len 1; verify rows: full context,
+    q_len = U{2..8} + 1, causal);
+  * the refresh layer: append + full-context attention of every row with the
+    first/last logit dump;
+  * page scoring + top-k re-selection written in place into the draft table.
+
+Every layer reads one resident single-layer KV cache (8.7 GB at TP 1, far
+larger than the 126 MB L2, so nothing is served from cache between layers);
+a real model holds 36 such caches, which do not fit one GPU.  Under torchrun
+each rank holds its tensor-parallel share of the heads (KV-head ranges, as
+the reference's aspire/tp.py shards them) for the same batch.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl aspire_b200|reference]
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "mixed-attn HBM GB/s (% of peak); accepted tokens/s per box at 1/2/4/8 B200"
+UNIT = "GB/s"
+
+CFG = dict(model="qwen3-8b-heads", n_layer=36, refresh_layer=34, num_qo_heads=32, num_kv_heads=8, batch=64,
+           ctx=32768, pages_per_row=2080, draft_fraction=0.5, budget_pages=128, L=8, seed=0)
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="aspire_b200", choices=["aspire_b200", "reference"])
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def tp_heads(num_heads: int, rank: int, world: int) -> range:
+    """Contiguous head range of a rank, remainder to the low ranks (aspire/tp.py:35-51)."""
+    base, rem = divmod(num_heads, world)
+    start = rank * base + min(rank, rem)
+    return range(start, start + base + (1 if rank < rem else 0))
+
+
+def measured_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """Samples nvidia-smi clocks and throttle reasons while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu_index = gpu_index
+        self.rows = []
+        self._stop = threading.Event()
+        self._thread = None
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                out = subprocess.run(["nvidia-smi", f"--id={self.gpu_index}", f"--query-gpu={self.FIELDS}",
+                                      "--format=csv,noheader,nounits"], capture_output=True, text=True, timeout=5)
+                for line in out.stdout.strip().splitlines():
+                    self.rows.append([x.strip() for x in line.split(",")])
+            except Exception:
+                pass
+            self._stop.wait(0.2)
+
+    def __enter__(self):
+        self._thread = threading.Thread(target=self._run, daemon=True)
+        self._thread.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._thread:
+            self._thread.join(timeout=10)
+
+    def summary(self):
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = set()
+        for r in self.rows:
+            for name, val in zip(names, r[5:9]):
+                if val.strip().lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(self.rows)}
+
+
+# ----------------------------------------------------------------------------- workload
+def build_workload(device, rank: int, world: int):
+    from aspire_b200.workloads import full_context_layout, make_layout, last_page_lens
+
+    hq_r = tp_heads(CFG["num_qo_heads"], rank, world)
+    hkv_r = tp_heads(CFG["num_kv_heads"], rank, world)
+    hq, hkv = len(hq_r), len(hkv_r)
+    lay = make_layout(batch=CFG["batch"], ctx=CFG["ctx"], num_qo_heads=hq, num_kv_heads=hkv,
+                      draft_fraction=CFG["draft_fraction"], budget_pages=CFG["budget_pages"],
+                      pages_per_row=CFG["pages_per_row"], seed=CFG["seed"])
+    full = full_context_layout(lay)
+    return lay, full, last_page_lens(lay), last_page_lens(full)
+
+
+def step_bytes(lay, full, n_layer: int, kv_stride: int, k: int) -> dict:
+    """Algorithmic bytes of one step (each byte counted once per layer-call)."""
+    hd = 128
+    T = lay.total_q
+    append = T * lay.num_kv_heads * hd * 2 * 2 * 2          # read new K,V + write them
+    mixed = lay.algorithmic_bytes()
+    refresh = full.algorithmic_bytes()
+    dump_write = sum(int(full.kv_lens[b]) * (2 if full.q_lens[b] > 1 else 1) for b in range(full.batch)) \
+        * full.num_qo_heads * 2
+    select = full.batch * full.num_qo_heads * 2 * min(kv_stride, lay.pages_per_row * 16) * 2 \
+        + full.batch * lay.pages_per_row * 4 + full.batch * k * 4 + T * full.num_qo_heads * 4
+    total = (n_layer - 1) * mixed + refresh + n_layer * append + dump_write + select
+    return dict(total=total, mixed=mixed, refresh=refresh, append=append, dump_write=dump_write, select=select)
+
+
+class HotPath:
+    """All device state of the benchmark step, driven through the public API."""
+
+    def __init__(self, device, lay, full, lpl_mixed, lpl_full):
+        from aspire_b200.attention import HolisticAttentionWrapper, first_last_dump_jit_args
+        from aspire_b200.kv_ops import append_kv
+        from aspire_b200.page_selector import PageSelectorFirstLastAvg
+        from aspire_b200.workloads import fill_tensors
+
+        self.append_kv = append_kv
+        self.device = device
+        self.lay, self.full = lay, full
+        n_layer = CFG["n_layer"]
+        T, hq, hkv = lay.total_q, lay.num_qo_heads, lay.num_kv_heads
+        # Inputs: per-layer q and new K/V (rows of the bucket), one resident layer cache.
+        _, self.kv = fill_tensors(lay, device=device, seed=CFG["seed"])
+        g = torch.Generator(device=device)
+        g.manual_seed(CFG["seed"] + 1)
+        self.q = torch.randn(n_layer, T, hq, 128, generator=g, device=device).to(torch.bfloat16)
+        self.k_new = torch.randn(n_layer, T, hkv, 128, generator=g, device=device).to(torch.bfloat16)
+        self.v_new = torch.randn(n_layer, T, hkv, 128, generator=g, device=device).to(torch.bfloat16)
+        self.out = torch.empty_like(self.q)
+        self.lse = torch.empty(T, hq, device=device, dtype=torch.float32)
+        i32 = lambda a: torch.from_numpy(np.ascontiguousarray(a, dtype=np.int32)).to(device)  # noqa: E731
+        self.qo_indptr = i32(lay.qo_indptr)
+        self.mixed_indices, self.mixed_indptr, self.mixed_last = i32(lay.kv_indices), i32(lay.kv_indptr), i32(lpl_mixed)
+        self.full_indices, self.full_indptr, self.full_last = i32(full.kv_indices), i32(full.kv_indptr), i32(lpl_full)
+        self.block_table = i32(lay.block_table)
+        self.num_pages = i32((lay.ctx_lens + 15) // 16)
+        self.kv_stride = lay.pages_per_row * 16
+        self.dump = torch.full((lay.batch * hq * 2 * self.kv_stride,), float("-inf"), dtype=torch.float16,
+                               device=device)
+        self.k_sel = CFG["budget_pages"]
+        self.draft_table = torch.zeros(lay.batch, self.k_sel, dtype=torch.int32, device=device)
+        self.draft_counts = torch.zeros(lay.batch, dtype=torch.int32, device=device)
+        ws = torch.empty(1, device=device)
+        self.mixed = HolisticAttentionWrapper(ws)
+        self.refresh = HolisticAttentionWrapper(ws, jit_args=first_last_dump_jit_args())
+        self.selector = PageSelectorFirstLastAvg(
+            max_batch_size=lay.batch, pages_per_slot=lay.pages_per_row, subset_cache_size=self.k_sel, L=CFG["L"],
+            n_heads=hq, page_size=16, max_seq_length=self.kv_stride, device=device, bsz=lay.batch, dec_len=9,
+            kv_stride=self.kv_stride, draft_percent=None, min_draft_pages=self.k_sel)
+        self.graph = None
+
+    def plan(self):
+        lay, full = self.lay, self.full
+        t = lambda a: torch.from_numpy(np.ascontiguousarray(a, dtype=np.int32))  # noqa: E731
+        self.mixed.plan_host(t(lay.qo_indptr), t(lay.kv_indptr), t(lay.kv_lens), self.mixed_indices,
+                             lay.num_qo_heads, lay.num_kv_heads, 128, 16, causal=True)
+        self.refresh.plan_host(t(full.qo_indptr), t(full.kv_indptr), t(full.kv_lens), self.full_indices,
+                               full.num_qo_heads, full.num_kv_heads, 128, 16, causal=True)
+
+    def step_eager(self):
+        n_layer = CFG["n_layer"]
+        for layer in range(n_layer):
+            if layer == CFG["refresh_layer"]:
+                self.append_kv(self.k_new[layer], self.v_new[layer], self.qo_indptr, self.kv, self.full_indices,
+                               self.full_indptr, self.full_last, 16)
+                self.refresh.run(self.q[layer], self.kv, self.dump, self.lay.num_qo_heads, self.kv_stride,
+                                 out=self.out[layer], lse=self.lse)
+            else:
+                self.append_kv(self.k_new[layer], self.v_new[layer], self.qo_indptr, self.kv, self.mixed_indices,
+                               self.mixed_indptr, self.mixed_last, 16)
+                self.mixed.run(self.q[layer], self.kv, out=self.out[layer])
+        self.selector.select_into(self.draft_table, self.draft_counts, self.dump, self.lse, self.num_pages,
+                                  self.block_table, self.qo_indptr)
+
+    def capture(self):
+        self.step_eager()
+        torch.cuda.synchronize()
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            self.step_eager()
+        torch.cuda.current_stream().wait_stream(s)
+        torch.cuda.synchronize()
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self.step_eager()
+        torch.cuda.synchronize()
+
+    def launches_per_step(self) -> int:
+        # per layer: append + gather attention + tcgen05 attention (when enabled); + selection
+        per_attn = 1 + (1 if self.mixed.plan_info.tc_enabled else 0)
+        return CFG["n_layer"] * (1 + per_attn) + 1
+
+
+def time_device(fn, steps, warmup, dist_on):
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    if dist_on:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(steps):
+        fn()
+    end.record()
+    torch.cuda.synchronize()
+    if dist_on:
+        torch.distributed.barrier()
+    return start.elapsed_time(end) / steps
+
+
+def kernel_roofline(hp: HotPath, steps: int, peak: float, peak_kind: str):
+    """Average duration of the mixed attention launch (CUDA events on its stream)."""
+    q, out = hp.q[0], hp.out[0]
+    for _ in range(3):
+        hp.mixed.run(q, hp.kv, out=out)
+    torch.cuda.synchronize()
+    durs = []
+    stream = torch.cuda.current_stream()
+    for _ in range(max(steps, 5)):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        hp.mixed.run(q, hp.kv, out=out)
+        b.record(stream)
+        durs.append((a, b))
+    torch.cuda.synchronize()
+    ms = statistics.mean(a.elapsed_time(b) for a, b in durs)
+    bytes_ = hp.lay.algorithmic_bytes()
+    achieved = bytes_ / (ms * 1e-3) / 1e9
+    traffic = None
+    tp = ROOT / "profiles" / "traffic.json"
+    if tp.exists():
+        try:
+            traffic = json.loads(tp.read_text()).get("mixed_attention_bytes_per_launch")
+        except Exception:
+            traffic = None
+    return {"kernel": "mixed attention layer-call (aspire_attn_gather_kernel + aspire_attn_tc_kernel)",
+            "bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "peak_source": peak_kind,
+            "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": traffic, "ms_per_launch": round(ms, 4),
+            "algorithmic_bytes_per_launch": int(bytes_)}
+
+
+def e2e_measure(hp: HotPath, steps: int, warmup: int, bytes_per_step: int):
+    """Through the public API with host buffers: H2D of the step's q / new K,V, host
+    planning of both attention programs, the step, D2H of outputs and tables."""
+    q_h = hp.q.cpu().pin_memory()
+    k_h = hp.k_new.cpu().pin_memory()
+    v_h = hp.v_new.cpu().pin_memory()
+    out_h = torch.empty(hp.out.shape, dtype=hp.out.dtype, pin_memory=True)
+    tab_h = torch.empty(hp.draft_table.shape, dtype=torch.int32, pin_memory=True)
+    cnt_h = torch.empty(hp.draft_counts.shape, dtype=torch.int32, pin_memory=True)
+
+    def one():
+        hp.q.copy_(q_h, non_blocking=True)
+        hp.k_new.copy_(k_h, non_blocking=True)
+        hp.v_new.copy_(v_h, non_blocking=True)
+        hp.plan()
+        hp.graph.replay()
+        out_h.copy_(hp.out, non_blocking=True)
+        tab_h.copy_(hp.draft_table, non_blocking=True)
+        cnt_h.copy_(hp.draft_counts, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+
+    for _ in range(warmup):
+        one()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        one()
+    dt = (time.perf_counter() - t0) / steps
+    h2d = q_h.numel() * 2 + k_h.numel() * 2 + v_h.numel() * 2
+    d2h = out_h.numel() * 2 + tab_h.numel() * 4 + cnt_h.numel() * 4
+    return dt, h2d, d2h
+
+
+# ----------------------------------------------------------------------------- CPU baseline
+def cpu_baseline(lay, full, n_rows: int = 4):
+    """The oracle (fp32 torch on the host cores) on a bounded sample of the workload:
+    the mixed attention of `n_rows` draft + `n_rows` verify rows at full context."""
+    from oracle import attention as oracle_attn
+
+    cores = len(os.sched_getaffinity(0))
+    torch.set_num_threads(cores)
+    rows = [int(r) for r in np.flatnonzero(lay.modes == 0)[:n_rows]] + \
+           [int(r) for r in np.flatnonzero(lay.modes == 1)[:n_rows]]
+    # Sub-layout with those rows; their pages copied to a compact CPU cache.
+    from aspire_b200.workloads import MixedLayout
+    g = torch.Generator().manual_seed(1)
+    qo = [0]
+    kvp = [0]
+    idx = []
+    used = {}
+    for r in rows:
+        qo.append(qo[-1] + int(lay.q_lens[r]))
+        pages = lay.kv_indices[lay.kv_indptr[r]:lay.kv_indptr[r + 1]]
+        for pg in pages:
+            used.setdefault(int(pg), len(used))
+        idx.extend(used[int(pg)] for pg in pages)
+        kvp.append(len(idx))
+    P = len(used)
+    kv = torch.randn(P, 2, 16, lay.num_kv_heads, 128, generator=g).to(torch.bfloat16).float()
+    q = torch.randn(qo[-1], lay.num_qo_heads, 128, generator=g).to(torch.bfloat16).float()
+    kvl = np.array([int(lay.kv_lens[r]) for r in rows], np.int32)
+    sub = MixedLayout(num_qo_heads=lay.num_qo_heads, num_kv_heads=lay.num_kv_heads,
+                      modes=lay.modes[rows], q_lens=lay.q_lens[rows], kv_lens=kvl, qo_indptr=np.array(qo, np.int32),
+                      kv_indptr=np.array(kvp, np.int32), kv_indices=np.array(idx, np.int32),
+                      block_table=lay.block_table[rows], ctx_lens=lay.ctx_lens[rows], pages_per_row=lay.pages_per_row,
+                      num_pages_total=P)
+    oracle_attn.paged_attention(q[:1], kv, [0, 1], [0, 1], [0], [16])  # warm
+    t0 = time.perf_counter()
+    oracle_attn.paged_attention(q, kv, sub.qo_indptr, sub.kv_indptr, sub.kv_indices, sub.kv_lens, causal=True)
+    dt = time.perf_counter() - t0
+    b = sub.algorithmic_bytes()
+    return {"value": round(b / dt / 1e9, 3), "unit": UNIT, "cores": cores, "kind": "port",
+            "sample": f"oracle fp32 mixed attention of {n_rows} draft + {n_rows} verify rows of the bench workload "
+                      f"({b / 1e9:.3f} GB algorithmic) in {dt:.2f} s"}
+
+
+def reference_arm(args, rank, world):
+    """The reference's attention path has no CPU implementation (its ops are CUDA
+    only); the oracle port, run on the host cores, stands in for it."""
+    if rank != 0:
+        return
+    from aspire_b200.workloads import full_context_layout
+    hq = len(tp_heads(CFG["num_qo_heads"], 0, world))
+    hkv = len(tp_heads(CFG["num_kv_heads"], 0, world))
+    from aspire_b200.workloads import make_layout
+    lay = make_layout(batch=CFG["batch"], ctx=CFG["ctx"], num_qo_heads=hq, num_kv_heads=hkv,
+                      draft_fraction=CFG["draft_fraction"], budget_pages=CFG["budget_pages"],
+                      pages_per_row=CFG["pages_per_row"], seed=CFG["seed"])
+    full = full_context_layout(lay)
+    vals = []
+    for _ in range(args.warmup):
+        cpu_baseline(lay, full, n_rows=1)
+    for _ in range(max(1, args.steps)):
+        vals.append(cpu_baseline(lay, full, n_rows=1))
+    v = statistics.median(x["value"] for x in vals)
+    cb = dict(vals[-1])
+    cb["value"] = v
+    line = {"impl": "reference", "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "mixed draft/verify attention layer-call, Qwen3-8B heads, B=64, 32k ctx (sample)",
+                       "sample_rows": 2},
+            "cpu_baseline": cb, "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------------------------- main
+def main():
+    args = parse_args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        reference_arm(args, rank, world)
+        return
+    dist_on = world > 1
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    if dist_on:
+        import datetime
+        torch.distributed.init_process_group("nccl", device_id=device, timeout=datetime.timedelta(seconds=120))
+
+    from aspire_b200 import load_library
+    load_library()
+    lay, full, lpl_m, lpl_f = build_workload(device, rank, world)
+    hp = HotPath(device, lay, full, lpl_m, lpl_f)
+    hp.plan()
+    hp.capture()
+    sb = step_bytes(lay, full, CFG["n_layer"], hp.kv_stride, hp.k_sel)
+
+    peak, peak_kind = measured_peaks()
+    with ClockSampler(local_rank) as clocks:
+        ms = time_device(hp.graph.replay, args.steps, args.warmup, dist_on)
+    t = torch.tensor([ms], device=device)
+    tot_bytes = torch.tensor([float(sb["total"])], device=device)
+    if dist_on:
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        torch.distributed.all_reduce(tot_bytes, op=torch.distributed.ReduceOp.SUM)
+    ms_max = float(t.item())
+    value = float(tot_bytes.item()) / (ms_max * 1e-3) / 1e9
+
+    roof = kernel_roofline(hp, args.steps, peak, peak_kind)
+    e2e = None
+    if not args.no_e2e:
+        dt, h2d, d2h = e2e_measure(hp, max(2, args.steps // 2), 1, sb["total"])
+        tt = torch.tensor([dt], device=device)
+        if dist_on:
+            torch.distributed.all_reduce(tt, op=torch.distributed.ReduceOp.MAX)
+        e2e = {"value": round(float(tot_bytes.item()) / float(tt.item()) / 1e9, 1), "unit": UNIT,
+               "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h), "ms_per_step": round(float(tt.item()) * 1e3, 3)}
+    cb = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cb = cpu_baseline(lay, full, n_rows=2)
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_max, 4), "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "one decode step of the attention hot path: 35 x (append + mixed draft/verify "
+                                   "attention) + refresh layer (append + full attention + first/last dump) + page "
+                                   "selection; Qwen3-8B heads 32/8/128, 36 layers, B=64, 32k ctx, draft fraction 0.5, "
+                                   "verify q_len U{3..9}, budget 128 pages, one resident layer cache",
+                       "batch": CFG["batch"], "ctx": CFG["ctx"], "tp": world, "heads_per_rank": [lay.num_qo_heads, lay.num_kv_heads],
+                       "l2": "inputs larger than L2 (8.7 GB cache at TP1)", "bytes_per_step": sb},
+            "roofline": roof, "clocks": clocks.summary(), "e2e": e2e,
+            "gpu_launches": hp.launches_per_step() * args.steps,
+            "cpu_baseline": cb,
+        }
+        print(json.dumps(line), flush=True)
+    if dist_on:
+        hp.graph = None
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,254 @@
+/*
+ * aspire_b200.h - C ABI of libaspire_b200.so, the sm_100a implementation of
+ * ASPIRE's unified mixed forward hot path:
+ *
+ *   1. paged mixed draft/verify attention (draft rows attend a sparse page
+ *      list with q_len 1, verify rows attend the full cache with a causal
+ *      multi-token query), optionally dumping first/last-query logits at the
+ *      refresh layer;
+ *   2. refresh-layer page scoring + top-k page re-selection, written in place
+ *      into the draft page table;
+ *   3. the paged KV append of the step's new tokens.
+ *
+ * Every entry point takes plain pointers, sizes and a CUDA stream handle
+ * (passed as void*); no framework types cross this boundary.  Every entry
+ * point returns 0 on success or a negative ASPIRE_ERR_* code; the message of
+ * the last failure on the calling thread is returned by aspire_last_error().
+ *
+ * Tensor layouts (all device pointers unless stated otherwise):
+ *   q        bf16 [tokens, num_qo_heads, 128], head_dim contiguous, strides given
+ *   kv_cache bf16 [num_pages_total, 2, 16, num_kv_heads, 128] contiguous
+ *            (index 0 of dim 1 = K, 1 = V; "NHD" paged layout)
+ *   out      bf16 [tokens, num_qo_heads, 128], strides given
+ *   lse      fp32 [tokens, num_qo_heads], base-2 log-sum-exp of the scaled logits
+ *   dump     fp16 [batch, dump_num_heads, 2, dump_kv_stride] first/last logits
+ *
+ * Only page_size 16 and head_dim 128 are supported (every ASPIRE config).
+ */
+#ifndef ASPIRE_B200_H_
+#define ASPIRE_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define ASPIRE_API __attribute__((visibility("default")))
+#else
+#define ASPIRE_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define ASPIRE_B200_ABI_VERSION 1
+
+#define ASPIRE_OK 0
+#define ASPIRE_ERR_INVALID (-1)  /* bad argument (shape, size, alignment)       */
+#define ASPIRE_ERR_CUDA (-2)     /* a CUDA runtime call failed                   */
+#define ASPIRE_ERR_CAPACITY (-3) /* a workspace or plan buffer is too small      */
+#define ASPIRE_ERR_DEVICE (-4)   /* a kernel reported bad input via the status word */
+
+/* Device status word bits (written by kernels instead of faulting). */
+#define ASPIRE_STATUS_BAD_PAGE 1u  /* a page id >= num_pages_total was skipped */
+#define ASPIRE_STATUS_BAD_PLAN 2u  /* a work item was inconsistent and skipped */
+#define ASPIRE_STATUS_BAD_ROW 4u   /* selection row/argument out of range      */
+
+/* ------------------------------------------------------------------------ */
+/* Plan (host).                                                             */
+/* ------------------------------------------------------------------------ */
+
+/*
+ * Result of aspire_plan: where the work list lives inside the device int
+ * workspace and how much of each workspace it needs.  Returned to the
+ * caller, who passes it back unchanged to aspire_mixed_attention.  The
+ * kernels read every plan-dependent quantity from the device int workspace,
+ * so a CUDA graph captured around aspire_mixed_attention stays valid when a
+ * later aspire_plan call rewrites the work list in place.
+ */
+typedef struct AspirePlanInfo {
+  int32_t num_items;        /* work items over all kernel classes            */
+  int32_t num_items_gather; /* items for the CUDA-core gather kernel         */
+  int32_t num_items_tc;     /* items for the tcgen05 kernel                  */
+  int32_t num_ctas;         /* persistent grid of each kernel class          */
+  int32_t num_merge;        /* (row, kv-head, q-tile) groups split over chunks */
+  int32_t chunk_tokens;     /* KV tokens per split-KV chunk                   */
+  int64_t partial_rows;     /* fp32 partial rows needed in the float workspace */
+  int64_t int_bytes;        /* bytes of the int workspace used (and uploaded) */
+  int64_t float_bytes;      /* bytes of the float workspace needed            */
+  int32_t num_qo_heads;
+  int32_t num_kv_heads;
+  int32_t causal;
+  int32_t batch_size;       /* rows planned (including padding rows)          */
+  int32_t max_q_len;
+  int32_t tc_enabled;       /* 1 when wide query tiles use the tcgen05 kernel */
+} AspirePlanInfo;
+
+/*
+ * Builds the split-KV work list for one attention program and uploads it.
+ * Replaces FlashInfer's TwoStageHolisticPlan as driven by
+ * HolisticAttentionWrapper.plan / plan_host
+ * (aspire/attention/holistic_wrapper.py:253-265, :323-335).
+ *
+ *   qo_indptr  host int32 [batch_size + 1]  query-row offsets per request
+ *   kv_indptr  host int32 [batch_size + 1]  page-list offsets per request
+ *   kv_len     host int32 [batch_size]      attended KV tokens per request
+ *   host_buf   pinned host buffer the work list is rendered into
+ *   dev_int_ws device int workspace (the work list is copied to its start)
+ *
+ * The copy host_buf -> dev_int_ws is enqueued on `stream` with
+ * cudaMemcpyAsync; the caller must not reuse host_buf until that copy has
+ * completed (the wrapper fences a small ring of pinned buffers with events).
+ * num_ctas <= 0 selects one CTA per SM of the current device.
+ */
+ASPIRE_API int aspire_plan(const int32_t* qo_indptr, const int32_t* kv_indptr, const int32_t* kv_len,
+                int32_t batch_size, int32_t num_qo_heads, int32_t num_kv_heads, int32_t head_dim,
+                int32_t page_size, int32_t causal, int32_t num_ctas, void* host_buf,
+                size_t host_buf_bytes, void* dev_int_ws, size_t dev_int_ws_bytes,
+                size_t float_ws_bytes, void* stream, AspirePlanInfo* info);
+
+/* Host-only variant of aspire_plan: renders the work list into host_buf
+ * without touching the device (used by tests and by callers that upload the
+ * list themselves).  num_ctas must be > 0. */
+ASPIRE_API int aspire_plan_host_only(const int32_t* qo_indptr, const int32_t* kv_indptr,
+                          const int32_t* kv_len, int32_t batch_size, int32_t num_qo_heads,
+                          int32_t num_kv_heads, int32_t head_dim, int32_t page_size,
+                          int32_t causal, int32_t num_ctas, void* host_buf,
+                          size_t host_buf_bytes, size_t float_ws_bytes, AspirePlanInfo* info);
+
+/* ------------------------------------------------------------------------ */
+/* Mixed paged attention (device).                                          */
+/* ------------------------------------------------------------------------ */
+
+typedef struct AspireAttnArgs {
+  const void* q;            /* bf16 [tokens, num_qo_heads, 128]                   */
+  int64_t q_stride_n;       /* elements between tokens                            */
+  int64_t q_stride_h;       /* elements between heads                             */
+  const void* kv_cache;     /* bf16 [num_pages_total, 2, 16, num_kv_heads, 128]   */
+  int64_t num_pages_total;
+  const int32_t* kv_indices; /* int32 page ids, indexed by the plan's kv_indptr    */
+  void* out;                /* bf16 [tokens, num_qo_heads, 128]                   */
+  int64_t o_stride_n;
+  int64_t o_stride_h;
+  float* lse;               /* optional fp32 [tokens, num_qo_heads] (NULL = skip) */
+  void* dump;               /* optional fp16 first/last logit dump (NULL = skip)  */
+  int64_t dump_num_heads;   /* heads dimension of the dump buffer                 */
+  int64_t dump_kv_stride;   /* last dimension of the dump buffer                  */
+  float sm_scale;           /* <= 0 selects 1/sqrt(128)                           */
+  int32_t num_qo_heads;
+  int32_t num_kv_heads;
+  int32_t head_dim;         /* must be 128                                        */
+  int32_t page_size;        /* must be 16                                         */
+  void* int_ws;             /* device int workspace holding the uploaded plan     */
+  size_t int_ws_bytes;
+  void* float_ws;           /* device float workspace for split-KV partials       */
+  size_t float_ws_bytes;
+} AspireAttnArgs;
+
+/*
+ * Runs the planned attention program on `stream`.  Replaces
+ * HolisticAttentionWrapper.run (aspire/attention/holistic_wrapper.py:344-386)
+ * and the persistent FlashInfer kernel with its split-KV merge; with `dump`
+ * set it also replaces the first/last logit-dump variant
+ * (aspire/backends/jit_kernels.py:188-193, :252-256).
+ * Capturable in a CUDA graph; allocates nothing.
+ */
+ASPIRE_API int aspire_mixed_attention(const AspireAttnArgs* args, const AspirePlanInfo* plan, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* Paged KV append (device).                                                */
+/* ------------------------------------------------------------------------ */
+
+typedef struct AspireAppendArgs {
+  const void* k;            /* bf16 [num_tokens, num_kv_heads, 128]              */
+  const void* v;
+  int64_t k_stride_n, k_stride_h, v_stride_n, v_stride_h;
+  int64_t num_tokens;       /* bucket tokens (rows past the last request skipped) */
+  const int32_t* append_indptr; /* int32 [num_rows + 1] new-token offsets        */
+  void* kv_cache;           /* bf16 [num_pages_total, 2, 16, num_kv_heads, 128]  */
+  int64_t num_pages_total;
+  const int32_t* page_indices;  /* int32 page ids                                */
+  const int32_t* page_indptr;   /* int32 [num_rows + 1]                          */
+  const int32_t* last_page_len; /* int32 [num_rows]                              */
+  int32_t num_rows;
+  int32_t num_kv_heads;
+  int32_t head_dim;         /* must be 128 */
+  int32_t page_size;        /* must be 16  */
+  uint32_t* status;         /* optional device status word (NULL = none)         */
+} AspireAppendArgs;
+
+/*
+ * Writes each new token's K and V row into its page.  Replaces
+ * mylib::update_kv_padded (aspire/attention/kv_ops.py:63-187): a token whose
+ * position is negative (bucket padding) or past its row's length is skipped.
+ */
+ASPIRE_API int aspire_append_kv(const AspireAppendArgs* args, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* Page scoring + top-k re-selection (device).                              */
+/* ------------------------------------------------------------------------ */
+
+typedef struct AspireSelectArgs {
+  const uint16_t* dump;     /* fp16 [dump_batch, num_heads, 2, kv_stride]; NULL when scores_in set */
+  int64_t kv_stride;
+  int64_t max_seq_len;      /* logits past this position are ignored              */
+  const float* lse;         /* fp32 [lse_rows, num_heads]                         */
+  int64_t lse_rows;
+  const int32_t* qo_indptr; /* int32 [>= rows + 1] of the dump program            */
+  const int32_t* row_ids;   /* optional int32 [batch]: dump / qo_indptr row of each
+                               output row (NULL = identity), for select_subset      */
+  const float* scores_in;   /* optional fp32 [batch, pages_per_slot] raw page scores:
+                               when set, scoring is skipped and only the top-k runs */
+  const int32_t* num_pages; /* int32 [batch] valid pages per request              */
+  const int32_t* block_table; /* int32 [batch, block_table_stride]                */
+  int64_t block_table_stride;
+  int32_t batch;
+  int32_t num_heads;
+  int32_t page_size;        /* must be 16 */
+  int32_t pages_per_slot;
+  int32_t L;                /* trailing pages always kept                          */
+  int32_t subset_cache_size;/* k of the top-k                                      */
+  int32_t min_draft_pages;  /* < 0 means None                                      */
+  float draft_percent;      /* < 0 means None                                      */
+  float sm_scale;           /* <= 0 selects 1/sqrt(head_dim)                       */
+  int32_t head_dim;
+  int32_t* table_out;       /* int32 [batch, table_stride]: sorted ids, zero tail  */
+  int64_t table_stride;
+  int32_t table_width;      /* columns written per row                             */
+  int32_t* counts_out;      /* int32 [batch] valid counts                          */
+  float* scores_out;        /* optional fp32 [batch, pages_per_slot] final scores  */
+  uint32_t* status;         /* optional device status word                         */
+} AspireSelectArgs;
+
+/*
+ * Scores pages from the first/last logit dump and the dump program's LSE,
+ * selects the top pages (ties broken by the lower page index) and writes the
+ * ascending page-id rows plus the valid counts in place.  Replaces
+ * PageSelectorFirstLastAvg.select (aspire/backends/page_selector.py:206-214,
+ * :163-181, :79-108) followed by LMBackendBase._store_draft_rows
+ * (aspire/backends/base.py:1421-1471).
+ */
+ASPIRE_API int aspire_select_pages(const AspireSelectArgs* args, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* Utilities.                                                               */
+/* ------------------------------------------------------------------------ */
+
+/* Message of the last failing call on this thread ("" when none). */
+ASPIRE_API const char* aspire_last_error(void);
+
+/* ABI version of the loaded library (ASPIRE_B200_ABI_VERSION). */
+ASPIRE_API int aspire_abi_version(void);
+
+/* Bytes of the int workspace reserved ahead of the plan for the status word;
+ * the status word is the first uint32 of the int workspace. */
+ASPIRE_API size_t aspire_status_offset(void);
+
+/* Names of the kernels the library launches, one per line (diagnostics). */
+ASPIRE_API const char* aspire_kernel_names(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ASPIRE_B200_H_ */

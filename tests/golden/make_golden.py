@@ -1,0 +1,182 @@
+"""Generates the golden fixtures of tests/golden/ from the reference's own code.
+
+Run in a container that has the reference tree (default /root/reference, or
+$ASPIRE_REFERENCE):
+
+    python tests/golden/make_golden.py
+
+* page_selector_*.pt : inputs and outputs of the reference's
+  aspire.backends.page_selector.PageSelectorFirstLastAvg.select (imported
+  unchanged from the reference tree, run on CPU), including its page-score
+  buffer before the +/-inf forcing; tie cases run its _finalize_scores.
+* kv_append.pt : the reference's Triton kernels
+  (aspire.attention.kv_ops._append_paged_kv_cache_padded_kernel and
+  FlashInfer's get_batch_indices_positions_kernel) executed by Triton's CPU
+  interpreter (TRITON_INTERPRET=1) on a padded mixed batch.
+
+The fixtures are small (< 2 MB total) and committed; tests never read the
+reference tree.
+"""
+
+from __future__ import annotations
+
+import math
+import os
+import subprocess
+import sys
+from pathlib import Path
+
+import torch
+
+HERE = Path(__file__).resolve().parent
+REF = Path(os.environ.get("ASPIRE_REFERENCE", "/root/reference"))
+
+
+def _ref_selector_cls():
+    sys.path.insert(0, str(REF))
+    from aspire.backends.page_selector import PageSelectorFirstLastAvg  # noqa: E402
+
+    return PageSelectorFirstLastAvg
+
+
+def _make_dump(gen, B, H, kv_stride, lens, stale_slot1_rows):
+    """fp16 dump [B*H*2*kv_stride] with -inf fill beyond each row's length."""
+    d = torch.full((B, H, 2, kv_stride), float("-inf"), dtype=torch.float16)
+    for b in range(B):
+        L = int(lens[b])
+        vals = (torch.randn(H, 2, L, generator=gen) * 11.3).to(torch.float16)
+        d[b, :, :, :L] = vals
+        if b in stale_slot1_rows:
+            # slot 1 holds older logits over a shorter prefix (q_len == 1 rows)
+            d[b, :, 1, L // 2:] = float("-inf")
+    return d.reshape(-1)
+
+
+def selector_case(name, *, B, H, max_seq_len, kv_stride, top_k_pages, L, draft_percent, seed,
+                  q_lens, lens, stale_rows=(), lse_neg_inf_rows=()):
+    cls = _ref_selector_cls()
+    gen = torch.Generator().manual_seed(seed)
+    page = 16
+    pps = (max_seq_len + page - 1) // page
+    if draft_percent is not None:
+        k = max(top_k_pages, math.ceil(pps * draft_percent / 100))
+    else:
+        k = top_k_pages
+    sel = cls(max_batch_size=B, pages_per_slot=pps, subset_cache_size=k, L=L, n_heads=H, page_size=page,
+              max_seq_length=max_seq_len, device="cpu", bsz=B, dec_len=9, head_dim=128,
+              kv_stride=kv_stride, draft_percent=draft_percent, min_draft_pages=top_k_pages)
+    dump = _make_dump(gen, B, H, kv_stride, lens, set(stale_rows))
+    qo = torch.zeros(B + 1, dtype=torch.int32)
+    qo[1:] = torch.cumsum(torch.tensor(q_lens, dtype=torch.int32), 0)
+    T = int(qo[-1]) + 3
+    # LSE of a random logit row is around log2(len) + a few; keep it realistic.
+    lse = (torch.randn(T, H, generator=gen) * 2.0 + 12.0).float()
+    dview = dump.view(B, H, 2, kv_stride)
+    for b in lse_neg_inf_rows:
+        # A first query that saw no keys: -inf LSE and -inf logits, so the
+        # normalised logit is NaN and the selector maps it to -inf.
+        lse[int(qo[b])] = float("-inf")
+        dview[b, :, 0, :] = float("-inf")
+    num_pages = torch.tensor([(int(x) + page - 1) // page for x in lens], dtype=torch.int32)
+    block_table = torch.stack([b * pps + torch.randperm(pps, generator=gen) for b in range(B)]).to(torch.int32)
+
+    captured = {}
+    orig = sel._finalize_scores
+
+    def capture(scores, num_pages_, block_table_):
+        captured["scores_raw"] = scores.clone()
+        return orig(scores, num_pages_, block_table_)
+
+    sel._finalize_scores = capture
+    selected, valid = sel.select(dump, lse, num_pages, block_table, qo)
+    out = {
+        "params": dict(B=B, H=H, max_seq_len=max_seq_len, kv_stride=kv_stride, pps=pps, k=k, L=L,
+                       draft_percent=draft_percent, min_draft_pages=top_k_pages, page_size=page),
+        "dump": dump, "lse": lse, "num_pages": num_pages, "block_table": block_table, "qo_indptr": qo,
+        "scores_raw": captured["scores_raw"], "selected": selected.clone(), "valid": valid.clone(),
+    }
+    torch.save(out, HERE / f"page_selector_{name}.pt")
+    print(f"page_selector_{name}: k={k} valid={valid.tolist()}")
+
+
+def tie_case():
+    """_finalize_scores on scores with exact ties (finite and +inf)."""
+    cls = _ref_selector_cls()
+    B, pps, k, L = 4, 48, 12, 3
+    sel = cls(max_batch_size=B, pages_per_slot=pps, subset_cache_size=k, L=L, n_heads=2, page_size=16,
+              max_seq_length=pps * 16, device="cpu", bsz=B, dec_len=1, head_dim=128,
+              draft_percent=None, min_draft_pages=None)
+    gen = torch.Generator().manual_seed(7)
+    scores = torch.randint(0, 6, (B, pps), generator=gen).float()  # many exact ties
+    scores[1, 10:20] = 3.0
+    num_pages = torch.tensor([48, 30, 5, 13], dtype=torch.int32)
+    block_table = torch.stack([torch.randperm(1000, generator=gen)[:pps] for _ in range(B)]).to(torch.int32)
+    raw = scores.clone()
+    selected, valid = sel._finalize_scores(scores, num_pages, block_table)
+    torch.save({"params": dict(B=B, pps=pps, k=k, L=L), "scores_raw": raw, "num_pages": num_pages,
+                "block_table": block_table, "selected": selected.clone(), "valid": valid.clone()},
+               HERE / "page_selector_ties.pt")
+    print("page_selector_ties: valid", valid.tolist())
+
+
+_APPEND_SCRIPT = r"""
+import sys, torch
+sys.path.insert(0, sys.argv[1])
+from aspire.attention import kv_ops
+import flashinfer.triton.page as fpage
+torch.manual_seed(3)
+H, D, page = 2, 128, 16
+# rows: draft (1 token through its sparse table), verify (5 tokens), verify
+# starting a fresh page, an empty row, then the bucket padding row.
+append_indptr = torch.tensor([0, 1, 6, 9, 9, 12], dtype=torch.int32)
+T = 12
+page_indptr = torch.tensor([0, 3, 6, 8, 8, 8], dtype=torch.int32)
+page_indices = torch.tensor([7, 2, 11, 0, 4, 9, 13, 5], dtype=torch.int32)
+last = torch.tensor([9, 12, 3, 0, 0], dtype=torch.int32)
+P = 16
+k = torch.randn(T, H, D)
+v = torch.randn(T, H, D)
+cache = torch.randn(P, 2, page, H, D)
+cache0 = cache.clone()
+seq_lens = torch.clamp(page_indptr[1:] - page_indptr[:-1] - 1, min=0) * page + last
+bi = torch.zeros(T, dtype=torch.int32)
+pos = torch.full((T,), -1, dtype=torch.int32)
+fpage.get_batch_indices_positions_kernel[(seq_lens.shape[0],)](append_indptr, seq_lens, bi, pos, num_stages=2)
+kv_ops._append_paged_kv_cache_padded_kernel[(T, H)](
+    k, v, bi, pos, cache, page_indices, page_indptr, last,
+    k.stride(0), k.stride(1), v.stride(0), v.stride(1),
+    cache.stride(0), cache.stride(1), cache.stride(2), cache.stride(3), HEAD_DIM=D, PAGE_SIZE=page)
+torch.save({"k": k, "v": v, "append_indptr": append_indptr, "page_indices": page_indices,
+            "page_indptr": page_indptr, "last_page_len": last, "cache_before": cache0,
+            "cache_after": cache, "batch_indices": bi, "positions": pos}, sys.argv[2])
+print("kv_append positions", pos.tolist())
+"""
+
+
+def append_case():
+    env = dict(os.environ, TRITON_INTERPRET="1")
+    subprocess.run([sys.executable, "-c", _APPEND_SCRIPT, str(REF), str(HERE / "kv_append.pt")], check=True,
+                   env=env)
+
+
+def main():
+    if not REF.exists():
+        raise SystemExit(f"reference tree {REF} not found")
+    # BASELINE config 1 geometry: 16 heads, 1024-token cache, 8 selected pages.
+    selector_case("cfg1", B=4, H=16, max_seq_len=1024, kv_stride=1024, top_k_pages=8, L=2,
+                  draft_percent=None, seed=0, q_lens=[1, 1, 5, 5], lens=[1000, 1024, 1021, 1024],
+                  stale_rows=(0, 1))
+    # Engine defaults (top_k_pages 32, recent 8, draft_percent 7) on a long, padded-stride dump,
+    # with a tiny row (num_pages < L) and a row whose first-query LSE is -inf (NaN -> -inf path).
+    selector_case("pct", B=3, H=2, max_seq_len=16640, kv_stride=16768, top_k_pages=32, L=8,
+                  draft_percent=7.0, seed=1, q_lens=[5, 1, 9], lens=[16633, 70, 9001],
+                  stale_rows=(1,), lse_neg_inf_rows=(2,))
+    # Config-2-like (budget 128 pages, L 8, draft_percent unset), local heads of TP 4.
+    selector_case("budget", B=2, H=4, max_seq_len=16640, kv_stride=16640, top_k_pages=128, L=8,
+                  draft_percent=None, seed=2, q_lens=[5, 3], lens=[16500, 16001])
+    tie_case()
+    append_case()
+
+
+if __name__ == "__main__":
+    main()

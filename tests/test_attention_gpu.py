@@ -1,0 +1,136 @@
+"""GPU parity of the mixed paged attention against the fp32 CPU oracle."""
+
+import numpy as np
+import pytest
+import torch
+
+from aspire_b200.attention import HolisticAttentionWrapper
+from aspire_b200.workloads import MixedLayout, config1_layout, make_layout
+
+from gpu_helpers import (assert_attention_close, assert_dump_close, make_inputs, oracle_attention,
+                         run_attention)
+
+pytestmark = pytest.mark.gpu
+
+
+def test_config1_mixed_attention(cuda_device):
+    lay = config1_layout(seed=0)
+    q, kv = make_inputs(lay, cuda_device, seed=0)
+    out, lse, _, _ = run_attention(lay, q, kv)
+    ref_out, ref_lse, _ = oracle_attention(lay, q, kv)
+    assert_attention_close(out, lse, ref_out, ref_lse)
+
+
+def test_config1_refresh_dump(cuda_device):
+    lay = config1_layout(seed=1)
+    q, kv = make_inputs(lay, cuda_device, seed=1)
+    stride = 1024 + 64
+    out, lse, dump, _ = run_attention(lay, q, kv, dump=True, dump_stride=stride)
+    ref_out, ref_lse, ref_dump = oracle_attention(lay, q, kv, dump_stride=stride)
+    assert_attention_close(out, lse, ref_out, ref_lse)
+    assert_dump_close(dump, ref_dump, lay, stride)
+
+
+@pytest.mark.parametrize("hq,hkv", [(32, 8), (16, 8), (8, 1), (4, 2)])
+@pytest.mark.parametrize("draft_fraction", [0.0, 0.5, 1.0])
+def test_mixed_ragged_split_kv(cuda_device, hq, hkv, draft_fraction):
+    """Verify q_len 3..9, ragged contexts, split-KV chunks merged on device."""
+    lay = make_layout(batch=6, ctx=2999, num_qo_heads=hq, num_kv_heads=hkv, draft_fraction=draft_fraction,
+                      budget_pages=37, seed=hq + hkv)
+    q, kv = make_inputs(lay, cuda_device, seed=5)
+    out, lse, _, w = run_attention(lay, q, kv)
+    assert w.plan_info.num_merge > 0 or lay.kv_lens.max() <= w.plan_info.chunk_tokens
+    ref_out, ref_lse, _ = oracle_attention(lay, q, kv)
+    assert_attention_close(out, lse, ref_out, ref_lse)
+
+
+def _custom_layout(q_lens, kv_lens, hq=16, hkv=8, seed=0):
+    rng = np.random.default_rng(seed)
+    B = len(q_lens)
+    pages = [(k + 15) // 16 for k in kv_lens]
+    ppr = max(max(pages), 1)
+    bt = np.stack([r * ppr + rng.permutation(ppr) for r in range(B)]).astype(np.int32)
+    kv_indptr = np.zeros(B + 1, np.int32)
+    idx = []
+    for r in range(B):
+        idx.append(bt[r, :pages[r]])
+        kv_indptr[r + 1] = kv_indptr[r] + pages[r]
+    qo = np.zeros(B + 1, np.int32)
+    qo[1:] = np.cumsum(q_lens)
+    return MixedLayout(num_qo_heads=hq, num_kv_heads=hkv, modes=np.array([1 if q > 1 else 0 for q in q_lens]),
+                       q_lens=np.array(q_lens, np.int32), kv_lens=np.array(kv_lens, np.int32), qo_indptr=qo,
+                       kv_indptr=kv_indptr, kv_indices=np.concatenate(idx).astype(np.int32), block_table=bt,
+                       ctx_lens=np.array(kv_lens, np.int32), pages_per_row=ppr, num_pages_total=B * ppr)
+
+
+def test_edge_rows(cuda_device):
+    """Empty rows, a padding row (queries, no KV), kv shorter than q (fully masked
+    queries), single-token KV, lengths off the page boundary."""
+    lay = _custom_layout(q_lens=[0, 3, 1, 5, 9, 2, 1], kv_lens=[40, 0, 1, 3, 4100, 17, 1023], seed=2)
+    q, kv = make_inputs(lay, cuda_device, seed=2)
+    out, lse, _, _ = run_attention(lay, q, kv)
+    ref_out, ref_lse, _ = oracle_attention(lay, q, kv)
+    assert_attention_close(out, lse, ref_out, ref_lse)
+    # padding row: zero output, -inf lse
+    r0, r1 = int(lay.qo_indptr[1]), int(lay.qo_indptr[2])
+    assert out[r0:r1].abs().max().item() == 0.0
+    assert torch.isinf(lse[r0:r1]).all()
+
+
+def test_long_context_rows(cuda_device):
+    lay = make_layout(batch=3, ctx=32768 + 7, num_qo_heads=32, num_kv_heads=8, draft_fraction=0.34,
+                      budget_pages=128, seed=11)
+    q, kv = make_inputs(lay, cuda_device, seed=11)
+    out, lse, _, _ = run_attention(lay, q, kv)
+    ref_out, ref_lse, _ = oracle_attention(lay, q, kv)
+    assert_attention_close(out, lse, ref_out, ref_lse)
+
+
+def test_deterministic_and_graph_replay(cuda_device):
+    """Bitwise-identical reruns; a captured graph stays valid across re-plans that
+    rewrite the static page-index buffer in place (as the engine's step loop does)."""
+    common = dict(batch=5, num_qo_heads=32, num_kv_heads=8, draft_fraction=0.4, budget_pages=20,
+                  verify_q_len=5, draft_rows=[1, 3], pages_per_row=128)
+    lay1 = make_layout(ctx=2048, seed=4, **common)
+    lay2 = make_layout(ctx=1500, seed=9, **common)
+    q, kv = make_inputs(lay1, cuda_device, seed=4)
+    static_idx = torch.zeros(lay1.kv_indices.shape[0] + lay2.kv_indices.shape[0], dtype=torch.int32,
+                             device=cuda_device)
+    w = HolisticAttentionWrapper(torch.empty(1, device=cuda_device))
+
+    def plan(lay):
+        n = lay.kv_indices.shape[0]
+        static_idx[:n] = torch.from_numpy(lay.kv_indices).to(cuda_device)
+        w.plan_host(torch.from_numpy(lay.qo_indptr), torch.from_numpy(lay.kv_indptr),
+                    torch.from_numpy(lay.kv_lens), static_idx, 32, 8, 128, 16, causal=True)
+
+    out = torch.empty_like(q)
+    lse = torch.empty(q.shape[0], q.shape[1], device=cuda_device, dtype=torch.float32)
+    plan(lay1)
+    w.run(q, kv, out=out, lse=lse)
+    first = out.clone(), lse.clone()
+    w.run(q, kv, out=out, lse=lse)
+    torch.cuda.synchronize()
+    assert torch.equal(first[0], out) and torch.equal(first[1], lse)
+
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        w.run(q, kv, out=out, lse=lse)
+    for lay in (lay2, lay1):
+        plan(lay)
+        g.replay()
+        torch.cuda.synchronize()
+        ref_out, ref_lse, _ = oracle_attention(lay, q, kv)
+        assert_attention_close(out, lse, ref_out, ref_lse)
+
+
+def test_bad_page_ids_are_reported_not_faulted(cuda_device):
+    lay = config1_layout(seed=3)
+    q, kv = make_inputs(lay, cuda_device, seed=3)
+    lay.kv_indices = lay.kv_indices.copy()
+    lay.kv_indices[3] = lay.num_pages_total + 5  # out of range: the kernel skips it and flags it
+    w = HolisticAttentionWrapper(torch.empty(1, device=cuda_device))
+    w.clear_device_status()
+    run_attention(lay, q, kv, wrapper=w)
+    torch.cuda.synchronize()
+    assert w.device_status() & 1

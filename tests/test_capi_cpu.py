@@ -1,0 +1,114 @@
+"""C ABI checks that need no GPU: the library loads, exports every symbol the
+header declares, and the host planner covers every (row, head, token) once."""
+
+import ctypes
+import re
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from aspire_b200 import _capi
+from aspire_b200.workloads import make_layout
+
+HEADER = Path(__file__).resolve().parent.parent / "include" / "aspire_b200.h"
+ITEM_FIELDS = ["row", "kv_head", "q_start", "q_len", "kv_page_base", "kv_len", "tok_begin", "tok_end",
+               "pq_begin", "pq_end", "chunk", "n_chunks", "partial_base", "merge_id", "kind", "reserved"]
+
+
+def header_functions():
+    text = HEADER.read_text()
+    return sorted(set(re.findall(r"ASPIRE_API\s+[\w\s\*]+?\b(aspire_\w+)\s*\(", text)))
+
+
+def test_library_exports_every_declared_symbol(built_library):
+    declared = header_functions()
+    assert declared, "no ASPIRE_API declarations found"
+    for name in declared:
+        assert hasattr(built_library, name), name
+    assert set(declared) == set(_capi.exported_symbols())
+    assert built_library.aspire_abi_version() == 1
+    assert built_library.aspire_status_offset() == 256
+
+
+def _plan(lib, qo, kvp, kvl, hq, hkv, num_sms=8, float_ws=1 << 30, causal=1):
+    qo = np.ascontiguousarray(qo, dtype=np.int32)
+    kvp = np.ascontiguousarray(kvp, dtype=np.int32)
+    kvl = np.ascontiguousarray(kvl, dtype=np.int32)
+    buf = np.zeros(1 << 22, dtype=np.uint8)
+    info = _capi.AspirePlanInfo()
+    p = lambda a: a.ctypes.data_as(_capi.c_int32_p)  # noqa: E731
+    rc = lib.aspire_plan_host_only(p(qo), p(kvp), p(kvl), len(kvl), hq, hkv, 128, 16, causal, num_sms,
+                                   buf.ctypes.data_as(ctypes.c_void_p), buf.nbytes, float_ws, ctypes.byref(info))
+    return rc, info, buf
+
+
+def _decode(buf, info):
+    w = buf.view(np.int32)
+    off_items = w[5]
+    items = w[off_items: off_items + info.num_items * 16].reshape(-1, 16)
+    return w, [dict(zip(ITEM_FIELDS, map(int, r))) for r in items]
+
+
+@pytest.mark.parametrize("draft_fraction", [0.0, 0.5, 1.0])
+def test_plan_covers_every_token_once(built_library, draft_fraction):
+    lay = make_layout(batch=12, ctx=3000, num_qo_heads=32, num_kv_heads=8, draft_fraction=draft_fraction,
+                      budget_pages=40, seed=3)
+    rc, info, buf = _plan(built_library, lay.qo_indptr, lay.kv_indptr, lay.kv_lens, 32, 8)
+    assert rc == 0, built_library.aspire_last_error()
+    w, items = _decode(buf, info)
+    assert w[0] == 0x41535042
+    group = 4
+    cover = {}
+    for it in items:
+        for pq in range(it["pq_begin"], it["pq_end"]):
+            key = (it["row"], it["kv_head"], pq)
+            cover.setdefault(key, []).append((it["tok_begin"], it["tok_end"]))
+        assert 0 <= it["chunk"] < it["n_chunks"]
+        assert (it["merge_id"] >= 0) == (it["n_chunks"] > 1)
+    for b in range(lay.batch):
+        nq = int(lay.q_lens[b]) * group
+        for h in range(8):
+            for pq in range(nq):
+                ranges = sorted(cover[(b, h, pq)])
+                assert ranges[0][0] == 0 and ranges[-1][1] == int(lay.kv_lens[b])
+                for (a0, a1), (b0, b1) in zip(ranges, ranges[1:]):
+                    assert a1 == b0
+    # CTA indptrs partition the item list.
+    g_ctas = w[2]
+    g_indptr = w[w[3]: w[3] + g_ctas + 1]
+    assert g_indptr[0] == 0 and np.all(np.diff(g_indptr) >= 0)
+    assert g_indptr[-1] == info.num_items_gather
+
+
+def test_plan_balances_ctas(built_library):
+    lay = make_layout(batch=64, ctx=32768, num_qo_heads=32, num_kv_heads=8, draft_fraction=0.5,
+                      budget_pages=128, seed=0)
+    rc, info, buf = _plan(built_library, lay.qo_indptr, lay.kv_indptr, lay.kv_lens, 32, 8, num_sms=148)
+    assert rc == 0, built_library.aspire_last_error()
+    w, items = _decode(buf, info)
+    loads = {}
+    for i, it in enumerate(items):
+        loads.setdefault(it["kind"], []).append(it["tok_end"] - it["tok_begin"])
+    assert info.partial_rows * 129 * 4 == info.float_bytes
+    assert info.float_bytes < 128 * 1024 * 1024
+
+
+def test_plan_rejects_bad_input(built_library):
+    rc, _, _ = _plan(built_library, [0, 1], [0, 1], [17], 32, 8)  # 17 tokens need 2 pages
+    assert rc == _capi.ASPIRE_ERR_INVALID
+    assert b"exceeds its page list" in built_library.aspire_last_error()
+    rc, _, _ = _plan(built_library, [0, 1], [0, 1], [5], 30, 8)  # heads not a multiple
+    assert rc == _capi.ASPIRE_ERR_INVALID
+    rc, _, _ = _plan(built_library, [0, 1], [0, 4096], [65536], 32, 8, float_ws=16)
+    assert rc == _capi.ASPIRE_ERR_CAPACITY
+
+
+def test_plan_handles_empty_and_padding_rows(built_library):
+    # row 0 empty (q_len 0), row 1 kv_len 0 with queries (bucket padding), row 2 normal.
+    rc, info, buf = _plan(built_library, [0, 0, 3, 4], [0, 0, 0, 2], [0, 0, 20], 16, 8)
+    assert rc == 0, built_library.aspire_last_error()
+    _, items = _decode(buf, info)
+    rows = {it["row"] for it in items}
+    assert rows == {1, 2}
+    assert all(it["tok_begin"] == it["tok_end"] == 0 for it in items if it["row"] == 1)

@@ -1,0 +1,113 @@
+"""GPU parity of the fused page scoring + radix top-k (aspire_select_pages)."""
+
+import pytest
+import torch
+
+from aspire_b200.page_selector import PageSelectorFirstLastAvg
+from oracle import page_selector as oracle_sel
+
+pytestmark = pytest.mark.gpu
+
+CASES = ["cfg1", "pct", "budget"]
+SCORE_RTOL = 2e-5
+
+
+def _selector(p, dev):
+    return PageSelectorFirstLastAvg(max_batch_size=p["B"], pages_per_slot=p["pps"], subset_cache_size=p["k"],
+                                    L=p["L"], n_heads=p["H"], page_size=16, max_seq_length=p["max_seq_len"],
+                                    device=dev, bsz=p["B"], dec_len=9, head_dim=128, kv_stride=p["kv_stride"],
+                                    draft_percent=p["draft_percent"], min_draft_pages=p["min_draft_pages"])
+
+
+def _assert_scores_close(got, ref):
+    fin = torch.isfinite(ref)
+    assert torch.equal(torch.isfinite(got), fin)
+    assert torch.equal(got[~fin], ref[~fin])
+    err = (got[fin] - ref[fin]).abs() / ref[fin].abs().clamp(min=1e-6)
+    assert err.max().item() <= SCORE_RTOL, err.max().item()
+
+
+@pytest.mark.parametrize("case", CASES)
+def test_fused_select_matches_reference(cuda_device, golden_dir, case):
+    g = torch.load(golden_dir / f"page_selector_{case}.pt", weights_only=False)
+    p = g["params"]
+    dev = cuda_device
+    sel = _selector(p, dev)
+    scores = torch.empty(p["B"], p["pps"], dtype=torch.float32, device=dev)
+    selected, valid = sel.select(g["dump"].to(dev), g["lse"].to(dev), g["num_pages"].to(dev),
+                                 g["block_table"].to(dev), g["qo_indptr"].to(dev), scores_out=scores)
+    torch.cuda.synchronize()
+    _assert_scores_close(scores.cpu(), g["scores_raw"])
+    # Bit-exact given identical fp32 scores: the oracle's top-k on the kernel's own scores.
+    o_sel, o_valid = oracle_sel.finalize_scores(scores.cpu(), g["num_pages"], g["block_table"], p["k"], p["L"],
+                                                p["draft_percent"], p["min_draft_pages"])
+    assert torch.equal(valid.cpu(), o_valid)
+    assert torch.equal(selected.cpu(), o_sel)
+    # And the reference's own tables on these (tie-free) fixtures.
+    assert torch.equal(valid.cpu(), g["valid"])
+    assert torch.equal(selected.cpu(), g["selected"])
+
+
+def test_topk_ties_lower_index_first(cuda_device, golden_dir):
+    g = torch.load(golden_dir / "page_selector_ties.pt", weights_only=False)
+    p = g["params"]
+    sel = PageSelectorFirstLastAvg(max_batch_size=p["B"], pages_per_slot=p["pps"], subset_cache_size=p["k"],
+                                   L=p["L"], n_heads=2, page_size=16, max_seq_length=p["pps"] * 16,
+                                   device=cuda_device, bsz=p["B"], dec_len=1)
+    got_sel, got_valid = sel.finalize_scores(g["scores_raw"].to(cuda_device), g["num_pages"].to(cuda_device),
+                                             g["block_table"].to(cuda_device))
+    o_sel, o_valid = oracle_sel.finalize_scores(g["scores_raw"], g["num_pages"], g["block_table"], p["k"], p["L"])
+    assert torch.equal(got_valid.cpu(), o_valid)
+    assert torch.equal(got_sel.cpu(), o_sel)
+
+
+@pytest.mark.parametrize("pps,k,L", [(64, 8, 2), (2080, 128, 8), (5136, 256, 8), (300, 300, 0)])
+def test_topk_random_scores_with_ties(cuda_device, pps, k, L):
+    gen = torch.Generator().manual_seed(pps + k)
+    B = 7
+    scores = torch.randint(0, 50, (B, pps), generator=gen).float() * 0.25
+    scores[0] = 1.0  # all tied
+    scores[1, ::3] = float("inf")
+    num_pages = torch.randint(1, pps + 1, (B,), generator=gen).to(torch.int32)
+    num_pages[2] = pps
+    num_pages[3] = 1
+    block_table = torch.stack([torch.randperm(10 * pps, generator=gen)[:pps] for _ in range(B)]).to(torch.int32)
+    for dp, mdp in ((None, None), (7.0, 32), (None, 5), (None, 2 * k)):
+        sel = PageSelectorFirstLastAvg(max_batch_size=B, pages_per_slot=pps, subset_cache_size=k, L=L, n_heads=2,
+                                       page_size=16, max_seq_length=pps * 16, device=cuda_device, bsz=B, dec_len=1,
+                                       draft_percent=dp, min_draft_pages=mdp)
+        got_sel, got_valid = sel.finalize_scores(scores.to(cuda_device), num_pages.to(cuda_device),
+                                                 block_table.to(cuda_device))
+        o_sel, o_valid = oracle_sel.finalize_scores(scores, num_pages, block_table, k, L, dp, mdp)
+        assert torch.equal(got_valid.cpu(), o_valid)
+        assert torch.equal(got_sel.cpu(), o_sel)
+
+
+def test_select_into_writes_table_in_place(cuda_device, golden_dir):
+    g = torch.load(golden_dir / "page_selector_cfg1.pt", weights_only=False)
+    p = g["params"]
+    dev = cuda_device
+    sel = _selector(p, dev)
+    width = p["k"] + 5
+    table = torch.full((p["B"] + 2, width), 777, dtype=torch.int32, device=dev)
+    counts = torch.full((p["B"] + 2,), -1, dtype=torch.int32, device=dev)
+    sel.select_into(table, counts, g["dump"].to(dev), g["lse"].to(dev), g["num_pages"].to(dev),
+                    g["block_table"].to(dev), g["qo_indptr"].to(dev))
+    ref_table = torch.full((p["B"] + 2, width), 777, dtype=torch.int32)
+    ref_counts = torch.full((p["B"] + 2,), -1, dtype=torch.int32)
+    oracle_sel.store_draft_rows(ref_table, ref_counts, g["selected"], g["valid"])
+    torch.cuda.synchronize()
+    assert torch.equal(table.cpu(), ref_table)
+    assert torch.equal(counts.cpu(), ref_counts)
+
+
+def test_select_subset_rows(cuda_device, golden_dir):
+    g = torch.load(golden_dir / "page_selector_cfg1.pt", weights_only=False)
+    p = g["params"]
+    dev = cuda_device
+    sel = _selector(p, dev)
+    ids = torch.tensor([2, 0], device=dev)
+    got_sel, got_valid = sel.select_subset(ids, g["dump"].to(dev), g["lse"].to(dev), g["num_pages"].to(dev),
+                                           g["block_table"].to(dev), g["qo_indptr"].to(dev))
+    assert torch.equal(got_sel.cpu(), g["selected"][[2, 0]])
+    assert torch.equal(got_valid.cpu(), g["valid"][[2, 0]])
