@@ -110,6 +110,7 @@ class AspireSelectArgs(ctypes.Structure):
         ("num_pages", ctypes.c_void_p),
         ("block_table", ctypes.c_void_p),
         ("block_table_stride", ctypes.c_int64),
+        ("block_table_cols", ctypes.c_int32),
         ("batch", ctypes.c_int32),
         ("num_heads", ctypes.c_int32),
         ("page_size", ctypes.c_int32),

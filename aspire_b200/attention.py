@@ -215,6 +215,9 @@ class HolisticAttentionWrapper:
         self._pinned_slot = (slot + 1) % PINNED_RING_DEPTH
 
         self._plan_info = info
+        self._plan_q_total = int(qo[batch])
+        self._plan_max_kv_len = int(kvl.max()) if batch else 0
+        self._plan_rows = batch
         self._kv_indices = paged_kv_indices
         self._page_size = int(page_size)
         self._sm_scale = sm_scale
@@ -248,6 +251,8 @@ class HolisticAttentionWrapper:
             raise ValueError("q head_dim must be contiguous")
         if kv.shape[2] != self._page_size or kv.shape[3] != self._num_kv_heads:
             raise ValueError("paged_kv_cache geometry does not match the plan")
+        if q.shape[0] < self._plan_q_total:
+            raise ValueError(f"q has {q.shape[0]} rows but the plan addresses {self._plan_q_total}")
         if out is None:
             out = torch.empty(q.shape, dtype=q.dtype, device=q.device)
         if out.stride(2) != 1 or out.shape != q.shape:
@@ -270,6 +275,10 @@ class HolisticAttentionWrapper:
             dump_stride = int(args[2])
             if dump.dtype != torch.float16 or not dump.is_contiguous():
                 raise ValueError("dump buffer must be a contiguous float16 tensor")
+            if dump_heads < self._num_qo_heads or dump_stride < self._plan_max_kv_len:
+                raise ValueError("dump buffer heads/stride smaller than the planned heads/kv_len")
+            if dump.numel() < self._plan_rows * dump_heads * 2 * dump_stride:
+                raise ValueError("dump buffer smaller than rows * num_heads * 2 * kv_stride")
 
         sm_scale = self._sm_scale if self._sm_scale is not None else 1.0 / math.sqrt(q.shape[2])
         a = _capi.AspireAttnArgs()

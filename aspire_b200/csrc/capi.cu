@@ -242,6 +242,8 @@ int aspire_select_pages(const AspireSelectArgs* a, void* stream) {
   if (!a->scores_in && (!a->dump || !a->lse || !a->qo_indptr))
     return set_error(ASPIRE_ERR_INVALID,
                      "aspire_select_pages: dump, lse and qo_indptr are required without scores_in");
+  if (a->block_table_cols <= 0 || a->block_table_stride < a->block_table_cols)
+    return set_error(ASPIRE_ERR_INVALID, "aspire_select_pages: bad block_table geometry");
   if (a->num_heads <= 0 || a->num_heads > kMaxSelHeads)
     return set_error(ASPIRE_ERR_INVALID, "aspire_select_pages: num_heads must be in [1, 128]");
   if (a->pages_per_slot <= 0 || a->subset_cache_size <= 0 || a->L < 0)
@@ -265,6 +267,7 @@ int aspire_select_pages(const AspireSelectArgs* a, void* stream) {
   p.num_pages = a->num_pages;
   p.block_table = a->block_table;
   p.block_table_stride = a->block_table_stride;
+  p.block_table_cols = a->block_table_cols;
   p.num_heads = a->num_heads;
   p.pages_per_slot = a->pages_per_slot;
   p.L = a->L;

@@ -32,6 +32,7 @@ struct SelectParams {
   const int32_t* num_pages;
   const int32_t* block_table;
   int64_t block_table_stride;
+  int32_t block_table_cols;
   int32_t num_heads, pages_per_slot, L, subset_cache_size, min_draft_pages;
   float draft_percent;
   float scale_log2;

@@ -229,7 +229,7 @@ __global__ void __launch_bounds__(kSelThreads) aspire_select_pages_kernel(Select
       }
       if (take) {
         const int slot = atomicAdd(&sh_count, 1);
-        if (slot < p.sort_cap) sortbuf[slot] = bt[i];
+        if (slot < p.sort_cap) sortbuf[slot] = bt[min(i, p.block_table_cols - 1)];
       }
     }
   }

@@ -76,6 +76,19 @@ class PageSelectorFirstLastAvg:
                 raise ValueError(f"{name} must be int32, got {t.dtype}")
         if block_table.stride(1) != 1 or table_out.stride(1) != 1:
             raise ValueError("block_table and table rows must be contiguous")
+        if block_table.shape[0] < batch or num_pages.shape[0] < batch or table_out.shape[0] < batch \
+                or counts_out.shape[0] < batch:
+            raise ValueError("block_table / num_pages / outputs have fewer rows than the batch")
+        if dump is not None:
+            if dump.dtype != torch.float16 or not dump.is_contiguous():
+                raise ValueError("dump buffer must be a contiguous float16 tensor")
+            rows = int(row_ids.max().item()) + 1 if row_ids is not None else batch
+            if dump.numel() < rows * self.n_heads * 2 * self._kv_stride:
+                raise ValueError("dump buffer smaller than rows * n_heads * 2 * kv_stride")
+            if lse is None or lse.dtype != torch.float32 or not lse.is_contiguous() or lse.shape[1] != self.n_heads:
+                raise ValueError("lse must be a contiguous fp32 [tokens, n_heads] tensor")
+            if qo_indptr.shape[0] < rows + 1:
+                raise ValueError("qo_indptr needs rows + 1 entries")
         a = _capi.AspireSelectArgs()
         a.dump = ptr(dump)
         a.kv_stride = self._kv_stride
@@ -88,6 +101,7 @@ class PageSelectorFirstLastAvg:
         a.num_pages = num_pages.data_ptr()
         a.block_table = block_table.data_ptr()
         a.block_table_stride = block_table.stride(0)
+        a.block_table_cols = block_table.shape[1]
         a.batch = int(batch)
         a.num_heads = self.n_heads
         a.page_size = self.page_size

@@ -202,6 +202,7 @@ typedef struct AspireSelectArgs {
   const int32_t* num_pages; /* int32 [batch] valid pages per request              */
   const int32_t* block_table; /* int32 [batch, block_table_stride]                */
   int64_t block_table_stride;
+  int32_t block_table_cols; /* page indices are clamped to cols - 1 (as the reference's topk_idx) */
   int32_t batch;
   int32_t num_heads;
   int32_t page_size;        /* must be 16 */
