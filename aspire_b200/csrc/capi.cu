@@ -7,6 +7,8 @@
 #include <cstring>
 #include <string>
 
+#include <cudaTypedefs.h>
+
 #include "kernels.cuh"
 #include "errors.h"
 
@@ -53,6 +55,39 @@ int ensure_smem(const void* func, size_t bytes, int* configured_bytes) {
                       "cudaFuncSetAttribute(max dynamic smem)");
   if (rc == ASPIRE_OK) *configured_bytes = static_cast<int>(bytes);
   return rc;
+}
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no libcuda link).
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+  }
+  return fn;
+}
+
+// 5-D view of the paged cache [pages, 2, 16, Hkv, 128] (innermost first:
+// dim, head, token, K/V, page) with a 64-dim x 16-token box, 128-byte swizzle.
+int encode_kv_tensor_map(CUtensorMap* map, const void* kv, int64_t num_pages, int num_kv_heads) {
+  PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
+  if (!enc) return set_error(ASPIRE_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
+  const cuuint64_t row = kHeadDim * 2;  // bytes per (token, head)
+  cuuint64_t dims[5] = {cuuint64_t(kHeadDim), cuuint64_t(num_kv_heads), cuuint64_t(kPageSize), 2,
+                        cuuint64_t(num_pages)};
+  cuuint64_t strides[4] = {row, row * num_kv_heads, row * num_kv_heads * kPageSize,
+                           row * num_kv_heads * kPageSize * 2};
+  cuuint32_t box[5] = {64, 1, cuuint32_t(kPageSize), 1, 1};
+  cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 5, const_cast<void*>(kv), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return set_error(ASPIRE_ERR_INVALID, "cuTensorMapEncodeTiled failed with code " + std::to_string(int(r)));
+  return ASPIRE_OK;
 }
 
 bool tc_env_enabled() {
@@ -185,7 +220,12 @@ int aspire_mixed_attention(const AspireAttnArgs* a, const AspirePlanInfo* plan, 
     const size_t smem = tc_smem_bytes();
     rc = ensure_smem(reinterpret_cast<const void*>(&aspire_attn_tc_kernel), smem, &tc_smem_cfg);
     if (rc) return rc;
-    aspire_attn_tc_kernel<<<plan->num_ctas * kTcCtasPerSm, 192, smem, st>>>(p);
+    if (a->num_pages_total <= 0 || a->num_pages_total > INT32_MAX)
+      return set_error(ASPIRE_ERR_INVALID, "aspire_mixed_attention: num_pages_total out of range");
+    alignas(64) CUtensorMap tmap;
+    rc = encode_kv_tensor_map(&tmap, a->kv_cache, a->num_pages_total, a->num_kv_heads);
+    if (rc) return rc;
+    aspire_attn_tc_kernel<<<plan->num_ctas * kTcCtasPerSm, 192, smem, st>>>(p, tmap);
     rc = check_cuda(cudaGetLastError(), "aspire_attn_tc_kernel launch");
     if (rc) return rc;
   }

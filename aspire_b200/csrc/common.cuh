@@ -67,6 +67,6 @@ constexpr int kTcCtasPerSm = 1;
 // Packed query rows handled by one gather-kernel item.
 constexpr int kGatherQTile = 4;
 // Packed query rows handled by one tcgen05 item (N of the MMA after padding).
-constexpr int kTcQTile = 64;
+constexpr int kTcQTile = 48;
 
 }  // namespace aspire

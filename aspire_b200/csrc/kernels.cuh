@@ -1,6 +1,8 @@
 // Parameter blocks and declarations of every kernel of libaspire_b200.
 #pragma once
 
+#include <cuda.h>
+
 #include "attn_common.cuh"
 
 namespace aspire {
@@ -49,7 +51,7 @@ constexpr int kSelThreads = 512;
 constexpr int kMaxSelHeads = 128;
 
 __global__ void aspire_attn_gather_kernel(AttnParams p);
-__global__ void aspire_attn_tc_kernel(AttnParams p);
+__global__ void aspire_attn_tc_kernel(AttnParams p, const __grid_constant__ CUtensorMap tmap);
 __global__ void aspire_append_kv_kernel(AppendParams p);
 __global__ void aspire_select_pages_kernel(SelectParams p);
 
