@@ -119,9 +119,12 @@ __global__ void __launch_bounds__(kThreads, kGatherCtasPerSm) aspire_attn_gather
     const int npg = it.tok_end > it.tok_begin ? (it.tok_end + kPageSize - 1) / kPageSize - pg0 : 0;
     const __nv_bfloat16* kv_head_base = p.kv + int64_t(it.kv_head) * kHeadDim;
 
-    auto issue = [&](int pi) {
+    // Page ids are read one issue ahead so their latency is off the copy path.
+    auto page_of = [&](int pi) -> int32_t {
+      return pi < npg ? __ldg(p.kv_indices + it.kv_page_base + pg0 + pi) : 0;
+    };
+    auto issue = [&](int pi, int32_t page) {
       const int stage = pi % kStages;
-      int32_t page = p.kv_indices[it.kv_page_base + pg0 + pi];
       int bytes = 16;
       if (page < 0 || int64_t(page) >= p.num_pages_total) {
         if (tid == 0) record_status(p.status, ASPIRE_STATUS_BAD_PAGE);
@@ -139,16 +142,22 @@ __global__ void __launch_bounds__(kThreads, kGatherCtasPerSm) aspire_attn_gather
       }
     };
 
+    int32_t ids[kStages - 1];
+#pragma unroll
+    for (int s = 0; s < kStages - 1; ++s) ids[s] = page_of(s);
 #pragma unroll
     for (int s = 0; s < kStages - 1; ++s) {
-      if (s < npg) issue(s);
+      if (s < npg) issue(s, ids[s]);
       cp_async_commit();
     }
+    int32_t next_id = page_of(kStages - 1);
 
     for (int pi = 0; pi < npg; ++pi) {
       cp_async_wait<kStages - 2>();
       __syncthreads();
-      if (pi + kStages - 1 < npg) issue(pi + kStages - 1);
+      const int32_t id = next_id;
+      next_id = page_of(pi + kStages);
+      if (pi + kStages - 1 < npg) issue(pi + kStages - 1, id);
       cp_async_commit();
 
       const int stage = pi % kStages;

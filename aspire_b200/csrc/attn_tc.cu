@@ -8,22 +8,27 @@
 // 128-token K/V tile feeds the whole GQA group and N stays small:
 //
 //   S^T[128 tok x N]  = K[128 tok x 128 d]  . Q^T      (A: K, K-major SW128)
-//   O^T[128 d   x N]  = V^T[128 d x 128 tok] . P^T     (A: V, MN-major SW128)
+//   O^T[128 d   x N] += V^T[128 d x 128 tok] . P^T     (A: V, MN-major SW128)
 //
-// Warp roles (192 threads):
-//   warp 0     TMA producer: gathers the tile's 8 pages through the page table
-//              as 2 KiB boxes (16 tokens x 64 dims, 128-byte swizzle) of a
-//              5-D tensor map over the paged cache; two 64 KiB stages.
-//   warp 1     MMA issuer (one thread) and TMEM owner (256 columns: two S and
-//              two O buffers).
+// Warp roles (224 threads):
+//   warp 0     K producer: TMA-gathers the tile's 8 pages (2 KiB boxes of 16
+//              tokens x 64 dims, 128-byte swizzle, through a 5-D tensor map
+//              over the paged cache) into a 2-stage K ring.
+//   warp 6     V producer: the same into a 3-stage V ring.
+//   warp 1     MMA issuer (one thread) and TMEM owner (256 columns: two S
+//              tiles and the O accumulator).  A K stage is released as soon
+//              as its QK^T completes, a V stage when its PV completes.
 //   warps 2-5  softmax / epilogue: thread r owns TMEM lane r, i.e. token r of
-//              the S tile and dim r of the O tile.  Column maxima are reduced
-//              with warp shuffles and shared memory, P^T is written as bf16
-//              in the no-swizzle MN-major layout, O is accumulated in
-//              registers with the online-softmax rescale.
-// Every mbarrier wait is bounded: on timeout the CTA records
-// ASPIRE_STATUS_TIMEOUT, stops, drains its own TMA loads and MMAs, frees TMEM
-// and returns.
+//              the S tile and dim r of the O tile.  The running column max is
+//              kept lazily: a tile only triggers the cross-thread max
+//              reduction (warp reduce-scatter + shared memory) and the O/l
+//              rescale when one of its logits exceeds the current max by more
+//              than 2^8 in the exp2 domain, so P stays <= 256 and the common
+//              tile needs one warp vote and one 128-thread barrier.  P^T is
+//              written as bf16 (no-swizzle MN-major), O accumulates in TMEM.
+// Every mbarrier wait is time-bounded: on timeout the CTA records
+// ASPIRE_STATUS_TIMEOUT, stops, drains its own TMA loads and MMAs, frees
+// TMEM and returns.
 //
 // Semantics are those of the gather kernel (FlashInfer's persistent paged
 // attention as ASPIRE drives it): bottom-right causal mask, base-2 LSE of the
@@ -37,31 +42,35 @@ namespace aspire {
 
 namespace {
 
-constexpr int kTcThreads = 192;
+constexpr int kTcThreads = 224;
 constexpr int kTile = 128;
 constexpr int kPagesPerTile = kTile / kPageSize;
-constexpr int kTcStages = 2;
+constexpr int kKStages = 2;
+constexpr int kVStages = 3;
 constexpr int kNMax = kTcQTile;
 constexpr uint32_t kTmemCols = 256;
-constexpr uint32_t kKvHalfBytes = kTile * 128;          // 128 rows x 128 B
-constexpr uint32_t kStageBytes = 4 * kKvHalfBytes;      // K lo, K hi, V lo, V hi
+constexpr uint32_t kHalfBytes = kTile * 128;       // 128 rows x 128 B (64 dims)
+constexpr uint32_t kSlotBytes = 2 * kHalfBytes;    // one K or V tile: two 64-dim halves
 constexpr uint32_t kQHalfBytes = kNMax * 128;
 constexpr uint32_t kPBufBytes = (kNMax / 8) * kTile * 16;
-constexpr uint64_t kWaitLimitNs = 1000000000ull;  // 1 s: far above any legitimate wait
+constexpr uint64_t kWaitLimitNs = 1000000000ull;   // 1 s: far above any legitimate wait
+constexpr float kLazyLog2 = 8.0f;                  // max growth tolerated before a rescale
 
 __host__ __device__ constexpr uint32_t col_s(int b) { return uint32_t(b) * 64u; }
-__host__ __device__ constexpr uint32_t col_o(int b) { return 128u + uint32_t(b) * 64u; }
+constexpr uint32_t kColO = 128;
 
 struct TcShared {
-  uint8_t kv[kTcStages][kStageBytes];
+  uint8_t k[kKStages][kSlotBytes];
+  uint8_t v[kVStages][kSlotBytes];
   uint8_t q[2][kQHalfBytes];
   uint8_t p[2][kPBufBytes];
   float red[2][4][kNMax];
   float red_l[4][kNMax];
-  float mrun[3][kNMax];
-  uint64_t kv_full[kTcStages], kv_empty[kTcStages];
-  uint64_t s_full[2], s_empty[2], p_full[2], p_empty[2], o_full[2], o_empty[2];
-  uint64_t q_full, done, grp;
+  int flags[2][4];
+  uint64_t k_full[kKStages], k_empty[kKStages];
+  uint64_t v_full[kVStages], v_empty[kVStages];
+  uint64_t s_full[2], s_empty[2], p_full[2], p_empty[2];
+  uint64_t o_free, q_full, done, grp;
   uint32_t tmem_base;
   int abort_flag;
   int merge_flag;
@@ -125,11 +134,18 @@ __device__ __forceinline__ bool aborted(TcShared& sm) {
   return *reinterpret_cast<volatile int*>(&sm.abort_flag) != 0;
 }
 
-// ------------------------------------------------------------------ producer
-__device__ void run_producer(const AttnParams& p, const CUtensorMap* tmap, TcShared& sm, int item_begin,
-                             int item_end, int lane) {
+// ------------------------------------------------------------------ producers
+// Lane pg (< 8) owns page pg of every tile: it reads the page id one tile
+// ahead (the read overlaps the wait for a free slot) and issues the page's two
+// 64-dim boxes of K (kv_sel 0) or V (kv_sel 1) into the ring slot.
+template <int STAGES>
+__device__ void run_producer(const AttnParams& p, const CUtensorMap* tmap, TcShared& sm,
+                             uint8_t (*ring)[kSlotBytes], uint64_t* full, uint64_t* empty, int kv_sel,
+                             int item_begin, int item_end, int lane) {
   uint32_t g = 0;
-  int64_t last_issue[kTcStages] = {-1, -1};
+  int64_t last_issue[STAGES];
+#pragma unroll
+  for (int s = 0; s < STAGES; ++s) last_issue[s] = -1;
   bool ok = true;
   for (int ii = item_begin; ii < item_end && ok; ++ii) {
     const WorkItem it = load_item(p.plan, ii);
@@ -137,34 +153,36 @@ __device__ void run_producer(const AttnParams& p, const CUtensorMap* tmap, TcSha
     const int nt = n_tiles_of(it);
     const int first_page = it.tok_begin / kPageSize;
     const int end_page = (it.tok_end + kPageSize - 1) / kPageSize;
+    auto page_id = [&](int t) -> int32_t {
+      const int lp = first_page + t * kPagesPerTile + lane;
+      if (lane >= kPagesPerTile || lp >= end_page) return -1;
+      return __ldg(p.kv_indices + it.kv_page_base + lp);
+    };
+    int32_t next_id = nt > 0 ? page_id(0) : -1;
     for (int t = 0; t < nt; ++t, ++g) {
-      const int s = g % kTcStages;
-      const uint32_t ph = (g / kTcStages) & 1;
-      if (!wait_bar(sm, sm.kv_empty[s], ph ^ 1, p.status)) {
+      const int32_t id = next_id;
+      if (t + 1 < nt) next_id = page_id(t + 1);
+      const int s = g % STAGES;
+      const uint32_t ph = (g / STAGES) & 1;
+      if (!wait_bar(sm, empty[s], ph ^ 1, p.status)) {
         ok = false;
         break;
       }
-      if (lane == 0) {
-        const uint32_t full = ptx::smem_addr(&sm.kv_full[s]);
-        ptx::mbar_arrive_expect_tx(full, kStageBytes);
-        const uint32_t base = ptx::smem_addr(sm.kv[s]);
-        for (int pg = 0; pg < kPagesPerTile; ++pg) {
-          const int lp = first_page + t * kPagesPerTile + pg;
-          int page = static_cast<int>(p.num_pages_total);  // out of range: TMA fills zeros
-          if (lp < end_page) {
-            const int32_t id = p.kv_indices[it.kv_page_base + lp];
-            if (id < 0 || int64_t(id) >= p.num_pages_total) {
-              record_status(p.status, ASPIRE_STATUS_BAD_PAGE);
-            } else {
-              page = id;
-            }
-          }
-          const uint32_t off = uint32_t(pg) * kPageSize * 128;
-          ptx::tma_load_5d(base + 0 * kKvHalfBytes + off, tmap, full, 0, it.kv_head, 0, 0, page);
-          ptx::tma_load_5d(base + 1 * kKvHalfBytes + off, tmap, full, 64, it.kv_head, 0, 0, page);
-          ptx::tma_load_5d(base + 2 * kKvHalfBytes + off, tmap, full, 0, it.kv_head, 0, 1, page);
-          ptx::tma_load_5d(base + 3 * kKvHalfBytes + off, tmap, full, 64, it.kv_head, 0, 1, page);
+      const uint32_t fb = ptx::smem_addr(&full[s]);
+      if (lane == 0) ptx::mbar_arrive_expect_tx(fb, kSlotBytes);
+      __syncwarp();
+      if (lane < kPagesPerTile) {
+        int page = static_cast<int>(p.num_pages_total);  // out of range: TMA fills zeros
+        const int lp = first_page + t * kPagesPerTile + lane;
+        if (lp < end_page) {
+          if (id < 0 || int64_t(id) >= p.num_pages_total)
+            record_status(p.status, ASPIRE_STATUS_BAD_PAGE);
+          else
+            page = id;
         }
+        const uint32_t base = ptx::smem_addr(ring[s]) + uint32_t(lane) * kPageSize * 128;
+        ptx::tma_load_5d(base, tmap, fb, 0, it.kv_head, 0, kv_sel, page);
+        ptx::tma_load_5d(base + kHalfBytes, tmap, fb, 64, it.kv_head, 0, kv_sel, page);
       }
       last_issue[s] = g;
       __syncwarp();
@@ -172,8 +190,9 @@ __device__ void run_producer(const AttnParams& p, const CUtensorMap* tmap, TcSha
   }
   if (!ok || aborted(sm)) {
     // Let this CTA's own copies land before the CTA releases its shared memory.
-    for (int s = 0; s < kTcStages; ++s)
-      if (last_issue[s] >= 0) drain_bar(sm.kv_full[s], uint32_t(last_issue[s] / kTcStages) & 1);
+#pragma unroll
+    for (int s = 0; s < STAGES; ++s)
+      if (last_issue[s] >= 0) drain_bar(full[s], uint32_t(last_issue[s] / STAGES) & 1);
   }
 }
 
@@ -182,28 +201,28 @@ __device__ void run_mma(const AttnParams& p, TcShared& sm, int item_begin, int i
   const uint32_t tmem = sm.tmem_base;
   uint32_t g = 0, items_done = 0;
   bool ok = true;
-  const uint32_t kv0 = ptx::smem_addr(sm.kv[0]);
+  const uint32_t k0 = ptx::smem_addr(sm.k[0]);
+  const uint32_t v0 = ptx::smem_addr(sm.v[0]);
   const uint32_t q0 = ptx::smem_addr(sm.q[0]);
   const uint32_t p0 = ptx::smem_addr(sm.p[0]);
 
-  auto issue_pv = [&](uint32_t u, uint32_t idesc_pv) -> bool {
-    const int b = u % 2;
-    const uint32_t ph = (u / 2) & 1;
-    if (!wait_bar(sm, sm.p_full[b], ph, p.status)) return false;
-    if (!wait_bar(sm, sm.o_empty[b], ph ^ 1, p.status)) return false;
+  // PV of global tile u; `first` marks the item's first tile (fresh accumulator).
+  auto issue_pv = [&](uint32_t u, bool first, uint32_t idesc_pv) -> bool {
+    if (first && !wait_bar(sm, sm.o_free, (items_done & 1) ^ 1, p.status)) return false;
+    if (!wait_bar(sm, sm.v_full[u % kVStages], (u / kVStages) & 1, p.status)) return false;
+    if (!wait_bar(sm, sm.p_full[u % 2], (u / 2) & 1, p.status)) return false;
     ptx::tc_fence_after();
     if (lane == 0) {
-      const uint32_t vbase = kv0 + uint32_t(b) * kStageBytes + 2 * kKvHalfBytes;
-      const uint32_t pbase = p0 + uint32_t(b) * kPBufBytes;
+      const uint32_t vbase = v0 + (u % kVStages) * kSlotBytes;
+      const uint32_t pbase = p0 + (u % 2) * kPBufBytes;
 #pragma unroll
       for (int kk = 0; kk < kTile / 16; ++kk) {
-        const uint64_t a = ptx::smem_desc(vbase + kk * 2048, kKvHalfBytes, 1024, ptx::kLayoutSw128);
+        const uint64_t a = ptx::smem_desc(vbase + kk * 2048, kHalfBytes, 1024, ptx::kLayoutSw128);
         const uint64_t bd = ptx::smem_desc(pbase + kk * 256, 128, kTile * 16, ptx::kLayoutNone);
-        ptx::mma_bf16(tmem + col_o(b), a, bd, idesc_pv, kk > 0 ? 1u : 0u);
+        ptx::mma_bf16(tmem + kColO, a, bd, idesc_pv, (!first || kk > 0) ? 1u : 0u);
       }
-      ptx::mma_commit(ptx::smem_addr(&sm.o_full[b]));
-      ptx::mma_commit(ptx::smem_addr(&sm.kv_empty[b]));
-      ptx::mma_commit(ptx::smem_addr(&sm.p_empty[b]));
+      ptx::mma_commit(ptx::smem_addr(&sm.v_empty[u % kVStages]));
+      ptx::mma_commit(ptx::smem_addr(&sm.p_empty[u % 2]));
     }
     __syncwarp();
     return true;
@@ -222,36 +241,99 @@ __device__ void run_mma(const AttnParams& p, TcShared& sm, int item_begin, int i
       ok = false;
       break;
     }
+    const uint32_t g0 = g;
     for (int t = 0; t < nt && ok; ++t, ++g) {
-      const int b = g % 2;
-      const uint32_t ph = (g / 2) & 1;
-      if (!wait_bar(sm, sm.kv_full[b], ph, p.status) || !wait_bar(sm, sm.s_empty[b], ph ^ 1, p.status)) {
+      const int ks = g % kKStages, sb = g % 2;
+      if (!wait_bar(sm, sm.k_full[ks], (g / kKStages) & 1, p.status) ||
+          !wait_bar(sm, sm.s_empty[sb], ((g / 2) & 1) ^ 1, p.status)) {
         ok = false;
         break;
       }
       ptx::tc_fence_after();
       if (lane == 0) {
-        const uint32_t kbase = kv0 + uint32_t(b) * kStageBytes;
+        const uint32_t kbase = k0 + uint32_t(ks) * kSlotBytes;
 #pragma unroll
         for (int kk = 0; kk < 128 / 16; ++kk) {
-          const uint32_t koff = uint32_t(kk / 4) * kKvHalfBytes + uint32_t(kk % 4) * 32;
+          const uint32_t koff = uint32_t(kk / 4) * kHalfBytes + uint32_t(kk % 4) * 32;
           const uint32_t qoff = uint32_t(kk / 4) * kQHalfBytes + uint32_t(kk % 4) * 32;
           const uint64_t a = ptx::smem_desc(kbase + koff, 16, 1024, ptx::kLayoutSw128);
           const uint64_t bd = ptx::smem_desc(q0 + qoff, 16, 1024, ptx::kLayoutSw128);
-          ptx::mma_bf16(tmem + col_s(b), a, bd, idesc_qk, kk > 0 ? 1u : 0u);
+          ptx::mma_bf16(tmem + col_s(sb), a, bd, idesc_qk, kk > 0 ? 1u : 0u);
         }
-        ptx::mma_commit(ptx::smem_addr(&sm.s_full[b]));
+        ptx::mma_commit(ptx::smem_addr(&sm.s_full[sb]));
+        ptx::mma_commit(ptx::smem_addr(&sm.k_empty[ks]));
       }
       __syncwarp();
-      if (t > 0 && !issue_pv(g - 1, idesc_pv)) ok = false;
+      if (t > 0 && !issue_pv(g - 1, g - 1 == g0, idesc_pv)) ok = false;
     }
-    if (ok && !issue_pv(g - 1, idesc_pv)) ok = false;
+    if (ok && !issue_pv(g - 1, g - 1 == g0, idesc_pv)) ok = false;
     ++items_done;
   }
   // Every MMA this thread issued has completed once `done` fires.
   if (lane == 0) ptx::mma_commit(ptx::smem_addr(&sm.done));
   __syncwarp();
   drain_bar(sm.done, 0);
+}
+
+// ------------------------------------------------------------------ warp reductions
+template <bool kMax>
+__device__ __forceinline__ float combine(float a, float b) {
+  return kMax ? fmaxf(a, b) : a + b;
+}
+
+// v[0..2W) -> v[0..W): keep the half selected by this lane's `off` bit, send
+// the other half to the partner lane, combine.
+template <int W, bool kMax>
+__device__ __forceinline__ void scatter_step(float* v, int lane, int off) {
+  const bool hi = (lane & off) != 0;
+#pragma unroll
+  for (int i = 0; i < W; ++i) {
+    const float keep = hi ? v[W + i] : v[i];
+    const float send = hi ? v[i] : v[W + i];
+    v[i] = combine<kMax>(keep, __shfl_xor_sync(0xffffffffu, send, off));
+  }
+}
+
+// Reduce-scatter over the 32 lanes: lane l returns the reduction of column l.
+template <bool kMax>
+__device__ __forceinline__ float reduce_scatter32(const float* src, int lane) {
+  float v[32];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = src[i];
+  scatter_step<16, kMax>(v, lane, 16);
+  scatter_step<8, kMax>(v, lane, 8);
+  scatter_step<4, kMax>(v, lane, 4);
+  scatter_step<2, kMax>(v, lane, 2);
+  scatter_step<1, kMax>(v, lane, 1);
+  return v[0];
+}
+
+// 16 columns over 32 lanes: lane l returns the reduction of column l & 15.
+template <bool kMax>
+__device__ __forceinline__ float reduce_scatter16(const float* src, int lane) {
+  float v[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = combine<kMax>(src[i], __shfl_xor_sync(0xffffffffu, src[i], 16));
+  scatter_step<8, kMax>(v, lane, 8);
+  scatter_step<4, kMax>(v, lane, 4);
+  scatter_step<2, kMax>(v, lane, 2);
+  scatter_step<1, kMax>(v, lane, 1);
+  return v[0];
+}
+
+// Per-warp reduction of N columns over the 32 lanes, written to out[0..N).
+template <int N, bool kMax>
+__device__ __forceinline__ void warp_columns(const float* v, float* out, int lane) {
+  if constexpr (N >= 32) {
+    out[lane] = reduce_scatter32<kMax>(v, lane);
+    if constexpr (N == 48) {
+      const float r = reduce_scatter16<kMax>(v + 32, lane);
+      if (lane < 16) out[32 + lane] = r;
+    }
+  } else {
+    const float r = reduce_scatter16<kMax>(v, lane);
+    if (lane < 16) out[lane] = r;
+  }
 }
 
 // ------------------------------------------------------------------ softmax / epilogue
@@ -262,69 +344,38 @@ __device__ bool consume_item(const AttnParams& p, TcShared& sm, const WorkItem& 
   const int nt = n_tiles_of(it);
   const uint32_t tmem_lane = sm.tmem_base + (uint32_t(wq * 32) << 16);
   const float scale = p.scale_log2;
+  const float lazy_raw = kLazyLog2 / scale;  // tolerated growth of a raw logit
   const int group = p.group;
 
   // Stage Q (K-major, 128-byte swizzle; rows >= nrows are zero).
   for (int e = ctid; e < N * 16; e += 128) {
     const int j = e >> 4, c = e & 15;
-    uint4 v = make_uint4(0, 0, 0, 0);
+    uint4 val = make_uint4(0, 0, 0, 0);
     if (j < nrows) {
       int q_idx, head;
       packed_row(p, it, it.pq_begin + j, q_idx, head);
-      v = *reinterpret_cast<const uint4*>(p.q + int64_t(it.q_start + q_idx) * p.q_stride_n +
-                                          int64_t(head) * p.q_stride_h + c * 8);
+      val = *reinterpret_cast<const uint4*>(p.q + int64_t(it.q_start + q_idx) * p.q_stride_n +
+                                            int64_t(head) * p.q_stride_h + c * 8);
     }
-    uint8_t* dst = sm.q[c >> 3] + j * 128 + (((c & 7) ^ (j & 7)) << 4);
-    *reinterpret_cast<uint4*>(dst) = v;
+    *reinterpret_cast<uint4*>(sm.q[c >> 3] + j * 128 + (((c & 7) ^ (j & 7)) << 4)) = val;
   }
   ptx::fence_proxy_async_smem();
   ptx::mbar_arrive(ptx::smem_addr(&sm.q_full));
 
-  // Per-column facts: query index, causal limit, dump slot.
   const int q_idx0 = it.pq_begin / group;
-  float o_acc[N], l[N];
+  float m_ref[N], l[N];
 #pragma unroll
   for (int j = 0; j < N; ++j) {
-    o_acc[j] = 0.f;
+    m_ref[j] = -INFINITY;
     l[j] = 0.f;
   }
-  bool ok = true;
   const uint32_t g0 = g;
-
-  auto acc_o = [&](int u) -> bool {
-    const uint32_t gu = g0 + u;
-    const int b = gu % 2;
-    const uint32_t ph = (gu / 2) & 1;
-    if (!wait_bar(sm, sm.o_full[b], ph, p.status)) return false;
-    ptx::tc_fence_after();
-    float ov[N];
-#pragma unroll
-    for (int i = 0; i < N / 16; ++i) ptx::tmem_ld16(tmem_lane + col_o(b) + 16 * i, ov + 16 * i);
-    ptx::tmem_wait_ld();
-    ptx::tc_fence_before();
-    ptx::mbar_arrive(ptx::smem_addr(&sm.o_empty[b]));
-    const float* m_now = sm.mrun[u % 3];
-    const float* m_prev = sm.mrun[(u + 2) % 3];
-#pragma unroll
-    for (int j = 0; j < N; ++j) {
-      float alpha = 0.f;
-      if (u > 0) {
-        const float mp = m_prev[j], mn = m_now[j];
-        alpha = (mp == -INFINITY) ? 0.f : (mp == mn ? 1.f : ex2((mp - mn) * scale));
-      }
-      o_acc[j] = fmaf(o_acc[j], alpha, ov[j]);
-    }
-    return true;
-  };
 
   for (int t = 0; t < nt; ++t) {
     const uint32_t gt = g0 + t;
     const int b = gt % 2;
     const uint32_t ph = (gt / 2) & 1;
-    if (!wait_bar(sm, sm.s_full[b], ph, p.status)) {
-      ok = false;
-      break;
-    }
+    if (!wait_bar(sm, sm.s_full[b], ph, p.status)) return false;
     ptx::tc_fence_after();
     float sv[N];
 #pragma unroll
@@ -345,7 +396,8 @@ __device__ bool consume_item(const AttnParams& p, TcShared& sm, const WorkItem& 
           const bool s0 = q_idx == 0, s1 = q_idx != 0 && q_idx + 1 == it.q_len;
           if (s0 || s1) {
             const int head = it.kv_head * group + (pq - q_idx * group);
-            const int64_t idx = ((int64_t(it.row) * p.dump_num_heads + head) * 2 + (s0 ? 0 : 1)) * p.dump_kv_stride + tok;
+            const int64_t idx =
+                ((int64_t(it.row) * p.dump_num_heads + head) * 2 + (s0 ? 0 : 1)) * p.dump_kv_stride + tok;
             p.dump[idx] = __float2half_rn(sv[j]);
           }
         }
@@ -353,8 +405,7 @@ __device__ bool consume_item(const AttnParams& p, TcShared& sm, const WorkItem& 
     }
     const int limit_min = causal ? (it.kv_len - it.q_len + q_idx0 + 1) : it.kv_len;
     // Padded columns (j >= nrows) only feed ignored O columns: they need no mask.
-    const bool full_tile = tile0 + kTile <= it.tok_end && tile0 + kTile <= limit_min;
-    if (!full_tile) {
+    if (!(tile0 + kTile <= it.tok_end && tile0 + kTile <= limit_min)) {
 #pragma unroll
       for (int j = 0; j < N; ++j) {
         const int q_idx = (it.pq_begin + j) / group;
@@ -362,86 +413,108 @@ __device__ bool consume_item(const AttnParams& p, TcShared& sm, const WorkItem& 
         if (!(in_chunk && tok < lim)) sv[j] = -INFINITY;
       }
     }
-    // Column maxima of the tile: butterfly within the warp, then across the 4 warps.
-    float* red = sm.red[t & 1][wq];
+
+    // Lazy running max: does any logit of the tile exceed its column's reference by > 2^8?
+    bool exceed = false;
+#pragma unroll
+    for (int j = 0; j < N; ++j) exceed |= sv[j] > m_ref[j] + lazy_raw;
+    const bool warp_exceed = __any_sync(0xffffffffu, exceed);
+    if (lane == 0) sm.flags[t & 1][wq] = warp_exceed ? 1 : 0;
+    if (!group_sync(sm, grp_uses, p.status)) return false;
+    const bool any_exceed =
+        (sm.flags[t & 1][0] | sm.flags[t & 1][1] | sm.flags[t & 1][2] | sm.flags[t & 1][3]) != 0;
+    if (any_exceed) {
+      // Exact column maxima of the tile, then the new references.
+      warp_columns<N, true>(sv, sm.red[t & 1][wq], lane);
+      if (!group_sync(sm, grp_uses, p.status)) return false;
+      const float* r0 = sm.red[t & 1][0];
+      const float* r1 = sm.red[t & 1][1];
+      const float* r2 = sm.red[t & 1][2];
+      const float* r3 = sm.red[t & 1][3];
+      float alpha[N];
+      bool grew = false;
+#pragma unroll
+      for (int j = 0; j < N; ++j) {
+        const float mn = fmaxf(m_ref[j], fmaxf(fmaxf(r0[j], r1[j]), fmaxf(r2[j], r3[j])));
+        alpha[j] = (m_ref[j] == -INFINITY) ? 0.f : (mn == m_ref[j] ? 1.f : ex2((m_ref[j] - mn) * scale));
+        grew |= (mn != m_ref[j]) && (m_ref[j] != -INFINITY);
+        m_ref[j] = mn;
+        l[j] *= alpha[j];
+      }
+      // `grew` is uniform (every thread computed the same column maxima).
+      if (grew && t > 0) {
+        // Rescale the O accumulator once the previous tile's PV has landed.  PV
+        // completion is observed on its P buffer's empty barrier, whose phases
+        // this thread waits on in order (so the parity test is unambiguous).
+        const uint32_t prev = gt - 1;
+        if (!wait_bar(sm, sm.p_empty[prev % 2], (prev / 2) & 1, p.status)) return false;
+        ptx::tc_fence_after();
+        float ov[N];
+#pragma unroll
+        for (int i = 0; i < N / 16; ++i) ptx::tmem_ld16(tmem_lane + kColO + 16 * i, ov + 16 * i);
+        ptx::tmem_wait_ld();
+#pragma unroll
+        for (int j = 0; j < N; ++j) ov[j] *= alpha[j];
+#pragma unroll
+        for (int i = 0; i < N / 16; ++i) ptx::tmem_st16(tmem_lane + kColO + 16 * i, ov + 16 * i);
+        ptx::tmem_wait_st();
+        ptx::tc_fence_before();
+      }
+    }
+
 #pragma unroll
     for (int j = 0; j < N; ++j) {
-      float mx = sv[j];
-#pragma unroll
-      for (int off = 16; off >= 1; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
-      if (lane == (j & 31)) red[j] = mx;
-    }
-    if (!group_sync(sm, grp_uses, p.status)) {
-      ok = false;
-      break;
-    }
-    const float* r0 = sm.red[t & 1][0];
-    const float* r1 = sm.red[t & 1][1];
-    const float* r2 = sm.red[t & 1][2];
-    const float* r3 = sm.red[t & 1][3];
-    const float* m_prev = sm.mrun[(t + 2) % 3];
-    float* m_cur = sm.mrun[t % 3];
-#pragma unroll
-    for (int j = 0; j < N; ++j) {
-      const float tmax = fmaxf(fmaxf(r0[j], r1[j]), fmaxf(r2[j], r3[j]));
-      const float mp = t > 0 ? m_prev[j] : -INFINITY;
-      const float mn = fmaxf(mp, tmax);
-      if (ctid == j) m_cur[j] = mn;
-      const float alpha = (mp == -INFINITY) ? 0.f : (mp == mn ? 1.f : ex2((mp - mn) * scale));
-      const float pv = (mn == -INFINITY) ? 0.f : ex2(fmaf(sv[j], scale, -mn * scale));
-      l[j] = fmaf(l[j], alpha, pv);
+      const float pv = (m_ref[j] == -INFINITY) ? 0.f : ex2(fmaf(sv[j], scale, -m_ref[j] * scale));
+      l[j] += pv;
       sv[j] = pv;
     }
     // P^T as bf16, MN-major without swizzle: 8 queries x 16 B per token, token-major.
-    if (!wait_bar(sm, sm.p_empty[b], ph ^ 1, p.status)) {
-      ok = false;
-      break;
-    }
+    if (!wait_bar(sm, sm.p_empty[b], ph ^ 1, p.status)) return false;
     uint8_t* pbuf = sm.p[b];
 #pragma unroll
     for (int c = 0; c < N / 8; ++c) {
-      uint4 v;
+      uint4 val;
       __nv_bfloat162 h0 = __floats2bfloat162_rn(sv[8 * c + 0], sv[8 * c + 1]);
       __nv_bfloat162 h1 = __floats2bfloat162_rn(sv[8 * c + 2], sv[8 * c + 3]);
       __nv_bfloat162 h2 = __floats2bfloat162_rn(sv[8 * c + 4], sv[8 * c + 5]);
       __nv_bfloat162 h3 = __floats2bfloat162_rn(sv[8 * c + 6], sv[8 * c + 7]);
-      v.x = *reinterpret_cast<uint32_t*>(&h0);
-      v.y = *reinterpret_cast<uint32_t*>(&h1);
-      v.z = *reinterpret_cast<uint32_t*>(&h2);
-      v.w = *reinterpret_cast<uint32_t*>(&h3);
-      *reinterpret_cast<uint4*>(pbuf + c * (kTile * 16) + r * 16) = v;
+      val.x = *reinterpret_cast<uint32_t*>(&h0);
+      val.y = *reinterpret_cast<uint32_t*>(&h1);
+      val.z = *reinterpret_cast<uint32_t*>(&h2);
+      val.w = *reinterpret_cast<uint32_t*>(&h3);
+      *reinterpret_cast<uint4*>(pbuf + c * (kTile * 16) + r * 16) = val;
     }
     ptx::fence_proxy_async_smem();
     ptx::mbar_arrive(ptx::smem_addr(&sm.p_full[b]));
-    if (t > 0 && !acc_o(t - 1)) {
-      ok = false;
-      break;
-    }
   }
-  if (ok && nt > 0 && !acc_o(nt - 1)) ok = false;
   g = g0 + nt;
-  if (!ok) return false;
+
+  // Final O: wait for the item's last PV (on its P buffer's empty barrier),
+  // read this lane (dim r), free the accumulator.
+  if (!wait_bar(sm, sm.p_empty[(g - 1) % 2], ((g - 1) / 2) & 1, p.status)) return false;
+  ptx::tc_fence_after();
+  float o_fin[N];
+#pragma unroll
+  for (int i = 0; i < N / 16; ++i) ptx::tmem_ld16(tmem_lane + kColO + 16 * i, o_fin + 16 * i);
+  ptx::tmem_wait_ld();
+  ptx::tc_fence_before();
+  ptx::mbar_arrive(ptx::smem_addr(&sm.o_free));
 
   // Column sums of l across the 128 threads.
-#pragma unroll
-  for (int j = 0; j < N; ++j) {
-    float sum = l[j];
-#pragma unroll
-    for (int off = 16; off >= 1; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
-    if (lane == (j & 31)) sm.red_l[wq][j] = sum;
-  }
+  warp_columns<N, false>(l, sm.red_l[wq], lane);
   if (!group_sync(sm, grp_uses, p.status)) return false;
-  const float* m_fin = sm.mrun[(nt + 2) % 3];  // m of the last tile
-  float o_fin[N];
 #pragma unroll
   for (int j = 0; j < N; ++j) {
     const float L = sm.red_l[0][j] + sm.red_l[1][j] + sm.red_l[2][j] + sm.red_l[3][j];
-    o_fin[j] = L > 0.f ? o_acc[j] / L : 0.f;
+    o_fin[j] = L > 0.f ? o_fin[j] / L : 0.f;
   }
-  float my_lse = -INFINITY;  // LSE of column ctid
-  if (ctid < nrows) {
-    const float L = sm.red_l[0][ctid] + sm.red_l[1][ctid] + sm.red_l[2][ctid] + sm.red_l[3][ctid];
-    my_lse = L > 0.f ? fmaf(m_fin[ctid], scale, lg2(L)) : -INFINITY;
+  float my_lse = -INFINITY;  // LSE of column ctid (every thread holds all references)
+#pragma unroll
+  for (int j = 0; j < N; ++j) {
+    if (j == ctid) {
+      const float L = sm.red_l[0][j] + sm.red_l[1][j] + sm.red_l[2][j] + sm.red_l[3][j];
+      my_lse = L > 0.f ? fmaf(m_ref[j], scale, lg2(L)) : -INFINITY;
+    }
   }
   const int d = r;  // this thread's output dim
   if (it.n_chunks <= 1) {
@@ -495,7 +568,7 @@ __device__ bool consume_item(const AttnParams& p, TcShared& sm, const WorkItem& 
       if (ctid == 0) counters[it.merge_id] = 0;
     }
   }
-  // The ring buffers are reused by the next item.
+  // The reduction buffers are reused by the next item.
   return group_sync(sm, grp_uses, p.status);
 }
 
@@ -547,18 +620,21 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kTcStages; ++s) {
-      ptx::mbar_init(ptx::smem_addr(&sm.kv_full[s]), 1);
-      ptx::mbar_init(ptx::smem_addr(&sm.kv_empty[s]), 1);
+    for (int s = 0; s < kKStages; ++s) {
+      ptx::mbar_init(ptx::smem_addr(&sm.k_full[s]), 1);
+      ptx::mbar_init(ptx::smem_addr(&sm.k_empty[s]), 1);
+    }
+    for (int s = 0; s < kVStages; ++s) {
+      ptx::mbar_init(ptx::smem_addr(&sm.v_full[s]), 1);
+      ptx::mbar_init(ptx::smem_addr(&sm.v_empty[s]), 1);
     }
     for (int b = 0; b < 2; ++b) {
       ptx::mbar_init(ptx::smem_addr(&sm.s_full[b]), 1);
       ptx::mbar_init(ptx::smem_addr(&sm.s_empty[b]), 128);
       ptx::mbar_init(ptx::smem_addr(&sm.p_full[b]), 128);
       ptx::mbar_init(ptx::smem_addr(&sm.p_empty[b]), 1);
-      ptx::mbar_init(ptx::smem_addr(&sm.o_full[b]), 1);
-      ptx::mbar_init(ptx::smem_addr(&sm.o_empty[b]), 128);
     }
+    ptx::mbar_init(ptx::smem_addr(&sm.o_free), 128);
     ptx::mbar_init(ptx::smem_addr(&sm.q_full), 128);
     ptx::mbar_init(ptx::smem_addr(&sm.done), 1);
     ptx::mbar_init(ptx::smem_addr(&sm.grp), 128);
@@ -576,7 +652,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   ptx::tc_fence_after();
 
   if (warp == 0) {
-    run_producer(p, &tmap, sm, item_begin, item_end, lane);
+    run_producer<kKStages>(p, &tmap, sm, sm.k, sm.k_full, sm.k_empty, 0, item_begin, item_end, lane);
+  } else if (warp == 6) {
+    run_producer<kVStages>(p, &tmap, sm, sm.v, sm.v_full, sm.v_empty, 1, item_begin, item_end, lane);
   } else if (warp == 1) {
     run_mma(p, sm, item_begin, item_end, lane);
   } else {
@@ -590,6 +668,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 }
 
 size_t tc_smem_bytes() { return sizeof(TcShared) + 1024; }
+
+int tc_threads() { return kTcThreads; }
 
 bool tc_kernel_available() { return true; }
 

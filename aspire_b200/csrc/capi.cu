@@ -225,7 +225,7 @@ int aspire_mixed_attention(const AspireAttnArgs* a, const AspirePlanInfo* plan, 
     alignas(64) CUtensorMap tmap;
     rc = encode_kv_tensor_map(&tmap, a->kv_cache, a->num_pages_total, a->num_kv_heads);
     if (rc) return rc;
-    aspire_attn_tc_kernel<<<plan->num_ctas * kTcCtasPerSm, 192, smem, st>>>(p, tmap);
+    aspire_attn_tc_kernel<<<plan->num_ctas * kTcCtasPerSm, tc_threads(), smem, st>>>(p, tmap);
     rc = check_cuda(cudaGetLastError(), "aspire_attn_tc_kernel launch");
     if (rc) return rc;
   }

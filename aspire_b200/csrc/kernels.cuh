@@ -57,6 +57,7 @@ __global__ void aspire_select_pages_kernel(SelectParams p);
 
 size_t gather_smem_bytes();
 size_t tc_smem_bytes();
+int tc_threads();
 bool tc_kernel_available();
 size_t select_smem_bytes(int pages_per_slot, int sort_cap);
 

@@ -66,9 +66,16 @@ class MixedLayout:
 def make_layout(*, batch: int, ctx: int, num_qo_heads: int, num_kv_heads: int, draft_fraction: float,
                 verify_q_len: Optional[int] = None, draft_len_range=(2, 8), budget_pages: int = 128,
                 pages_per_row: Optional[int] = None, draft_rows: Optional[List[int]] = None,
-                seed: int = 0) -> MixedLayout:
-    """Builds a mixed layout.  verify_q_len=None draws q_len = U{lo..hi} + 1."""
+                seed: int = 0, block_table: str = "random") -> MixedLayout:
+    """Builds a mixed layout.  verify_q_len=None draws q_len = U{lo..hi} + 1.
+
+    block_table="random" permutes each row's pages (scattered physical pages);
+    "arange" gives row r the contiguous pages [r*pages_per_row, (r+1)*pages_per_row),
+    the layout of the reference engine (aspire/models/sparse_draft_runner.py:241-250)."""
     rng = np.random.default_rng(seed)
+    block_table_kind = block_table
+    if block_table_kind not in ("random", "arange"):
+        raise ValueError("block_table must be 'random' or 'arange'")
     if pages_per_row is None:
         pages_per_row = (ctx + PAGE - 1) // PAGE
     modes = np.ones(batch, dtype=np.int32)
@@ -83,7 +90,8 @@ def make_layout(*, batch: int, ctx: int, num_qo_heads: int, num_kv_heads: int, d
     indices: List[np.ndarray] = []
     kv_indptr = np.zeros(batch + 1, dtype=np.int32)
     for r in range(batch):
-        block_table[r] = r * pages_per_row + rng.permutation(pages_per_row).astype(np.int32)
+        perm = rng.permutation(pages_per_row).astype(np.int32)
+        block_table[r] = r * pages_per_row + (perm if block_table_kind == "random" else np.arange(pages_per_row, dtype=np.int32))
         ctx_pages = (ctx + PAGE - 1) // PAGE
         if modes[r] == 1:
             ql = verify_q_len if verify_q_len is not None else int(rng.integers(draft_len_range[0], draft_len_range[1] + 1)) + 1

@@ -53,7 +53,23 @@ def parse_args():
     ap.add_argument("--impl", default="aspire_b200", choices=["aspire_b200", "reference"])
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    return ap.parse_args()
+    # Smaller cases of the same step (profiling captures); the headline run uses the defaults.
+    ap.add_argument("--batch", type=int, default=None)
+    ap.add_argument("--ctx", type=int, default=None)
+    ap.add_argument("--layers", type=int, default=None)
+    ap.add_argument("--block-table", default="arange", choices=["arange", "random"],
+                    help="arange: the reference engine's contiguous per-row pages; random: scattered pages")
+    args = ap.parse_args()
+    if args.batch is not None:
+        CFG["batch"] = args.batch
+    if args.ctx is not None:
+        CFG["ctx"] = args.ctx
+        CFG["pages_per_row"] = (args.ctx + 512 + 15) // 16
+    CFG["block_table"] = args.block_table
+    if args.layers is not None:
+        CFG["n_layer"] = args.layers
+        CFG["refresh_layer"] = max(args.layers - 2, 0)
+    return args
 
 
 def tp_heads(num_heads: int, rank: int, world: int) -> range:
@@ -129,7 +145,8 @@ def build_workload(device, rank: int, world: int):
     hq, hkv = len(hq_r), len(hkv_r)
     lay = make_layout(batch=CFG["batch"], ctx=CFG["ctx"], num_qo_heads=hq, num_kv_heads=hkv,
                       draft_fraction=CFG["draft_fraction"], budget_pages=CFG["budget_pages"],
-                      pages_per_row=CFG["pages_per_row"], seed=CFG["seed"])
+                      pages_per_row=CFG["pages_per_row"], seed=CFG["seed"],
+                      block_table=CFG.get("block_table", "arange"))
     full = full_context_layout(lay)
     return lay, full, last_page_lens(lay), last_page_lens(full)
 
