@@ -24,6 +24,7 @@ SOURCES = [
     "planner.cpp",
     "attn_gather.cu",
     "attn_tc.cu",
+    "attn_merge.cu",
     "append_kv.cu",
     "select_pages.cu",
 ]

@@ -83,16 +83,13 @@ __device__ __forceinline__ void store_final(const AttnParams& p, const WorkItem&
   if (d == 0 && p.lse) p.lse[tok * p.num_qo_heads + head] = lse;
 }
 
-// Split-KV epilogue of one item, run by all `nthreads` threads of the CTA
-// after the normalised partial rows (o_rows[r][d], lse_rows[r]) of this chunk
-// are available through `get_o`/`get_lse`.  Items that own their whole KV
-// range write through; chunked items publish a partial, and the CTA that
-// completes a merge group combines all chunks in chunk order (deterministic).
-// No CTA ever waits for another: the last arriver does the merge.
+// Epilogue of one item, run by all `nthreads` threads of the CTA once the
+// normalised rows (get_o(r, d), get_lse(r)) of this chunk are available.
+// Items that own their whole KV range write through; chunked items write an
+// fp32 partial (normalised O and LSE), combined later by the merge kernel.
 template <typename GetO, typename GetLse>
 __device__ __forceinline__ void finish_item(const AttnParams& p, const WorkItem& it, int tid,
-                                            int nthreads, int* smem_flag, GetO get_o,
-                                            GetLse get_lse) {
+                                            int nthreads, GetO get_o, GetLse get_lse) {
   const int nrows = it.pq_end - it.pq_begin;
   if (it.n_chunks <= 1) {
     for (int e = tid; e < nrows * kHeadDim; e += nthreads) {
@@ -108,36 +105,6 @@ __device__ __forceinline__ void finish_item(const AttnParams& p, const WorkItem&
     p.partial_o[(base + r) * kHeadDim + d] = get_o(r, d);
     if (d == 0) plse[base + r] = get_lse(r);
   }
-  __threadfence();
-  __syncthreads();
-  int32_t* counters = const_cast<int32_t*>(p.plan) + p.plan[kHdrOffCounters];
-  if (tid == 0) {
-    const int prev = atomicAdd(&counters[it.merge_id], 1);
-    *smem_flag = (prev == it.n_chunks - 1);
-  }
-  __syncthreads();
-  if (!*smem_flag) return;
-  __threadfence();
-  for (int e = tid; e < nrows * kHeadDim; e += nthreads) {
-    const int r = e / kHeadDim, d = e - r * kHeadDim;
-    float m = -INFINITY;
-    for (int c = 0; c < it.n_chunks; ++c)
-      m = fmaxf(m, __ldcg(plse + it.partial_base + int64_t(c) * nrows + r));
-    float acc = 0.f, wsum = 0.f;
-    if (m != -INFINITY) {
-      for (int c = 0; c < it.n_chunks; ++c) {
-        const int64_t prow = it.partial_base + int64_t(c) * nrows + r;
-        const float l = __ldcg(plse + prow);
-        const float w = ex2(l - m);
-        wsum += w;
-        acc += w * __ldcg(p.partial_o + prow * kHeadDim + d);
-      }
-    }
-    const float o = wsum > 0.f ? acc / wsum : 0.f;
-    const float lse = wsum > 0.f ? m + lg2(wsum) : -INFINITY;
-    store_final(p, it, it.pq_begin + r, d, o, lse);
-  }
-  if (tid == 0) counters[it.merge_id] = 0;
 }
 
 }  // namespace aspire

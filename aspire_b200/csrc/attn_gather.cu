@@ -7,7 +7,7 @@
 // shares every staged K/V row.  Half-warps own tokens (16 lanes x 8 dims),
 // reduce q.k with warp shuffles and keep an online softmax per half-warp;
 // the eight half-warp states are merged through shared memory at the end of
-// the chunk, and split-KV chunks are merged by the last CTA to finish.
+// the chunk; split-KV chunks write partials combined by the merge kernel.
 //
 // Semantics follow FlashInfer's persistent paged attention as ASPIRE drives
 // it (flashinfer include/flashinfer/attention/persistent.cuh:178-497,
@@ -253,7 +253,7 @@ __global__ void __launch_bounds__(kThreads, kGatherCtasPerSm) aspire_attn_gather
     }
     __syncthreads();
     finish_item(
-        p, it, tid, kThreads, &sm.flag, [&](int r, int d) { return sm.red.fo[r][d]; },
+        p, it, tid, kThreads, [&](int r, int d) { return sm.red.fo[r][d]; },
         [&](int r) { return sm.red.flse[r]; });
     __syncthreads();
   }

@@ -66,6 +66,8 @@ struct TcShared {
   uint8_t p[2][kPBufBytes];
   float red[2][4][kNMax];
   float red_l[4][kNMax];
+  float alpha[2][kNMax];
+  float mref[2][kNMax];   // column reference max x scale (log2 domain), double buffered
   int flags[2][4];
   uint64_t k_full[kKStages], k_empty[kKStages];
   uint64_t v_full[kVStages], v_empty[kVStages];
@@ -73,7 +75,6 @@ struct TcShared {
   uint64_t o_free, q_full, done, grp;
   uint32_t tmem_base;
   int abort_flag;
-  int merge_flag;
 };
 static_assert(sizeof(TcShared) + 1024 <= 227 * 1024, "tcgen05 kernel shared memory too large");
 static_assert(kNMax % 16 == 0 && kNMax <= 64, "N tile must be a multiple of 16 and fit a 64-column buffer");
@@ -294,12 +295,10 @@ __device__ __forceinline__ void scatter_step(float* v, int lane, int off) {
   }
 }
 
-// Reduce-scatter over the 32 lanes: lane l returns the reduction of column l.
+// Reduce-scatter over the 32 lanes, in place (v is destroyed): lane l returns
+// the reduction of column l.
 template <bool kMax>
-__device__ __forceinline__ float reduce_scatter32(const float* src, int lane) {
-  float v[32];
-#pragma unroll
-  for (int i = 0; i < 32; ++i) v[i] = src[i];
+__device__ __forceinline__ float reduce_scatter32(float* v, int lane) {
   scatter_step<16, kMax>(v, lane, 16);
   scatter_step<8, kMax>(v, lane, 8);
   scatter_step<4, kMax>(v, lane, 4);
@@ -308,12 +307,11 @@ __device__ __forceinline__ float reduce_scatter32(const float* src, int lane) {
   return v[0];
 }
 
-// 16 columns over 32 lanes: lane l returns the reduction of column l & 15.
+// 16 columns over 32 lanes, in place: lane l returns the reduction of column l & 15.
 template <bool kMax>
-__device__ __forceinline__ float reduce_scatter16(const float* src, int lane) {
-  float v[16];
+__device__ __forceinline__ float reduce_scatter16(float* v, int lane) {
 #pragma unroll
-  for (int i = 0; i < 16; ++i) v[i] = combine<kMax>(src[i], __shfl_xor_sync(0xffffffffu, src[i], 16));
+  for (int i = 0; i < 16; ++i) v[i] = combine<kMax>(v[i], __shfl_xor_sync(0xffffffffu, v[i], 16));
   scatter_step<8, kMax>(v, lane, 8);
   scatter_step<4, kMax>(v, lane, 4);
   scatter_step<2, kMax>(v, lane, 2);
@@ -322,8 +320,9 @@ __device__ __forceinline__ float reduce_scatter16(const float* src, int lane) {
 }
 
 // Per-warp reduction of N columns over the 32 lanes, written to out[0..N).
+// Destroys v.
 template <int N, bool kMax>
-__device__ __forceinline__ void warp_columns(const float* v, float* out, int lane) {
+__device__ __forceinline__ void warp_columns(float* v, float* out, int lane) {
   if constexpr (N >= 32) {
     out[lane] = reduce_scatter32<kMax>(v, lane);
     if constexpr (N == 48) {
@@ -363,12 +362,32 @@ __device__ bool consume_item(const AttnParams& p, TcShared& sm, const WorkItem& 
   ptx::mbar_arrive(ptx::smem_addr(&sm.q_full));
 
   const int q_idx0 = it.pq_begin / group;
-  float m_ref[N], l[N];
-#pragma unroll
-  for (int j = 0; j < N; ++j) {
-    m_ref[j] = -INFINITY;
-    l[j] = 0.f;
+  // First/last-query dump: the item's columns of query 0 (slot 0) and of query
+  // q_len-1 (slot 1, only when q_len > 1) are two runs of at most `group`
+  // consecutive S columns; each tile reads just those runs from TMEM.
+  int dump_n0 = 0, dump_n1 = 0, dump_c1 = 0;
+  __half* dump_base0 = nullptr;
+  __half* dump_base1 = nullptr;
+  const int64_t dump_col_stride = 2 * p.dump_kv_stride;  // between heads
+  if (p.dump != nullptr) {
+    const int last_lo = (it.q_len - 1) * group;  // first packed row of the last query
+    const int64_t head0 = int64_t(it.row) * p.dump_num_heads + int64_t(it.kv_head) * group;
+    if (it.pq_begin < group) {
+      dump_n0 = min(group - it.pq_begin, nrows);
+      dump_base0 = p.dump + (head0 + it.pq_begin) * dump_col_stride;
+    }
+    if (it.q_len > 1 && last_lo < it.pq_end) {
+      dump_c1 = max(last_lo - it.pq_begin, 0);
+      dump_n1 = it.pq_end - (it.pq_begin + dump_c1);
+      dump_base1 = p.dump + (head0 + it.pq_begin + dump_c1 - last_lo) * dump_col_stride + p.dump_kv_stride;
+    }
   }
+  // The column reference max (times scale) is uniform across threads and lives
+  // in shared memory (mref[cur]); the first tile of an item always sets it.
+  float l[N];
+#pragma unroll
+  for (int j = 0; j < N; ++j) l[j] = 0.f;
+  int cur = 0;
   const uint32_t g0 = g;
 
   for (int t = 0; t < nt; ++t) {
@@ -377,71 +396,98 @@ __device__ bool consume_item(const AttnParams& p, TcShared& sm, const WorkItem& 
     const uint32_t ph = (gt / 2) & 1;
     if (!wait_bar(sm, sm.s_full[b], ph, p.status)) return false;
     ptx::tc_fence_after();
-    float sv[N];
-#pragma unroll
-    for (int i = 0; i < N / 16; ++i) ptx::tmem_ld16(tmem_lane + col_s(b) + 16 * i, sv + 16 * i);
-    ptx::tmem_wait_ld();
-    ptx::tc_fence_before();
-    ptx::mbar_arrive(ptx::smem_addr(&sm.s_empty[b]));
-
     const int tile0 = it.tok_begin + t * kTile;
     const int tok = tile0 + r;
     const bool in_chunk = tok < it.tok_end;
-    if (p.dump != nullptr && in_chunk) {
+    const int limit_min = causal ? (it.kv_len - it.q_len + q_idx0 + 1) : it.kv_len;
+    // Padded columns (j >= nrows) only feed ignored O columns: they need no mask.
+    const bool full_tile = tile0 + kTile <= it.tok_end && tile0 + kTile <= limit_min;
+    auto load_s = [&](float* sv) {
 #pragma unroll
-      for (int j = 0; j < N; ++j) {
-        if (j < nrows) {
-          const int pq = it.pq_begin + j;
-          const int q_idx = pq / group;
-          const bool s0 = q_idx == 0, s1 = q_idx != 0 && q_idx + 1 == it.q_len;
-          if (s0 || s1) {
-            const int head = it.kv_head * group + (pq - q_idx * group);
-            const int64_t idx =
-                ((int64_t(it.row) * p.dump_num_heads + head) * 2 + (s0 ? 0 : 1)) * p.dump_kv_stride + tok;
-            p.dump[idx] = __float2half_rn(sv[j]);
-          }
+      for (int i = 0; i < N / 16; ++i) ptx::tmem_ld16(tmem_lane + col_s(b) + 16 * i, sv + 16 * i);
+      ptx::tmem_wait_ld();
+    };
+    auto mask_s = [&](float* sv) {
+      if (!full_tile) {
+#pragma unroll
+        for (int j = 0; j < N; ++j) {
+          const int q_idx = (it.pq_begin + j) / group;
+          const int lim = causal ? (it.kv_len - it.q_len + q_idx + 1) : it.kv_len;
+          if (!(in_chunk && tok < lim)) sv[j] = -INFINITY;
+        }
+      }
+    };
+    float sv[N];
+    load_s(sv);
+    if (dump_n0 > 0 || dump_n1 > 0) {
+      // tcgen05.ld is warp-collective: every lane loads, in-range lanes store.
+      float dv[8];
+      for (int c = 0; c < dump_n0; c += 8) {
+        ptx::tmem_ld8(tmem_lane + col_s(b) + c, dv);
+        ptx::tmem_wait_ld();
+        if (in_chunk) {
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            if (c + i < dump_n0) dump_base0[(c + i) * dump_col_stride + tok] = __float2half_rn(dv[i]);
+        }
+      }
+      for (int c = 0; c < dump_n1; c += 8) {
+        ptx::tmem_ld8(tmem_lane + col_s(b) + dump_c1 + c, dv);
+        ptx::tmem_wait_ld();
+        if (in_chunk) {
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            if (c + i < dump_n1) dump_base1[(c + i) * dump_col_stride + tok] = __float2half_rn(dv[i]);
         }
       }
     }
-    const int limit_min = causal ? (it.kv_len - it.q_len + q_idx0 + 1) : it.kv_len;
-    // Padded columns (j >= nrows) only feed ignored O columns: they need no mask.
-    if (!(tile0 + kTile <= it.tok_end && tile0 + kTile <= limit_min)) {
-#pragma unroll
-      for (int j = 0; j < N; ++j) {
-        const int q_idx = (it.pq_begin + j) / group;
-        const int lim = causal ? (it.kv_len - it.q_len + q_idx + 1) : it.kv_len;
-        if (!(in_chunk && tok < lim)) sv[j] = -INFINITY;
-      }
-    }
+    mask_s(sv);
 
     // Lazy running max: does any logit of the tile exceed its column's reference by > 2^8?
-    bool exceed = false;
+    const float* mr = sm.mref[cur];
+    bool exceed = (t == 0);
+    if (t > 0) {
 #pragma unroll
-    for (int j = 0; j < N; ++j) exceed |= sv[j] > m_ref[j] + lazy_raw;
+      for (int j = 0; j < N; ++j) exceed |= fmaf(sv[j], scale, -mr[j]) > kLazyLog2;
+    }
     const bool warp_exceed = __any_sync(0xffffffffu, exceed);
     if (lane == 0) sm.flags[t & 1][wq] = warp_exceed ? 1 : 0;
     if (!group_sync(sm, grp_uses, p.status)) return false;
     const bool any_exceed =
         (sm.flags[t & 1][0] | sm.flags[t & 1][1] | sm.flags[t & 1][2] | sm.flags[t & 1][3]) != 0;
     if (any_exceed) {
-      // Exact column maxima of the tile, then the new references.
+      // Exact column maxima of the tile (reduced in place), then the new
+      // references (in mref[cur ^ 1]); S is read again from TMEM afterwards.
       warp_columns<N, true>(sv, sm.red[t & 1][wq], lane);
+      load_s(sv);
+      mask_s(sv);
+      ptx::tc_fence_before();
+      ptx::mbar_arrive(ptx::smem_addr(&sm.s_empty[b]));
       if (!group_sync(sm, grp_uses, p.status)) return false;
       const float* r0 = sm.red[t & 1][0];
       const float* r1 = sm.red[t & 1][1];
       const float* r2 = sm.red[t & 1][2];
       const float* r3 = sm.red[t & 1][3];
-      float alpha[N];
+      float* mnew = sm.mref[cur ^ 1];
+      float* alpha_s = sm.alpha[t & 1];
       bool grew = false;
 #pragma unroll
       for (int j = 0; j < N; ++j) {
-        const float mn = fmaxf(m_ref[j], fmaxf(fmaxf(r0[j], r1[j]), fmaxf(r2[j], r3[j])));
-        alpha[j] = (m_ref[j] == -INFINITY) ? 0.f : (mn == m_ref[j] ? 1.f : ex2((m_ref[j] - mn) * scale));
-        grew |= (mn != m_ref[j]) && (m_ref[j] != -INFINITY);
-        m_ref[j] = mn;
-        l[j] *= alpha[j];
+        const float mo = t > 0 ? mr[j] : -INFINITY;
+        const float mn = fmaxf(mo, fmaxf(fmaxf(r0[j], r1[j]), fmaxf(r2[j], r3[j])) * scale);
+        const float alpha = (mo == -INFINITY) ? 0.f : (mn == mo ? 1.f : ex2(mo - mn));
+        grew |= (mn != mo) && (mo != -INFINITY);
+        const float pv = (mn == -INFINITY) ? 0.f : ex2(fmaf(sv[j], scale, -mn));
+        l[j] = fmaf(l[j], alpha, pv);
+        sv[j] = pv;
+        if (ctid == j) {
+          mnew[j] = mn;
+          alpha_s[j] = alpha;
+        }
       }
-      // `grew` is uniform (every thread computed the same column maxima).
+      cur ^= 1;
+      // New references and alphas visible to every thread (uniform branch).
+      if (!group_sync(sm, grp_uses, p.status)) return false;
       if (grew && t > 0) {
         // Rescale the O accumulator once the previous tile's PV has landed.  PV
         // completion is observed on its P buffer's empty barrier, whose phases
@@ -449,24 +495,28 @@ __device__ bool consume_item(const AttnParams& p, TcShared& sm, const WorkItem& 
         const uint32_t prev = gt - 1;
         if (!wait_bar(sm, sm.p_empty[prev % 2], (prev / 2) & 1, p.status)) return false;
         ptx::tc_fence_after();
-        float ov[N];
 #pragma unroll
-        for (int i = 0; i < N / 16; ++i) ptx::tmem_ld16(tmem_lane + kColO + 16 * i, ov + 16 * i);
-        ptx::tmem_wait_ld();
+        for (int i = 0; i < N / 16; ++i) {
+          float ov[16];
+          ptx::tmem_ld16(tmem_lane + kColO + 16 * i, ov);
+          ptx::tmem_wait_ld();
 #pragma unroll
-        for (int j = 0; j < N; ++j) ov[j] *= alpha[j];
-#pragma unroll
-        for (int i = 0; i < N / 16; ++i) ptx::tmem_st16(tmem_lane + kColO + 16 * i, ov + 16 * i);
+          for (int c = 0; c < 16; ++c) ov[c] *= alpha_s[16 * i + c];
+          ptx::tmem_st16(tmem_lane + kColO + 16 * i, ov);
+        }
         ptx::tmem_wait_st();
         ptx::tc_fence_before();
       }
-    }
-
+    } else {
+      ptx::tc_fence_before();
+      ptx::mbar_arrive(ptx::smem_addr(&sm.s_empty[b]));
 #pragma unroll
-    for (int j = 0; j < N; ++j) {
-      const float pv = (m_ref[j] == -INFINITY) ? 0.f : ex2(fmaf(sv[j], scale, -m_ref[j] * scale));
-      l[j] += pv;
-      sv[j] = pv;
+      for (int j = 0; j < N; ++j) {
+        const float m = mr[j];
+        const float pv = (m == -INFINITY) ? 0.f : ex2(fmaf(sv[j], scale, -m));
+        l[j] += pv;
+        sv[j] = pv;
+      }
     }
     // P^T as bf16, MN-major without swizzle: 8 queries x 16 B per token, token-major.
     if (!wait_bar(sm, sm.p_empty[b], ph ^ 1, p.status)) return false;
@@ -513,7 +563,7 @@ __device__ bool consume_item(const AttnParams& p, TcShared& sm, const WorkItem& 
   for (int j = 0; j < N; ++j) {
     if (j == ctid) {
       const float L = sm.red_l[0][j] + sm.red_l[1][j] + sm.red_l[2][j] + sm.red_l[3][j];
-      my_lse = L > 0.f ? fmaf(m_ref[j], scale, lg2(L)) : -INFINITY;
+      my_lse = L > 0.f ? sm.mref[cur][j] + lg2(L) : -INFINITY;
     }
   }
   const int d = r;  // this thread's output dim
@@ -539,34 +589,6 @@ __device__ bool consume_item(const AttnParams& p, TcShared& sm, const WorkItem& 
     for (int j = 0; j < N; ++j)
       if (j < nrows) p.partial_o[(base + j) * kHeadDim + d] = o_fin[j];
     if (ctid < nrows) plse[base + ctid] = my_lse;
-    __threadfence();
-    if (!group_sync(sm, grp_uses, p.status)) return false;
-    int32_t* counters = const_cast<int32_t*>(p.plan) + p.plan[kHdrOffCounters];
-    if (ctid == 0) {
-      const int prev = atomicAdd(&counters[it.merge_id], 1);
-      sm.merge_flag = (prev == it.n_chunks - 1);
-    }
-    if (!group_sync(sm, grp_uses, p.status)) return false;
-    if (sm.merge_flag) {
-      __threadfence();
-      for (int j = 0; j < nrows; ++j) {
-        float m = -INFINITY;
-        for (int c = 0; c < it.n_chunks; ++c)
-          m = fmaxf(m, __ldcg(plse + it.partial_base + int64_t(c) * nrows + j));
-        float acc = 0.f, wsum = 0.f;
-        if (m != -INFINITY) {
-          for (int c = 0; c < it.n_chunks; ++c) {
-            const int64_t prow = it.partial_base + int64_t(c) * nrows + j;
-            const float w = ex2(__ldcg(plse + prow) - m);
-            wsum += w;
-            acc += w * __ldcg(p.partial_o + prow * kHeadDim + d);
-          }
-        }
-        store_final(p, it, it.pq_begin + j, d, wsum > 0.f ? acc / wsum : 0.f,
-                    wsum > 0.f ? m + lg2(wsum) : -INFINITY);
-      }
-      if (ctid == 0) counters[it.merge_id] = 0;
-    }
   }
   // The reduction buffers are reused by the next item.
   return group_sync(sm, grp_uses, p.status);
@@ -639,7 +661,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     ptx::mbar_init(ptx::smem_addr(&sm.done), 1);
     ptx::mbar_init(ptx::smem_addr(&sm.grp), 128);
     sm.abort_flag = 0;
-    sm.merge_flag = 0;
     ptx::mbar_fence_init();
   }
   if (warp == 1) {

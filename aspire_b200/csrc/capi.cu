@@ -33,8 +33,8 @@ int check_cuda(int st, const char* what) {
 
 int plan_impl(const int32_t* qo_indptr, const int32_t* kv_indptr, const int32_t* kv_len,
               int32_t batch_size, int32_t num_qo_heads, int32_t num_kv_heads, int32_t head_dim,
-              int32_t page_size, int32_t causal, int32_t num_sms, bool tc_enabled,
-              void* host_buf, size_t host_buf_bytes, size_t float_ws_bytes,
+              int32_t page_size, int32_t causal, int32_t num_sms, bool tc_enabled, int32_t tc_min_rows,
+              int32_t tc_min_kv, void* host_buf, size_t host_buf_bytes, size_t float_ws_bytes,
               AspirePlanInfo* info);
 
 namespace {
@@ -90,6 +90,15 @@ int encode_kv_tensor_map(CUtensorMap* map, const void* kv, int64_t num_pages, in
   return ASPIRE_OK;
 }
 
+// Routing thresholds of rows to the tcgen05 kernel (packed query rows, KV
+// tokens); overridable for measurements through the environment.
+int32_t env_int(const char* name, int32_t dflt) {
+  const char* e = std::getenv(name);
+  return (e && *e) ? static_cast<int32_t>(std::strtol(e, nullptr, 10)) : dflt;
+}
+int32_t tc_min_rows() { return env_int("ASPIRE_B200_TC_MIN_ROWS", 1); }
+int32_t tc_min_kv() { return env_int("ASPIRE_B200_TC_MIN_KV", 4096); }
+
 bool tc_env_enabled() {
   const char* e = std::getenv("ASPIRE_B200_DISABLE_TC");
   return !(e && e[0] == '1');
@@ -109,7 +118,7 @@ const char* aspire_last_error(void) { return aspire::last_error(); }
 size_t aspire_status_offset(void) { return kStatusBytes; }
 
 const char* aspire_kernel_names(void) {
-  return "aspire_attn_gather_kernel\naspire_attn_tc_kernel\naspire_append_kv_kernel\n"
+  return "aspire_attn_gather_kernel\naspire_attn_tc_kernel\naspire_attn_merge_kernel\naspire_append_kv_kernel\n"
          "aspire_select_pages_kernel\n";
 }
 
@@ -120,8 +129,8 @@ int aspire_plan_host_only(const int32_t* qo_indptr, const int32_t* kv_indptr,
                           size_t host_buf_bytes, size_t float_ws_bytes, AspirePlanInfo* info) {
   clear_error();
   return plan_impl(qo_indptr, kv_indptr, kv_len, batch_size, num_qo_heads, num_kv_heads, head_dim,
-                   page_size, causal, num_ctas, tc_kernel_available() && tc_env_enabled(),
-                   host_buf, host_buf_bytes, float_ws_bytes, info);
+                   page_size, causal, num_ctas, tc_kernel_available() && tc_env_enabled(), tc_min_rows(),
+                   tc_min_kv(), host_buf, host_buf_bytes, float_ws_bytes, info);
 }
 
 int aspire_plan(const int32_t* qo_indptr, const int32_t* kv_indptr, const int32_t* kv_len,
@@ -136,8 +145,8 @@ int aspire_plan(const int32_t* qo_indptr, const int32_t* kv_indptr, const int32_
     if (rc) return rc;
   }
   int rc = plan_impl(qo_indptr, kv_indptr, kv_len, batch_size, num_qo_heads, num_kv_heads, head_dim,
-                     page_size, causal, num_ctas, tc_kernel_available() && tc_env_enabled(),
-                     host_buf, host_buf_bytes, float_ws_bytes, info);
+                     page_size, causal, num_ctas, tc_kernel_available() && tc_env_enabled(), tc_min_rows(),
+                     tc_min_kv(), host_buf, host_buf_bytes, float_ws_bytes, info);
   if (rc) return rc;
   if (size_t(info->int_bytes) + kStatusBytes > dev_int_ws_bytes)
     return set_error(ASPIRE_ERR_CAPACITY, "aspire_plan: plan needs " +
@@ -229,7 +238,9 @@ int aspire_mixed_attention(const AspireAttnArgs* a, const AspirePlanInfo* plan, 
     rc = check_cuda(cudaGetLastError(), "aspire_attn_tc_kernel launch");
     if (rc) return rc;
   }
-  return ASPIRE_OK;
+  // Split-KV merge (exits at once when the current plan split nothing).
+  aspire_attn_merge_kernel<<<plan->num_ctas * kMergeCtasPerSm, kMergeThreads, 0, st>>>(p);
+  return check_cuda(cudaGetLastError(), "aspire_attn_merge_kernel launch");
 }
 
 int aspire_append_kv(const AspireAppendArgs* a, void* stream) {

@@ -27,12 +27,14 @@ enum PlanHeader : int {
   kHdrOffGatherIndptr = 3,   // int32 index of gather CTA indptr [num_ctas + 1]
   kHdrOffTcIndptr = 4,       // int32 index of tcgen05 CTA indptr [num_ctas + 1]
   kHdrOffItems = 5,          // int32 index of the item array
-  kHdrOffCounters = 6,       // int32 index of the merge counters [num_merge]
+  kHdrOffMerge = 6,          // int32 index of the merge descriptors [num_merge]
   kHdrNumMerge = 7,
   kHdrPartialLseLo = 8,      // float index of the partial LSE array (lo/hi words)
   kHdrPartialLseHi = 9,
   kHdrCausal = 10,
   kHdrNumTcCtas = 11,        // grid of the tcgen05 kernel the list was built for
+  kHdrOffMergeUnits = 12,    // int32 index of the merge units [num_merge_units]
+  kHdrNumMergeUnits = 13,    // (merge group, packed row) pairs, one warp each
   kHdrWords = 16,
 };
 constexpr int32_t kPlanMagic = 0x41535042;  // "ASPB"
@@ -52,13 +54,29 @@ struct WorkItem {
   int32_t chunk;         // chunk index within the merge group
   int32_t n_chunks;
   int32_t partial_base;  // partial row of chunk 0 of the merge group
-  int32_t merge_id;      // counter index, -1 when n_chunks == 1
+  int32_t merge_id;      // merge descriptor index, -1 when n_chunks == 1
   int32_t kind;          // 0 = CUDA-core gather kernel, 1 = tcgen05 kernel
   int32_t reserved;
 };
 static_assert(sizeof(WorkItem) == 64, "WorkItem must stay 64 bytes");
 
 constexpr int kItemWords = sizeof(WorkItem) / 4;
+
+// A (row, KV head, packed-query tile) whose KV range was split into chunks:
+// the merge kernel combines its chunk partials (chunk c of packed row j at
+// partial row partial_base + c * nrows + j).
+struct MergeDesc {
+  int32_t q_start;
+  int32_t pq_begin;
+  int32_t nrows;
+  int32_t kv_head;
+  int32_t partial_base;
+  int32_t n_chunks;
+  int32_t reserved0;
+  int32_t reserved1;
+};
+static_assert(sizeof(MergeDesc) == 32, "MergeDesc must stay 32 bytes");
+constexpr int kMergeWords = sizeof(MergeDesc) / 4;
 
 // Resident CTAs per SM of each kernel class (sets the persistent grids).
 constexpr int kGatherCtasPerSm = 4;

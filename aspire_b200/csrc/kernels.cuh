@@ -52,6 +52,9 @@ constexpr int kMaxSelHeads = 128;
 
 __global__ void aspire_attn_gather_kernel(AttnParams p);
 __global__ void aspire_attn_tc_kernel(AttnParams p, const __grid_constant__ CUtensorMap tmap);
+constexpr int kMergeThreads = 128;
+constexpr int kMergeCtasPerSm = 4;
+__global__ void aspire_attn_merge_kernel(AttnParams p);
 __global__ void aspire_append_kv_kernel(AppendParams p);
 __global__ void aspire_select_pages_kernel(SelectParams p);
 

@@ -66,8 +66,8 @@ void assign_lpt(std::vector<WorkItem>& items, int num_ctas, std::vector<int32_t>
 
 int plan_impl(const int32_t* qo_indptr, const int32_t* kv_indptr, const int32_t* kv_len,
               int32_t batch_size, int32_t num_qo_heads, int32_t num_kv_heads, int32_t head_dim,
-              int32_t page_size, int32_t causal, int32_t num_sms, bool tc_enabled,
-              void* host_buf, size_t host_buf_bytes, size_t float_ws_bytes,
+              int32_t page_size, int32_t causal, int32_t num_sms, bool tc_enabled, int32_t tc_min_rows,
+              int32_t tc_min_kv, void* host_buf, size_t host_buf_bytes, size_t float_ws_bytes,
               AspirePlanInfo* info) {
   if (!qo_indptr || !kv_indptr || !kv_len || !host_buf || !info)
     return set_error(ASPIRE_ERR_INVALID, "aspire_plan: null pointer argument");
@@ -108,7 +108,9 @@ int plan_impl(const int32_t* qo_indptr, const int32_t* kv_indptr, const int32_t*
     }
     max_q_len = std::max(max_q_len, ql);
     const int32_t nq = ql * group;
-    const bool wide = tc_enabled && nq > kGatherQTile;
+    // tcgen05 for wide query tiles, and for narrow rows with long contexts
+    // (the tensor-core tile streams K/V better than the CUDA-core gather).
+    const bool wide = tc_enabled && (nq > kGatherQTile || nq >= tc_min_rows || kl >= tc_min_kv);
     const int tile = wide ? kTcQTile : kGatherQTile;
     for (int h = 0; h < num_kv_heads; ++h) {
       for (int p0 = 0; p0 < nq; p0 += tile) {
@@ -127,6 +129,8 @@ int plan_impl(const int32_t* qo_indptr, const int32_t* kv_indptr, const int32_t*
   chunk = (chunk + 127) / 128 * 128;
 
   std::vector<WorkItem> gather_items, tc_items;
+  std::vector<MergeDesc> merges;
+  std::vector<int32_t> merge_units;  // (merge index << 8) | packed row within the tile
   int32_t num_merge = 0;
   int64_t partial_rows = 0;
   for (const GroupDesc& g : groups) {
@@ -140,6 +144,15 @@ int plan_impl(const int32_t* qo_indptr, const int32_t* kv_indptr, const int32_t*
         return set_error(ASPIRE_ERR_CAPACITY, "aspire_plan: too many partial rows");
       partial_base = static_cast<int32_t>(partial_rows);
       partial_rows += int64_t(n_chunks) * rows;
+      MergeDesc md{};
+      md.q_start = g.q_start;
+      md.pq_begin = g.pq_begin;
+      md.nrows = rows;
+      md.kv_head = g.kv_head;
+      md.partial_base = partial_base;
+      md.n_chunks = n_chunks;
+      merges.push_back(md);
+      for (int32_t j = 0; j < rows; ++j) merge_units.push_back((merge_id << 8) | j);
     }
     for (int32_t c = 0; c < n_chunks; ++c) {
       WorkItem it{};
@@ -171,13 +184,15 @@ int plan_impl(const int32_t* qo_indptr, const int32_t* kv_indptr, const int32_t*
   for (auto& v : tc_indptr) v += n_gather;
   const int32_t num_items = n_gather + static_cast<int32_t>(tc_ordered.size());
 
-  // Layout (int32 words): header | gather indptr | tc indptr | items | counters.
+  // Layout (int32 words): header | gather indptr | tc indptr | items | merges | merge units.
   const int64_t off_gather = kHdrWords;
   const int64_t off_tc = off_gather + gather_ctas + 1;
   int64_t off_items = off_tc + tc_ctas + 1;
   off_items = (off_items + 15) / 16 * 16;  // 64-byte aligned items
-  const int64_t off_counters = off_items + int64_t(num_items) * kItemWords;
-  const int64_t total_words = off_counters + num_merge;
+  const int64_t off_merge = off_items + int64_t(num_items) * kItemWords;
+  const int64_t off_units = off_merge + int64_t(num_merge) * kMergeWords;
+  const int32_t num_units = static_cast<int32_t>(merge_units.size());
+  const int64_t total_words = off_units + num_units;
   const int64_t int_bytes = total_words * 4;
   if (size_t(int_bytes) > host_buf_bytes)
     return set_error(ASPIRE_ERR_CAPACITY, "aspire_plan: plan needs " + std::to_string(int_bytes) +
@@ -199,8 +214,10 @@ int plan_impl(const int32_t* qo_indptr, const int32_t* kv_indptr, const int32_t*
   w[kHdrOffGatherIndptr] = static_cast<int32_t>(off_gather);
   w[kHdrOffTcIndptr] = static_cast<int32_t>(off_tc);
   w[kHdrOffItems] = static_cast<int32_t>(off_items);
-  w[kHdrOffCounters] = static_cast<int32_t>(off_counters);
+  w[kHdrOffMerge] = static_cast<int32_t>(off_merge);
   w[kHdrNumMerge] = num_merge;
+  w[kHdrOffMergeUnits] = static_cast<int32_t>(off_units);
+  w[kHdrNumMergeUnits] = num_units;
   const int64_t lse_off = partial_rows * kHeadDim;
   w[kHdrPartialLseLo] = static_cast<int32_t>(lse_off & 0xffffffff);
   w[kHdrPartialLseHi] = static_cast<int32_t>(lse_off >> 32);
@@ -211,7 +228,8 @@ int plan_impl(const int32_t* qo_indptr, const int32_t* kv_indptr, const int32_t*
   if (!tc_ordered.empty())
     std::memcpy(w + off_items + int64_t(n_gather) * kItemWords, tc_ordered.data(),
                 tc_ordered.size() * sizeof(WorkItem));
-  std::memset(w + off_counters, 0, size_t(num_merge) * 4);
+  if (num_merge) std::memcpy(w + off_merge, merges.data(), merges.size() * sizeof(MergeDesc));
+  if (num_units) std::memcpy(w + off_units, merge_units.data(), merge_units.size() * 4);
 
   std::memset(info, 0, sizeof(*info));
   info->num_items = num_items;

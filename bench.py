@@ -302,6 +302,40 @@ def kernel_roofline(hp: HotPath, steps: int, peak: float, peak_kind: str):
             "algorithmic_bytes_per_launch": int(bytes_)}
 
 
+def breakdown(hp: HotPath, reps: int = 5) -> dict:
+    """Average device time of each call of the step, timed alone (CUDA events)."""
+    L = CFG["n_layer"]
+    calls = {
+        "append": lambda: hp.append_kv(hp.k_new[0], hp.v_new[0], hp.qo_indptr, hp.kv, hp.mixed_indices,
+                                       hp.mixed_indptr, hp.mixed_last, 16),
+        "mixed_attention": lambda: hp.mixed.run(hp.q[0], hp.kv, out=hp.out[0]),
+        "refresh_attention": lambda: hp.refresh.run(hp.q[L - 2], hp.kv, hp.dump, hp.lay.num_qo_heads, hp.kv_stride,
+                                                    out=hp.out[L - 2], lse=hp.lse),
+        "refresh_nodump": lambda: hp.refresh_nodump.run(hp.q[L - 2], hp.kv, out=hp.out[L - 2], lse=hp.lse),
+        "select_pages": lambda: hp.selector.select_into(hp.draft_table, hp.draft_counts, hp.dump, hp.lse,
+                                                        hp.num_pages, hp.block_table, hp.qo_indptr),
+    }
+    if not hasattr(hp, "refresh_nodump"):
+        from aspire_b200.attention import HolisticAttentionWrapper
+        full = hp.full
+        hp.refresh_nodump = HolisticAttentionWrapper(torch.empty(1, device=hp.device))
+        t = lambda a: torch.from_numpy(np.ascontiguousarray(a, dtype=np.int32))  # noqa: E731
+        hp.refresh_nodump.plan_host(t(full.qo_indptr), t(full.kv_indptr), t(full.kv_lens), hp.full_indices,
+                                    full.num_qo_heads, full.num_kv_heads, 128, 16, causal=True)
+    res = {}
+    for name, fn in calls.items():
+        fn()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(reps):
+            fn()
+        b.record()
+        torch.cuda.synchronize()
+        res[name + "_ms"] = round(a.elapsed_time(b) / reps, 4)
+    return res
+
+
 def e2e_measure(hp: HotPath, steps: int, warmup: int, bytes_per_step: int):
     """Through the public API with host buffers: H2D of the step's q / new K,V, host
     planning of both attention programs, the step, D2H of outputs and tables."""
@@ -443,6 +477,11 @@ def main():
     value = float(tot_bytes.item()) / (ms_max * 1e-3) / 1e9
 
     roof = kernel_roofline(hp, args.steps, peak, peak_kind)
+    parts = breakdown(hp)
+    parts["refresh_attention_GBps"] = round(sb["refresh"] / (parts["refresh_attention_ms"] * 1e-3) / 1e9, 1)
+    parts["mixed_attention_GBps"] = round(sb["mixed"] / (parts["mixed_attention_ms"] * 1e-3) / 1e9, 1)
+    parts["tc_items"] = [hp.mixed.plan_info.num_items_tc, hp.refresh.plan_info.num_items_tc]
+    parts["gather_items"] = [hp.mixed.plan_info.num_items_gather, hp.refresh.plan_info.num_items_gather]
     e2e = None
     if not args.no_e2e:
         dt, h2d, d2h = e2e_measure(hp, max(2, args.steps // 2), 1, sb["total"])
@@ -466,7 +505,7 @@ def main():
                                    "verify q_len U{3..9}, budget 128 pages, one resident layer cache",
                        "batch": CFG["batch"], "ctx": CFG["ctx"], "tp": world, "heads_per_rank": [lay.num_qo_heads, lay.num_kv_heads],
                        "l2": "inputs larger than L2 (8.7 GB cache at TP1)", "bytes_per_step": sb},
-            "roofline": roof, "clocks": clocks.summary(), "e2e": e2e,
+            "roofline": roof, "breakdown": parts, "clocks": clocks.summary(), "e2e": e2e,
             "gpu_launches": hp.launches_per_step() * args.steps,
             "cpu_baseline": cb,
         }

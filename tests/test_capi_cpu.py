@@ -66,6 +66,10 @@ def test_plan_covers_every_token_once(built_library, draft_fraction):
             cover.setdefault(key, []).append((it["tok_begin"], it["tok_end"]))
         assert 0 <= it["chunk"] < it["n_chunks"]
         assert (it["merge_id"] >= 0) == (it["n_chunks"] > 1)
+        if it["merge_id"] >= 0:
+            md = w[w[6] + 8 * it["merge_id"]: w[6] + 8 * it["merge_id"] + 8]
+            assert md[2] == it["pq_end"] - it["pq_begin"] and md[5] == it["n_chunks"]
+            assert md[4] == it["partial_base"] and md[3] == it["kv_head"]
     for b in range(lay.batch):
         nq = int(lay.q_lens[b]) * group
         for h in range(8):
