@@ -38,6 +38,8 @@ import torch
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
+from aspire_b200.tp import local_head_counts  # noqa: E402
+
 METRIC = "mixed-attn HBM GB/s (% of peak); accepted tokens/s per box at 1/2/4/8 B200"
 UNIT = "GB/s"
 
@@ -70,13 +72,6 @@ def parse_args():
         CFG["n_layer"] = args.layers
         CFG["refresh_layer"] = max(args.layers - 2, 0)
     return args
-
-
-def tp_heads(num_heads: int, rank: int, world: int) -> range:
-    """Contiguous head range of a rank, remainder to the low ranks (aspire/tp.py:35-51)."""
-    base, rem = divmod(num_heads, world)
-    start = rank * base + min(rank, rem)
-    return range(start, start + base + (1 if rank < rem else 0))
 
 
 def measured_peaks():
@@ -140,9 +135,7 @@ class ClockSampler:
 def build_workload(device, rank: int, world: int):
     from aspire_b200.workloads import full_context_layout, make_layout, last_page_lens
 
-    hq_r = tp_heads(CFG["num_qo_heads"], rank, world)
-    hkv_r = tp_heads(CFG["num_kv_heads"], rank, world)
-    hq, hkv = len(hq_r), len(hkv_r)
+    hq, hkv = local_head_counts(CFG["num_qo_heads"], CFG["num_kv_heads"], rank, world)
     lay = make_layout(batch=CFG["batch"], ctx=CFG["ctx"], num_qo_heads=hq, num_kv_heads=hkv,
                       draft_fraction=CFG["draft_fraction"], budget_pages=CFG["budget_pages"],
                       pages_per_row=CFG["pages_per_row"], seed=CFG["seed"],
@@ -417,8 +410,7 @@ def reference_arm(args, rank, world):
     if rank != 0:
         return
     from aspire_b200.workloads import full_context_layout
-    hq = len(tp_heads(CFG["num_qo_heads"], 0, world))
-    hkv = len(tp_heads(CFG["num_kv_heads"], 0, world))
+    hq, hkv = local_head_counts(CFG["num_qo_heads"], CFG["num_kv_heads"], 0, world)
     from aspire_b200.workloads import make_layout
     lay = make_layout(batch=CFG["batch"], ctx=CFG["ctx"], num_qo_heads=hq, num_kv_heads=hkv,
                       draft_fraction=CFG["draft_fraction"], budget_pages=CFG["budget_pages"],
