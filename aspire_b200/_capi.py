@@ -20,6 +20,10 @@ ASPIRE_ERR_CUDA = -2
 ASPIRE_ERR_CAPACITY = -3
 ASPIRE_ERR_DEVICE = -4
 
+# Built-in workspaces of aspire_mixed_attention_noalloc (include/aspire_b200.h).
+NOALLOC_INT_BYTES = 512 * 1024
+NOALLOC_FLOAT_BYTES = 8 * 1024 * 1024
+
 STATUS_BAD_PAGE = 1
 STATUS_BAD_PLAN = 2
 STATUS_BAD_ROW = 4
@@ -148,6 +152,10 @@ _SIGNATURES = {
     "aspire_mixed_attention": (
         ctypes.c_int,
         [ctypes.POINTER(AspireAttnArgs), ctypes.POINTER(AspirePlanInfo), ctypes.c_void_p],
+    ),
+    "aspire_mixed_attention_noalloc": (
+        ctypes.c_int,
+        [ctypes.POINTER(AspireAttnArgs), ctypes.POINTER(AspirePlanInfo), ctypes.c_void_p, ctypes.c_void_p],
     ),
     "aspire_append_kv": (ctypes.c_int, [ctypes.POINTER(AspireAppendArgs), ctypes.c_void_p]),
     "aspire_select_pages": (ctypes.c_int, [ctypes.POINTER(AspireSelectArgs), ctypes.c_void_p]),

@@ -27,6 +27,7 @@ SOURCES = [
     "attn_merge.cu",
     "append_kv.cu",
     "select_pages.cu",
+    "noalloc.cu",
 ]
 
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]

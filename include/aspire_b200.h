@@ -156,6 +156,36 @@ typedef struct AspireAttnArgs {
  */
 ASPIRE_API int aspire_mixed_attention(const AspireAttnArgs* args, const AspirePlanInfo* plan, void* stream);
 
+/*
+ * Sizes of the two device arrays that aspire_mixed_attention_noalloc uses
+ * instead of caller-provided workspaces: the plan array (status word + work
+ * list) and the split-KV partials array.  Every GPU that loads the library
+ * holds both (8.5 MiB in total) until the process exits.
+ */
+#define ASPIRE_NOALLOC_INT_BYTES ((size_t)512 * 1024)
+#define ASPIRE_NOALLOC_FLOAT_BYTES ((size_t)8 * 1024 * 1024)
+
+/*
+ * aspire_mixed_attention for callers that cannot allocate device memory --
+ * a plug-in whose host application owns every byte of GPU memory, or a
+ * serving loop whose device memory is fixed at start-up (cudaMalloc would
+ * also synchronise the device mid-step).  This entry point has no
+ * counterpart in the reference; it allocates nothing.
+ *
+ * The caller renders the plan on the host with aspire_plan_host_only (its
+ * num_ctas = the device's SM count) into `host_plan` and passes the returned
+ * info; the call uploads that plan into the library's built-in plan array on
+ * `stream` (pinned host memory keeps the copy asynchronous) and runs the
+ * attention with the built-in partials array.  The int_ws / float_ws fields
+ * of `args` are ignored.  Plans larger than ASPIRE_NOALLOC_INT_BYTES or
+ * needing more than ASPIRE_NOALLOC_FLOAT_BYTES of partials are rejected with
+ * ASPIRE_ERR_CAPACITY.  The first call on a device looks up the arrays'
+ * device addresses (make it before any stream capture).  All calls share
+ * the arrays: calls that overlap on the GPU race and must be serialised.
+ */
+ASPIRE_API int aspire_mixed_attention_noalloc(const AspireAttnArgs* args, const AspirePlanInfo* plan,
+                                              const void* host_plan, void* stream);
+
 /* ------------------------------------------------------------------------ */
 /* Paged KV append (device).                                                */
 /* ------------------------------------------------------------------------ */
