@@ -343,7 +343,6 @@ __device__ bool consume_item(const AttnParams& p, TcShared& sm, const WorkItem& 
   const int nt = n_tiles_of(it);
   const uint32_t tmem_lane = sm.tmem_base + (uint32_t(wq * 32) << 16);
   const float scale = p.scale_log2;
-  const float lazy_raw = kLazyLog2 / scale;  // tolerated growth of a raw logit
   const int group = p.group;
 
   // Stage Q (K-major, 128-byte swizzle; rows >= nrows are zero).
