@@ -134,3 +134,18 @@ def test_bad_page_ids_are_reported_not_faulted(cuda_device):
     run_attention(lay, q, kv, wrapper=w)
     torch.cuda.synchronize()
     assert w.device_status() & 1
+
+
+@pytest.mark.parametrize("case", ["cfg1", "qwen8b_mixed", "qwen8b_full", "qwen8b_q9"])
+def test_matches_flashinfer_golden(cuda_device, golden_dir, case):
+    """The sm_100a kernels against FlashInfer's persistent attention on the same
+    seeded inputs (fixture from tests/golden/make_flashinfer_golden.py)."""
+    from aspire_b200.workloads import fill_tensors
+
+    g = torch.load(golden_dir / "flashinfer_attention.pt", weights_only=False)["cases"][case]
+    lay = MixedLayout(**g["layout"])
+    q, kv = fill_tensors(lay, device="cpu", dtype=torch.bfloat16, seed=g["seed"])
+    out, lse, _, _ = run_attention(lay, q.to(cuda_device), kv.to(cuda_device))
+    err = (out.float().cpu() - g["out"].float()).abs()
+    assert err.max().item() <= 2e-2 and err.mean().item() <= 2e-3, err.max().item()
+    assert (lse.cpu() - g["lse"]).abs().max().item() <= 2e-3

@@ -115,3 +115,25 @@ def test_fp16_scalar_multiply_rounds_through_fp32():
     mine = (x.float() * torch.tensor(c, dtype=torch.float32)).half()
     same = (ref.view(torch.int16) == mine.view(torch.int16)) | (torch.isnan(ref) & torch.isnan(mine))
     assert bool(same.all())
+
+
+FI_CASES = ["cfg1", "qwen8b_mixed", "qwen8b_full", "qwen8b_q9"]
+
+
+@pytest.mark.parametrize("case", FI_CASES)
+def test_attention_oracle_matches_flashinfer(golden_dir, case):
+    """The fp32 attention oracle against FlashInfer's persistent attention (the
+    reference's kernel family), run on the same seeded inputs by
+    tests/golden/make_flashinfer_golden.py: pins the causal alignment, the
+    base-2 LSE and the GQA mapping."""
+    from aspire_b200.workloads import MixedLayout, fill_tensors
+    from oracle import attention as oracle_attn
+
+    g = _load(golden_dir, "flashinfer_attention.pt")["cases"][case]
+    lay = MixedLayout(**g["layout"])
+    q, kv = fill_tensors(lay, device="cpu", dtype=torch.bfloat16, seed=g["seed"])
+    out, lse = oracle_attn.paged_attention(q.float(), kv, lay.qo_indptr, lay.kv_indptr, lay.kv_indices,
+                                           lay.kv_lens)
+    err = (out - g["out"].float()).abs()
+    assert err.max().item() <= 2e-2 and err.mean().item() <= 2e-3
+    assert (lse - g["lse"]).abs().max().item() <= 2e-3
