@@ -134,6 +134,24 @@ class AspireSelectArgs(ctypes.Structure):
     ]
 
 
+class AspireIndicesArgs(ctypes.Structure):
+    _fields_ = [
+        ("mode_flags", ctypes.c_void_p),
+        ("draft_indices", ctypes.c_void_p),
+        ("draft_stride", ctypes.c_int64),
+        ("draft_cols", ctypes.c_int32),
+        ("verify_indices", ctypes.c_void_p),
+        ("verify_stride", ctypes.c_int64),
+        ("verify_cols", ctypes.c_int32),
+        ("draft_num_pages", ctypes.c_void_p),
+        ("verify_num_pages", ctypes.c_void_p),
+        ("batch", ctypes.c_int32),
+        ("indices_out", ctypes.c_void_p),
+        ("indptr_out", ctypes.c_void_p),
+        ("status", ctypes.c_void_p),
+    ]
+
+
 # Exported symbols and their signatures (must match include/aspire_b200.h).
 _SIGNATURES = {
     "aspire_plan": (
@@ -159,6 +177,7 @@ _SIGNATURES = {
     ),
     "aspire_append_kv": (ctypes.c_int, [ctypes.POINTER(AspireAppendArgs), ctypes.c_void_p]),
     "aspire_select_pages": (ctypes.c_int, [ctypes.POINTER(AspireSelectArgs), ctypes.c_void_p]),
+    "aspire_build_unified_indices": (ctypes.c_int, [ctypes.POINTER(AspireIndicesArgs), ctypes.c_void_p]),
     "aspire_last_error": (ctypes.c_char_p, []),
     "aspire_abi_version": (ctypes.c_int, []),
     "aspire_status_offset": (ctypes.c_size_t, []),

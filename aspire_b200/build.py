@@ -27,6 +27,7 @@ SOURCES = [
     "attn_merge.cu",
     "append_kv.cu",
     "select_pages.cu",
+    "unified_indices.cu",
     "noalloc.cu",
 ]
 

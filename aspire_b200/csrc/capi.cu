@@ -96,8 +96,14 @@ int32_t env_int(const char* name, int32_t dflt) {
   const char* e = std::getenv(name);
   return (e && *e) ? static_cast<int32_t>(std::strtol(e, nullptr, 10)) : dflt;
 }
-int32_t tc_min_rows() { return env_int("ASPIRE_B200_TC_MIN_ROWS", 1); }
-int32_t tc_min_kv() { return env_int("ASPIRE_B200_TC_MIN_KV", 4096); }
+int32_t tc_min_rows() {
+  static const int32_t v = env_int("ASPIRE_B200_TC_MIN_ROWS", 1);
+  return v;
+}
+int32_t tc_min_kv() {
+  static const int32_t v = env_int("ASPIRE_B200_TC_MIN_KV", 4096);
+  return v;
+}
 
 bool tc_env_enabled() {
   const char* e = std::getenv("ASPIRE_B200_DISABLE_TC");
@@ -119,7 +125,7 @@ size_t aspire_status_offset(void) { return kStatusBytes; }
 
 const char* aspire_kernel_names(void) {
   return "aspire_attn_gather_kernel\naspire_attn_tc_kernel\naspire_attn_merge_kernel\naspire_append_kv_kernel\n"
-         "aspire_select_pages_kernel\n";
+         "aspire_select_pages_kernel\naspire_build_indices_kernel\n";
 }
 
 int aspire_plan_host_only(const int32_t* qo_indptr, const int32_t* kv_indptr,
@@ -212,10 +218,14 @@ int aspire_mixed_attention(const AspireAttnArgs* a, const AspirePlanInfo* plan, 
 
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   int rc;
-  // Both kernel classes are launched on every call with plan-independent
-  // grids: items live in device memory, so a captured graph stays valid.
+  // Kernels are launched with plan-independent grids: items live in device
+  // memory, so a captured graph stays valid across re-plans.  The CUDA-core
+  // kernel is left out only when the routing thresholds send every row to
+  // the tcgen05 kernel (no plan can then hold a CUDA-core item); the
+  // thresholds are read from the environment once per process.
   static thread_local int gather_smem_cfg = 48 * 1024;
-  {
+  static const bool all_rows_tc = tc_min_rows() <= 1;
+  if (!(plan->tc_enabled && all_rows_tc)) {
     const size_t smem = gather_smem_bytes();
     rc = ensure_smem(reinterpret_cast<const void*>(&aspire_attn_gather_kernel), smem,
                      &gather_smem_cfg);
@@ -280,6 +290,38 @@ int aspire_append_kv(const AspireAppendArgs* a, void* stream) {
   aspire_append_kv_kernel<<<static_cast<unsigned>(blocks), 256, 0,
                             static_cast<cudaStream_t>(stream)>>>(p);
   return check_cuda(cudaGetLastError(), "aspire_append_kv_kernel launch");
+}
+
+int aspire_build_unified_indices(const AspireIndicesArgs* a, void* stream) {
+  clear_error();
+  if (!a) return set_error(ASPIRE_ERR_INVALID, "aspire_build_unified_indices: null argument");
+  if (a->batch < 0) return set_error(ASPIRE_ERR_INVALID, "aspire_build_unified_indices: negative batch");
+  if (a->batch == 0) {  // the reference still writes indptr[0] = 0
+    if (!a->indptr_out) return set_error(ASPIRE_ERR_INVALID, "aspire_build_unified_indices: null indptr");
+    return check_cuda(cudaMemsetAsync(a->indptr_out, 0, sizeof(int32_t), static_cast<cudaStream_t>(stream)),
+                      "aspire_build_unified_indices memset");
+  }
+  if (!a->mode_flags || !a->draft_indices || !a->verify_indices || !a->draft_num_pages ||
+      !a->verify_num_pages || !a->indices_out || !a->indptr_out)
+    return set_error(ASPIRE_ERR_INVALID, "aspire_build_unified_indices: null pointer");
+  if (a->draft_cols < 0 || a->verify_cols < 0 || a->draft_stride < a->draft_cols ||
+      a->verify_stride < a->verify_cols)
+    return set_error(ASPIRE_ERR_INVALID, "aspire_build_unified_indices: bad table geometry");
+  IndicesParams p;
+  p.mode_flags = a->mode_flags;
+  p.draft_indices = a->draft_indices;
+  p.draft_stride = a->draft_stride;
+  p.draft_cols = a->draft_cols;
+  p.verify_indices = a->verify_indices;
+  p.verify_stride = a->verify_stride;
+  p.verify_cols = a->verify_cols;
+  p.draft_num_pages = a->draft_num_pages;
+  p.verify_num_pages = a->verify_num_pages;
+  p.indices_out = a->indices_out;
+  p.indptr_out = a->indptr_out;
+  p.status = a->status;
+  aspire_build_indices_kernel<<<a->batch, kIndicesThreads, 0, static_cast<cudaStream_t>(stream)>>>(p);
+  return check_cuda(cudaGetLastError(), "aspire_build_indices_kernel launch");
 }
 
 int aspire_select_pages(const AspireSelectArgs* a, void* stream) {

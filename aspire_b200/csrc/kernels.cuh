@@ -47,6 +47,24 @@ struct SelectParams {
   int32_t sort_cap;  // power of two >= pages_per_slot
 };
 
+struct IndicesParams {
+  const int32_t* mode_flags;
+  const int32_t* draft_indices;
+  int64_t draft_stride;
+  int32_t draft_cols;
+  const int32_t* verify_indices;
+  int64_t verify_stride;
+  int32_t verify_cols;
+  const int32_t* draft_num_pages;
+  const int32_t* verify_num_pages;
+  int32_t* indices_out;
+  int32_t* indptr_out;
+  uint32_t* status;
+};
+
+constexpr int kIndicesThreads = 128;
+__global__ void aspire_build_indices_kernel(IndicesParams p);
+
 constexpr int kSelThreads = 512;
 constexpr int kMaxSelHeads = 128;
 

@@ -92,3 +92,46 @@ def update_kv_padded(k, v, kv_append_indptr, kv_cache, kv_page_indices, kv_page_
 def _update_kv_padded_fake(k, v, kv_append_indptr, kv_cache, kv_page_indices, kv_page_indptr,
                            kv_last_page_len, page_size):
     return None
+
+
+def build_unified_indices(mode_flags: torch.Tensor, draft_indices: torch.Tensor, verify_indices: torch.Tensor,
+                          draft_num_pages: torch.Tensor, verify_num_pages: torch.Tensor,
+                          paged_kv_indices: torch.Tensor, paged_kv_indptr: torch.Tensor,
+                          status: torch.Tensor | None = None) -> None:
+    """Drop-in for the reference's build_unified_indices
+    (aspire/models/sparse_draft_runner.py:126-153): fills paged_kv_indptr[:B+1]
+    and paged_kv_indices with each row's draft-table or block-table prefix
+    (mode 0 = draft), in one kernel (C ABI ``aspire_build_unified_indices``)."""
+    batch = mode_flags.shape[0]
+    tensors = {"mode_flags": mode_flags, "draft_indices": draft_indices, "verify_indices": verify_indices,
+               "draft_num_pages": draft_num_pages, "verify_num_pages": verify_num_pages,
+               "paged_kv_indices": paged_kv_indices, "paged_kv_indptr": paged_kv_indptr}
+    for name, t in tensors.items():
+        if t.dtype != torch.int32:
+            raise ValueError(f"{name} must be int32, got {t.dtype}")
+        if t.device.type != "cuda":
+            raise ValueError(f"{name} must be a CUDA tensor")
+    if draft_indices.stride(-1) != 1 or verify_indices.stride(-1) != 1:
+        raise ValueError("draft / verify tables need contiguous rows")
+    if not (mode_flags.is_contiguous() and draft_num_pages.is_contiguous() and verify_num_pages.is_contiguous()
+            and paged_kv_indices.is_contiguous() and paged_kv_indptr.is_contiguous()):
+        raise ValueError("flags, counts and outputs must be contiguous")
+    if paged_kv_indptr.shape[0] < batch + 1 or draft_indices.shape[0] < batch or verify_indices.shape[0] < batch:
+        raise ValueError("tables / indptr have fewer rows than mode_flags")
+    a = _capi.AspireIndicesArgs()
+    a.mode_flags = mode_flags.data_ptr()
+    a.draft_indices = draft_indices.data_ptr()
+    a.draft_stride = draft_indices.stride(0)
+    a.draft_cols = draft_indices.shape[1]
+    a.verify_indices = verify_indices.data_ptr()
+    a.verify_stride = verify_indices.stride(0)
+    a.verify_cols = verify_indices.shape[1]
+    a.draft_num_pages = draft_num_pages.data_ptr()
+    a.verify_num_pages = verify_num_pages.data_ptr()
+    a.batch = batch
+    a.indices_out = paged_kv_indices.data_ptr()
+    a.indptr_out = paged_kv_indptr.data_ptr()
+    a.status = status.data_ptr() if status is not None else None
+    stream = torch.cuda.current_stream(mode_flags.device).cuda_stream
+    rc = _capi.load_library().aspire_build_unified_indices(ctypes.byref(a), ctypes.c_void_p(stream))
+    _capi.check(rc, "aspire_build_unified_indices")

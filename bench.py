@@ -4,6 +4,7 @@ One step = one decode step's hot path of a Qwen3-8B-shaped model (config 3 of
 the reference's benchmark list: 36 layers, 32 q / 8 KV heads, head_dim 128,
 batch 64, 32k context, sparse budget 128 pages, refresh layer -2):
 
+  * the mixed page-list build (each row's draft table or block-table prefix);
   * 35 ordinary layers: paged KV append + mixed draft/verify attention
     (draft rows: 128 selected pages, q_len 1; verify rows: full context,
     q_len = U{2..8} + 1, causal);
@@ -155,8 +156,10 @@ def step_bytes(lay, full, n_layer: int, kv_stride: int, k: int) -> dict:
         * full.num_qo_heads * 2
     select = full.batch * full.num_qo_heads * 2 * min(kv_stride, lay.pages_per_row * 16) * 2 \
         + full.batch * lay.pages_per_row * 4 + full.batch * k * 4 + T * full.num_qo_heads * 4
-    total = (n_layer - 1) * mixed + refresh + n_layer * append + dump_write + select
-    return dict(total=total, mixed=mixed, refresh=refresh, append=append, dump_write=dump_write, select=select)
+    indices = int(lay.kv_indptr[-1]) * 4 * 2 + lay.batch * 4 * 4       # page ids read + written, flags/counts
+    total = (n_layer - 1) * mixed + refresh + n_layer * append + dump_write + select + indices
+    return dict(total=total, mixed=mixed, refresh=refresh, append=append, dump_write=dump_write, select=select,
+                indices=indices)
 
 
 class HotPath:
@@ -164,11 +167,12 @@ class HotPath:
 
     def __init__(self, device, lay, full, lpl_mixed, lpl_full):
         from aspire_b200.attention import HolisticAttentionWrapper, first_last_dump_jit_args
-        from aspire_b200.kv_ops import append_kv
+        from aspire_b200.kv_ops import append_kv, build_unified_indices
         from aspire_b200.page_selector import PageSelectorFirstLastAvg
         from aspire_b200.workloads import fill_tensors
 
         self.append_kv = append_kv
+        self.build_unified_indices = build_unified_indices
         self.device = device
         self.lay, self.full = lay, full
         n_layer = CFG["n_layer"]
@@ -188,6 +192,17 @@ class HotPath:
         self.full_indices, self.full_indptr, self.full_last = i32(full.kv_indices), i32(full.kv_indptr), i32(lpl_full)
         self.block_table = i32(lay.block_table)
         self.num_pages = i32((lay.ctx_lens + 15) // 16)
+        # Inputs of the step's page-list build: mode flags, the draft rows' page
+        # tables and each row's page count (draft: its table, verify: its context).
+        counts = np.diff(lay.kv_indptr)
+        draft_tab = np.zeros((lay.batch, max(1, int(counts.max()))), np.int32)
+        for b in range(lay.batch):
+            if lay.modes[b] == 0:
+                draft_tab[b, :counts[b]] = lay.kv_indices[lay.kv_indptr[b]:lay.kv_indptr[b + 1]]
+        self.mode_flags = i32(lay.modes)
+        self.draft_indices = i32(draft_tab)
+        self.draft_num_pages = i32(np.where(lay.modes == 0, counts, 0))
+        self.verify_num_pages = i32(np.where(lay.modes == 0, 0, counts))
         self.kv_stride = lay.pages_per_row * 16
         self.dump = torch.full((lay.batch * hq * 2 * self.kv_stride,), float("-inf"), dtype=torch.float16,
                                device=device)
@@ -211,8 +226,13 @@ class HotPath:
         self.refresh.plan_host(t(full.qo_indptr), t(full.kv_indptr), t(full.kv_lens), self.full_indices,
                                full.num_qo_heads, full.num_kv_heads, 128, 16, causal=True)
 
+    def build_indices(self):
+        self.build_unified_indices(self.mode_flags, self.draft_indices, self.block_table, self.draft_num_pages,
+                                   self.verify_num_pages, self.mixed_indices, self.mixed_indptr)
+
     def step_eager(self):
         n_layer = CFG["n_layer"]
+        self.build_indices()
         for layer in range(n_layer):
             if layer == CFG["refresh_layer"]:
                 self.append_kv(self.k_new[layer], self.v_new[layer], self.qo_indptr, self.kv, self.full_indices,
@@ -229,6 +249,10 @@ class HotPath:
     def capture(self):
         self.step_eager()
         torch.cuda.synchronize()
+        lay = self.lay
+        if not (np.array_equal(self.mixed_indices.cpu().numpy(), lay.kv_indices)
+                and np.array_equal(self.mixed_indptr.cpu().numpy(), lay.kv_indptr)):
+            raise RuntimeError("page-list build disagrees with the layout's page list")
         s = torch.cuda.Stream()
         s.wait_stream(torch.cuda.current_stream())
         with torch.cuda.stream(s):
@@ -241,9 +265,13 @@ class HotPath:
         torch.cuda.synchronize()
 
     def launches_per_step(self) -> int:
-        # per layer: append + gather attention + tcgen05 attention (when enabled); + selection
-        per_attn = 1 + (1 if self.mixed.plan_info.tc_enabled else 0)
-        return CFG["n_layer"] * (1 + per_attn) + 1
+        # page-list build; per layer: append + attention (tcgen05 kernel, plus the
+        # CUDA-core kernel unless every row routes to tcgen05, plus the split-KV
+        # merge); then the selection.
+        tc = bool(self.mixed.plan_info.tc_enabled)
+        all_tc = tc and int(os.environ.get("ASPIRE_B200_TC_MIN_ROWS", "1") or "1") <= 1
+        per_attn = (1 if tc else 0) + (0 if all_tc else 1) + 1
+        return 1 + CFG["n_layer"] * (1 + per_attn) + 1
 
 
 def time_device(fn, steps, warmup, dist_on):
@@ -299,6 +327,7 @@ def breakdown(hp: HotPath, reps: int = 5) -> dict:
     """Average device time of each call of the step, timed alone (CUDA events)."""
     L = CFG["n_layer"]
     calls = {
+        "page_list": hp.build_indices,
         "append": lambda: hp.append_kv(hp.k_new[0], hp.v_new[0], hp.qo_indptr, hp.kv, hp.mixed_indices,
                                        hp.mixed_indptr, hp.mixed_last, 16),
         "mixed_attention": lambda: hp.mixed.run(hp.q[0], hp.kv, out=hp.out[0]),

@@ -263,6 +263,37 @@ typedef struct AspireSelectArgs {
 ASPIRE_API int aspire_select_pages(const AspireSelectArgs* args, void* stream);
 
 /* ------------------------------------------------------------------------ */
+/* Mixed page list (device).                                                */
+/* ------------------------------------------------------------------------ */
+
+typedef struct AspireIndicesArgs {
+  const int32_t* mode_flags;      /* int32 [batch]: 0 = draft row, otherwise verify row   */
+  const int32_t* draft_indices;   /* int32 [batch, draft_stride] draft page tables        */
+  int64_t draft_stride;
+  int32_t draft_cols;             /* usable columns of a draft table row                  */
+  const int32_t* verify_indices;  /* int32 [batch, verify_stride] block tables            */
+  int64_t verify_stride;
+  int32_t verify_cols;
+  const int32_t* draft_num_pages; /* int32 [batch]                                        */
+  const int32_t* verify_num_pages;/* int32 [batch]                                        */
+  int32_t batch;
+  int32_t* indices_out;           /* int32 [sum of the rows' page counts]                 */
+  int32_t* indptr_out;            /* int32 [batch + 1]: exclusive prefix sum              */
+  uint32_t* status;               /* optional device status word                          */
+} AspireIndicesArgs;
+
+/*
+ * Builds the mixed page list of one step: row b's pages are its draft table
+ * prefix (draft rows) or its block-table prefix (verify rows), concatenated
+ * in row order, with indptr the prefix sum of the counts.  Replaces
+ * build_unified_indices (aspire/models/sparse_draft_runner.py:126-153) and
+ * its Triton _copy_indices_kernel (:93-123).  A count larger than its table's
+ * width copies the width and sets ASPIRE_STATUS_BAD_ROW.  With batch 0 only
+ * indptr_out[0] = 0 is written, as the reference does.
+ */
+ASPIRE_API int aspire_build_unified_indices(const AspireIndicesArgs* args, void* stream);
+
+/* ------------------------------------------------------------------------ */
 /* Utilities.                                                               */
 /* ------------------------------------------------------------------------ */
 

@@ -9,6 +9,9 @@ $ASPIRE_REFERENCE):
   aspire.backends.page_selector.PageSelectorFirstLastAvg.select (imported
   unchanged from the reference tree, run on CPU), including its page-score
   buffer before the +/-inf forcing; tie cases run its _finalize_scores.
+* unified_indices.pt : the reference's build_unified_indices
+  (aspire/models/sparse_draft_runner.py, with its Triton _copy_indices_kernel)
+  under the Triton CPU interpreter.
 * kv_append.pt : the reference's Triton kernels
   (aspire.attention.kv_ops._append_paged_kv_cache_padded_kernel and
   FlashInfer's get_batch_indices_positions_kernel) executed by Triton's CPU
@@ -159,6 +162,37 @@ def append_case():
                    env=env)
 
 
+_INDICES_SCRIPT = r"""
+import sys, torch
+sys.path.insert(0, sys.argv[1])
+from aspire.models.sparse_draft_runner import build_unified_indices
+g = torch.Generator().manual_seed(11)
+# draft rows, verify rows, an empty row of each kind, and a verify row longer
+# than one 128-wide Triton block; the output buffers are oversized and
+# pre-filled so untouched entries are visible.
+mode = torch.tensor([0, 1, 0, 1, 1, 0, 1, 0], dtype=torch.int32)
+dn = torch.tensor([5, 0, 40, 3, 0, 0, 131, 17], dtype=torch.int32)
+vn = torch.tensor([9, 300, 2, 3, 0, 12, 131, 4], dtype=torch.int32)
+B = mode.shape[0]
+draft = torch.randint(0, 5000, (B, 40), generator=g, dtype=torch.int32)
+verify = torch.randint(0, 5000, (B, 300), generator=g, dtype=torch.int32)
+indices = torch.full((700,), -7, dtype=torch.int32)
+indptr = torch.full((B + 2,), -9, dtype=torch.int32)
+build_unified_indices(mode, draft, verify, dn, vn, indices, indptr)
+torch.save({"mode_flags": mode, "draft_indices": draft, "verify_indices": verify, "draft_num_pages": dn,
+            "verify_num_pages": vn, "indices_before": torch.full((700,), -7, dtype=torch.int32),
+            "indptr_before": torch.full((B + 2,), -9, dtype=torch.int32), "indices": indices,
+            "indptr": indptr}, sys.argv[2])
+print("unified_indices indptr", indptr.tolist())
+"""
+
+
+def indices_case():
+    env = dict(os.environ, TRITON_INTERPRET="1")
+    subprocess.run([sys.executable, "-c", _INDICES_SCRIPT, str(REF), str(HERE / "unified_indices.pt")],
+                   check=True, env=env)
+
+
 def main():
     if not REF.exists():
         raise SystemExit(f"reference tree {REF} not found")
@@ -176,6 +210,7 @@ def main():
                   draft_percent=None, seed=2, q_lens=[5, 3], lens=[16500, 16001])
     tie_case()
     append_case()
+    indices_case()
 
 
 if __name__ == "__main__":

@@ -2,10 +2,13 @@
 
 import math
 
+import numpy as np
+
 import pytest
 import torch
 
 from oracle import kv_append as oracle_append
+from oracle import unified_indices as oracle_indices
 from oracle import page_selector as oracle_sel
 
 CASES = ["cfg1", "pct", "budget"]
@@ -137,3 +140,16 @@ def test_attention_oracle_matches_flashinfer(golden_dir, case):
     err = (out - g["out"].float()).abs()
     assert err.max().item() <= 2e-2 and err.mean().item() <= 2e-3
     assert (lse - g["lse"]).abs().max().item() <= 2e-3
+
+
+def test_unified_indices_oracle_matches_reference_golden(golden_dir):
+    """The restatement of build_unified_indices reproduces the reference's
+    output (Triton interpreter) bit for bit, untouched entries included."""
+    g = _load(golden_dir, "unified_indices.pt")
+    indices = g["indices_before"].numpy().copy()
+    indptr = g["indptr_before"].numpy().copy()
+    oracle_indices.build_unified_indices(g["mode_flags"].numpy(), g["draft_indices"].numpy(),
+                                         g["verify_indices"].numpy(), g["draft_num_pages"].numpy(),
+                                         g["verify_num_pages"].numpy(), indices, indptr)
+    np.testing.assert_array_equal(indptr, g["indptr"].numpy())
+    np.testing.assert_array_equal(indices, g["indices"].numpy())
