@@ -75,6 +75,7 @@ class AspireAttnArgs(ctypes.Structure):
         ("int_ws_bytes", ctypes.c_size_t),
         ("float_ws", ctypes.c_void_p),
         ("float_ws_bytes", ctypes.c_size_t),
+        ("q_rows", ctypes.c_int64),
     ]
 
 
@@ -184,7 +185,7 @@ _SIGNATURES = {
     "aspire_kernel_names": (ctypes.c_char_p, []),
 }
 
-EXPECTED_ABI_VERSION = 1
+EXPECTED_ABI_VERSION = 2
 
 _lib = None
 _lock = threading.Lock()

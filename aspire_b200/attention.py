@@ -285,6 +285,7 @@ class HolisticAttentionWrapper:
         a.q = q.data_ptr()
         a.q_stride_n = q.stride(0)
         a.q_stride_h = q.stride(1)
+        a.q_rows = q.shape[0]
         a.kv_cache = kv.data_ptr()
         a.num_pages_total = kv.shape[0]
         a.kv_indices = self._kv_indices.data_ptr()

@@ -67,12 +67,13 @@ struct TcShared {
   float red[2][4][kNMax];
   float red_l[4][kNMax];
   float alpha[2][kNMax];
+  float inv_l[kNMax];     // 1 / column sum of the finished item
   float mref[2][kNMax];   // column reference max x scale (log2 domain), double buffered
   int flags[2][4];
   uint64_t k_full[kKStages], k_empty[kKStages];
   uint64_t v_full[kVStages], v_empty[kVStages];
   uint64_t s_full[2], s_empty[2], p_full[2], p_empty[2];
-  uint64_t o_free, q_full, done, grp;
+  uint64_t o_free, q_full, q_empty, done, grp;
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -198,7 +199,32 @@ __device__ void run_producer(const AttnParams& p, const CUtensorMap* tmap, TcSha
 }
 
 // ------------------------------------------------------------------ MMA issuer
-__device__ void run_mma(const AttnParams& p, TcShared& sm, int item_begin, int item_end, int lane) {
+// Next item at or after `from` that has KV tiles (the roles skip the same items).
+__device__ __forceinline__ int next_tc_item(const AttnParams& p, int from, int item_end) {
+  for (int j = from; j < item_end; ++j) {
+    const WorkItem it = load_item(p.plan, j);
+    if (item_valid(p, it) && n_tiles_of(it) > 0) return j;
+  }
+  return item_end;
+}
+
+// Requests item `idx`'s query tile: one box of (64 dims x group heads x
+// q_box_tokens tokens, at most kNMax rows) per 64-dim half, starting at the
+// item's first query.
+// Rows past the item's queries are other queries or zero fill; they only feed
+// ignored columns.
+__device__ __forceinline__ void issue_q(const AttnParams& p, const CUtensorMap* qmap, TcShared& sm, int idx) {
+  const WorkItem it = load_item(p.plan, idx);
+  const int q_idx0 = it.pq_begin / p.group;
+  const uint32_t bytes = 2u * 128u * uint32_t(p.group) * uint32_t(p.q_box_tokens);
+  const uint32_t bar = ptx::smem_addr(&sm.q_full);
+  ptx::mbar_arrive_expect_tx(bar, bytes);
+  ptx::tma_load_3d(ptx::smem_addr(sm.q[0]), qmap, bar, 0, it.kv_head * p.group, it.q_start + q_idx0);
+  ptx::tma_load_3d(ptx::smem_addr(sm.q[1]), qmap, bar, 64, it.kv_head * p.group, it.q_start + q_idx0);
+}
+
+__device__ void run_mma(const AttnParams& p, const CUtensorMap* qmap, TcShared& sm, int item_begin,
+                        int item_end, int lane) {
   const uint32_t tmem = sm.tmem_base;
   uint32_t g = 0, items_done = 0;
   bool ok = true;
@@ -206,6 +232,7 @@ __device__ void run_mma(const AttnParams& p, TcShared& sm, int item_begin, int i
   const uint32_t v0 = ptx::smem_addr(sm.v[0]);
   const uint32_t q0 = ptx::smem_addr(sm.q[0]);
   const uint32_t p0 = ptx::smem_addr(sm.p[0]);
+  bool q_pending = false;  // a query-tile load is in flight
 
   // PV of global tile u; `first` marks the item's first tile (fresh accumulator).
   auto issue_pv = [&](uint32_t u, bool first, uint32_t idesc_pv) -> bool {
@@ -229,11 +256,14 @@ __device__ void run_mma(const AttnParams& p, TcShared& sm, int item_begin, int i
     return true;
   };
 
-  for (int ii = item_begin; ii < item_end && ok; ++ii) {
+  int ii = next_tc_item(p, item_begin, item_end);
+  if (ii < item_end) {
+    if (lane == 0) issue_q(p, qmap, sm, ii);
+    q_pending = true;
+  }
+  while (ii < item_end && ok) {
     const WorkItem it = load_item(p.plan, ii);
-    if (!item_valid(p, it)) continue;
     const int nt = n_tiles_of(it);
-    if (nt == 0) continue;
     const int nrows = it.pq_end - it.pq_begin;
     const uint32_t N = uint32_t((nrows + 15) / 16 * 16);
     const uint32_t idesc_qk = ptx::idesc_bf16(128, N, false, false);
@@ -242,6 +272,7 @@ __device__ void run_mma(const AttnParams& p, TcShared& sm, int item_begin, int i
       ok = false;
       break;
     }
+    q_pending = false;
     const uint32_t g0 = g;
     for (int t = 0; t < nt && ok; ++t, ++g) {
       const int ks = g % kKStages, sb = g % 2;
@@ -263,13 +294,29 @@ __device__ void run_mma(const AttnParams& p, TcShared& sm, int item_begin, int i
         }
         ptx::mma_commit(ptx::smem_addr(&sm.s_full[sb]));
         ptx::mma_commit(ptx::smem_addr(&sm.k_empty[ks]));
+        if (t == nt - 1) ptx::mma_commit(ptx::smem_addr(&sm.q_empty));
       }
       __syncwarp();
       if (t > 0 && !issue_pv(g - 1, g - 1 == g0, idesc_pv)) ok = false;
     }
-    if (ok && !issue_pv(g - 1, g - 1 == g0, idesc_pv)) ok = false;
+    if (!ok) break;
+    // The next item's query tile loads while this item's last PV and epilogue run.
+    const int nxt = next_tc_item(p, ii + 1, item_end);
+    if (nxt < item_end) {
+      if (!wait_bar(sm, sm.q_empty, items_done & 1, p.status)) {
+        ok = false;
+        break;
+      }
+      if (lane == 0) issue_q(p, qmap, sm, nxt);
+      q_pending = true;
+      __syncwarp();
+    }
+    if (!issue_pv(g - 1, g - 1 == g0, idesc_pv)) ok = false;
     ++items_done;
+    ii = nxt;
   }
+  // A query load still in flight lands before the CTA releases its memory.
+  if (q_pending) drain_bar(sm.q_full, items_done & 1);
   // Every MMA this thread issued has completed once `done` fires.
   if (lane == 0) ptx::mma_commit(ptx::smem_addr(&sm.done));
   __syncwarp();
@@ -345,20 +392,10 @@ __device__ bool consume_item(const AttnParams& p, TcShared& sm, const WorkItem& 
   const float scale = p.scale_log2;
   const int group = p.group;
 
-  // Stage Q (K-major, 128-byte swizzle; rows >= nrows are zero).
-  for (int e = ctid; e < N * 16; e += 128) {
-    const int j = e >> 4, c = e & 15;
-    uint4 val = make_uint4(0, 0, 0, 0);
-    if (j < nrows) {
-      int q_idx, head;
-      packed_row(p, it, it.pq_begin + j, q_idx, head);
-      val = *reinterpret_cast<const uint4*>(p.q + int64_t(it.q_start + q_idx) * p.q_stride_n +
-                                            int64_t(head) * p.q_stride_h + c * 8);
-    }
-    *reinterpret_cast<uint4*>(sm.q[c >> 3] + j * 128 + (((c & 7) ^ (j & 7)) << 4)) = val;
-  }
-  ptx::fence_proxy_async_smem();
-  ptx::mbar_arrive(ptx::smem_addr(&sm.q_full));
+  // The previous item's output left through the P buffers: its bulk stores
+  // must have read them before this item writes P (the other threads wait at
+  // the first tile's barrier).
+  if (ctid == 0) ptx::bulk_wait_read();
 
   const int q_idx0 = it.pq_begin / group;
   // First/last-query dump: the item's columns of query 0 (slot 0) and of query
@@ -549,52 +586,62 @@ __device__ bool consume_item(const AttnParams& p, TcShared& sm, const WorkItem& 
   ptx::tc_fence_before();
   ptx::mbar_arrive(ptx::smem_addr(&sm.o_free));
 
-  // Column sums of l across the 128 threads.
+  // Column sums of l across the 128 threads; thread j < N then turns column j
+  // into its reciprocal and LSE once.
   warp_columns<N, false>(l, sm.red_l[wq], lane);
   if (!group_sync(sm, grp_uses, p.status)) return false;
-#pragma unroll
-  for (int j = 0; j < N; ++j) {
-    const float L = sm.red_l[0][j] + sm.red_l[1][j] + sm.red_l[2][j] + sm.red_l[3][j];
-    o_fin[j] = L > 0.f ? o_fin[j] / L : 0.f;
+  float my_lse = -INFINITY;  // LSE of column ctid
+  if (ctid < N) {
+    const float L = sm.red_l[0][ctid] + sm.red_l[1][ctid] + sm.red_l[2][ctid] + sm.red_l[3][ctid];
+    sm.inv_l[ctid] = L > 0.f ? 1.f / L : 0.f;
+    my_lse = L > 0.f ? sm.mref[cur][ctid] + lg2(L) : -INFINITY;
   }
-  float my_lse = -INFINITY;  // LSE of column ctid (every thread holds all references)
-#pragma unroll
-  for (int j = 0; j < N; ++j) {
-    if (j == ctid) {
-      const float L = sm.red_l[0][j] + sm.red_l[1][j] + sm.red_l[2][j] + sm.red_l[3][j];
-      my_lse = L > 0.f ? sm.mref[cur][j] + lg2(L) : -INFINITY;
-    }
-  }
+  if (!group_sync(sm, grp_uses, p.status)) return false;
+
+  // Normalised rows are staged in the P buffers (idle until this CTA's next
+  // item writes P) and leave by bulk stores, so the threads move on at once.
   const int d = r;  // this thread's output dim
-  if (it.n_chunks <= 1) {
+  uint8_t* stage = sm.p[0];
+  const bool final_rows = it.n_chunks <= 1;
+  if (final_rows) {
+    __nv_bfloat16* st = reinterpret_cast<__nv_bfloat16*>(stage);
 #pragma unroll
-    for (int j = 0; j < N; ++j) {
-      if (j < nrows) {
-        int q_idx, head;
-        packed_row(p, it, it.pq_begin + j, q_idx, head);
-        const int64_t tokrow = int64_t(it.q_start) + q_idx;
-        p.out[tokrow * p.o_stride_n + int64_t(head) * p.o_stride_h + d] = __float2bfloat16_rn(o_fin[j]);
-      }
-    }
+    for (int j = 0; j < N; ++j)
+      if (j < nrows) st[j * kHeadDim + d] = __float2bfloat16_rn(o_fin[j] * sm.inv_l[j]);
     if (ctid < nrows && p.lse) {
       int q_idx, head;
       packed_row(p, it, it.pq_begin + ctid, q_idx, head);
       p.lse[(int64_t(it.q_start) + q_idx) * p.num_qo_heads + head] = my_lse;
     }
   } else {
-    float* plse = partial_lse_ptr(p);
-    const int64_t base = int64_t(it.partial_base) + int64_t(it.chunk) * nrows;
+    float* st = reinterpret_cast<float*>(stage);
 #pragma unroll
     for (int j = 0; j < N; ++j)
-      if (j < nrows) p.partial_o[(base + j) * kHeadDim + d] = o_fin[j];
-    if (ctid < nrows) plse[base + ctid] = my_lse;
+      if (j < nrows) st[j * kHeadDim + d] = o_fin[j] * sm.inv_l[j];
+    if (ctid < nrows) partial_lse_ptr(p)[int64_t(it.partial_base) + int64_t(it.chunk) * nrows + ctid] = my_lse;
   }
-  // The reduction buffers are reused by the next item.
-  return group_sync(sm, grp_uses, p.status);
+  ptx::fence_proxy_async_smem();
+  if (!group_sync(sm, grp_uses, p.status)) return false;
+  if (ctid == 0) {
+    const uint32_t src = ptx::smem_addr(stage);
+    if (final_rows) {
+      for (int j = 0; j < nrows; ++j) {
+        int q_idx, head;
+        packed_row(p, it, it.pq_begin + j, q_idx, head);
+        __nv_bfloat16* dst = p.out + (int64_t(it.q_start) + q_idx) * p.o_stride_n + int64_t(head) * p.o_stride_h;
+        ptx::bulk_store(dst, src + uint32_t(j) * kHeadDim * 2, kHeadDim * 2);
+      }
+    } else {
+      const int64_t base = int64_t(it.partial_base) + int64_t(it.chunk) * nrows;
+      ptx::bulk_store(p.partial_o + base * kHeadDim, src, uint32_t(nrows) * kHeadDim * 4);
+    }
+    ptx::bulk_commit();
+  }
+  return true;
 }
 
-__device__ void run_consumer(const AttnParams& p, TcShared& sm, int item_begin, int item_end, bool causal,
-                             int warp, int lane) {
+__device__ void consume_items(const AttnParams& p, TcShared& sm, int item_begin, int item_end, bool causal,
+                              int warp, int lane) {
   const int wq = warp & 3;
   const int r = wq * 32 + lane;          // TMEM lane = S-tile token = O-tile dim
   const int ctid = threadIdx.x - 64;     // 0..127
@@ -624,10 +671,19 @@ __device__ void run_consumer(const AttnParams& p, TcShared& sm, int item_begin, 
   }
 }
 
+__device__ void run_consumer(const AttnParams& p, TcShared& sm, int item_begin, int item_end, bool causal,
+                             int warp, int lane) {
+  consume_items(p, sm, item_begin, item_end, causal, warp, lane);
+  // The bulk stores of the last item (issued by thread 0 of the group) finish
+  // before the CTA exits.
+  if (threadIdx.x == 64) ptx::bulk_wait_all();
+}
+
 }  // namespace
 
 __global__ void __launch_bounds__(kTcThreads, 1)
-    aspire_attn_tc_kernel(AttnParams p, const __grid_constant__ CUtensorMap tmap) {
+    aspire_attn_tc_kernel(AttnParams p, const __grid_constant__ CUtensorMap tmap,
+                          const __grid_constant__ CUtensorMap qmap) {
   extern __shared__ __align__(1024) uint8_t tc_smem_raw[];
   const uint32_t raw = ptx::smem_addr(tc_smem_raw);
   TcShared& sm = *reinterpret_cast<TcShared*>(tc_smem_raw + ((1024 - (raw & 1023)) & 1023));
@@ -656,7 +712,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       ptx::mbar_init(ptx::smem_addr(&sm.p_empty[b]), 1);
     }
     ptx::mbar_init(ptx::smem_addr(&sm.o_free), 128);
-    ptx::mbar_init(ptx::smem_addr(&sm.q_full), 128);
+    ptx::mbar_init(ptx::smem_addr(&sm.q_full), 1);
+    ptx::mbar_init(ptx::smem_addr(&sm.q_empty), 1);
     ptx::mbar_init(ptx::smem_addr(&sm.done), 1);
     ptx::mbar_init(ptx::smem_addr(&sm.grp), 128);
     sm.abort_flag = 0;
@@ -667,6 +724,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     ptx::tmem_relinquish();
   }
   if (warp == 0 && lane == 0) ptx::prefetch_tmap(&tmap);
+  if (warp == 1 && lane == 0) ptx::prefetch_tmap(&qmap);
+  // Query rows that no load writes (when kNMax is not a multiple of the group)
+  // stay zero.
+  for (int i = threadIdx.x; i < int(sizeof(sm.q) / 16); i += blockDim.x)
+    reinterpret_cast<uint4*>(&sm.q[0][0])[i] = make_uint4(0, 0, 0, 0);
+  ptx::fence_proxy_async_smem();
   ptx::tc_fence_before();
   __syncthreads();
   ptx::tc_fence_after();
@@ -676,7 +739,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   } else if (warp == 6) {
     run_producer<kVStages>(p, &tmap, sm, sm.v, sm.v_full, sm.v_empty, 1, item_begin, item_end, lane);
   } else if (warp == 1) {
-    run_mma(p, sm, item_begin, item_end, lane);
+    run_mma(p, &qmap, sm, item_begin, item_end, lane);
   } else {
     run_consumer(p, sm, item_begin, item_end, causal, warp, lane);
   }

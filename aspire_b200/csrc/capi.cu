@@ -72,6 +72,25 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
 
 // 5-D view of the paged cache [pages, 2, 16, Hkv, 128] (innermost first:
 // dim, head, token, K/V, page) with a 64-dim x 16-token box, 128-byte swizzle.
+// Query tile map over q [q_rows, num_qo_heads, 128]: boxes of 64 dims x
+// `group` heads x `box_tokens` tokens, 128-byte swizzle (the K-major B operand
+// of Q.K^T).
+int encode_q_tensor_map(CUtensorMap* map, const void* q, int64_t q_rows, int num_qo_heads, int64_t stride_n,
+                        int64_t stride_h, int group, int box_tokens) {
+  PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
+  if (!enc) return set_error(ASPIRE_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
+  cuuint64_t dims[3] = {cuuint64_t(kHeadDim), cuuint64_t(num_qo_heads), cuuint64_t(q_rows)};
+  cuuint64_t strides[2] = {cuuint64_t(stride_h) * 2, cuuint64_t(stride_n) * 2};
+  cuuint32_t box[3] = {64, cuuint32_t(group), cuuint32_t(box_tokens)};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(q), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return set_error(ASPIRE_ERR_INVALID, "cuTensorMapEncodeTiled (q) failed with code " + std::to_string(int(r)));
+  return ASPIRE_OK;
+}
+
 int encode_kv_tensor_map(CUtensorMap* map, const void* kv, int64_t num_pages, int num_kv_heads) {
   PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
   if (!enc) return set_error(ASPIRE_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
@@ -192,6 +211,14 @@ int aspire_mixed_attention(const AspireAttnArgs* a, const AspirePlanInfo* plan, 
     return set_error(ASPIRE_ERR_CAPACITY, "aspire_mixed_attention: float workspace smaller than plan");
   if (plan->num_merge > 0 && !a->float_ws)
     return set_error(ASPIRE_ERR_INVALID, "aspire_mixed_attention: split-KV needs a float workspace");
+  if (a->q_rows <= 0 || a->q_rows > INT32_MAX)
+    return set_error(ASPIRE_ERR_INVALID, "aspire_mixed_attention: q_rows (rows of q) must be set");
+  const int group = a->num_qo_heads / a->num_kv_heads;
+  // The tcgen05 kernel takes rows only when a whole query position fits its tile.
+  const bool run_tc = plan->tc_enabled && group <= kTcQTile;
+  if (run_tc && ((reinterpret_cast<uintptr_t>(a->out) & 15) || ((a->o_stride_n | a->o_stride_h) & 7)))
+    return set_error(ASPIRE_ERR_INVALID,
+                     "aspire_mixed_attention: out must be 16-byte aligned with strides in multiples of 8");
 
   AttnParams p;
   p.q = static_cast<const __nv_bfloat16*>(a->q);
@@ -211,7 +238,8 @@ int aspire_mixed_attention(const AspireAttnArgs* a, const AspirePlanInfo* plan, 
   p.scale_log2 = sm_scale * 1.44269504088896340736f;
   p.num_qo_heads = a->num_qo_heads;
   p.num_kv_heads = a->num_kv_heads;
-  p.group = a->num_qo_heads / a->num_kv_heads;
+  p.group = group;
+  p.q_box_tokens = static_cast<int32_t>(std::min<int64_t>(kTcQTile / group, a->q_rows));
   p.plan = reinterpret_cast<const int32_t*>(static_cast<const char*>(a->int_ws) + kStatusBytes);
   p.status = static_cast<uint32_t*>(a->int_ws);
   p.partial_o = static_cast<float*>(a->float_ws);
@@ -225,7 +253,7 @@ int aspire_mixed_attention(const AspireAttnArgs* a, const AspirePlanInfo* plan, 
   // thresholds are read from the environment once per process.
   static thread_local int gather_smem_cfg = 48 * 1024;
   static const bool all_rows_tc = tc_min_rows() <= 1;
-  if (!(plan->tc_enabled && all_rows_tc)) {
+  if (!(run_tc && all_rows_tc)) {
     const size_t smem = gather_smem_bytes();
     rc = ensure_smem(reinterpret_cast<const void*>(&aspire_attn_gather_kernel), smem,
                      &gather_smem_cfg);
@@ -234,7 +262,7 @@ int aspire_mixed_attention(const AspireAttnArgs* a, const AspirePlanInfo* plan, 
     rc = check_cuda(cudaGetLastError(), "aspire_attn_gather_kernel launch");
     if (rc) return rc;
   }
-  if (plan->tc_enabled) {
+  if (run_tc) {
     static thread_local int tc_smem_cfg = 48 * 1024;
     const size_t smem = tc_smem_bytes();
     rc = ensure_smem(reinterpret_cast<const void*>(&aspire_attn_tc_kernel), smem, &tc_smem_cfg);
@@ -244,7 +272,11 @@ int aspire_mixed_attention(const AspireAttnArgs* a, const AspirePlanInfo* plan, 
     alignas(64) CUtensorMap tmap;
     rc = encode_kv_tensor_map(&tmap, a->kv_cache, a->num_pages_total, a->num_kv_heads);
     if (rc) return rc;
-    aspire_attn_tc_kernel<<<plan->num_ctas * kTcCtasPerSm, tc_threads(), smem, st>>>(p, tmap);
+    alignas(64) CUtensorMap qmap;
+    rc = encode_q_tensor_map(&qmap, a->q, a->q_rows, a->num_qo_heads, a->q_stride_n, a->q_stride_h, group,
+                             p.q_box_tokens);
+    if (rc) return rc;
+    aspire_attn_tc_kernel<<<plan->num_ctas * kTcCtasPerSm, tc_threads(), smem, st>>>(p, tmap, qmap);
     rc = check_cuda(cudaGetLastError(), "aspire_attn_tc_kernel launch");
     if (rc) return rc;
   }

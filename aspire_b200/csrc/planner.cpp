@@ -110,8 +110,11 @@ int plan_impl(const int32_t* qo_indptr, const int32_t* kv_indptr, const int32_t*
     const int32_t nq = ql * group;
     // tcgen05 for wide query tiles, and for narrow rows with long contexts
     // (the tensor-core tile streams K/V better than the CUDA-core gather).
-    const bool wide = tc_enabled && (nq > kGatherQTile || nq >= tc_min_rows || kl >= tc_min_kv);
-    const int tile = wide ? kTcQTile : kGatherQTile;
+    // A tcgen05 q-tile holds whole query positions (all `group` heads of each),
+    // so that one TMA box loads it.
+    const bool wide = tc_enabled && group <= kTcQTile &&
+                      (nq > kGatherQTile || nq >= tc_min_rows || kl >= tc_min_kv);
+    const int tile = wide ? (kTcQTile / group) * group : kGatherQTile;
     for (int h = 0; h < num_kv_heads; ++h) {
       for (int p0 = 0; p0 < nq; p0 += tile) {
         GroupDesc g{b, h, q0, ql, kv_indptr[b], kl, p0, std::min(nq, p0 + tile), wide ? 1 : 0};

@@ -41,7 +41,7 @@
 extern "C" {
 #endif
 
-#define ASPIRE_B200_ABI_VERSION 1
+#define ASPIRE_B200_ABI_VERSION 2
 
 #define ASPIRE_OK 0
 #define ASPIRE_ERR_INVALID (-1)  /* bad argument (shape, size, alignment)       */
@@ -144,6 +144,7 @@ typedef struct AspireAttnArgs {
   size_t int_ws_bytes;
   void* float_ws;           /* device float workspace for split-KV partials       */
   size_t float_ws_bytes;
+  int64_t q_rows;           /* first dimension of q (rows the kernels may read)   */
 } AspireAttnArgs;
 
 /*

@@ -30,6 +30,7 @@ def _attn_args(q, kv, kv_indices, out, lse, hq, hkv):
     a = _capi.AspireAttnArgs()
     a.q = q.data_ptr()
     a.q_stride_n, a.q_stride_h = q.stride(0), q.stride(1)
+    a.q_rows = q.shape[0]
     a.kv_cache = kv.data_ptr()
     a.num_pages_total = kv.shape[0]
     a.kv_indices = kv_indices.data_ptr()
