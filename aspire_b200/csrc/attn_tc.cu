@@ -70,6 +70,7 @@ struct TcShared {
   float inv_l[kNMax];     // 1 / column sum of the finished item
   float mref[2][kNMax];   // column reference max x scale (log2 domain), double buffered
   int flags[2][4];
+  int grew[2];            // some column reference grew in the tile (exceed path)
   uint64_t k_full[kKStages], k_empty[kKStages];
   uint64_t v_full[kVStages], v_empty[kVStages];
   uint64_t s_full[2], s_empty[2], p_full[2], p_empty[2];
@@ -443,14 +444,23 @@ __device__ bool consume_item(const AttnParams& p, TcShared& sm, const WorkItem& 
       for (int i = 0; i < N / 16; ++i) ptx::tmem_ld16(tmem_lane + col_s(b) + 16 * i, sv + 16 * i);
       ptx::tmem_wait_ld();
     };
+    // Token `tok` is visible to packed column j iff it lies in the chunk and,
+    // under the bottom-right causal mask, q_idx(j) >= tok - (kv_len - q_len),
+    // i.e. j >= jmin: one threshold per thread instead of a division per column.
+    int jmin = 0;
+    if (!full_tile) {
+      if (!in_chunk || tok >= it.kv_len) {
+        jmin = N;
+      } else if (causal) {
+        const int d0 = tok - (it.kv_len - it.q_len);
+        jmin = d0 <= 0 ? 0 : min(d0 * group - it.pq_begin, N);
+      }
+    }
     auto mask_s = [&](float* sv) {
       if (!full_tile) {
 #pragma unroll
-        for (int j = 0; j < N; ++j) {
-          const int q_idx = (it.pq_begin + j) / group;
-          const int lim = causal ? (it.kv_len - it.q_len + q_idx + 1) : it.kv_len;
-          if (!(in_chunk && tok < lim)) sv[j] = -INFINITY;
-        }
+        for (int j = 0; j < N; ++j)
+          if (j < jmin) sv[j] = -INFINITY;
       }
     };
     float sv[N];
@@ -492,39 +502,33 @@ __device__ bool consume_item(const AttnParams& p, TcShared& sm, const WorkItem& 
     const bool any_exceed =
         (sm.flags[t & 1][0] | sm.flags[t & 1][1] | sm.flags[t & 1][2] | sm.flags[t & 1][3]) != 0;
     if (any_exceed) {
-      // Exact column maxima of the tile (reduced in place), then the new
-      // references (in mref[cur ^ 1]); S is read again from TMEM afterwards.
+      // Exact column maxima of the tile (reduced in place; S is read again from
+      // TMEM afterwards).  Thread j < N then updates column j's reference
+      // (mref[cur ^ 1]) and its rescale factor alpha; the per-column work is
+      // spread over threads so that this once-per-item path stays short.
       warp_columns<N, true>(sv, sm.red[t & 1][wq], lane);
+      if (ctid == 0) sm.grew[t & 1] = 0;
+      if (!group_sync(sm, grp_uses, p.status)) return false;
+      if (ctid < N) {
+        const float mo = t > 0 ? mr[ctid] : -INFINITY;
+        const float tmax = fmaxf(fmaxf(sm.red[t & 1][0][ctid], sm.red[t & 1][1][ctid]),
+                                 fmaxf(sm.red[t & 1][2][ctid], sm.red[t & 1][3][ctid]));
+        const float mn = fmaxf(mo, tmax * scale);
+        sm.mref[cur ^ 1][ctid] = mn;
+        sm.alpha[t & 1][ctid] = (mo == -INFINITY) ? 0.f : (mn == mo ? 1.f : ex2(mo - mn));
+        if (mn != mo && mo != -INFINITY) sm.grew[t & 1] = 1;
+      }
       load_s(sv);
       mask_s(sv);
       ptx::tc_fence_before();
       ptx::mbar_arrive(ptx::smem_addr(&sm.s_empty[b]));
-      if (!group_sync(sm, grp_uses, p.status)) return false;
-      const float* r0 = sm.red[t & 1][0];
-      const float* r1 = sm.red[t & 1][1];
-      const float* r2 = sm.red[t & 1][2];
-      const float* r3 = sm.red[t & 1][3];
-      float* mnew = sm.mref[cur ^ 1];
-      float* alpha_s = sm.alpha[t & 1];
-      bool grew = false;
-#pragma unroll
-      for (int j = 0; j < N; ++j) {
-        const float mo = t > 0 ? mr[j] : -INFINITY;
-        const float mn = fmaxf(mo, fmaxf(fmaxf(r0[j], r1[j]), fmaxf(r2[j], r3[j])) * scale);
-        const float alpha = (mo == -INFINITY) ? 0.f : (mn == mo ? 1.f : ex2(mo - mn));
-        grew |= (mn != mo) && (mo != -INFINITY);
-        const float pv = (mn == -INFINITY) ? 0.f : ex2(fmaf(sv[j], scale, -mn));
-        l[j] = fmaf(l[j], alpha, pv);
-        sv[j] = pv;
-        if (ctid == j) {
-          mnew[j] = mn;
-          alpha_s[j] = alpha;
-        }
-      }
-      cur ^= 1;
       // New references and alphas visible to every thread (uniform branch).
       if (!group_sync(sm, grp_uses, p.status)) return false;
-      if (grew && t > 0) {
+      cur ^= 1;
+      if (t > 0 && sm.grew[t & 1]) {
+        const float* alpha_s = sm.alpha[t & 1];
+#pragma unroll
+        for (int j = 0; j < N; ++j) l[j] *= alpha_s[j];
         // Rescale the O accumulator once the previous tile's PV has landed.  PV
         // completion is observed on its P buffer's empty barrier, whose phases
         // this thread waits on in order (so the parity test is unambiguous).
@@ -546,10 +550,12 @@ __device__ bool consume_item(const AttnParams& p, TcShared& sm, const WorkItem& 
     } else {
       ptx::tc_fence_before();
       ptx::mbar_arrive(ptx::smem_addr(&sm.s_empty[b]));
+    }
+    {
+      const float* m = sm.mref[cur];
 #pragma unroll
       for (int j = 0; j < N; ++j) {
-        const float m = mr[j];
-        const float pv = (m == -INFINITY) ? 0.f : ex2(fmaf(sv[j], scale, -m));
+        const float pv = (m[j] == -INFINITY) ? 0.f : ex2(fmaf(sv[j], scale, -m[j]));
         l[j] += pv;
         sv[j] = pv;
       }
