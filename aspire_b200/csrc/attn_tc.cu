@@ -10,22 +10,27 @@
 //   S^T[128 tok x N]  = K[128 tok x 128 d]  . Q^T      (A: K, K-major SW128)
 //   O^T[128 d   x N] += V^T[128 d x 128 tok] . P^T     (A: V, MN-major SW128)
 //
-// Warp roles (224 threads):
+// Warp roles (352 threads):
 //   warp 0     K producer: TMA-gathers the tile's 8 pages (2 KiB boxes of 16
 //              tokens x 64 dims, 128-byte swizzle, through a 5-D tensor map
 //              over the paged cache) into a 2-stage K ring.
-//   warp 6     V producer: the same into a 3-stage V ring.
+//   warp 10    V producer: the same into a 3-stage V ring.
 //   warp 1     MMA issuer (one thread) and TMEM owner (256 columns: two S
 //              tiles and the O accumulator).  A K stage is released as soon
-//              as its QK^T completes, a V stage when its PV completes.
-//   warps 2-5  softmax / epilogue: thread r owns TMEM lane r, i.e. token r of
-//              the S tile and dim r of the O tile.  The running column max is
-//              kept lazily: a tile only triggers the cross-thread max
-//              reduction (warp reduce-scatter + shared memory) and the O/l
-//              rescale when one of its logits exceeds the current max by more
-//              than 2^8 in the exp2 domain, so P stays <= 256 and the common
-//              tile needs one warp vote and one 128-thread barrier.  P^T is
-//              written as bf16 (no-swizzle MN-major), O accumulates in TMEM.
+//              as its QK^T completes, a V stage when its PV completes.  It
+//              also TMA-loads each item's query tile while the previous item
+//              finishes.
+//   warps 2-9  softmax / epilogue in two warpgroups that split the item's N
+//              columns in halves: thread r of a group owns TMEM lane r, i.e.
+//              token r of the S tile and dim r of the O tile, for the group's
+//              columns.  The running column max is kept lazily: a tile only
+//              triggers the cross-thread max reduction (warp reduce-scatter +
+//              shared memory) and the O/l rescale when one of its logits
+//              exceeds the current max by more than 2^8 in the exp2 domain,
+//              so P stays <= 256 and the common tile needs one warp vote and
+//              one 128-thread barrier per group.  P^T is written as bf16
+//              (no-swizzle MN-major), O accumulates in TMEM, finished rows
+//              leave through shared memory by bulk stores.
 // Every mbarrier wait is time-bounded: on timeout the CTA records
 // ASPIRE_STATUS_TIMEOUT, stops, drains its own TMA loads and MMAs, frees
 // TMEM and returns.
@@ -42,7 +47,9 @@ namespace aspire {
 
 namespace {
 
-constexpr int kTcThreads = 224;
+constexpr int kTcThreads = 352;
+constexpr int kFirstSoftmaxWarp = 2;  // warps 2-5: softmax group 0, warps 6-9: group 1
+constexpr int kVProducerWarp = 10;
 constexpr int kTile = 128;
 constexpr int kPagesPerTile = kTile / kPageSize;
 constexpr int kKStages = 2;
@@ -64,17 +71,18 @@ struct TcShared {
   uint8_t v[kVStages][kSlotBytes];
   uint8_t q[2][kQHalfBytes];
   uint8_t p[2][kPBufBytes];
+  uint8_t out_stage[kNMax * kHeadDim * 4];  // finished rows (fp32 partial or bf16) on their way out
   float red[2][4][kNMax];
   float red_l[4][kNMax];
   float alpha[2][kNMax];
   float inv_l[kNMax];     // 1 / column sum of the finished item
   float mref[2][kNMax];   // column reference max x scale (log2 domain), double buffered
-  int flags[2][4];
-  int grew[2];            // some column reference grew in the tile (exceed path)
+  int flags[2][2][4];     // per softmax group: per-warp exceed votes, double buffered
+  int grew[2][2];         // per softmax group: some column reference grew (exceed path)
   uint64_t k_full[kKStages], k_empty[kKStages];
   uint64_t v_full[kVStages], v_empty[kVStages];
   uint64_t s_full[2], s_empty[2], p_full[2], p_empty[2];
-  uint64_t o_free, q_full, q_empty, done, grp;
+  uint64_t o_free, q_full, q_empty, done, grp[2];
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -113,13 +121,13 @@ __device__ __forceinline__ void drain_bar(uint64_t& bar, uint32_t parity) {
   }
 }
 
-// Barrier of the 128 softmax threads on an mbarrier (bounded, so that a thread
+// Barrier of one softmax warpgroup's 128 threads on an mbarrier (bounded, so that a thread
 // that stopped on a timeout cannot leave the others blocked).
-__device__ __forceinline__ bool group_sync(TcShared& sm, uint32_t& uses, uint32_t* status) {
-  ptx::mbar_arrive(ptx::smem_addr(&sm.grp));
+__device__ __forceinline__ bool group_sync(TcShared& sm, uint64_t& grp, uint32_t& uses, uint32_t* status) {
+  ptx::mbar_arrive(ptx::smem_addr(&grp));
   const uint32_t parity = uses & 1;
   ++uses;
-  return wait_bar(sm, sm.grp, parity, status);
+  return wait_bar(sm, grp, parity, status);
 }
 
 __device__ __forceinline__ int n_tiles_of(const WorkItem& it) {
@@ -367,42 +375,69 @@ __device__ __forceinline__ float reduce_scatter16(float* v, int lane) {
   return v[0];
 }
 
-// Per-warp reduction of N columns over the 32 lanes, written to out[0..N).
-// Destroys v.
-template <int N, bool kMax>
+// 8 columns over 32 lanes, in place: lane l returns the reduction of column l & 7.
+template <bool kMax>
+__device__ __forceinline__ float reduce_scatter8(float* v, int lane) {
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] = combine<kMax>(v[i], __shfl_xor_sync(0xffffffffu, v[i], 16));
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] = combine<kMax>(v[i], __shfl_xor_sync(0xffffffffu, v[i], 8));
+  scatter_step<4, kMax>(v, lane, 4);
+  scatter_step<2, kMax>(v, lane, 2);
+  scatter_step<1, kMax>(v, lane, 1);
+  return v[0];
+}
+
+// Per-warp reduction of NH (8, 16 or 24) columns over the 32 lanes, written to
+// out[0..NH).  Destroys v.
+template <int NH, bool kMax>
 __device__ __forceinline__ void warp_columns(float* v, float* out, int lane) {
-  if constexpr (N >= 32) {
-    out[lane] = reduce_scatter32<kMax>(v, lane);
-    if constexpr (N == 48) {
-      const float r = reduce_scatter16<kMax>(v + 32, lane);
-      if (lane < 16) out[32 + lane] = r;
-    }
+  if constexpr (NH == 8) {
+    const float r8 = reduce_scatter8<kMax>(v, lane);
+    if (lane < 8) out[lane] = r8;
   } else {
-    const float r = reduce_scatter16<kMax>(v, lane);
-    if (lane < 16) out[lane] = r;
+    const float r16 = reduce_scatter16<kMax>(v, lane);
+    if (lane < 16) out[lane] = r16;
+    if constexpr (NH == 24) {
+      const float r8 = reduce_scatter8<kMax>(v + 16, lane);
+      if (lane < 8) out[16 + lane] = r8;
+    }
   }
 }
 
+// NH consecutive TMEM columns of this warp's lanes (NH = 8, 16 or 24).
+template <int NH>
+__device__ __forceinline__ void tmem_load_cols(uint32_t taddr, float* v) {
+  if constexpr (NH >= 16) ptx::tmem_ld16(taddr, v);
+  if constexpr (NH == 8) ptx::tmem_ld8(taddr, v);
+  if constexpr (NH == 24) ptx::tmem_ld8(taddr + 16, v + 16);
+}
+
 // ------------------------------------------------------------------ softmax / epilogue
-template <int N>
+// The item's N packed columns are split between the two softmax warpgroups:
+// warpgroup wg owns columns [c0, c0 + NH) with c0 = wg * NH, NH = N / 2.  A
+// column's running statistics (reference max, sum, rescale factor) live with
+// its owner, so the two groups never wait for each other; they meet only on
+// the S / P / O barriers shared with the MMA warp.
+template <int NH>
 __device__ bool consume_item(const AttnParams& p, TcShared& sm, const WorkItem& it, bool causal, int r,
-                             int ctid, int wq, int lane, uint32_t& g, uint32_t& grp_uses) {
+                             int ctid, int wg, int wq, int lane, uint32_t& g, uint32_t& grp_uses) {
+  constexpr int N = 2 * NH;
+  const int c0 = wg * NH;
   const int nrows = it.pq_end - it.pq_begin;
   const int nt = n_tiles_of(it);
   const uint32_t tmem_lane = sm.tmem_base + (uint32_t(wq * 32) << 16);
   const float scale = p.scale_log2;
   const int group = p.group;
-
-  // The previous item's output left through the P buffers: its bulk stores
-  // must have read them before this item writes P (the other threads wait at
-  // the first tile's barrier).
-  if (ctid == 0) ptx::bulk_wait_read();
+  uint64_t& grp = sm.grp[wg];
+  int(*flags)[4] = sm.flags[wg];
+  int* grew = sm.grew[wg];
 
   const int q_idx0 = it.pq_begin / group;
   // First/last-query dump: the item's columns of query 0 (slot 0) and of query
   // q_len-1 (slot 1, only when q_len > 1) are two runs of at most `group`
-  // consecutive S columns; each tile reads just those runs from TMEM.
-  int dump_n0 = 0, dump_n1 = 0, dump_c1 = 0;
+  // consecutive S columns; each tile reads this group's part of those runs.
+  int d0_lo = 0, d0_hi = 0, d1_lo = 0, d1_hi = 0, dump_c1 = 0;
   __half* dump_base0 = nullptr;
   __half* dump_base1 = nullptr;
   const int64_t dump_col_stride = 2 * p.dump_kv_stride;  // between heads
@@ -410,20 +445,25 @@ __device__ bool consume_item(const AttnParams& p, TcShared& sm, const WorkItem& 
     const int last_lo = (it.q_len - 1) * group;  // first packed row of the last query
     const int64_t head0 = int64_t(it.row) * p.dump_num_heads + int64_t(it.kv_head) * group;
     if (it.pq_begin < group) {
-      dump_n0 = min(group - it.pq_begin, nrows);
+      const int n0 = min(group - it.pq_begin, nrows);
+      d0_lo = c0;
+      d0_hi = min(n0, c0 + NH);
       dump_base0 = p.dump + (head0 + it.pq_begin) * dump_col_stride;
     }
     if (it.q_len > 1 && last_lo < it.pq_end) {
       dump_c1 = max(last_lo - it.pq_begin, 0);
-      dump_n1 = it.pq_end - (it.pq_begin + dump_c1);
+      d1_lo = max(dump_c1, c0);
+      d1_hi = min(nrows, c0 + NH);
       dump_base1 = p.dump + (head0 + it.pq_begin + dump_c1 - last_lo) * dump_col_stride + p.dump_kv_stride;
     }
   }
-  // The column reference max (times scale) is uniform across threads and lives
-  // in shared memory (mref[cur]); the first tile of an item always sets it.
-  float l[N];
+  const bool dumping = d0_lo < d0_hi || d1_lo < d1_hi;
+  // The column reference max (times scale) is uniform across the group's
+  // threads and lives in shared memory (mref[cur]); the first tile of an item
+  // always sets it.
+  float l[NH];
 #pragma unroll
-  for (int j = 0; j < N; ++j) l[j] = 0.f;
+  for (int j = 0; j < NH; ++j) l[j] = 0.f;
   int cur = 0;
   const uint32_t g0 = g;
 
@@ -439,9 +479,9 @@ __device__ bool consume_item(const AttnParams& p, TcShared& sm, const WorkItem& 
     const int limit_min = causal ? (it.kv_len - it.q_len + q_idx0 + 1) : it.kv_len;
     // Padded columns (j >= nrows) only feed ignored O columns: they need no mask.
     const bool full_tile = tile0 + kTile <= it.tok_end && tile0 + kTile <= limit_min;
+    const uint32_t s_cols = tmem_lane + col_s(b) + c0;
     auto load_s = [&](float* sv) {
-#pragma unroll
-      for (int i = 0; i < N / 16; ++i) ptx::tmem_ld16(tmem_lane + col_s(b) + 16 * i, sv + 16 * i);
+      tmem_load_cols<NH>(s_cols, sv);
       ptx::tmem_wait_ld();
     };
     // Token `tok` is visible to packed column j iff it lies in the chunk and,
@@ -459,91 +499,87 @@ __device__ bool consume_item(const AttnParams& p, TcShared& sm, const WorkItem& 
     auto mask_s = [&](float* sv) {
       if (!full_tile) {
 #pragma unroll
-        for (int j = 0; j < N; ++j)
-          if (j < jmin) sv[j] = -INFINITY;
+        for (int j = 0; j < NH; ++j)
+          if (c0 + j < jmin) sv[j] = -INFINITY;
       }
     };
-    float sv[N];
+    float sv[NH];
     load_s(sv);
-    if (dump_n0 > 0 || dump_n1 > 0) {
-      // tcgen05.ld is warp-collective: every lane loads, in-range lanes store.
-      float dv[8];
-      for (int c = 0; c < dump_n0; c += 8) {
-        ptx::tmem_ld8(tmem_lane + col_s(b) + c, dv);
-        ptx::tmem_wait_ld();
-        if (in_chunk) {
+    if (dumping) {
+      // Raw logits before scale and mask.  tcgen05.ld is warp-collective:
+      // every lane loads, in-chunk lanes store.
+      auto dump_run = [&](int lo, int hi, __half* base, int base_col) {
+        float dv[8];
+        for (int c = lo; c < hi; c += 8) {
+          ptx::tmem_ld8(tmem_lane + col_s(b) + c, dv);
+          ptx::tmem_wait_ld();
+          if (in_chunk) {
 #pragma unroll
-          for (int i = 0; i < 8; ++i)
-            if (c + i < dump_n0) dump_base0[(c + i) * dump_col_stride + tok] = __float2half_rn(dv[i]);
+            for (int i = 0; i < 8; ++i)
+              if (c + i < hi) base[(c + i - base_col) * dump_col_stride + tok] = __float2half_rn(dv[i]);
+          }
         }
-      }
-      for (int c = 0; c < dump_n1; c += 8) {
-        ptx::tmem_ld8(tmem_lane + col_s(b) + dump_c1 + c, dv);
-        ptx::tmem_wait_ld();
-        if (in_chunk) {
-#pragma unroll
-          for (int i = 0; i < 8; ++i)
-            if (c + i < dump_n1) dump_base1[(c + i) * dump_col_stride + tok] = __float2half_rn(dv[i]);
-        }
-      }
+      };
+      dump_run(d0_lo, d0_hi, dump_base0, 0);
+      dump_run(d1_lo, d1_hi, dump_base1, dump_c1);
     }
     mask_s(sv);
 
     // Lazy running max: does any logit of the tile exceed its column's reference by > 2^8?
-    const float* mr = sm.mref[cur];
+    const float* mr = sm.mref[cur] + c0;
     bool exceed = (t == 0);
     if (t > 0) {
 #pragma unroll
-      for (int j = 0; j < N; ++j) exceed |= fmaf(sv[j], scale, -mr[j]) > kLazyLog2;
+      for (int j = 0; j < NH; ++j) exceed |= fmaf(sv[j], scale, -mr[j]) > kLazyLog2;
     }
     const bool warp_exceed = __any_sync(0xffffffffu, exceed);
-    if (lane == 0) sm.flags[t & 1][wq] = warp_exceed ? 1 : 0;
-    if (!group_sync(sm, grp_uses, p.status)) return false;
-    const bool any_exceed =
-        (sm.flags[t & 1][0] | sm.flags[t & 1][1] | sm.flags[t & 1][2] | sm.flags[t & 1][3]) != 0;
+    if (lane == 0) flags[t & 1][wq] = warp_exceed ? 1 : 0;
+    if (!group_sync(sm, grp, grp_uses, p.status)) return false;
+    const bool any_exceed = (flags[t & 1][0] | flags[t & 1][1] | flags[t & 1][2] | flags[t & 1][3]) != 0;
     if (any_exceed) {
       // Exact column maxima of the tile (reduced in place; S is read again from
-      // TMEM afterwards).  Thread j < N then updates column j's reference
+      // TMEM afterwards).  Thread j < NH then updates column c0 + j's reference
       // (mref[cur ^ 1]) and its rescale factor alpha; the per-column work is
       // spread over threads so that this once-per-item path stays short.
-      warp_columns<N, true>(sv, sm.red[t & 1][wq], lane);
-      if (ctid == 0) sm.grew[t & 1] = 0;
-      if (!group_sync(sm, grp_uses, p.status)) return false;
-      if (ctid < N) {
-        const float mo = t > 0 ? mr[ctid] : -INFINITY;
-        const float tmax = fmaxf(fmaxf(sm.red[t & 1][0][ctid], sm.red[t & 1][1][ctid]),
-                                 fmaxf(sm.red[t & 1][2][ctid], sm.red[t & 1][3][ctid]));
+      warp_columns<NH, true>(sv, sm.red[t & 1][wq] + c0, lane);
+      if (ctid == 0) grew[t & 1] = 0;
+      if (!group_sync(sm, grp, grp_uses, p.status)) return false;
+      if (ctid < NH) {
+        const int c = c0 + ctid;
+        const float mo = t > 0 ? sm.mref[cur][c] : -INFINITY;
+        const float tmax = fmaxf(fmaxf(sm.red[t & 1][0][c], sm.red[t & 1][1][c]),
+                                 fmaxf(sm.red[t & 1][2][c], sm.red[t & 1][3][c]));
         const float mn = fmaxf(mo, tmax * scale);
-        sm.mref[cur ^ 1][ctid] = mn;
-        sm.alpha[t & 1][ctid] = (mo == -INFINITY) ? 0.f : (mn == mo ? 1.f : ex2(mo - mn));
-        if (mn != mo && mo != -INFINITY) sm.grew[t & 1] = 1;
+        sm.mref[cur ^ 1][c] = mn;
+        sm.alpha[t & 1][c] = (mo == -INFINITY) ? 0.f : (mn == mo ? 1.f : ex2(mo - mn));
+        if (mn != mo && mo != -INFINITY) grew[t & 1] = 1;
       }
       load_s(sv);
       mask_s(sv);
       ptx::tc_fence_before();
       ptx::mbar_arrive(ptx::smem_addr(&sm.s_empty[b]));
       // New references and alphas visible to every thread (uniform branch).
-      if (!group_sync(sm, grp_uses, p.status)) return false;
+      if (!group_sync(sm, grp, grp_uses, p.status)) return false;
       cur ^= 1;
-      if (t > 0 && sm.grew[t & 1]) {
-        const float* alpha_s = sm.alpha[t & 1];
+      if (t > 0 && grew[t & 1]) {
+        const float* alpha_s = sm.alpha[t & 1] + c0;
 #pragma unroll
-        for (int j = 0; j < N; ++j) l[j] *= alpha_s[j];
-        // Rescale the O accumulator once the previous tile's PV has landed.  PV
-        // completion is observed on its P buffer's empty barrier, whose phases
-        // this thread waits on in order (so the parity test is unambiguous).
+        for (int j = 0; j < NH; ++j) l[j] *= alpha_s[j];
+        // Rescale this group's O columns once the previous tile's PV has
+        // landed.  PV completion is observed on its P buffer's empty barrier,
+        // whose phases this thread waits on in order (so the parity test is
+        // unambiguous).
         const uint32_t prev = gt - 1;
         if (!wait_bar(sm, sm.p_empty[prev % 2], (prev / 2) & 1, p.status)) return false;
         ptx::tc_fence_after();
+        float ov[NH];
+        tmem_load_cols<NH>(tmem_lane + kColO + c0, ov);
+        ptx::tmem_wait_ld();
 #pragma unroll
-        for (int i = 0; i < N / 16; ++i) {
-          float ov[16];
-          ptx::tmem_ld16(tmem_lane + kColO + 16 * i, ov);
-          ptx::tmem_wait_ld();
-#pragma unroll
-          for (int c = 0; c < 16; ++c) ov[c] *= alpha_s[16 * i + c];
-          ptx::tmem_st16(tmem_lane + kColO + 16 * i, ov);
-        }
+        for (int j = 0; j < NH; ++j) ov[j] *= alpha_s[j];
+        if constexpr (NH >= 16) ptx::tmem_st16(tmem_lane + kColO + c0, ov);
+        if constexpr (NH == 8) ptx::tmem_st8(tmem_lane + kColO + c0, ov);
+        if constexpr (NH == 24) ptx::tmem_st8(tmem_lane + kColO + c0 + 16, ov + 16);
         ptx::tmem_wait_st();
         ptx::tc_fence_before();
       }
@@ -552,9 +588,9 @@ __device__ bool consume_item(const AttnParams& p, TcShared& sm, const WorkItem& 
       ptx::mbar_arrive(ptx::smem_addr(&sm.s_empty[b]));
     }
     {
-      const float* m = sm.mref[cur];
+      const float* m = sm.mref[cur] + c0;
 #pragma unroll
-      for (int j = 0; j < N; ++j) {
+      for (int j = 0; j < NH; ++j) {
         const float pv = (m[j] == -INFINITY) ? 0.f : ex2(fmaf(sv[j], scale, -m[j]));
         l[j] += pv;
         sv[j] = pv;
@@ -562,9 +598,9 @@ __device__ bool consume_item(const AttnParams& p, TcShared& sm, const WorkItem& 
     }
     // P^T as bf16, MN-major without swizzle: 8 queries x 16 B per token, token-major.
     if (!wait_bar(sm, sm.p_empty[b], ph ^ 1, p.status)) return false;
-    uint8_t* pbuf = sm.p[b];
+    uint8_t* pbuf = sm.p[b] + (c0 / 8) * (kTile * 16);
 #pragma unroll
-    for (int c = 0; c < N / 8; ++c) {
+    for (int c = 0; c < NH / 8; ++c) {
       uint4 val;
       __nv_bfloat162 h0 = __floats2bfloat162_rn(sv[8 * c + 0], sv[8 * c + 1]);
       __nv_bfloat162 h1 = __floats2bfloat162_rn(sv[8 * c + 2], sv[8 * c + 3]);
@@ -582,64 +618,70 @@ __device__ bool consume_item(const AttnParams& p, TcShared& sm, const WorkItem& 
   g = g0 + nt;
 
   // Final O: wait for the item's last PV (on its P buffer's empty barrier),
-  // read this lane (dim r), free the accumulator.
+  // read this lane (dim r) of the group's columns, free the accumulator.
   if (!wait_bar(sm, sm.p_empty[(g - 1) % 2], ((g - 1) / 2) & 1, p.status)) return false;
   ptx::tc_fence_after();
-  float o_fin[N];
-#pragma unroll
-  for (int i = 0; i < N / 16; ++i) ptx::tmem_ld16(tmem_lane + kColO + 16 * i, o_fin + 16 * i);
+  float o_fin[NH];
+  tmem_load_cols<NH>(tmem_lane + kColO + c0, o_fin);
   ptx::tmem_wait_ld();
   ptx::tc_fence_before();
   ptx::mbar_arrive(ptx::smem_addr(&sm.o_free));
 
-  // Column sums of l across the 128 threads; thread j < N then turns column j
-  // into its reciprocal and LSE once.
-  warp_columns<N, false>(l, sm.red_l[wq], lane);
-  if (!group_sync(sm, grp_uses, p.status)) return false;
-  float my_lse = -INFINITY;  // LSE of column ctid
-  if (ctid < N) {
-    const float L = sm.red_l[0][ctid] + sm.red_l[1][ctid] + sm.red_l[2][ctid] + sm.red_l[3][ctid];
-    sm.inv_l[ctid] = L > 0.f ? 1.f / L : 0.f;
-    my_lse = L > 0.f ? sm.mref[cur][ctid] + lg2(L) : -INFINITY;
+  // Column sums of l across the group's 128 threads; thread j < NH then turns
+  // column c0 + j into its reciprocal and LSE once.
+  warp_columns<NH, false>(l, sm.red_l[wq] + c0, lane);
+  if (!group_sync(sm, grp, grp_uses, p.status)) return false;
+  float my_lse = -INFINITY;  // LSE of column c0 + ctid
+  if (ctid < NH) {
+    const int c = c0 + ctid;
+    const float L = sm.red_l[0][c] + sm.red_l[1][c] + sm.red_l[2][c] + sm.red_l[3][c];
+    sm.inv_l[c] = L > 0.f ? 1.f / L : 0.f;
+    my_lse = L > 0.f ? sm.mref[cur][c] + lg2(L) : -INFINITY;
   }
-  if (!group_sync(sm, grp_uses, p.status)) return false;
+  // The previous item's bulk stores (issued by this group's thread 0) have
+  // read the group's staging rows before anyone rewrites them.
+  if (ctid == 0) ptx::bulk_wait_read();
+  if (!group_sync(sm, grp, grp_uses, p.status)) return false;
 
-  // Normalised rows are staged in the P buffers (idle until this CTA's next
-  // item writes P) and leave by bulk stores, so the threads move on at once.
+  // Normalised rows are staged in shared memory and leave by bulk stores, so
+  // the threads move on to the next item at once.
   const int d = r;  // this thread's output dim
-  uint8_t* stage = sm.p[0];
+  uint8_t* stage = sm.out_stage;
   const bool final_rows = it.n_chunks <= 1;
+  const int row_end = min(c0 + NH, nrows);  // this group's rows are [c0, row_end)
   if (final_rows) {
     __nv_bfloat16* st = reinterpret_cast<__nv_bfloat16*>(stage);
 #pragma unroll
-    for (int j = 0; j < N; ++j)
-      if (j < nrows) st[j * kHeadDim + d] = __float2bfloat16_rn(o_fin[j] * sm.inv_l[j]);
-    if (ctid < nrows && p.lse) {
+    for (int j = 0; j < NH; ++j)
+      if (c0 + j < nrows) st[(c0 + j) * kHeadDim + d] = __float2bfloat16_rn(o_fin[j] * sm.inv_l[c0 + j]);
+    if (ctid < NH && c0 + ctid < nrows && p.lse) {
       int q_idx, head;
-      packed_row(p, it, it.pq_begin + ctid, q_idx, head);
+      packed_row(p, it, it.pq_begin + c0 + ctid, q_idx, head);
       p.lse[(int64_t(it.q_start) + q_idx) * p.num_qo_heads + head] = my_lse;
     }
   } else {
     float* st = reinterpret_cast<float*>(stage);
 #pragma unroll
-    for (int j = 0; j < N; ++j)
-      if (j < nrows) st[j * kHeadDim + d] = o_fin[j] * sm.inv_l[j];
-    if (ctid < nrows) partial_lse_ptr(p)[int64_t(it.partial_base) + int64_t(it.chunk) * nrows + ctid] = my_lse;
+    for (int j = 0; j < NH; ++j)
+      if (c0 + j < nrows) st[(c0 + j) * kHeadDim + d] = o_fin[j] * sm.inv_l[c0 + j];
+    if (ctid < NH && c0 + ctid < nrows)
+      partial_lse_ptr(p)[int64_t(it.partial_base) + int64_t(it.chunk) * nrows + c0 + ctid] = my_lse;
   }
   ptx::fence_proxy_async_smem();
-  if (!group_sync(sm, grp_uses, p.status)) return false;
-  if (ctid == 0) {
-    const uint32_t src = ptx::smem_addr(stage);
+  if (!group_sync(sm, grp, grp_uses, p.status)) return false;
+  if (ctid == 0 && c0 < row_end) {
     if (final_rows) {
-      for (int j = 0; j < nrows; ++j) {
+      const uint32_t src = ptx::smem_addr(stage);
+      for (int j = c0; j < row_end; ++j) {
         int q_idx, head;
         packed_row(p, it, it.pq_begin + j, q_idx, head);
         __nv_bfloat16* dst = p.out + (int64_t(it.q_start) + q_idx) * p.o_stride_n + int64_t(head) * p.o_stride_h;
         ptx::bulk_store(dst, src + uint32_t(j) * kHeadDim * 2, kHeadDim * 2);
       }
     } else {
-      const int64_t base = int64_t(it.partial_base) + int64_t(it.chunk) * nrows;
-      ptx::bulk_store(p.partial_o + base * kHeadDim, src, uint32_t(nrows) * kHeadDim * 4);
+      const uint32_t src = ptx::smem_addr(stage) + uint32_t(c0) * kHeadDim * 4;
+      const int64_t base = int64_t(it.partial_base) + int64_t(it.chunk) * nrows + c0;
+      ptx::bulk_store(p.partial_o + base * kHeadDim, src, uint32_t(row_end - c0) * kHeadDim * 4);
     }
     ptx::bulk_commit();
   }
@@ -649,30 +691,31 @@ __device__ bool consume_item(const AttnParams& p, TcShared& sm, const WorkItem& 
 __device__ void consume_items(const AttnParams& p, TcShared& sm, int item_begin, int item_end, bool causal,
                               int warp, int lane) {
   const int wq = warp & 3;
-  const int r = wq * 32 + lane;          // TMEM lane = S-tile token = O-tile dim
-  const int ctid = threadIdx.x - 64;     // 0..127
+  const int wg = (warp - kFirstSoftmaxWarp) / 4;  // softmax warpgroup 0 or 1
+  const int r = wq * 32 + lane;                    // TMEM lane = S-tile token = O-tile dim
+  const int ctid = (warp - kFirstSoftmaxWarp - 4 * wg) * 32 + lane;  // 0..127 within the group
   uint32_t g = 0, grp_uses = 0;
   for (int ii = item_begin; ii < item_end; ++ii) {
     if (aborted(sm)) return;
     const WorkItem it = load_item(p.plan, ii);
     const int nrows = it.pq_end - it.pq_begin;
     if (!item_valid(p, it)) {
-      if (ctid == 0) record_status(p.status, ASPIRE_STATUS_BAD_PLAN);
+      if (ctid == 0 && wg == 0) record_status(p.status, ASPIRE_STATUS_BAD_PLAN);
       continue;
     }
     if (n_tiles_of(it) == 0) {
       // No keys: zero output, -inf LSE (chunked items always have keys).
-      for (int j = 0; j < nrows; ++j) store_final(p, it, it.pq_begin + j, r, 0.f, -INFINITY);
+      for (int j = wg; j < nrows; j += 2) store_final(p, it, it.pq_begin + j, r, 0.f, -INFINITY);
       continue;
     }
     const int N = (nrows + 15) / 16 * 16;
     bool ok;
     if (N == 16)
-      ok = consume_item<16>(p, sm, it, causal, r, ctid, wq, lane, g, grp_uses);
+      ok = consume_item<8>(p, sm, it, causal, r, ctid, wg, wq, lane, g, grp_uses);
     else if (N == 32)
-      ok = consume_item<32>(p, sm, it, causal, r, ctid, wq, lane, g, grp_uses);
+      ok = consume_item<16>(p, sm, it, causal, r, ctid, wg, wq, lane, g, grp_uses);
     else
-      ok = consume_item<48>(p, sm, it, causal, r, ctid, wq, lane, g, grp_uses);
+      ok = consume_item<24>(p, sm, it, causal, r, ctid, wg, wq, lane, g, grp_uses);
     if (!ok) return;
   }
 }
@@ -680,9 +723,9 @@ __device__ void consume_items(const AttnParams& p, TcShared& sm, int item_begin,
 __device__ void run_consumer(const AttnParams& p, TcShared& sm, int item_begin, int item_end, bool causal,
                              int warp, int lane) {
   consume_items(p, sm, item_begin, item_end, causal, warp, lane);
-  // The bulk stores of the last item (issued by thread 0 of the group) finish
+  // The bulk stores of each group's last item (issued by its thread 0) finish
   // before the CTA exits.
-  if (threadIdx.x == 64) ptx::bulk_wait_all();
+  if (lane == 0 && (warp - kFirstSoftmaxWarp) % 4 == 0) ptx::bulk_wait_all();
 }
 
 }  // namespace
@@ -713,15 +756,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       ptx::mbar_init(ptx::smem_addr(&sm.s_full[b]), 1);
-      ptx::mbar_init(ptx::smem_addr(&sm.s_empty[b]), 128);
-      ptx::mbar_init(ptx::smem_addr(&sm.p_full[b]), 128);
+      ptx::mbar_init(ptx::smem_addr(&sm.s_empty[b]), 256);
+      ptx::mbar_init(ptx::smem_addr(&sm.p_full[b]), 256);
       ptx::mbar_init(ptx::smem_addr(&sm.p_empty[b]), 1);
     }
-    ptx::mbar_init(ptx::smem_addr(&sm.o_free), 128);
+    ptx::mbar_init(ptx::smem_addr(&sm.o_free), 256);
     ptx::mbar_init(ptx::smem_addr(&sm.q_full), 1);
     ptx::mbar_init(ptx::smem_addr(&sm.q_empty), 1);
     ptx::mbar_init(ptx::smem_addr(&sm.done), 1);
-    ptx::mbar_init(ptx::smem_addr(&sm.grp), 128);
+    ptx::mbar_init(ptx::smem_addr(&sm.grp[0]), 128);
+    ptx::mbar_init(ptx::smem_addr(&sm.grp[1]), 128);
     sm.abort_flag = 0;
     ptx::mbar_fence_init();
   }
@@ -742,7 +786,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
   if (warp == 0) {
     run_producer<kKStages>(p, &tmap, sm, sm.k, sm.k_full, sm.k_empty, 0, item_begin, item_end, lane);
-  } else if (warp == 6) {
+  } else if (warp == kVProducerWarp) {
     run_producer<kVStages>(p, &tmap, sm, sm.v, sm.v_full, sm.v_empty, 1, item_begin, item_end, lane);
   } else if (warp == 1) {
     run_mma(p, &qmap, sm, item_begin, item_end, lane);
