@@ -1,8 +1,8 @@
 // tcgen05 paged-attention kernel for wide packed-query tiles (verify rows,
 // and any row whose q_len x group exceeds the gather kernel's 4-row tile).
 //
-// One persistent CTA per SM walks its list of work items (a KV chunk of one
-// (row, KV head, packed-query tile)).  The contraction is laid out "swapped":
+// One persistent CTA per SM claims work items (a KV chunk of one (row, KV
+// head, packed-query tile)) from the plan's shared list, longest first.  The contraction is laid out "swapped":
 // the 128 KV tokens of a tile are the MMA's M dimension and the packed
 // (query, head-in-group) rows are its N dimension (16, 32 or 48), so one
 // 128-token K/V tile feeds the whole GQA group and N stays small:
@@ -50,6 +50,8 @@ namespace {
 constexpr int kTcThreads = 352;
 constexpr int kFirstSoftmaxWarp = 2;  // warps 2-5: softmax group 0, warps 6-9: group 1
 constexpr int kVProducerWarp = 10;
+constexpr int kSeqDepth = 8;          // item-sequence ring (claimed items in flight per CTA)
+constexpr int kSeqReaders = 10;       // V producer, MMA warp and the 8 softmax warps
 constexpr int kTile = 128;
 constexpr int kPagesPerTile = kTile / kPageSize;
 constexpr int kKStages = 2;
@@ -83,6 +85,8 @@ struct TcShared {
   uint64_t v_full[kVStages], v_empty[kVStages];
   uint64_t s_full[2], s_empty[2], p_full[2], p_empty[2];
   uint64_t o_free, q_full, q_empty, done, grp[2];
+  uint64_t seq_full[kSeqDepth], seq_empty[kSeqDepth];
+  int seq[kSeqDepth];
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -145,6 +149,42 @@ __device__ __forceinline__ bool aborted(TcShared& sm) {
   return *reinterpret_cast<volatile int*>(&sm.abort_flag) != 0;
 }
 
+// ------------------------------------------------------------------ item sequence
+// The CTAs share the plan's tcgen05 item list and claim items from it at run
+// time, longest first (a global counter in the plan header).  In each CTA the
+// K producer claims an item when it is ready to load it and publishes the
+// index (-1 once the list is exhausted) in a small ring; the other roles read
+// the same sequence in order.  Every warp reads through its lane 0, which
+// returns -2 when a wait times out.
+__device__ __forceinline__ int seq_claim(const AttnParams& p, TcShared& sm, uint32_t& k, int lane, int tc_first,
+                                         int n_tc) {
+  int item = -2;
+  if (lane == 0) {
+    const int s = int(k % kSeqDepth);
+    if (wait_bar(sm, sm.seq_empty[s], ((k / kSeqDepth) & 1) ^ 1, p.status)) {
+      const int c = atomicAdd(const_cast<int32_t*>(p.plan) + kHdrTcClaim, 1);
+      item = c < n_tc ? tc_first + c : -1;
+      *reinterpret_cast<volatile int*>(&sm.seq[s]) = item;
+      ptx::mbar_arrive(ptx::smem_addr(&sm.seq_full[s]));
+    }
+  }
+  ++k;
+  return __shfl_sync(0xffffffffu, item, 0);
+}
+
+__device__ __forceinline__ int seq_read(TcShared& sm, uint32_t& k, int lane, uint32_t* status) {
+  int item = -2;
+  if (lane == 0) {
+    const int s = int(k % kSeqDepth);
+    if (wait_bar(sm, sm.seq_full[s], (k / kSeqDepth) & 1, status)) {
+      item = *reinterpret_cast<volatile int*>(&sm.seq[s]);
+      ptx::mbar_arrive(ptx::smem_addr(&sm.seq_empty[s]));
+    }
+  }
+  ++k;
+  return __shfl_sync(0xffffffffu, item, 0);
+}
+
 // ------------------------------------------------------------------ producers
 // Lane pg (< 8) owns page pg of every tile: it reads the page id one tile
 // ahead (the read overlaps the wait for a free slot) and issues the page's two
@@ -152,13 +192,16 @@ __device__ __forceinline__ bool aborted(TcShared& sm) {
 template <int STAGES>
 __device__ void run_producer(const AttnParams& p, const CUtensorMap* tmap, TcShared& sm,
                              uint8_t (*ring)[kSlotBytes], uint64_t* full, uint64_t* empty, int kv_sel,
-                             int item_begin, int item_end, int lane) {
-  uint32_t g = 0;
+                             bool leader, int tc_first, int n_tc, int lane) {
+  uint32_t g = 0, k = 0;
   int64_t last_issue[STAGES];
 #pragma unroll
   for (int s = 0; s < STAGES; ++s) last_issue[s] = -1;
   bool ok = true;
-  for (int ii = item_begin; ii < item_end && ok; ++ii) {
+  while (ok) {
+    const int ii = leader ? seq_claim(p, sm, k, lane, tc_first, n_tc) : seq_read(sm, k, lane, p.status);
+    if (ii == -2) ok = false;
+    if (ii < 0) break;
     const WorkItem it = load_item(p.plan, ii);
     if (!item_valid(p, it)) continue;
     const int nt = n_tiles_of(it);
@@ -208,13 +251,15 @@ __device__ void run_producer(const AttnParams& p, const CUtensorMap* tmap, TcSha
 }
 
 // ------------------------------------------------------------------ MMA issuer
-// Next item at or after `from` that has KV tiles (the roles skip the same items).
-__device__ __forceinline__ int next_tc_item(const AttnParams& p, int from, int item_end) {
-  for (int j = from; j < item_end; ++j) {
-    const WorkItem it = load_item(p.plan, j);
-    if (item_valid(p, it) && n_tiles_of(it) > 0) return j;
+// Next item of the sequence that has KV tiles (the roles skip the same items);
+// -1 at the end of the sequence, -2 on a timeout.
+__device__ __forceinline__ int next_tc_item(const AttnParams& p, TcShared& sm, uint32_t& k, int lane) {
+  for (;;) {
+    const int ii = seq_read(sm, k, lane, p.status);
+    if (ii < 0) return ii;
+    const WorkItem it = load_item(p.plan, ii);
+    if (item_valid(p, it) && n_tiles_of(it) > 0) return ii;
   }
-  return item_end;
 }
 
 // Requests item `idx`'s query tile: one box of (64 dims x group heads x
@@ -232,10 +277,9 @@ __device__ __forceinline__ void issue_q(const AttnParams& p, const CUtensorMap* 
   ptx::tma_load_3d(ptx::smem_addr(sm.q[1]), qmap, bar, 64, it.kv_head * p.group, it.q_start + q_idx0);
 }
 
-__device__ void run_mma(const AttnParams& p, const CUtensorMap* qmap, TcShared& sm, int item_begin,
-                        int item_end, int lane) {
+__device__ void run_mma(const AttnParams& p, const CUtensorMap* qmap, TcShared& sm, int lane) {
   const uint32_t tmem = sm.tmem_base;
-  uint32_t g = 0, items_done = 0;
+  uint32_t g = 0, items_done = 0, k = 0;
   bool ok = true;
   const uint32_t k0 = ptx::smem_addr(sm.k[0]);
   const uint32_t v0 = ptx::smem_addr(sm.v[0]);
@@ -265,12 +309,13 @@ __device__ void run_mma(const AttnParams& p, const CUtensorMap* qmap, TcShared& 
     return true;
   };
 
-  int ii = next_tc_item(p, item_begin, item_end);
-  if (ii < item_end) {
+  int ii = next_tc_item(p, sm, k, lane);
+  if (ii == -2) ok = false;
+  if (ii >= 0) {
     if (lane == 0) issue_q(p, qmap, sm, ii);
     q_pending = true;
   }
-  while (ii < item_end && ok) {
+  while (ii >= 0 && ok) {
     const WorkItem it = load_item(p.plan, ii);
     const int nt = n_tiles_of(it);
     const int nrows = it.pq_end - it.pq_begin;
@@ -310,8 +355,12 @@ __device__ void run_mma(const AttnParams& p, const CUtensorMap* qmap, TcShared& 
     }
     if (!ok) break;
     // The next item's query tile loads while this item's last PV and epilogue run.
-    const int nxt = next_tc_item(p, ii + 1, item_end);
-    if (nxt < item_end) {
+    const int nxt = next_tc_item(p, sm, k, lane);
+    if (nxt == -2) {
+      ok = false;
+      break;
+    }
+    if (nxt >= 0) {
       if (!wait_bar(sm, sm.q_empty, items_done & 1, p.status)) {
         ok = false;
         break;
@@ -688,15 +737,16 @@ __device__ bool consume_item(const AttnParams& p, TcShared& sm, const WorkItem& 
   return true;
 }
 
-__device__ void consume_items(const AttnParams& p, TcShared& sm, int item_begin, int item_end, bool causal,
-                              int warp, int lane) {
+__device__ void consume_items(const AttnParams& p, TcShared& sm, bool causal, int warp, int lane) {
   const int wq = warp & 3;
   const int wg = (warp - kFirstSoftmaxWarp) / 4;  // softmax warpgroup 0 or 1
   const int r = wq * 32 + lane;                    // TMEM lane = S-tile token = O-tile dim
   const int ctid = (warp - kFirstSoftmaxWarp - 4 * wg) * 32 + lane;  // 0..127 within the group
-  uint32_t g = 0, grp_uses = 0;
-  for (int ii = item_begin; ii < item_end; ++ii) {
+  uint32_t g = 0, grp_uses = 0, k = 0;
+  for (;;) {
     if (aborted(sm)) return;
+    const int ii = seq_read(sm, k, lane, p.status);
+    if (ii < 0) return;
     const WorkItem it = load_item(p.plan, ii);
     const int nrows = it.pq_end - it.pq_begin;
     if (!item_valid(p, it)) {
@@ -720,9 +770,8 @@ __device__ void consume_items(const AttnParams& p, TcShared& sm, int item_begin,
   }
 }
 
-__device__ void run_consumer(const AttnParams& p, TcShared& sm, int item_begin, int item_end, bool causal,
-                             int warp, int lane) {
-  consume_items(p, sm, item_begin, item_end, causal, warp, lane);
+__device__ void run_consumer(const AttnParams& p, TcShared& sm, bool causal, int warp, int lane) {
+  consume_items(p, sm, causal, warp, lane);
   // The bulk stores of each group's last item (issued by its thread 0) finish
   // before the CTA exits.
   if (lane == 0 && (warp - kFirstSoftmaxWarp) % 4 == 0) ptx::bulk_wait_all();
@@ -739,9 +788,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const int32_t* plan = p.plan;
   if (plan[kHdrMagic] != kPlanMagic) return;
   if (int(blockIdx.x) >= plan[kHdrNumTcCtas]) return;
-  const int32_t* indptr = plan + plan[kHdrOffTcIndptr];
-  const int item_begin = indptr[blockIdx.x], item_end = indptr[blockIdx.x + 1];
-  if (item_begin >= item_end) return;
+  const int tc_first = plan[kHdrTcFirst];
+  const int n_tc = plan[kHdrNumItems] - tc_first;
+  if (n_tc <= 0) return;
   const bool causal = plan[kHdrCausal] != 0;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
@@ -766,6 +815,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     ptx::mbar_init(ptx::smem_addr(&sm.done), 1);
     ptx::mbar_init(ptx::smem_addr(&sm.grp[0]), 128);
     ptx::mbar_init(ptx::smem_addr(&sm.grp[1]), 128);
+    for (int s = 0; s < kSeqDepth; ++s) {
+      ptx::mbar_init(ptx::smem_addr(&sm.seq_full[s]), 1);
+      ptx::mbar_init(ptx::smem_addr(&sm.seq_empty[s]), kSeqReaders);
+    }
     sm.abort_flag = 0;
     ptx::mbar_fence_init();
   }
@@ -785,13 +838,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   ptx::tc_fence_after();
 
   if (warp == 0) {
-    run_producer<kKStages>(p, &tmap, sm, sm.k, sm.k_full, sm.k_empty, 0, item_begin, item_end, lane);
+    run_producer<kKStages>(p, &tmap, sm, sm.k, sm.k_full, sm.k_empty, 0, true, tc_first, n_tc, lane);
   } else if (warp == kVProducerWarp) {
-    run_producer<kVStages>(p, &tmap, sm, sm.v, sm.v_full, sm.v_empty, 1, item_begin, item_end, lane);
+    run_producer<kVStages>(p, &tmap, sm, sm.v, sm.v_full, sm.v_empty, 1, false, tc_first, n_tc, lane);
   } else if (warp == 1) {
-    run_mma(p, &qmap, sm, item_begin, item_end, lane);
+    run_mma(p, &qmap, sm, lane);
   } else {
-    run_consumer(p, sm, item_begin, item_end, causal, warp, lane);
+    run_consumer(p, sm, causal, warp, lane);
   }
 
   ptx::tc_fence_before();

@@ -25,7 +25,7 @@ enum PlanHeader : int {
   kHdrNumItems = 1,
   kHdrNumGatherCtas = 2,     // grid of the gather kernel the list was built for
   kHdrOffGatherIndptr = 3,   // int32 index of gather CTA indptr [num_ctas + 1]
-  kHdrOffTcIndptr = 4,       // int32 index of tcgen05 CTA indptr [num_ctas + 1]
+  kHdrTcFirst = 4,           // index of the first tcgen05 item; they run to kHdrNumItems
   kHdrOffItems = 5,          // int32 index of the item array
   kHdrOffMerge = 6,          // int32 index of the merge descriptors [num_merge]
   kHdrNumMerge = 7,
@@ -35,6 +35,7 @@ enum PlanHeader : int {
   kHdrNumTcCtas = 11,        // grid of the tcgen05 kernel the list was built for
   kHdrOffMergeUnits = 12,    // int32 index of the merge units [num_merge_units]
   kHdrNumMergeUnits = 13,    // (merge group, packed row) pairs, one warp each
+  kHdrTcClaim = 14,          // tcgen05 items claimed so far (0 at upload; the merge kernel resets it)
   kHdrWords = 16,
 };
 constexpr int32_t kPlanMagic = 0x41535042;  // "ASPB"

@@ -28,9 +28,16 @@ struct GroupDesc {
 };
 
 // Item cost in "tokens": the KV tokens streamed plus a fixed per-item
-// overhead covering setup, Q load and the epilogue.
+// overhead covering setup, the first tile's reduction and the epilogue.
 inline int64_t item_cost(const WorkItem& it) {
-  return int64_t(it.tok_end - it.tok_begin) + 96;
+  return int64_t(it.tok_end - it.tok_begin) + 512;
+}
+
+// Longest first: the order in which the tcgen05 CTAs claim items at run time.
+void order_by_cost(std::vector<WorkItem>& items) {
+  std::stable_sort(items.begin(), items.end(), [](const WorkItem& a, const WorkItem& b) {
+    return item_cost(a) > item_cost(b);
+  });
 }
 
 void assign_lpt(std::vector<WorkItem>& items, int num_ctas, std::vector<int32_t>& indptr,
@@ -178,19 +185,20 @@ int plan_impl(const int32_t* qo_indptr, const int32_t* kv_indptr, const int32_t*
     }
   }
 
-  std::vector<int32_t> gather_indptr, tc_indptr;
-  std::vector<WorkItem> gather_ordered, tc_ordered;
+  // CUDA-core items are placed on CTAs ahead of time (LPT); tcgen05 items are
+  // claimed by the persistent CTAs at run time, longest first.
+  std::vector<int32_t> gather_indptr;
+  std::vector<WorkItem> gather_ordered;
   assign_lpt(gather_items, gather_ctas, gather_indptr, gather_ordered);
-  assign_lpt(tc_items, tc_ctas, tc_indptr, tc_ordered);
+  order_by_cost(tc_items);
+  const std::vector<WorkItem>& tc_ordered = tc_items;
   // The tcgen05 list is stored after the gather list in one item array.
   const int32_t n_gather = static_cast<int32_t>(gather_ordered.size());
-  for (auto& v : tc_indptr) v += n_gather;
   const int32_t num_items = n_gather + static_cast<int32_t>(tc_ordered.size());
 
-  // Layout (int32 words): header | gather indptr | tc indptr | items | merges | merge units.
+  // Layout (int32 words): header | gather indptr | items | merges | merge units.
   const int64_t off_gather = kHdrWords;
-  const int64_t off_tc = off_gather + gather_ctas + 1;
-  int64_t off_items = off_tc + tc_ctas + 1;
+  int64_t off_items = off_gather + gather_ctas + 1;
   off_items = (off_items + 15) / 16 * 16;  // 64-byte aligned items
   const int64_t off_merge = off_items + int64_t(num_items) * kItemWords;
   const int64_t off_units = off_merge + int64_t(num_merge) * kMergeWords;
@@ -215,7 +223,8 @@ int plan_impl(const int32_t* qo_indptr, const int32_t* kv_indptr, const int32_t*
   w[kHdrNumTcCtas] = tc_ctas;
   w[kHdrCausal] = causal ? 1 : 0;
   w[kHdrOffGatherIndptr] = static_cast<int32_t>(off_gather);
-  w[kHdrOffTcIndptr] = static_cast<int32_t>(off_tc);
+  w[kHdrTcFirst] = n_gather;
+  w[kHdrTcClaim] = 0;
   w[kHdrOffItems] = static_cast<int32_t>(off_items);
   w[kHdrOffMerge] = static_cast<int32_t>(off_merge);
   w[kHdrNumMerge] = num_merge;
@@ -225,8 +234,7 @@ int plan_impl(const int32_t* qo_indptr, const int32_t* kv_indptr, const int32_t*
   w[kHdrPartialLseLo] = static_cast<int32_t>(lse_off & 0xffffffff);
   w[kHdrPartialLseHi] = static_cast<int32_t>(lse_off >> 32);
   std::memcpy(w + off_gather, gather_indptr.data(), size_t(gather_ctas + 1) * 4);
-  std::memcpy(w + off_tc, tc_indptr.data(), size_t(tc_ctas + 1) * 4);
-  for (int64_t i = off_tc + tc_ctas + 1; i < off_items; ++i) w[i] = 0;
+  for (int64_t i = off_gather + gather_ctas + 1; i < off_items; ++i) w[i] = 0;
   if (n_gather) std::memcpy(w + off_items, gather_ordered.data(), size_t(n_gather) * sizeof(WorkItem));
   if (!tc_ordered.empty())
     std::memcpy(w + off_items + int64_t(n_gather) * kItemWords, tc_ordered.data(),

@@ -78,7 +78,12 @@ def test_plan_covers_every_token_once(built_library, draft_fraction):
                 assert ranges[0][0] == 0 and ranges[-1][1] == int(lay.kv_lens[b])
                 for (a0, a1), (b0, b1) in zip(ranges, ranges[1:]):
                     assert a1 == b0
-    # CTA indptrs partition the item list.
+    # tcgen05 items follow the CUDA-core items, longest first (claimed in that
+    # order at run time); the claim counter starts at zero.
+    assert w[4] == info.num_items_gather and w[14] == 0
+    tc_cost = [it["tok_end"] - it["tok_begin"] for it in items[info.num_items_gather:]]
+    assert all(a >= b for a, b in zip(tc_cost, tc_cost[1:]))
+    # CTA indptrs partition the CUDA-core item list.
     g_ctas = w[2]
     g_indptr = w[w[3]: w[3] + g_ctas + 1]
     assert g_indptr[0] == 0 and np.all(np.diff(g_indptr) >= 0)
