@@ -132,6 +132,7 @@ class AspireSelectArgs(ctypes.Structure):
         ("counts_out", ctypes.c_void_p),
         ("scores_out", ctypes.c_void_p),
         ("status", ctypes.c_void_p),
+        ("scores_ws", ctypes.c_void_p),
     ]
 
 

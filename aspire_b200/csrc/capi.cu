@@ -144,7 +144,7 @@ size_t aspire_status_offset(void) { return kStatusBytes; }
 
 const char* aspire_kernel_names(void) {
   return "aspire_attn_gather_kernel\naspire_attn_tc_kernel\naspire_attn_merge_kernel\naspire_append_kv_kernel\n"
-         "aspire_select_pages_kernel\naspire_build_indices_kernel\n";
+         "aspire_select_pages_kernel\naspire_page_scores_kernel\naspire_build_indices_kernel\n";
 }
 
 int aspire_plan_host_only(const int32_t* qo_indptr, const int32_t* kv_indptr,
@@ -317,9 +317,11 @@ int aspire_append_kv(const AspireAppendArgs* a, void* stream) {
   p.num_rows = a->num_rows;
   p.num_kv_heads = a->num_kv_heads;
   p.status = a->status;
-  const int64_t warps = a->num_tokens * a->num_kv_heads;
-  const int64_t blocks = (warps * 32 + 255) / 256;
-  aspire_append_kv_kernel<<<static_cast<unsigned>(blocks), 256, 0,
+  // One CTA column per row; enough CTAs per row that each warp moves a few
+  // (token, head) pairs when the rows hold a long append (prefill chunks).
+  const int64_t pairs_per_row = (a->num_tokens * a->num_kv_heads + a->num_rows - 1) / a->num_rows;
+  const unsigned ny = static_cast<unsigned>(std::min<int64_t>(std::max<int64_t>((pairs_per_row + 31) / 32, 1), 64));
+  aspire_append_kv_kernel<<<dim3(static_cast<unsigned>(a->num_rows), ny), 256, 0,
                             static_cast<cudaStream_t>(stream)>>>(p);
   return check_cuda(cudaGetLastError(), "aspire_append_kv_kernel launch");
 }
@@ -419,7 +421,22 @@ int aspire_select_pages(const AspireSelectArgs* a, void* stream) {
   static thread_local int sel_smem_cfg = 48 * 1024;
   int rc = ensure_smem(reinterpret_cast<const void*>(&aspire_select_pages_kernel), smem, &sel_smem_cfg);
   if (rc) return rc;
-  aspire_select_pages_kernel<<<a->batch, kSelThreads, smem, static_cast<cudaStream_t>(stream)>>>(p);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (!a->scores_in) {
+    // Scoring on its own wide grid into scores_out (or the scratch), then the
+    // per-row selection reads it back.
+    float* ws = a->scores_out ? a->scores_out : a->scores_ws;
+    if (!ws)
+      return set_error(ASPIRE_ERR_INVALID, "aspire_select_pages: scores_ws is required without scores_out");
+    p.scores_out = ws;
+    const unsigned splits = static_cast<unsigned>((a->pages_per_slot + kScoreThreads - 1) / kScoreThreads);
+    aspire_page_scores_kernel<<<dim3(static_cast<unsigned>(a->batch), splits), kScoreThreads, 0, st>>>(p);
+    rc = check_cuda(cudaGetLastError(), "aspire_page_scores_kernel launch");
+    if (rc) return rc;
+    p.scores_in = ws;
+    p.scores_out = nullptr;
+  }
+  aspire_select_pages_kernel<<<a->batch, kSelThreads, smem, st>>>(p);
   return check_cuda(cudaGetLastError(), "aspire_select_pages_kernel launch");
 }
 

@@ -1,13 +1,14 @@
 // Refresh-layer page scoring + block radix top-k page re-selection.
 //
-// One CTA per request row.  Phase 1 turns the first/last logit dump of the
-// refresh layer into fp32 page scores, restating
+// Phase 1 (its own launch over rows x page splits) turns the first/last logit
+// dump of the refresh layer into fp32 page scores, restating
 // PageSelectorFirstLastAvg._select_first_last_impl
 // (aspire/backends/page_selector.py:163-181):
 //   norm  = float(half(float(logit) * sm_scale*log2e)) - lse      (NaN -> -inf)
 //   tok   = max_h exp2(norm[slot 0]) + max_h exp2(norm[slot 1])
 //   score = sum of the 16 token scores of the page + (-page * 1e-7)
-// with tokens past max_seq_len counting as zero.  Phase 2 restates
+// with tokens past max_seq_len counting as zero.  One CTA per request row
+// then runs phase 2, which restates
 // _finalize_scores (page_selector.py:79-108) and compute_valid_counts
 // (:52-62): the last L valid pages are forced to +inf, pages past num_pages
 // to -inf, and the top `valid` pages are taken with ties broken by the lower
@@ -41,6 +42,83 @@ __device__ __forceinline__ int valid_count(const SelectParams& p, int np) {
   const float prod = __fmul_rn(float(np), p.draft_percent);
   const int target = static_cast<int>(ceilf(__fdiv_rn(prod, 100.0f)));
   return min(max(target, lo), hi);
+}
+
+// Phase 1 on its own grid (rows x page splits), one page per thread: the
+// scores go to p.scores_out, which the selection launch then reads as its
+// scores_in.  exp2 is monotonic, so the max over heads is taken on the
+// normalised logits and exponentiated once per (token, slot).
+__global__ void __launch_bounds__(kScoreThreads) aspire_page_scores_kernel(SelectParams p) {
+  __shared__ float lse_s[2][kMaxSelHeads];
+  const int b = blockIdx.x;
+  const int src_row = p.row_ids ? p.row_ids[b] : b;
+  const int tid = threadIdx.x;
+  const int pps = p.pages_per_slot;
+  const int64_t max_q = p.lse_rows > 0 ? p.lse_rows - 1 : 0;
+  int64_t q_first = p.qo_indptr[src_row];
+  int64_t q_last = int64_t(p.qo_indptr[src_row + 1]) - 1;
+  q_first = q_first < 0 ? 0 : (q_first > max_q ? max_q : q_first);
+  q_last = q_last < 0 ? 0 : (q_last > max_q ? max_q : q_last);
+  for (int h = tid; h < p.num_heads; h += blockDim.x) {
+    lse_s[0][h] = p.lse[q_first * p.num_heads + h];
+    lse_s[1][h] = p.lse[q_last * p.num_heads + h];
+  }
+  __syncthreads();
+  const int pg = blockIdx.y * blockDim.x + tid;
+  if (pg >= pps) return;
+  float tok[kPageSize];
+#pragma unroll
+  for (int i = 0; i < kPageSize; ++i) tok[i] = 0.f;
+  const int64_t t0 = int64_t(pg) * kPageSize;
+  if (t0 < p.max_seq_len) {
+    float mx[2][kPageSize];
+#pragma unroll
+    for (int s = 0; s < 2; ++s)
+#pragma unroll
+      for (int i = 0; i < kPageSize; ++i) mx[s][i] = -INFINITY;
+    const bool full = t0 + kPageSize <= p.max_seq_len;
+    const __half* row = p.dump + int64_t(src_row) * p.num_heads * 2 * p.kv_stride + t0;
+    const bool vec = full && ((reinterpret_cast<uintptr_t>(row) | uintptr_t(p.kv_stride * 2)) & 15) == 0;
+    for (int h = 0; h < p.num_heads; ++h) {
+#pragma unroll
+      for (int s = 0; s < 2; ++s) {
+        const __half* src = row + (int64_t(h) * 2 + s) * p.kv_stride;
+        const float ls = lse_s[s][h];
+        __half2 vals[kPageSize / 2];
+        if (vec) {
+          *reinterpret_cast<uint4*>(vals) = __ldcs(reinterpret_cast<const uint4*>(src));
+          *reinterpret_cast<uint4*>(vals + 4) = __ldcs(reinterpret_cast<const uint4*>(src) + 1);
+        } else {
+#pragma unroll
+          for (int i = 0; i < kPageSize / 2; ++i) {
+            const __half lo = (t0 + 2 * i < p.max_seq_len) ? src[2 * i] : __float2half_rn(-INFINITY);
+            const __half hi = (t0 + 2 * i + 1 < p.max_seq_len) ? src[2 * i + 1] : __float2half_rn(-INFINITY);
+            vals[i] = __halves2half2(lo, hi);
+          }
+        }
+#pragma unroll
+        for (int i = 0; i < kPageSize / 2; ++i) {
+          // fp16 * scalar is computed in fp32 and rounded back to fp16.
+          const float2 f = __half22float2(vals[i]);
+          const float2 r = __half22float2(__floats2half2_rn(f.x * p.scale_log2, f.y * p.scale_log2));
+          float n0 = r.x - ls, n1 = r.y - ls;
+          if (isnan(n0)) n0 = -INFINITY;
+          if (isnan(n1)) n1 = -INFINITY;
+          mx[s][2 * i] = fmaxf(mx[s][2 * i], n0);
+          mx[s][2 * i + 1] = fmaxf(mx[s][2 * i + 1], n1);
+        }
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < kPageSize; ++i)
+      tok[i] = (t0 + i < p.max_seq_len) ? (exp2f(mx[0][i]) + exp2f(mx[1][i])) : 0.f;
+  }
+  // Pairwise sum of the 16 token scores.
+#pragma unroll
+  for (int w = kPageSize / 2; w >= 1; w >>= 1)
+#pragma unroll
+    for (int i = 0; i < w; ++i) tok[i] = tok[i] + tok[i + w];
+  p.scores_out[int64_t(b) * pps + pg] = tok[0] + (-(float(pg) * 1e-7f));
 }
 
 __global__ void __launch_bounds__(kSelThreads) aspire_select_pages_kernel(SelectParams p) {

@@ -117,6 +117,7 @@ class PageSelectorFirstLastAvg:
         a.table_width = int(table_width)
         a.counts_out = counts_out.data_ptr()
         a.scores_out = ptr(scores_out)
+        a.scores_ws = self._scores.data_ptr()
         a.status = ptr(status)
         stream = torch.cuda.current_stream(self.device).cuda_stream
         _capi.check(self._lib.aspire_select_pages(ctypes.byref(a), ctypes.c_void_p(stream)),

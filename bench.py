@@ -299,17 +299,9 @@ def kernel_roofline(hp: HotPath, steps: int, peak: float, peak_kind: str):
     for _ in range(3):
         hp.mixed.run(q, hp.kv, out=out)
     torch.cuda.synchronize()
-    # Back-to-back launches between two events on the launching stream, so the
-    # interval holds device time only (the host queues ahead of the GPU).
-    stream = torch.cuda.current_stream()
-    reps = max(steps, 10)
-    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    a.record(stream)
-    for _ in range(reps):
-        hp.mixed.run(q, hp.kv, out=out)
-    b.record(stream)
-    torch.cuda.synchronize()
-    ms = a.elapsed_time(b) / reps
+    # A CUDA graph of back-to-back launches timed between two events on the
+    # launching stream: device time only, under the sustained load of a step.
+    ms = graph_time(lambda: hp.mixed.run(q, hp.kv, out=out), max(steps, 30))
     bytes_ = hp.lay.algorithmic_bytes()
     achieved = bytes_ / (ms * 1e-3) / 1e9
     traffic = None
@@ -325,20 +317,37 @@ def kernel_roofline(hp: HotPath, steps: int, peak: float, peak_kind: str):
             "algorithmic_bytes_per_launch": int(bytes_)}
 
 
-def breakdown(hp: HotPath, reps: int = 5) -> dict:
-    """Average device time of each call of the step, timed alone (CUDA events)."""
+def graph_time(fn, reps: int) -> float:
+    """Device milliseconds per call of `fn`, from one replay of a CUDA graph that
+    holds `reps` back-to-back calls (no host time in the interval)."""
+    fn()
+    torch.cuda.synchronize()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        fn()
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for _ in range(reps):
+            fn()
+    g.replay()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    g.replay()
+    b.record()
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / reps
+    del g
+    return ms
+
+
+def breakdown(hp: HotPath) -> dict:
+    """Device time of each call of the step: a CUDA graph of back-to-back calls
+    of one kind, sized to run for tens of milliseconds like the step itself."""
     L = CFG["n_layer"]
-    calls = {
-        "page_list": hp.build_indices,
-        "append": lambda: hp.append_kv(hp.k_new[0], hp.v_new[0], hp.qo_indptr, hp.kv, hp.mixed_indices,
-                                       hp.mixed_indptr, hp.mixed_last, 16),
-        "mixed_attention": lambda: hp.mixed.run(hp.q[0], hp.kv, out=hp.out[0]),
-        "refresh_attention": lambda: hp.refresh.run(hp.q[L - 2], hp.kv, hp.dump, hp.lay.num_qo_heads, hp.kv_stride,
-                                                    out=hp.out[L - 2], lse=hp.lse),
-        "refresh_nodump": lambda: hp.refresh_nodump.run(hp.q[L - 2], hp.kv, out=hp.out[L - 2], lse=hp.lse),
-        "select_pages": lambda: hp.selector.select_into(hp.draft_table, hp.draft_counts, hp.dump, hp.lse,
-                                                        hp.num_pages, hp.block_table, hp.qo_indptr),
-    }
     if not hasattr(hp, "refresh_nodump"):
         from aspire_b200.attention import HolisticAttentionWrapper
         full = hp.full
@@ -346,17 +355,20 @@ def breakdown(hp: HotPath, reps: int = 5) -> dict:
         t = lambda a: torch.from_numpy(np.ascontiguousarray(a, dtype=np.int32))  # noqa: E731
         hp.refresh_nodump.plan_host(t(full.qo_indptr), t(full.kv_indptr), t(full.kv_lens), hp.full_indices,
                                     full.num_qo_heads, full.num_kv_heads, 128, 16, causal=True)
+    calls = {
+        "page_list": (hp.build_indices, 200),
+        "append": (lambda: hp.append_kv(hp.k_new[0], hp.v_new[0], hp.qo_indptr, hp.kv, hp.mixed_indices,
+                                        hp.mixed_indptr, hp.mixed_last, 16), 200),
+        "mixed_attention": (lambda: hp.mixed.run(hp.q[0], hp.kv, out=hp.out[0]), 30),
+        "refresh_attention": (lambda: hp.refresh.run(hp.q[L - 2], hp.kv, hp.dump, hp.lay.num_qo_heads,
+                                                     hp.kv_stride, out=hp.out[L - 2], lse=hp.lse), 15),
+        "refresh_nodump": (lambda: hp.refresh_nodump.run(hp.q[L - 2], hp.kv, out=hp.out[L - 2], lse=hp.lse), 15),
+        "select_pages": (lambda: hp.selector.select_into(hp.draft_table, hp.draft_counts, hp.dump, hp.lse,
+                                                         hp.num_pages, hp.block_table, hp.qo_indptr), 100),
+    }
     res = {}
-    for name, fn in calls.items():
-        fn()
-        torch.cuda.synchronize()
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record()
-        for _ in range(reps):
-            fn()
-        b.record()
-        torch.cuda.synchronize()
-        res[name + "_ms"] = round(a.elapsed_time(b) / reps, 4)
+    for name, (fn, reps) in calls.items():
+        res[name + "_ms"] = round(graph_time(fn, reps), 4)
     return res
 
 

@@ -251,6 +251,9 @@ typedef struct AspireSelectArgs {
   int32_t* counts_out;      /* int32 [batch] valid counts                          */
   float* scores_out;        /* optional fp32 [batch, pages_per_slot] final scores  */
   uint32_t* status;         /* optional device status word                         */
+  float* scores_ws;         /* fp32 [batch, pages_per_slot] scratch for the page
+                               scores; required when scores_in and scores_out are
+                               both NULL                                           */
 } AspireSelectArgs;
 
 /*
