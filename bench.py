@@ -304,11 +304,14 @@ def kernel_roofline(hp: HotPath, steps: int, peak: float, peak_kind: str):
     ms = graph_time(lambda: hp.mixed.run(q, hp.kv, out=out), max(steps, 30))
     bytes_ = hp.lay.algorithmic_bytes()
     achieved = bytes_ / (ms * 1e-3) / 1e9
+    # DRAM bytes (read + write) per algorithmic byte of the mixed layer-call,
+    # from the ncu capture summarised under profiles/, scaled to this launch.
     traffic = None
     tp = ROOT / "profiles" / "traffic.json"
     if tp.exists():
         try:
-            traffic = json.loads(tp.read_text()).get("mixed_attention_bytes_per_launch")
+            ratio = json.loads(tp.read_text()).get("dram_bytes_over_algorithmic")
+            traffic = int(round(ratio * bytes_)) if ratio else None
         except Exception:
             traffic = None
     return {"kernel": "mixed attention layer-call (aspire_attn_tc_kernel + aspire_attn_merge_kernel)",
