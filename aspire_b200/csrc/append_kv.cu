@@ -19,6 +19,7 @@ namespace aspire {
 // in its 8 warps, so the row's offsets and lengths are read once and nothing
 // searches for a token's row (the reference's helper grids over rows too).
 __global__ void __launch_bounds__(256) aspire_append_kv_kernel(AppendParams p) {
+  pdl_begin();
   const int b = blockIdx.x;
   const int32_t start = p.append_indptr[b], end = p.append_indptr[b + 1];
   const int32_t page_begin = p.page_indptr[b];

@@ -58,6 +58,7 @@ __device__ __forceinline__ void cp_async_wait() {
 }  // namespace
 
 __global__ void __launch_bounds__(kThreads, kGatherCtasPerSm) aspire_attn_gather_kernel(AttnParams p) {
+  pdl_begin();
   extern __shared__ __align__(128) unsigned char smem_raw[];
   GatherSmem& sm = *reinterpret_cast<GatherSmem*>(smem_raw);
   const int32_t* plan = p.plan;

@@ -17,6 +17,7 @@
 namespace aspire {
 
 __global__ void __launch_bounds__(kMergeThreads) aspire_attn_merge_kernel(AttnParams p) {
+  pdl_begin();
   const int32_t* plan = p.plan;
   if (plan[kHdrMagic] != kPlanMagic) return;
   // The tcgen05 kernel of this call has finished: rearm its item counter for

@@ -782,6 +782,7 @@ __device__ void run_consumer(const AttnParams& p, TcShared& sm, bool causal, int
 __global__ void __launch_bounds__(kTcThreads, 1)
     aspire_attn_tc_kernel(AttnParams p, const __grid_constant__ CUtensorMap tmap,
                           const __grid_constant__ CUtensorMap qmap) {
+  pdl_begin();
   extern __shared__ __align__(1024) uint8_t tc_smem_raw[];
   const uint32_t raw = ptx::smem_addr(tc_smem_raw);
   TcShared& sm = *reinterpret_cast<TcShared*>(tc_smem_raw + ((1024 - (raw & 1023)) & 1023));

@@ -6,6 +6,7 @@
 #include <algorithm>
 #include <cstring>
 #include <string>
+#include <utility>
 
 #include <cudaTypedefs.h>
 
@@ -29,6 +30,26 @@ int check_cuda(int st, const char* what) {
   if (st == cudaSuccess) return ASPIRE_OK;
   return set_error(ASPIRE_ERR_CUDA, std::string(what) + ": " +
                                         cudaGetErrorString(static_cast<cudaError_t>(st)));
+}
+
+// Launches `kernel` with a programmatic dependency on the preceding work in
+// the stream (every kernel begins with griddepcontrol.launch_dependents +
+// wait, so it is scheduled early but reads nothing before its predecessor
+// has finished).
+template <typename... KArgs, typename... Args>
+int launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream, const char* what,
+           Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return check_cuda(cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...), what);
 }
 
 int plan_impl(const int32_t* qo_indptr, const int32_t* kv_indptr, const int32_t* kv_len,
@@ -258,8 +279,8 @@ int aspire_mixed_attention(const AspireAttnArgs* a, const AspirePlanInfo* plan, 
     rc = ensure_smem(reinterpret_cast<const void*>(&aspire_attn_gather_kernel), smem,
                      &gather_smem_cfg);
     if (rc) return rc;
-    aspire_attn_gather_kernel<<<plan->num_ctas * kGatherCtasPerSm, 128, smem, st>>>(p);
-    rc = check_cuda(cudaGetLastError(), "aspire_attn_gather_kernel launch");
+    rc = launch(aspire_attn_gather_kernel, dim3(plan->num_ctas * kGatherCtasPerSm), dim3(128), smem, st,
+                "aspire_attn_gather_kernel launch", p);
     if (rc) return rc;
   }
   if (run_tc) {
@@ -276,13 +297,13 @@ int aspire_mixed_attention(const AspireAttnArgs* a, const AspirePlanInfo* plan, 
     rc = encode_q_tensor_map(&qmap, a->q, a->q_rows, a->num_qo_heads, a->q_stride_n, a->q_stride_h, group,
                              p.q_box_tokens);
     if (rc) return rc;
-    aspire_attn_tc_kernel<<<plan->num_ctas * kTcCtasPerSm, tc_threads(), smem, st>>>(p, tmap, qmap);
-    rc = check_cuda(cudaGetLastError(), "aspire_attn_tc_kernel launch");
+    rc = launch(aspire_attn_tc_kernel, dim3(plan->num_ctas * kTcCtasPerSm), dim3(tc_threads()), smem, st,
+                "aspire_attn_tc_kernel launch", p, tmap, qmap);
     if (rc) return rc;
   }
   // Split-KV merge (exits at once when the current plan split nothing).
-  aspire_attn_merge_kernel<<<plan->num_ctas * kMergeCtasPerSm, kMergeThreads, 0, st>>>(p);
-  return check_cuda(cudaGetLastError(), "aspire_attn_merge_kernel launch");
+  return launch(aspire_attn_merge_kernel, dim3(plan->num_ctas * kMergeCtasPerSm), dim3(kMergeThreads), 0, st,
+                "aspire_attn_merge_kernel launch", p);
 }
 
 int aspire_append_kv(const AspireAppendArgs* a, void* stream) {
@@ -321,9 +342,8 @@ int aspire_append_kv(const AspireAppendArgs* a, void* stream) {
   // (token, head) pairs when the rows hold a long append (prefill chunks).
   const int64_t pairs_per_row = (a->num_tokens * a->num_kv_heads + a->num_rows - 1) / a->num_rows;
   const unsigned ny = static_cast<unsigned>(std::min<int64_t>(std::max<int64_t>((pairs_per_row + 31) / 32, 1), 64));
-  aspire_append_kv_kernel<<<dim3(static_cast<unsigned>(a->num_rows), ny), 256, 0,
-                            static_cast<cudaStream_t>(stream)>>>(p);
-  return check_cuda(cudaGetLastError(), "aspire_append_kv_kernel launch");
+  return launch(aspire_append_kv_kernel, dim3(static_cast<unsigned>(a->num_rows), ny), dim3(256), 0,
+                static_cast<cudaStream_t>(stream), "aspire_append_kv_kernel launch", p);
 }
 
 int aspire_build_unified_indices(const AspireIndicesArgs* a, void* stream) {
@@ -354,8 +374,8 @@ int aspire_build_unified_indices(const AspireIndicesArgs* a, void* stream) {
   p.indices_out = a->indices_out;
   p.indptr_out = a->indptr_out;
   p.status = a->status;
-  aspire_build_indices_kernel<<<a->batch, kIndicesThreads, 0, static_cast<cudaStream_t>(stream)>>>(p);
-  return check_cuda(cudaGetLastError(), "aspire_build_indices_kernel launch");
+  return launch(aspire_build_indices_kernel, dim3(a->batch), dim3(kIndicesThreads), 0,
+                static_cast<cudaStream_t>(stream), "aspire_build_indices_kernel launch", p);
 }
 
 int aspire_select_pages(const AspireSelectArgs* a, void* stream) {
@@ -430,14 +450,14 @@ int aspire_select_pages(const AspireSelectArgs* a, void* stream) {
       return set_error(ASPIRE_ERR_INVALID, "aspire_select_pages: scores_ws is required without scores_out");
     p.scores_out = ws;
     const unsigned splits = static_cast<unsigned>((a->pages_per_slot + kScoreThreads - 1) / kScoreThreads);
-    aspire_page_scores_kernel<<<dim3(static_cast<unsigned>(a->batch), splits), kScoreThreads, 0, st>>>(p);
-    rc = check_cuda(cudaGetLastError(), "aspire_page_scores_kernel launch");
+    rc = launch(aspire_page_scores_kernel, dim3(static_cast<unsigned>(a->batch), splits), dim3(kScoreThreads), 0, st,
+                "aspire_page_scores_kernel launch", p);
     if (rc) return rc;
     p.scores_in = ws;
     p.scores_out = nullptr;
   }
-  aspire_select_pages_kernel<<<a->batch, kSelThreads, smem, st>>>(p);
-  return check_cuda(cudaGetLastError(), "aspire_select_pages_kernel launch");
+  return launch(aspire_select_pages_kernel, dim3(a->batch), dim3(kSelThreads), smem, st,
+                "aspire_select_pages_kernel launch", p);
 }
 
 }  // extern "C"

@@ -7,6 +7,18 @@
 
 namespace aspire {
 
+// Programmatic dependent launch.  Every kernel of the library is launched
+// with a programmatic dependency on the work before it in the stream and
+// starts with both calls: the next kernel may then be scheduled while this
+// one runs (its launch latency hides under this kernel's tail), and wait
+// blocks until the preceding kernel has completed and its writes are visible.
+// Without such a dependency both are no-ops.
+__device__ __forceinline__ void pdl_begin() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
+
 struct AppendParams {
   const __nv_bfloat16* k;
   const __nv_bfloat16* v;

@@ -49,6 +49,7 @@ __device__ __forceinline__ int valid_count(const SelectParams& p, int np) {
 // scores_in.  exp2 is monotonic, so the max over heads is taken on the
 // normalised logits and exponentiated once per (token, slot).
 __global__ void __launch_bounds__(kScoreThreads) aspire_page_scores_kernel(SelectParams p) {
+  pdl_begin();
   __shared__ float lse_s[2][kMaxSelHeads];
   const int b = blockIdx.x;
   const int src_row = p.row_ids ? p.row_ids[b] : b;
@@ -122,6 +123,7 @@ __global__ void __launch_bounds__(kScoreThreads) aspire_page_scores_kernel(Selec
 }
 
 __global__ void __launch_bounds__(kSelThreads) aspire_select_pages_kernel(SelectParams p) {
+  pdl_begin();
   extern __shared__ __align__(16) unsigned char smem_raw[];
   const int pps = p.pages_per_slot;
   uint32_t* keys = reinterpret_cast<uint32_t*>(smem_raw);         // [pps]

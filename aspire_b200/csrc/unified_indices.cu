@@ -14,6 +14,7 @@
 namespace aspire {
 
 __global__ void __launch_bounds__(kIndicesThreads) aspire_build_indices_kernel(IndicesParams p) {
+  pdl_begin();
   const int b = blockIdx.x;
   const int tid = threadIdx.x;
   __shared__ int32_t partial[kIndicesThreads];
