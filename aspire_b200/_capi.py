@@ -76,6 +76,11 @@ class AspireAttnArgs(ctypes.Structure):
         ("float_ws", ctypes.c_void_p),
         ("float_ws_bytes", ctypes.c_size_t),
         ("q_rows", ctypes.c_int64),
+        ("mode_flags", ctypes.c_void_p),
+        ("draft_table", ctypes.c_void_p),
+        ("draft_stride", ctypes.c_int64),
+        ("block_table", ctypes.c_void_p),
+        ("block_table_stride", ctypes.c_int64),
     ]
 
 
@@ -99,6 +104,11 @@ class AspireAppendArgs(ctypes.Structure):
         ("head_dim", ctypes.c_int32),
         ("page_size", ctypes.c_int32),
         ("status", ctypes.c_void_p),
+        ("mode_flags", ctypes.c_void_p),
+        ("draft_table", ctypes.c_void_p),
+        ("draft_stride", ctypes.c_int64),
+        ("block_table", ctypes.c_void_p),
+        ("block_table_stride", ctypes.c_int64),
     ]
 
 

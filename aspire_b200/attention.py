@@ -131,6 +131,7 @@ class HolisticAttentionWrapper:
 
         self._plan_info: Optional[_capi.AspirePlanInfo] = None
         self._kv_indices: Optional[torch.Tensor] = None
+        self._page_tables: Optional[Tuple[torch.Tensor, torch.Tensor, torch.Tensor]] = None
         self._page_size = 0
         self._sm_scale: Optional[float] = None
         self._causal = False
@@ -139,12 +140,35 @@ class HolisticAttentionWrapper:
         self._id = id(self)
         _WRAPPER_REGISTRY[self._id] = self
 
+    # ------------------------------------------------------------ page tables
+    def set_page_tables(self, mode_flags: Optional[torch.Tensor], draft_table: Optional[torch.Tensor] = None,
+                        block_table: Optional[torch.Tensor] = None) -> None:
+        """Lets run() read each row's pages straight from the engine's tables
+        instead of a flat page list: row b's logical page p is
+        ``draft_table[b, p]`` when ``mode_flags[b] == 0`` (draft row) and
+        ``block_table[b, p]`` otherwise.  This absorbs ``build_unified_indices``
+        (aspire/models/sparse_draft_runner.py:126-153) into the attention; a
+        plan's ``paged_kv_indices`` may then be None.  The tensors must stay
+        allocated (CUDA graphs capture their addresses).  ``None`` turns the
+        tables off."""
+        if mode_flags is None:
+            self._page_tables = None
+            return
+        for name, t in (("mode_flags", mode_flags), ("draft_table", draft_table), ("block_table", block_table)):
+            if t is None or t.dtype != torch.int32 or t.device.type != "cuda":
+                raise ValueError(f"{name} must be an int32 CUDA tensor")
+        if draft_table.dim() != 2 or block_table.dim() != 2 or draft_table.stride(1) != 1 or block_table.stride(1) != 1:
+            raise ValueError("draft_table / block_table must be 2-D with contiguous rows")
+        if not mode_flags.is_contiguous():
+            raise ValueError("mode_flags must be contiguous")
+        self._page_tables = (mode_flags, draft_table, block_table)
+
     # ------------------------------------------------------------------ plan
     def plan(
         self,
         qo_indptr: torch.Tensor,
         paged_kv_indptr: torch.Tensor,
-        paged_kv_indices: torch.Tensor,
+        paged_kv_indices: Optional[torch.Tensor],
         paged_kv_last_page_len: torch.Tensor,
         num_qo_heads: int,
         num_kv_heads: int,
@@ -174,7 +198,7 @@ class HolisticAttentionWrapper:
         qo_indptr_host: torch.Tensor,
         kv_indptr_host: torch.Tensor,
         kv_len_host: torch.Tensor,
-        paged_kv_indices: torch.Tensor,
+        paged_kv_indices: Optional[torch.Tensor],
         num_qo_heads: int,
         num_kv_heads: int,
         head_dim_qk: int,
@@ -186,6 +210,8 @@ class HolisticAttentionWrapper:
         """Plans from host arrays with no device readback or synchronisation."""
         if head_dim_vo is not None and head_dim_vo != head_dim_qk:
             raise ValueError("head_dim_vo must equal head_dim_qk")
+        if paged_kv_indices is None and self._page_tables is None:
+            raise ValueError("paged_kv_indices is required unless set_page_tables() was called")
         qo = _i32_host(qo_indptr_host)
         kvp = _i32_host(kv_indptr_host)
         kvl = _i32_host(kv_len_host)
@@ -288,7 +314,18 @@ class HolisticAttentionWrapper:
         a.q_rows = q.shape[0]
         a.kv_cache = kv.data_ptr()
         a.num_pages_total = kv.shape[0]
-        a.kv_indices = self._kv_indices.data_ptr()
+        if self._kv_indices is not None and self._page_tables is None:
+            a.kv_indices = self._kv_indices.data_ptr()
+        else:
+            if self._page_tables is None:
+                raise RuntimeError("no page list: plan with paged_kv_indices or call set_page_tables()")
+            mode_flags, draft_table, block_table = self._page_tables
+            a.kv_indices = None
+            a.mode_flags = mode_flags.data_ptr()
+            a.draft_table = draft_table.data_ptr()
+            a.draft_stride = draft_table.stride(0)
+            a.block_table = block_table.data_ptr()
+            a.block_table_stride = block_table.stride(0)
         a.out = out.data_ptr()
         a.o_stride_n = out.stride(0)
         a.o_stride_h = out.stride(1)

@@ -41,7 +41,8 @@ __global__ void __launch_bounds__(256) aspire_append_kv_kernel(AppendParams p) {
     if (t >= p.num_tokens) break;
     const int64_t pos = int64_t(i) + seq_len - n;  // = t + seq_len - append_indptr[b + 1]
     if (pos < 0 || pos >= seq_len) continue;
-    const int32_t page = p.page_indices[page_begin + pos / kPageSize];
+    const int32_t page = row_page(p.page_indices, page_begin, p.mode_flags, p.draft_table, p.draft_stride,
+                                  p.block_table, p.block_table_stride, b, pos / kPageSize);
     if (page < 0 || int64_t(page) >= p.num_pages_total) {
       if (lane == 0 && p.status) atomicOr(p.status, ASPIRE_STATUS_BAD_PAGE);
       continue;

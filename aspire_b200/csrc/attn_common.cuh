@@ -11,7 +11,12 @@ struct AttnParams {
   int64_t q_stride_n, q_stride_h;
   const __nv_bfloat16* kv;
   int64_t num_pages_total;
-  const int32_t* kv_indices;
+  const int32_t* kv_indices;  // flat page list, or NULL for the page tables below
+  const int32_t* mode_flags;  // page tables: draft rows (mode 0) read draft_table,
+  const int32_t* draft_table; // the others block_table
+  int64_t draft_stride;
+  const int32_t* block_table;
+  int64_t block_table_stride;
   __nv_bfloat16* out;
   int64_t o_stride_n, o_stride_h;
   float* lse;                // optional
@@ -24,6 +29,17 @@ struct AttnParams {
   uint32_t* status;          // int workspace (first word)
   float* partial_o;          // float workspace
 };
+
+// Page id of logical page lp of a row: from the flat page list at the row's
+// base, or from the row's draft / block table by its mode flag.
+__device__ __forceinline__ int32_t row_page(const int32_t* kv_indices, int64_t page_base, const int32_t* mode_flags,
+                                            const int32_t* draft_table, int64_t draft_stride,
+                                            const int32_t* block_table, int64_t block_table_stride, int row,
+                                            int64_t lp) {
+  if (kv_indices) return __ldg(kv_indices + page_base + lp);
+  return __ldg(mode_flags + row) == 0 ? __ldg(draft_table + row * draft_stride + lp)
+                                      : __ldg(block_table + row * block_table_stride + lp);
+}
 
 __device__ __forceinline__ float ex2(float x) {
   float y;

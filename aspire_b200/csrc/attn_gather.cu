@@ -122,7 +122,9 @@ __global__ void __launch_bounds__(kThreads, kGatherCtasPerSm) aspire_attn_gather
 
     // Page ids are read one issue ahead so their latency is off the copy path.
     auto page_of = [&](int pi) -> int32_t {
-      return pi < npg ? __ldg(p.kv_indices + it.kv_page_base + pg0 + pi) : 0;
+      return pi < npg ? row_page(p.kv_indices, it.kv_page_base, p.mode_flags, p.draft_table, p.draft_stride,
+                                 p.block_table, p.block_table_stride, it.row, pg0 + pi)
+                      : 0;
     };
     auto issue = [&](int pi, int32_t page) {
       const int stage = pi % kStages;

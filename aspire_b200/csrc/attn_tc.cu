@@ -210,7 +210,8 @@ __device__ void run_producer(const AttnParams& p, const CUtensorMap* tmap, TcSha
     auto page_id = [&](int t) -> int32_t {
       const int lp = first_page + t * kPagesPerTile + lane;
       if (lane >= kPagesPerTile || lp >= end_page) return -1;
-      return __ldg(p.kv_indices + it.kv_page_base + lp);
+      return row_page(p.kv_indices, it.kv_page_base, p.mode_flags, p.draft_table, p.draft_stride, p.block_table,
+                      p.block_table_stride, it.row, lp);
     };
     int32_t next_id = nt > 0 ? page_id(0) : -1;
     for (int t = 0; t < nt; ++t, ++g) {

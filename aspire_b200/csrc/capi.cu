@@ -217,8 +217,10 @@ int aspire_mixed_attention(const AspireAttnArgs* a, const AspirePlanInfo* plan, 
   if (a->num_qo_heads != plan->num_qo_heads || a->num_kv_heads != plan->num_kv_heads)
     return set_error(ASPIRE_ERR_INVALID,
                      "aspire_mixed_attention: head counts differ from the plan's");
-  if (!a->q || !a->kv_cache || !a->kv_indices || !a->out || !a->int_ws)
+  if (!a->q || !a->kv_cache || !a->out || !a->int_ws)
     return set_error(ASPIRE_ERR_INVALID, "aspire_mixed_attention: null tensor pointer");
+  if (!a->kv_indices && (!a->mode_flags || !a->draft_table || !a->block_table))
+    return set_error(ASPIRE_ERR_INVALID, "aspire_mixed_attention: kv_indices or the three page tables are required");
   if ((reinterpret_cast<uintptr_t>(a->q) | reinterpret_cast<uintptr_t>(a->kv_cache)) & 15)
     return set_error(ASPIRE_ERR_INVALID, "aspire_mixed_attention: q / kv_cache not 16-byte aligned");
   if ((a->q_stride_n | a->q_stride_h) & 7)
@@ -248,6 +250,11 @@ int aspire_mixed_attention(const AspireAttnArgs* a, const AspirePlanInfo* plan, 
   p.kv = static_cast<const __nv_bfloat16*>(a->kv_cache);
   p.num_pages_total = a->num_pages_total;
   p.kv_indices = a->kv_indices;
+  p.mode_flags = a->mode_flags;
+  p.draft_table = a->draft_table;
+  p.draft_stride = a->draft_stride;
+  p.block_table = a->block_table;
+  p.block_table_stride = a->block_table_stride;
   p.out = static_cast<__nv_bfloat16*>(a->out);
   p.o_stride_n = a->o_stride_n;
   p.o_stride_h = a->o_stride_h;
@@ -312,7 +319,9 @@ int aspire_append_kv(const AspireAppendArgs* a, void* stream) {
   if (a->head_dim != kHeadDim || a->page_size != kPageSize)
     return set_error(ASPIRE_ERR_INVALID, "aspire_append_kv: head_dim must be 128 and page_size 16");
   if (a->num_tokens <= 0 || a->num_rows <= 0) return ASPIRE_OK;
-  if (!a->k || !a->v || !a->kv_cache || !a->append_indptr || !a->page_indices || !a->page_indptr ||
+  if (!a->page_indices && (!a->mode_flags || !a->draft_table || !a->block_table))
+    return set_error(ASPIRE_ERR_INVALID, "aspire_append_kv: page_indices or the three page tables are required");
+  if (!a->k || !a->v || !a->kv_cache || !a->append_indptr || !a->page_indptr ||
       !a->last_page_len)
     return set_error(ASPIRE_ERR_INVALID, "aspire_append_kv: null pointer");
   if (((a->k_stride_n | a->k_stride_h | a->v_stride_n | a->v_stride_h) & 7) ||
@@ -333,6 +342,11 @@ int aspire_append_kv(const AspireAppendArgs* a, void* stream) {
   p.kv = static_cast<__nv_bfloat16*>(a->kv_cache);
   p.num_pages_total = a->num_pages_total;
   p.page_indices = a->page_indices;
+  p.mode_flags = a->mode_flags;
+  p.draft_table = a->draft_table;
+  p.draft_stride = a->draft_stride;
+  p.block_table = a->block_table;
+  p.block_table_stride = a->block_table_stride;
   p.page_indptr = a->page_indptr;
   p.last_page_len = a->last_page_len;
   p.num_rows = a->num_rows;

@@ -27,7 +27,12 @@ struct AppendParams {
   const int32_t* append_indptr;
   __nv_bfloat16* kv;
   int64_t num_pages_total;
-  const int32_t* page_indices;
+  const int32_t* page_indices;  // flat page list, or NULL for the page tables below
+  const int32_t* mode_flags;
+  const int32_t* draft_table;
+  int64_t draft_stride;
+  const int32_t* block_table;
+  int64_t block_table_stride;
   const int32_t* page_indptr;
   const int32_t* last_page_len;
   int32_t num_rows;

@@ -27,8 +27,14 @@ def append_kv(
     kv_last_page_len: torch.Tensor,
     page_size: int,
     status: torch.Tensor | None = None,
+    page_tables: tuple[torch.Tensor, torch.Tensor, torch.Tensor] | None = None,
 ) -> None:
-    """Writes the step's new K/V rows into their pages (C ABI ``aspire_append_kv``)."""
+    """Writes the step's new K/V rows into their pages (C ABI ``aspire_append_kv``).
+
+    With ``page_tables=(mode_flags, draft_table, block_table)`` and
+    ``kv_page_indices=None``, row b's logical page p is read from
+    ``draft_table[b, p]`` (mode 0) or ``block_table[b, p]``, as the attention's
+    page-table mode does; no flat page list is needed."""
     total_tokens = k.shape[0]
     if total_tokens == 0:
         return
@@ -44,8 +50,18 @@ def append_kv(
         raise ValueError("aspire_b200 append requires a contiguous [pages, 2, page, heads, dim] cache")
     if k.dtype != torch.bfloat16 or v.dtype != torch.bfloat16 or kv_cache.dtype != torch.bfloat16:
         raise ValueError("aspire_b200 append requires bfloat16 k, v and kv_cache")
-    for name, t in (("kv_append_indptr", kv_append_indptr), ("kv_page_indices", kv_page_indices),
-                    ("kv_page_indptr", kv_page_indptr), ("kv_last_page_len", kv_last_page_len)):
+    if kv_page_indices is None and page_tables is None:
+        raise ValueError("kv_page_indices or page_tables is required")
+    checked = [("kv_append_indptr", kv_append_indptr), ("kv_page_indptr", kv_page_indptr),
+               ("kv_last_page_len", kv_last_page_len)]
+    if kv_page_indices is not None:
+        checked.append(("kv_page_indices", kv_page_indices))
+    else:
+        checked.append(("mode_flags", page_tables[0]))
+        for name, t in (("draft_table", page_tables[1]), ("block_table", page_tables[2])):
+            if t.dtype != torch.int32 or t.dim() != 2 or t.stride(1) != 1:
+                raise ValueError(f"{name} must be a 2-D int32 tensor with contiguous rows")
+    for name, t in checked:
         if t.dtype != torch.int32 or not t.is_contiguous():
             raise ValueError(f"{name} must be a contiguous int32 tensor")
     num_rows = kv_last_page_len.shape[0]
@@ -60,7 +76,15 @@ def append_kv(
     a.append_indptr = kv_append_indptr.data_ptr()
     a.kv_cache = kv_cache.data_ptr()
     a.num_pages_total = kv_cache.shape[0]
-    a.page_indices = kv_page_indices.data_ptr()
+    if kv_page_indices is not None:
+        a.page_indices = kv_page_indices.data_ptr()
+    else:
+        a.page_indices = None
+        a.mode_flags = page_tables[0].data_ptr()
+        a.draft_table = page_tables[1].data_ptr()
+        a.draft_stride = page_tables[1].stride(0)
+        a.block_table = page_tables[2].data_ptr()
+        a.block_table_stride = page_tables[2].stride(0)
     a.page_indptr = kv_page_indptr.data_ptr()
     a.last_page_len = kv_last_page_len.data_ptr()
     a.num_rows = num_rows

@@ -4,7 +4,6 @@ One step = one decode step's hot path of a Qwen3-8B-shaped model (config 3 of
 the reference's benchmark list: 36 layers, 32 q / 8 KV heads, head_dim 128,
 batch 64, 32k context, sparse budget 128 pages, refresh layer -2):
 
-  * the mixed page-list build (each row's draft table or block-table prefix);
   * 35 ordinary layers: paged KV append + mixed draft/verify attention
     (draft rows: 128 selected pages, q_len 1; verify rows: full context,
     q_len = U{2..8} + 1, causal);
@@ -156,10 +155,8 @@ def step_bytes(lay, full, n_layer: int, kv_stride: int, k: int) -> dict:
         * full.num_qo_heads * 2
     select = full.batch * full.num_qo_heads * 2 * min(kv_stride, lay.pages_per_row * 16) * 2 \
         + full.batch * lay.pages_per_row * 4 + full.batch * k * 4 + T * full.num_qo_heads * 4
-    indices = int(lay.kv_indptr[-1]) * 4 * 2 + lay.batch * 4 * 4       # page ids read + written, flags/counts
-    total = (n_layer - 1) * mixed + refresh + n_layer * append + dump_write + select + indices
-    return dict(total=total, mixed=mixed, refresh=refresh, append=append, dump_write=dump_write, select=select,
-                indices=indices)
+    total = (n_layer - 1) * mixed + refresh + n_layer * append + dump_write + select
+    return dict(total=total, mixed=mixed, refresh=refresh, append=append, dump_write=dump_write, select=select)
 
 
 class HotPath:
@@ -167,12 +164,11 @@ class HotPath:
 
     def __init__(self, device, lay, full, lpl_mixed, lpl_full):
         from aspire_b200.attention import HolisticAttentionWrapper, first_last_dump_jit_args
-        from aspire_b200.kv_ops import append_kv, build_unified_indices
+        from aspire_b200.kv_ops import append_kv
         from aspire_b200.page_selector import PageSelectorFirstLastAvg
         from aspire_b200.workloads import fill_tensors
 
         self.append_kv = append_kv
-        self.build_unified_indices = build_unified_indices
         self.device = device
         self.lay, self.full = lay, full
         n_layer = CFG["n_layer"]
@@ -188,21 +184,25 @@ class HotPath:
         self.lse = torch.empty(T, hq, device=device, dtype=torch.float32)
         i32 = lambda a: torch.from_numpy(np.ascontiguousarray(a, dtype=np.int32)).to(device)  # noqa: E731
         self.qo_indptr = i32(lay.qo_indptr)
-        self.mixed_indices, self.mixed_indptr, self.mixed_last = i32(lay.kv_indices), i32(lay.kv_indptr), i32(lpl_mixed)
-        self.full_indices, self.full_indptr, self.full_last = i32(full.kv_indices), i32(full.kv_indptr), i32(lpl_full)
+        self.mixed_indptr, self.mixed_last = i32(lay.kv_indptr), i32(lpl_mixed)
+        self.full_indptr, self.full_last = i32(full.kv_indptr), i32(lpl_full)
         self.block_table = i32(lay.block_table)
         self.num_pages = i32((lay.ctx_lens + 15) // 16)
-        # Inputs of the step's page-list build: mode flags, the draft rows' page
-        # tables and each row's page count (draft: its table, verify: its context).
+        # The engine's page tables, read directly by the kernels (page-table
+        # mode: the reference's build_unified_indices copy is absorbed): mode
+        # flags, the draft rows' page tables and the block table.  The mixed
+        # program reads draft rows from their tables; the refresh program reads
+        # every row's block-table prefix (all rows in verify mode).
         counts = np.diff(lay.kv_indptr)
         draft_tab = np.zeros((lay.batch, max(1, int(counts.max()))), np.int32)
         for b in range(lay.batch):
             if lay.modes[b] == 0:
                 draft_tab[b, :counts[b]] = lay.kv_indices[lay.kv_indptr[b]:lay.kv_indptr[b + 1]]
         self.mode_flags = i32(lay.modes)
+        self.full_modes = i32(np.ones(lay.batch, np.int32))
         self.draft_indices = i32(draft_tab)
-        self.draft_num_pages = i32(np.where(lay.modes == 0, counts, 0))
-        self.verify_num_pages = i32(np.where(lay.modes == 0, 0, counts))
+        self.mixed_tables = (self.mode_flags, self.draft_indices, self.block_table)
+        self.full_tables = (self.full_modes, self.draft_indices, self.block_table)
         self.kv_stride = lay.pages_per_row * 16
         self.dump = torch.full((lay.batch * hq * 2 * self.kv_stride,), float("-inf"), dtype=torch.float16,
                                device=device)
@@ -211,7 +211,9 @@ class HotPath:
         self.draft_counts = torch.zeros(lay.batch, dtype=torch.int32, device=device)
         ws = torch.empty(1, device=device)
         self.mixed = HolisticAttentionWrapper(ws)
+        self.mixed.set_page_tables(*self.mixed_tables)
         self.refresh = HolisticAttentionWrapper(ws, jit_args=first_last_dump_jit_args())
+        self.refresh.set_page_tables(*self.full_tables)
         self.selector = PageSelectorFirstLastAvg(
             max_batch_size=lay.batch, pages_per_slot=lay.pages_per_row, subset_cache_size=self.k_sel, L=CFG["L"],
             n_heads=hq, page_size=16, max_seq_length=self.kv_stride, device=device, bsz=lay.batch, dec_len=9,
@@ -221,27 +223,22 @@ class HotPath:
     def plan(self):
         lay, full = self.lay, self.full
         t = lambda a: torch.from_numpy(np.ascontiguousarray(a, dtype=np.int32))  # noqa: E731
-        self.mixed.plan_host(t(lay.qo_indptr), t(lay.kv_indptr), t(lay.kv_lens), self.mixed_indices,
+        self.mixed.plan_host(t(lay.qo_indptr), t(lay.kv_indptr), t(lay.kv_lens), None,
                              lay.num_qo_heads, lay.num_kv_heads, 128, 16, causal=True)
-        self.refresh.plan_host(t(full.qo_indptr), t(full.kv_indptr), t(full.kv_lens), self.full_indices,
+        self.refresh.plan_host(t(full.qo_indptr), t(full.kv_indptr), t(full.kv_lens), None,
                                full.num_qo_heads, full.num_kv_heads, 128, 16, causal=True)
-
-    def build_indices(self):
-        self.build_unified_indices(self.mode_flags, self.draft_indices, self.block_table, self.draft_num_pages,
-                                   self.verify_num_pages, self.mixed_indices, self.mixed_indptr)
 
     def step_eager(self):
         n_layer = CFG["n_layer"]
-        self.build_indices()
         for layer in range(n_layer):
             if layer == CFG["refresh_layer"]:
-                self.append_kv(self.k_new[layer], self.v_new[layer], self.qo_indptr, self.kv, self.full_indices,
-                               self.full_indptr, self.full_last, 16)
+                self.append_kv(self.k_new[layer], self.v_new[layer], self.qo_indptr, self.kv, None,
+                               self.full_indptr, self.full_last, 16, page_tables=self.full_tables)
                 self.refresh.run(self.q[layer], self.kv, self.dump, self.lay.num_qo_heads, self.kv_stride,
                                  out=self.out[layer], lse=self.lse)
             else:
-                self.append_kv(self.k_new[layer], self.v_new[layer], self.qo_indptr, self.kv, self.mixed_indices,
-                               self.mixed_indptr, self.mixed_last, 16)
+                self.append_kv(self.k_new[layer], self.v_new[layer], self.qo_indptr, self.kv, None,
+                               self.mixed_indptr, self.mixed_last, 16, page_tables=self.mixed_tables)
                 self.mixed.run(self.q[layer], self.kv, out=self.out[layer])
         self.selector.select_into(self.draft_table, self.draft_counts, self.dump, self.lse, self.num_pages,
                                   self.block_table, self.qo_indptr)
@@ -249,10 +246,6 @@ class HotPath:
     def capture(self):
         self.step_eager()
         torch.cuda.synchronize()
-        lay = self.lay
-        if not (np.array_equal(self.mixed_indices.cpu().numpy(), lay.kv_indices)
-                and np.array_equal(self.mixed_indptr.cpu().numpy(), lay.kv_indptr)):
-            raise RuntimeError("page-list build disagrees with the layout's page list")
         s = torch.cuda.Stream()
         s.wait_stream(torch.cuda.current_stream())
         with torch.cuda.stream(s):
@@ -265,13 +258,13 @@ class HotPath:
         torch.cuda.synchronize()
 
     def launches_per_step(self) -> int:
-        # page-list build; per layer: append + attention (tcgen05 kernel, plus the
-        # CUDA-core kernel unless every row routes to tcgen05, plus the split-KV
-        # merge); then the selection.
+        # Per layer: append + attention (tcgen05 kernel, plus the CUDA-core
+        # kernel unless every row routes to tcgen05, plus the split-KV merge);
+        # then the selection (page scoring + top-k).
         tc = bool(self.mixed.plan_info.tc_enabled)
         all_tc = tc and int(os.environ.get("ASPIRE_B200_TC_MIN_ROWS", "1") or "1") <= 1
         per_attn = (1 if tc else 0) + (0 if all_tc else 1) + 1
-        return 1 + CFG["n_layer"] * (1 + per_attn) + 1
+        return CFG["n_layer"] * (1 + per_attn) + 2
 
 
 def time_device(fn, steps, warmup, dist_on):
@@ -356,12 +349,12 @@ def breakdown(hp: HotPath) -> dict:
         full = hp.full
         hp.refresh_nodump = HolisticAttentionWrapper(torch.empty(1, device=hp.device))
         t = lambda a: torch.from_numpy(np.ascontiguousarray(a, dtype=np.int32))  # noqa: E731
-        hp.refresh_nodump.plan_host(t(full.qo_indptr), t(full.kv_indptr), t(full.kv_lens), hp.full_indices,
+        hp.refresh_nodump.set_page_tables(*hp.full_tables)
+        hp.refresh_nodump.plan_host(t(full.qo_indptr), t(full.kv_indptr), t(full.kv_lens), None,
                                     full.num_qo_heads, full.num_kv_heads, 128, 16, causal=True)
     calls = {
-        "page_list": (hp.build_indices, 200),
-        "append": (lambda: hp.append_kv(hp.k_new[0], hp.v_new[0], hp.qo_indptr, hp.kv, hp.mixed_indices,
-                                        hp.mixed_indptr, hp.mixed_last, 16), 200),
+        "append": (lambda: hp.append_kv(hp.k_new[0], hp.v_new[0], hp.qo_indptr, hp.kv, None,
+                                        hp.mixed_indptr, hp.mixed_last, 16, page_tables=hp.mixed_tables), 200),
         "mixed_attention": (lambda: hp.mixed.run(hp.q[0], hp.kv, out=hp.out[0]), 30),
         "refresh_attention": (lambda: hp.refresh.run(hp.q[L - 2], hp.kv, hp.dump, hp.lay.num_qo_heads,
                                                      hp.kv_stride, out=hp.out[L - 2], lse=hp.lse), 15),
@@ -536,7 +529,8 @@ def main():
             "config": {"workload": "one decode step of the attention hot path: 35 x (append + mixed draft/verify "
                                    "attention) + refresh layer (append + full attention + first/last dump) + page "
                                    "selection; Qwen3-8B heads 32/8/128, 36 layers, B=64, 32k ctx, draft fraction 0.5, "
-                                   "verify q_len U{3..9}, budget 128 pages, one resident layer cache",
+                                   "verify q_len U{3..9}, budget 128 pages, one resident layer cache; pages read "
+                                   "straight from the draft / block tables (page-list build absorbed)",
                        "batch": CFG["batch"], "ctx": CFG["ctx"], "tp": world, "heads_per_rank": [lay.num_qo_heads, lay.num_kv_heads],
                        "l2": "inputs larger than L2 (8.7 GB cache at TP1)", "bytes_per_step": sb},
             "roofline": roof, "breakdown": parts, "clocks": clocks.summary(), "e2e": e2e,

@@ -145,6 +145,18 @@ typedef struct AspireAttnArgs {
   void* float_ws;           /* device float workspace for split-KV partials       */
   size_t float_ws_bytes;
   int64_t q_rows;           /* first dimension of q (rows the kernels may read)   */
+  /* Page tables, read instead of kv_indices when kv_indices is NULL: logical
+   * page lp of request row b is draft_table[b * draft_stride + lp] when
+   * mode_flags[b] == 0 (draft row), else block_table[b * block_table_stride
+   * + lp].  This absorbs build_unified_indices (aspire/models/
+   * sparse_draft_runner.py:126-153) into the attention: the plan's kv_indptr
+   * still gives each row's page count.  No counterpart in the reference's
+   * attention interface. */
+  const int32_t* mode_flags;
+  const int32_t* draft_table;
+  int64_t draft_stride;
+  const int32_t* block_table;
+  int64_t block_table_stride;
 } AspireAttnArgs;
 
 /*
@@ -207,6 +219,13 @@ typedef struct AspireAppendArgs {
   int32_t head_dim;         /* must be 128 */
   int32_t page_size;        /* must be 16  */
   uint32_t* status;         /* optional device status word (NULL = none)         */
+  /* Page tables, read instead of page_indices when page_indices is NULL (the
+   * same rule as AspireAttnArgs). */
+  const int32_t* mode_flags;
+  const int32_t* draft_table;
+  int64_t draft_stride;
+  const int32_t* block_table;
+  int64_t block_table_stride;
 } AspireAppendArgs;
 
 /*

@@ -1,0 +1,106 @@
+"""Page-table mode: the attention and the append read each row's pages from
+the draft table / block table by mode flag (build_unified_indices absorbed,
+the reference's aspire/models/sparse_draft_runner.py:126-153).  Results must
+be bit-identical to the flat page-list mode on the same pages."""
+
+import numpy as np
+import pytest
+import torch
+
+from aspire_b200.attention import HolisticAttentionWrapper, first_last_dump_jit_args
+from aspire_b200.kv_ops import append_kv
+from aspire_b200.workloads import fill_tensors, full_context_layout, last_page_lens, make_layout
+
+pytestmark = pytest.mark.gpu
+
+
+def _tables(lay, dev, table_cols=None):
+    """Mode flags, a draft table holding each draft row's page list (padded
+    with garbage past the count) and the block table, as the engine keeps them."""
+    counts = np.diff(lay.kv_indptr)
+    cols = table_cols or int(counts.max())
+    rng = np.random.default_rng(7)
+    draft = rng.integers(0, lay.num_pages_total, size=(lay.batch, cols)).astype(np.int32)
+    for b in range(lay.batch):
+        if lay.modes[b] == 0:
+            draft[b, :counts[b]] = lay.kv_indices[lay.kv_indptr[b]:lay.kv_indptr[b + 1]]
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a, dtype=np.int32)).to(dev)  # noqa: E731
+    # The block table gets padding columns too, so its row stride differs from its width.
+    bt = np.full((lay.batch, lay.block_table.shape[1] + 5), -1, np.int32)
+    bt[:, :lay.block_table.shape[1]] = lay.block_table
+    return t(lay.modes), t(draft), t(bt)[:, :lay.block_table.shape[1]]
+
+
+def _plan(w, lay, dev, indices):
+    w.plan_host(torch.from_numpy(lay.qo_indptr), torch.from_numpy(lay.kv_indptr), torch.from_numpy(lay.kv_lens),
+                indices, lay.num_qo_heads, lay.num_kv_heads, 128, 16, causal=True)
+
+
+@pytest.mark.parametrize("hq,hkv", [(32, 8), (16, 8)])
+def test_attention_page_tables_match_flat_list(cuda_device, hq, hkv):
+    dev = cuda_device
+    lay = make_layout(batch=9, ctx=3000, num_qo_heads=hq, num_kv_heads=hkv, draft_fraction=0.5, budget_pages=40,
+                      seed=11, block_table="random")
+    q, kv = fill_tensors(lay, device=dev, seed=12)
+    flat = HolisticAttentionWrapper(torch.empty(1, device=dev))
+    _plan(flat, lay, dev, torch.from_numpy(lay.kv_indices).to(dev))
+    out_flat, lse_flat = flat.run(q, kv, return_lse=True)
+    tab = HolisticAttentionWrapper(torch.empty(1, device=dev))
+    tab.set_page_tables(*_tables(lay, dev))
+    _plan(tab, lay, dev, None)
+    out_tab, lse_tab = tab.run(q, kv, return_lse=True)
+    torch.cuda.synchronize()
+    assert torch.equal(out_flat, out_tab)
+    assert torch.equal(lse_flat, lse_tab)
+
+
+def test_refresh_dump_page_tables_match_flat_list(cuda_device):
+    dev = cuda_device
+    lay = make_layout(batch=6, ctx=2000, num_qo_heads=32, num_kv_heads=8, draft_fraction=0.5, budget_pages=24,
+                      seed=13, block_table="random")
+    full = full_context_layout(lay)
+    q, kv = fill_tensors(full, device=dev, seed=14)
+    stride = lay.pages_per_row * 16
+    outs = []
+    for use_tables in (False, True):
+        w = HolisticAttentionWrapper(torch.empty(1, device=dev), jit_args=first_last_dump_jit_args())
+        if use_tables:
+            _, draft, bt = _tables(full, dev)
+            w.set_page_tables(torch.ones(full.batch, dtype=torch.int32, device=dev), draft, bt)
+            _plan(w, full, dev, None)
+        else:
+            _plan(w, full, dev, torch.from_numpy(full.kv_indices).to(dev))
+        dump = torch.full((full.batch * 32 * 2 * stride,), float("-inf"), dtype=torch.float16, device=dev)
+        out, lse = w.run(q, kv, dump, 32, stride, return_lse=True)
+        outs.append((out, lse, dump))
+    torch.cuda.synchronize()
+    for a, b in zip(outs[0], outs[1]):
+        assert torch.equal(a, b)
+
+
+def test_append_page_tables_match_flat_list(cuda_device):
+    dev = cuda_device
+    lay = make_layout(batch=10, ctx=700, num_qo_heads=32, num_kv_heads=8, draft_fraction=0.5, budget_pages=12,
+                      seed=15, block_table="random")
+    _, kv0 = fill_tensors(lay, device=dev, seed=16)
+    T = int(lay.qo_indptr[-1])
+    g = torch.Generator(device=dev)
+    g.manual_seed(17)
+    k = torch.randn(T + 3, 8, 128, generator=g, device=dev).to(torch.bfloat16)
+    v = torch.randn(T + 3, 8, 128, generator=g, device=dev).to(torch.bfloat16)
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a, dtype=np.int32)).to(dev)  # noqa: E731
+    indptr, lpl = t(lay.kv_indptr), t(last_page_lens(lay))
+    app = t(lay.qo_indptr)
+    flat = kv0.clone()
+    append_kv(k, v, app, flat, t(lay.kv_indices), indptr, lpl, 16)
+    tab = kv0.clone()
+    append_kv(k, v, app, tab, None, indptr, lpl, 16, page_tables=_tables(lay, dev))
+    torch.cuda.synchronize()
+    assert torch.equal(flat, tab)
+    assert not torch.equal(flat, kv0)
+
+
+def test_page_tables_require_a_page_source(cuda_device):
+    w = HolisticAttentionWrapper(torch.empty(1, device=cuda_device))
+    with pytest.raises(ValueError):
+        w.plan_host(torch.tensor([0, 1]), torch.tensor([0, 1]), torch.tensor([5]), None, 32, 8, 128, 16)
