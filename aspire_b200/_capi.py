@@ -164,6 +164,50 @@ class AspireIndicesArgs(ctypes.Structure):
     ]
 
 
+class AspirePrologueArgs(ctypes.Structure):
+    _fields_ = [
+        ("q", ctypes.c_void_p),
+        ("q_stride_n", ctypes.c_int64),
+        ("q_stride_h", ctypes.c_int64),
+        ("k", ctypes.c_void_p),
+        ("k_stride_n", ctypes.c_int64),
+        ("k_stride_h", ctypes.c_int64),
+        ("v", ctypes.c_void_p),
+        ("v_stride_n", ctypes.c_int64),
+        ("v_stride_h", ctypes.c_int64),
+        ("q_out", ctypes.c_void_p),
+        ("qo_stride_n", ctypes.c_int64),
+        ("qo_stride_h", ctypes.c_int64),
+        ("num_tokens", ctypes.c_int64),
+        ("num_qo_heads", ctypes.c_int32),
+        ("num_kv_heads", ctypes.c_int32),
+        ("head_dim", ctypes.c_int32),
+        ("q_norm_weight", ctypes.c_void_p),
+        ("k_norm_weight", ctypes.c_void_p),
+        ("norm_eps", ctypes.c_float),
+        ("rope_offsets", ctypes.c_void_p),
+        ("rope_theta", ctypes.c_float),
+        ("rope_scale", ctypes.c_float),
+        ("low_freq_factor", ctypes.c_float),
+        ("high_freq_factor", ctypes.c_float),
+        ("old_context_len", ctypes.c_float),
+        ("append_indptr", ctypes.c_void_p),
+        ("num_rows", ctypes.c_int32),
+        ("kv_cache", ctypes.c_void_p),
+        ("num_pages_total", ctypes.c_int64),
+        ("page_size", ctypes.c_int32),
+        ("page_indices", ctypes.c_void_p),
+        ("page_indptr", ctypes.c_void_p),
+        ("last_page_len", ctypes.c_void_p),
+        ("mode_flags", ctypes.c_void_p),
+        ("draft_table", ctypes.c_void_p),
+        ("draft_stride", ctypes.c_int64),
+        ("block_table", ctypes.c_void_p),
+        ("block_table_stride", ctypes.c_int64),
+        ("status", ctypes.c_void_p),
+    ]
+
+
 # Exported symbols and their signatures (must match include/aspire_b200.h).
 _SIGNATURES = {
     "aspire_plan": (
@@ -190,6 +234,7 @@ _SIGNATURES = {
     "aspire_append_kv": (ctypes.c_int, [ctypes.POINTER(AspireAppendArgs), ctypes.c_void_p]),
     "aspire_select_pages": (ctypes.c_int, [ctypes.POINTER(AspireSelectArgs), ctypes.c_void_p]),
     "aspire_build_unified_indices": (ctypes.c_int, [ctypes.POINTER(AspireIndicesArgs), ctypes.c_void_p]),
+    "aspire_qkv_prologue": (ctypes.c_int, [ctypes.POINTER(AspirePrologueArgs), ctypes.c_void_p]),
     "aspire_last_error": (ctypes.c_char_p, []),
     "aspire_abi_version": (ctypes.c_int, []),
     "aspire_status_offset": (ctypes.c_size_t, []),

@@ -28,6 +28,7 @@ SOURCES = [
     "append_kv.cu",
     "select_pages.cu",
     "unified_indices.cu",
+    "qkv_prologue.cu",
     "noalloc.cu",
 ]
 

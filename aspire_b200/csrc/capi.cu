@@ -165,7 +165,7 @@ size_t aspire_status_offset(void) { return kStatusBytes; }
 
 const char* aspire_kernel_names(void) {
   return "aspire_attn_gather_kernel\naspire_attn_tc_kernel\naspire_attn_merge_kernel\naspire_append_kv_kernel\n"
-         "aspire_select_pages_kernel\naspire_page_scores_kernel\naspire_build_indices_kernel\n";
+         "aspire_select_pages_kernel\naspire_page_scores_kernel\naspire_build_indices_kernel\naspire_qkv_prologue_kernel\n";
 }
 
 int aspire_plan_host_only(const int32_t* qo_indptr, const int32_t* kv_indptr,
@@ -358,6 +358,84 @@ int aspire_append_kv(const AspireAppendArgs* a, void* stream) {
   const unsigned ny = static_cast<unsigned>(std::min<int64_t>(std::max<int64_t>((pairs_per_row + 31) / 32, 1), 64));
   return launch(aspire_append_kv_kernel, dim3(static_cast<unsigned>(a->num_rows), ny), dim3(256), 0,
                 static_cast<cudaStream_t>(stream), "aspire_append_kv_kernel launch", p);
+}
+
+int aspire_qkv_prologue(const AspirePrologueArgs* a, void* stream) {
+  clear_error();
+  if (!a) return set_error(ASPIRE_ERR_INVALID, "aspire_qkv_prologue: null argument");
+  if (a->head_dim != kHeadDim || a->page_size != kPageSize)
+    return set_error(ASPIRE_ERR_INVALID, "aspire_qkv_prologue: head_dim must be 128 and page_size 16");
+  if (a->num_tokens <= 0 || a->num_rows < 0) return ASPIRE_OK;
+  if (!a->q || !a->k || !a->v || !a->q_out || !a->kv_cache || !a->append_indptr || !a->page_indptr ||
+      !a->last_page_len || (a->num_rows > 0 && !a->rope_offsets))
+    return set_error(ASPIRE_ERR_INVALID, "aspire_qkv_prologue: null pointer");
+  if (!a->page_indices && (!a->mode_flags || !a->draft_table || !a->block_table))
+    return set_error(ASPIRE_ERR_INVALID, "aspire_qkv_prologue: page_indices or the three page tables are required");
+  if ((a->q_norm_weight == nullptr) != (a->k_norm_weight == nullptr))
+    return set_error(ASPIRE_ERR_INVALID, "aspire_qkv_prologue: give both norm weights or neither");
+  if (a->num_qo_heads <= 0 || a->num_kv_heads <= 0)
+    return set_error(ASPIRE_ERR_INVALID, "aspire_qkv_prologue: bad head counts");
+  if (!(a->rope_theta > 0.f) || !(a->rope_scale > 0.f))
+    return set_error(ASPIRE_ERR_INVALID, "aspire_qkv_prologue: rope_theta and rope_scale must be > 0");
+  const uintptr_t ptrs = reinterpret_cast<uintptr_t>(a->q) | reinterpret_cast<uintptr_t>(a->k) |
+                         reinterpret_cast<uintptr_t>(a->v) | reinterpret_cast<uintptr_t>(a->q_out) |
+                         reinterpret_cast<uintptr_t>(a->kv_cache);
+  const int64_t strides = a->q_stride_n | a->q_stride_h | a->k_stride_n | a->k_stride_h | a->v_stride_n |
+                          a->v_stride_h | a->qo_stride_n | a->qo_stride_h;
+  if ((ptrs & 15) || (strides & 7))
+    return set_error(ASPIRE_ERR_INVALID,
+                     "aspire_qkv_prologue: tensors must be 16-byte aligned with strides in multiples of 8");
+  PrologueParams p;
+  AppendParams& ap = p.ap;
+  ap.k = static_cast<const __nv_bfloat16*>(a->k);
+  ap.v = static_cast<const __nv_bfloat16*>(a->v);
+  ap.k_stride_n = a->k_stride_n;
+  ap.k_stride_h = a->k_stride_h;
+  ap.v_stride_n = a->v_stride_n;
+  ap.v_stride_h = a->v_stride_h;
+  ap.num_tokens = a->num_tokens;
+  ap.append_indptr = a->append_indptr;
+  ap.kv = static_cast<__nv_bfloat16*>(a->kv_cache);
+  ap.num_pages_total = a->num_pages_total;
+  ap.page_indices = a->page_indices;
+  ap.mode_flags = a->mode_flags;
+  ap.draft_table = a->draft_table;
+  ap.draft_stride = a->draft_stride;
+  ap.block_table = a->block_table;
+  ap.block_table_stride = a->block_table_stride;
+  ap.page_indptr = a->page_indptr;
+  ap.last_page_len = a->last_page_len;
+  ap.num_rows = a->num_rows;
+  ap.num_kv_heads = a->num_kv_heads;
+  ap.status = a->status;
+  p.q = static_cast<const __nv_bfloat16*>(a->q);
+  p.q_stride_n = a->q_stride_n;
+  p.q_stride_h = a->q_stride_h;
+  p.q_out = static_cast<__nv_bfloat16*>(a->q_out);
+  p.qo_stride_n = a->qo_stride_n;
+  p.qo_stride_h = a->qo_stride_h;
+  p.q_norm_w = static_cast<const __nv_bfloat16*>(a->q_norm_weight);
+  p.k_norm_w = static_cast<const __nv_bfloat16*>(a->k_norm_weight);
+  p.eps = a->norm_eps;
+  p.rope_offsets = a->rope_offsets;
+  // The constants FlashInfer derives on the host: reciprocals in fp32, the
+  // Llama-3.1 smoothing line from double-precision pi.
+  p.rcp_theta = 1.0f / a->rope_theta;
+  p.rcp_scale = 1.0f / a->rope_scale;
+  p.smooth_a = 0.f;
+  p.smooth_b = 0.f;
+  if (a->low_freq_factor > 0.f && a->high_freq_factor > a->low_freq_factor) {
+    const double pi = 3.14159265358979323846;
+    p.smooth_a = static_cast<float>(a->old_context_len /
+                                    (2 * pi * a->high_freq_factor - 2 * pi * a->low_freq_factor));
+    p.smooth_b = -1.0f / (a->high_freq_factor / a->low_freq_factor - 1.0f);
+  }
+  p.num_qo_heads = a->num_qo_heads;
+  const int64_t units_per_row = (a->num_tokens * (a->num_qo_heads + 2 * a->num_kv_heads) + a->num_rows) /
+                                std::max<int64_t>(a->num_rows, 1);
+  const unsigned ny = static_cast<unsigned>(std::min<int64_t>(std::max<int64_t>((units_per_row + 31) / 32, 1), 64));
+  return launch(aspire_qkv_prologue_kernel, dim3(static_cast<unsigned>(a->num_rows + 1), ny), dim3(256), 0,
+                static_cast<cudaStream_t>(stream), "aspire_qkv_prologue_kernel launch", p);
 }
 
 int aspire_build_unified_indices(const AspireIndicesArgs* a, void* stream) {

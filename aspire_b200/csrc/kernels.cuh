@@ -40,6 +40,21 @@ struct AppendParams {
   uint32_t* status;
 };
 
+struct PrologueParams {
+  AppendParams ap;              // k (before norm / rotation), v, rows, pages, cache
+  const __nv_bfloat16* q;
+  int64_t q_stride_n, q_stride_h;
+  __nv_bfloat16* q_out;         // may alias q
+  int64_t qo_stride_n, qo_stride_h;
+  const __nv_bfloat16* q_norm_w;  // [128] bf16; NULL (with k_norm_w) = no norm / permutation
+  const __nv_bfloat16* k_norm_w;
+  float eps;
+  const int32_t* rope_offsets;  // position of each row's first new token
+  float rcp_theta, rcp_scale, smooth_a, smooth_b;
+  int32_t num_qo_heads;
+};
+__global__ void aspire_qkv_prologue_kernel(PrologueParams p);
+
 struct SelectParams {
   const __half* dump;
   int64_t kv_stride, max_seq_len;

@@ -159,3 +159,88 @@ def build_unified_indices(mode_flags: torch.Tensor, draft_indices: torch.Tensor,
     stream = torch.cuda.current_stream(mode_flags.device).cuda_stream
     rc = _capi.load_library().aspire_build_unified_indices(ctypes.byref(a), ctypes.c_void_p(stream))
     _capi.check(rc, "aspire_build_unified_indices")
+
+
+def qkv_prologue(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, kv_append_indptr: torch.Tensor,
+                 rope_offsets: torch.Tensor, kv_cache: torch.Tensor, kv_page_indices: torch.Tensor | None,
+                 kv_page_indptr: torch.Tensor, kv_last_page_len: torch.Tensor, page_size: int = 16, *,
+                 q_norm_weight: torch.Tensor | None = None, k_norm_weight: torch.Tensor | None = None,
+                 norm_eps: float = 1e-6, rope_theta: float = 1e4, rope_scale: float = 1.0,
+                 llama31: tuple[float, float, float] | None = None, q_out: torch.Tensor | None = None,
+                 page_tables: tuple[torch.Tensor, torch.Tensor, torch.Tensor] | None = None,
+                 status: torch.Tensor | None = None) -> torch.Tensor:
+    """One launch for a layer's attention prologue (C ABI ``aspire_qkv_prologue``):
+    ``q_norm`` / ``k_norm`` with the HF-to-interleaved permutation
+    (aspire/models/sparse_draft_transformer.py:150-158) when the norm weights
+    are given, the interleaved RoPE of ``mylib::rope`` (FlashInfer
+    ``apply_rope_inplace`` or, with ``llama31=(low_freq_factor,
+    high_freq_factor, old_context_len)``, ``apply_llama31_rope_inplace``;
+    aspire/models/mixed_transformer.py:159-197) at positions
+    ``rope_offsets[b] + (t - kv_append_indptr[b])``, and the paged append of
+    the rotated k and of v (``mylib::update_kv_padded``).  Returns the rotated
+    q (``q_out``, which may be ``q`` itself for the reference's in-place form)."""
+    total = q.shape[0]
+    if q_out is None:
+        q_out = torch.empty_like(q)
+    if total == 0:
+        return q_out
+    for name, t in (("q", q), ("k", k), ("v", v), ("q_out", q_out), ("kv_cache", kv_cache)):
+        if t.dtype != torch.bfloat16:
+            raise ValueError(f"{name} must be bfloat16")
+        if t.stride(-1) != 1:
+            raise ValueError(f"{name} needs a contiguous head dimension")
+    if not kv_cache.is_contiguous():
+        raise ValueError("kv_cache must be a contiguous [pages, 2, page, heads, dim] tensor")
+    if (q_norm_weight is None) != (k_norm_weight is None):
+        raise ValueError("give both norm weights or neither")
+    for w in (q_norm_weight, k_norm_weight):
+        if w is not None and (w.dtype != torch.bfloat16 or w.numel() != q.shape[2] or not w.is_contiguous()):
+            raise ValueError("norm weights must be contiguous bfloat16 [head_dim] tensors")
+    ints = [("kv_append_indptr", kv_append_indptr), ("rope_offsets", rope_offsets),
+            ("kv_page_indptr", kv_page_indptr), ("kv_last_page_len", kv_last_page_len)]
+    if kv_page_indices is not None:
+        ints.append(("kv_page_indices", kv_page_indices))
+    elif page_tables is None:
+        raise ValueError("kv_page_indices or page_tables is required")
+    for name, t in ints:
+        if t.dtype != torch.int32 or not t.is_contiguous():
+            raise ValueError(f"{name} must be a contiguous int32 tensor")
+    num_rows = kv_last_page_len.shape[0]
+    if kv_append_indptr.shape[0] < num_rows + 1 or kv_page_indptr.shape[0] < num_rows + 1:
+        raise ValueError("kv_append_indptr / kv_page_indptr need len(kv_last_page_len) + 1 entries")
+    if rope_offsets.shape[0] < num_rows:
+        raise ValueError("rope_offsets needs one entry per row")
+    a = _capi.AspirePrologueArgs()
+    a.q, a.q_stride_n, a.q_stride_h = q.data_ptr(), q.stride(0), q.stride(1)
+    a.k, a.k_stride_n, a.k_stride_h = k.data_ptr(), k.stride(0), k.stride(1)
+    a.v, a.v_stride_n, a.v_stride_h = v.data_ptr(), v.stride(0), v.stride(1)
+    a.q_out, a.qo_stride_n, a.qo_stride_h = q_out.data_ptr(), q_out.stride(0), q_out.stride(1)
+    a.num_tokens = total
+    a.num_qo_heads, a.num_kv_heads, a.head_dim = q.shape[1], k.shape[1], q.shape[2]
+    a.q_norm_weight = q_norm_weight.data_ptr() if q_norm_weight is not None else None
+    a.k_norm_weight = k_norm_weight.data_ptr() if k_norm_weight is not None else None
+    a.norm_eps = float(norm_eps)
+    a.rope_offsets = rope_offsets.data_ptr()
+    a.rope_theta, a.rope_scale = float(rope_theta), float(rope_scale)
+    if llama31 is not None:
+        a.low_freq_factor, a.high_freq_factor, a.old_context_len = (float(x) for x in llama31)
+    a.append_indptr = kv_append_indptr.data_ptr()
+    a.num_rows = num_rows
+    a.kv_cache = kv_cache.data_ptr()
+    a.num_pages_total = kv_cache.shape[0]
+    a.page_size = int(page_size)
+    a.page_indptr = kv_page_indptr.data_ptr()
+    a.last_page_len = kv_last_page_len.data_ptr()
+    if kv_page_indices is not None:
+        a.page_indices = kv_page_indices.data_ptr()
+    else:
+        a.mode_flags = page_tables[0].data_ptr()
+        a.draft_table = page_tables[1].data_ptr()
+        a.draft_stride = page_tables[1].stride(0)
+        a.block_table = page_tables[2].data_ptr()
+        a.block_table_stride = page_tables[2].stride(0)
+    a.status = status.data_ptr() if status is not None else None
+    stream = torch.cuda.current_stream(q.device).cuda_stream
+    rc = _capi.load_library().aspire_qkv_prologue(ctypes.byref(a), ctypes.c_void_p(stream))
+    _capi.check(rc, "aspire_qkv_prologue")
+    return q_out

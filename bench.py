@@ -352,7 +352,23 @@ def breakdown(hp: HotPath) -> dict:
         hp.refresh_nodump.set_page_tables(*hp.full_tables)
         hp.refresh_nodump.plan_host(t(full.qo_indptr), t(full.kv_indptr), t(full.kv_lens), None,
                                     full.num_qo_heads, full.num_kv_heads, 128, 16, causal=True)
+    if not hasattr(hp, "prologue_args"):
+        # The fused prologue (q/k norm + RoPE + append) on the step's q and new
+        # K/V, Qwen3-8B settings (qk-norm, theta 1e6), RoPE positions at the
+        # end of each row's context.
+        from aspire_b200.kv_ops import qkv_prologue
+        g = torch.Generator(device=hp.device)
+        g.manual_seed(5)
+        w = (1 + 0.1 * torch.randn(2, 128, generator=g, device=hp.device)).to(torch.bfloat16)
+        offs = torch.from_numpy((hp.lay.kv_lens - hp.lay.q_lens).astype(np.int32)).to(hp.device)
+        q_rot = torch.empty_like(hp.q[0])
+        hp.prologue_args = (qkv_prologue, w, offs, q_rot)
+    qkv_prologue, w, offs, q_rot = hp.prologue_args
     calls = {
+        "prologue": (lambda: qkv_prologue(hp.q[0], hp.k_new[0], hp.v_new[0], hp.qo_indptr, offs, hp.kv, None,
+                                          hp.mixed_indptr, hp.mixed_last, 16, q_norm_weight=w[0],
+                                          k_norm_weight=w[1], rope_theta=1e6, q_out=q_rot,
+                                          page_tables=hp.mixed_tables), 200),
         "append": (lambda: hp.append_kv(hp.k_new[0], hp.v_new[0], hp.qo_indptr, hp.kv, None,
                                         hp.mixed_indptr, hp.mixed_last, 16, page_tables=hp.mixed_tables), 200),
         "mixed_attention": (lambda: hp.mixed.run(hp.q[0], hp.kv, out=hp.out[0]), 30),

@@ -286,6 +286,61 @@ typedef struct AspireSelectArgs {
 ASPIRE_API int aspire_select_pages(const AspireSelectArgs* args, void* stream);
 
 /* ------------------------------------------------------------------------ */
+/* Fused attention prologue: q/k norm + RoPE + paged append (device).       */
+/* ------------------------------------------------------------------------ */
+
+typedef struct AspirePrologueArgs {
+  const void* q;            /* bf16 [num_tokens, num_qo_heads, 128] (wqkv output view) */
+  int64_t q_stride_n, q_stride_h;
+  const void* k;            /* bf16 [num_tokens, num_kv_heads, 128]               */
+  int64_t k_stride_n, k_stride_h;
+  const void* v;            /* bf16 [num_tokens, num_kv_heads, 128]               */
+  int64_t v_stride_n, v_stride_h;
+  void* q_out;              /* bf16 [num_tokens, num_qo_heads, 128]; may equal q  */
+  int64_t qo_stride_n, qo_stride_h;
+  int64_t num_tokens;
+  int32_t num_qo_heads;
+  int32_t num_kv_heads;
+  int32_t head_dim;         /* must be 128 */
+  const void* q_norm_weight;/* bf16 [128]; NULL together with k_norm_weight: no
+                               qk-norm and no permutation (models without it)     */
+  const void* k_norm_weight;
+  float norm_eps;
+  const int32_t* rope_offsets; /* int32 [num_rows]: position of each row's first new token */
+  float rope_theta;
+  float rope_scale;
+  float low_freq_factor;    /* Llama-3.1 smoothing when > 0, else plain RoPE      */
+  float high_freq_factor;
+  float old_context_len;
+  const int32_t* append_indptr; /* int32 [num_rows + 1]                           */
+  int32_t num_rows;
+  void* kv_cache;           /* bf16 [num_pages_total, 2, 16, num_kv_heads, 128]  */
+  int64_t num_pages_total;
+  int32_t page_size;        /* must be 16 */
+  const int32_t* page_indices;  /* flat page list, or NULL for the page tables     */
+  const int32_t* page_indptr;
+  const int32_t* last_page_len;
+  const int32_t* mode_flags;
+  const int32_t* draft_table;
+  int64_t draft_stride;
+  const int32_t* block_table;
+  int64_t block_table_stride;
+  uint32_t* status;
+} AspirePrologueArgs;
+
+/*
+ * One launch for the per-layer attention prologue: q_norm / k_norm with the
+ * HF-to-interleaved permutation (aspire/models/sparse_draft_transformer.py:
+ * 150-158, transformer.py:360-364, 505-515), the interleaved RoPE of q and k
+ * (mylib::rope -> FlashInfer apply_rope_inplace / apply_llama31_rope_inplace,
+ * aspire/models/mixed_transformer.py:159-197) and the paged append of the
+ * rotated k and of v (mylib::update_kv_padded, aspire/attention/kv_ops.py:
+ * 127-187).  Writes the rotated q to q_out.  No single counterpart in the
+ * reference: it replaces three of its ops.
+ */
+ASPIRE_API int aspire_qkv_prologue(const AspirePrologueArgs* args, void* stream);
+
+/* ------------------------------------------------------------------------ */
 /* Mixed page list (device).                                                */
 /* ------------------------------------------------------------------------ */
 

@@ -153,3 +153,35 @@ def test_unified_indices_oracle_matches_reference_golden(golden_dir):
                                          g["verify_num_pages"].numpy(), indices, indptr)
     np.testing.assert_array_equal(indptr, g["indptr"].numpy())
     np.testing.assert_array_equal(indices, g["indices"].numpy())
+
+
+def test_prologue_oracle_matches_flashinfer_rope_golden(golden_dir):
+    """The prologue restatement against the reference's math run on the GPU
+    (its RMSNorm module and FlashInfer's interleaved RoPE): the norm and the
+    permutation agree bit for bit; the rotation agrees to the error of
+    FlashInfer's fast sincosf / powf intrinsics, which the float64 oracle
+    does not share (largest at the 32k+ positions of the qwen3_8b case)."""
+    import sys
+    sys.path.insert(0, str(golden_dir))
+    import make_rope_golden as mg
+    from oracle import prologue as op
+
+    g = torch.load(golden_dir / "rope_prologue.pt", weights_only=False)
+    for name, c in g["cases"].items():
+        p = c["params"]
+        q, k, v, qw, kw, indptr, offsets = mg.case_inputs(p["seed"], p["T"], p["hq"], p["hkv"], p["rows"],
+                                                          p["pos_base"])
+        if p["norm"]:
+            qn = op.permute_for_rope(op.rms_norm(q, qw, p["eps"]))
+            kn = op.permute_for_rope(op.rms_norm(k, kw, p["eps"]))
+        else:
+            qn, kn = q, k
+        assert torch.equal(qn, c["q_normed"]) and torch.equal(kn, c["k_normed"]), name
+        for x, ref in ((qn, c["q_rot"]), (kn, c["k_rot"])):
+            got = op.rope_interleaved(x, indptr.tolist(), offsets.tolist(), p["theta"], p["scale"], p["llama31"])
+            d = (got.float() - ref.float()).abs()
+            assert d.max().item() <= 0.04, (name, d.max().item())
+            assert d.mean().item() <= 5e-4, (name, d.mean().item())
+            # Tokens outside the rows are not rotated.
+            tail = int(indptr[-1])
+            assert torch.equal(got[tail:], x[tail:]) and torch.equal(ref[tail:], x[tail:])
