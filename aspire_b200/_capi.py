@@ -48,6 +48,7 @@ class AspirePlanInfo(ctypes.Structure):
         ("batch_size", ctypes.c_int32),
         ("max_q_len", ctypes.c_int32),
         ("tc_enabled", ctypes.c_int32),
+        ("on_device", ctypes.c_int32),
     ]
 
 
@@ -235,6 +236,12 @@ _SIGNATURES = {
     "aspire_select_pages": (ctypes.c_int, [ctypes.POINTER(AspireSelectArgs), ctypes.c_void_p]),
     "aspire_build_unified_indices": (ctypes.c_int, [ctypes.POINTER(AspireIndicesArgs), ctypes.c_void_p]),
     "aspire_qkv_prologue": (ctypes.c_int, [ctypes.POINTER(AspirePrologueArgs), ctypes.c_void_p]),
+    "aspire_plan_device": (
+        ctypes.c_int,
+        [c_int32_p, c_int32_p, c_int32_p, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
+         ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_size_t,
+         ctypes.c_void_p, ctypes.POINTER(AspirePlanInfo)],
+    ),
     "aspire_last_error": (ctypes.c_char_p, []),
     "aspire_abi_version": (ctypes.c_int, []),
     "aspire_status_offset": (ctypes.c_size_t, []),

@@ -251,6 +251,59 @@ class HolisticAttentionWrapper:
         self._num_qo_heads = int(num_qo_heads)
         self._num_kv_heads = int(num_kv_heads)
 
+    def plan_device(
+        self,
+        qo_indptr: torch.Tensor,
+        paged_kv_indptr: torch.Tensor,
+        paged_kv_last_page_len: torch.Tensor,
+        num_qo_heads: int,
+        num_kv_heads: int,
+        head_dim_qk: int,
+        page_size: int,
+        paged_kv_indices: Optional[torch.Tensor] = None,
+        causal: bool = False,
+        sm_scale: Optional[float] = None,
+        batch_size: Optional[int] = None,
+    ) -> None:
+        """Plans on the device from device arrays (C ABI ``aspire_plan_device``):
+        no readback and no synchronisation, so the call can be captured in a
+        CUDA graph with the step and re-plans on every replay from whatever the
+        arrays then hold.  Replaces the per-step host planning of
+        ``plan`` / ``plan_host`` (aspire/attention/holistic_wrapper.py:200-342).
+        Row b attends ``max(pages_b - 1, 0) * page_size + last_page_len[b]``
+        tokens.  Problems found on the device (a malformed row, a plan beyond
+        the workspaces) are reported in ``device_status()`` and the program
+        then writes nothing."""
+        batch = int(paged_kv_last_page_len.shape[0] if batch_size is None else batch_size)
+        for name, t in (("qo_indptr", qo_indptr), ("paged_kv_indptr", paged_kv_indptr),
+                        ("paged_kv_last_page_len", paged_kv_last_page_len)):
+            if t.dtype != torch.int32 or not t.is_contiguous() or t.device.type != "cuda":
+                raise ValueError(f"{name} must be a contiguous int32 CUDA tensor")
+        if qo_indptr.shape[0] < batch + 1 or paged_kv_indptr.shape[0] < batch + 1 or \
+                paged_kv_last_page_len.shape[0] < batch:
+            raise ValueError("qo_indptr / paged_kv_indptr need batch_size + 1 entries")
+        if paged_kv_indices is None and self._page_tables is None:
+            raise ValueError("paged_kv_indices is required unless set_page_tables() was called")
+        info = _capi.AspirePlanInfo()
+        stream = torch.cuda.current_stream(self._device).cuda_stream
+        rc = self._lib.aspire_plan_device(
+            _dev_i32(qo_indptr), _dev_i32(paged_kv_indptr), _dev_i32(paged_kv_last_page_len), batch, int(num_qo_heads), int(num_kv_heads),
+            int(head_dim_qk), int(page_size), 1 if causal else 0, self._num_sms,
+            ctypes.c_void_p(self._int_workspace.data_ptr()), self._int_workspace.numel(),
+            self._float_workspace.numel(), ctypes.c_void_p(stream), ctypes.byref(info),
+        )
+        _capi.check(rc, "aspire_plan_device")
+        self._plan_info = info
+        self._plan_q_total = 0      # checked on the device: rows past q are skipped
+        self._plan_max_kv_len = 0   # checked on the device: dump writes past kv_stride are skipped
+        self._plan_rows = batch
+        self._kv_indices = paged_kv_indices
+        self._page_size = int(page_size)
+        self._sm_scale = sm_scale
+        self._causal = bool(causal)
+        self._num_qo_heads = int(num_qo_heads)
+        self._num_kv_heads = int(num_kv_heads)
+
     @property
     def plan_info(self) -> Optional[_capi.AspirePlanInfo]:
         return self._plan_info
@@ -358,6 +411,11 @@ class HolisticAttentionWrapper:
 
     def clear_device_status(self) -> None:
         self._int_workspace[:4].zero_()
+
+
+def _dev_i32(t: torch.Tensor):
+    """Device address of an int32 tensor as the C ABI's int32 pointer."""
+    return ctypes.cast(ctypes.c_void_p(t.data_ptr()), _capi.c_int32_p)
 
 
 def wrapper_from_id(wrapper_id: int) -> HolisticAttentionWrapper:

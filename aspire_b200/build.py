@@ -29,6 +29,7 @@ SOURCES = [
     "select_pages.cu",
     "unified_indices.cu",
     "qkv_prologue.cu",
+    "plan_device.cu",
     "noalloc.cu",
 ]
 

@@ -25,6 +25,7 @@ struct AttnParams {
   float scale_log2;          // sm_scale * log2(e)
   int32_t num_qo_heads, num_kv_heads, group;
   int32_t q_box_tokens;      // tokens per query-tile TMA box (tcgen05 kernel)
+  int64_t q_rows;            // rows of q and out: plan rows past them are skipped (BAD_ROW)
   const int32_t* plan;       // int workspace + kStatusBytes
   uint32_t* status;          // int workspace (first word)
   float* partial_o;          // float workspace
@@ -96,6 +97,10 @@ __device__ __forceinline__ void store_final(const AttnParams& p, const WorkItem&
   int q_idx, head;
   packed_row(p, it, pq, q_idx, head);
   const int64_t tok = int64_t(it.q_start) + q_idx;
+  if (tok >= p.q_rows) {
+    if (d == 0) record_status(p.status, ASPIRE_STATUS_BAD_ROW);
+    return;
+  }
   p.out[tok * p.o_stride_n + int64_t(head) * p.o_stride_h + d] = __float2bfloat16_rn(o);
   if (d == 0 && p.lse) p.lse[tok * p.num_qo_heads + head] = lse;
 }

@@ -96,7 +96,7 @@ __global__ void __launch_bounds__(kThreads, kGatherCtasPerSm) aspire_attn_gather
       lim[j] = causal ? (it.kv_len - it.q_len + q_idx + 1) : it.kv_len;
       slot0[j] = (j < nq) && q_idx == 0;
       slot1[j] = (j < nq) && q_idx != 0 && q_idx + 1 == it.q_len;
-      if (j < nq) {
+      if (j < nq && int64_t(it.q_start) + q_idx < p.q_rows) {
         const uint4 u = *reinterpret_cast<const uint4*>(
             p.q + int64_t(it.q_start + q_idx) * p.q_stride_n + int64_t(head) * p.q_stride_h +
             l16 * 8);
@@ -188,7 +188,7 @@ __global__ void __launch_bounds__(kThreads, kGatherCtasPerSm) aspire_attn_gather
           for (int j = 0; j < kQT; ++j) s[j] += __shfl_xor_sync(0xffffffffu, s[j], off);
         }
         const bool in_chunk = tok >= it.tok_begin && tok < it.tok_end;
-        if (p.dump != nullptr && in_chunk) {
+        if (p.dump != nullptr && in_chunk && tok < p.dump_kv_stride) {
 #pragma unroll
           for (int j = 0; j < kQT; ++j) {
             if (l16 == j && (slot0[j] || slot1[j])) {

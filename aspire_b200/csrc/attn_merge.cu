@@ -71,6 +71,10 @@ __global__ void __launch_bounds__(kMergeThreads) aspire_attn_merge_kernel(AttnPa
     const int q_idx = pq / p.group;
     const int head = md.kv_head * p.group + (pq - q_idx * p.group);
     const int64_t tok = int64_t(md.q_start) + q_idx;
+    if (tok >= p.q_rows) {
+      if (lane == 0) record_status(p.status, ASPIRE_STATUS_BAD_ROW);
+      continue;
+    }
     __nv_bfloat162 lo = __floats2bfloat162_rn(acc.x * inv, acc.y * inv);
     __nv_bfloat162 hi = __floats2bfloat162_rn(acc.z * inv, acc.w * inv);
     uint2 packed;

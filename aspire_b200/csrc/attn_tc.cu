@@ -563,7 +563,7 @@ __device__ bool consume_item(const AttnParams& p, TcShared& sm, const WorkItem& 
         for (int c = lo; c < hi; c += 8) {
           ptx::tmem_ld8(tmem_lane + col_s(b) + c, dv);
           ptx::tmem_wait_ld();
-          if (in_chunk) {
+          if (in_chunk && tok < p.dump_kv_stride) {
 #pragma unroll
             for (int i = 0; i < 8; ++i)
               if (c + i < hi) base[(c + i - base_col) * dump_col_stride + tok] = __float2half_rn(dv[i]);
@@ -707,7 +707,7 @@ __device__ bool consume_item(const AttnParams& p, TcShared& sm, const WorkItem& 
     if (ctid < NH && c0 + ctid < nrows && p.lse) {
       int q_idx, head;
       packed_row(p, it, it.pq_begin + c0 + ctid, q_idx, head);
-      p.lse[(int64_t(it.q_start) + q_idx) * p.num_qo_heads + head] = my_lse;
+      if (int64_t(it.q_start) + q_idx < p.q_rows) p.lse[(int64_t(it.q_start) + q_idx) * p.num_qo_heads + head] = my_lse;
     }
   } else {
     float* st = reinterpret_cast<float*>(stage);
@@ -725,6 +725,10 @@ __device__ bool consume_item(const AttnParams& p, TcShared& sm, const WorkItem& 
       for (int j = c0; j < row_end; ++j) {
         int q_idx, head;
         packed_row(p, it, it.pq_begin + j, q_idx, head);
+        if (int64_t(it.q_start) + q_idx >= p.q_rows) {
+          record_status(p.status, ASPIRE_STATUS_BAD_ROW);
+          continue;
+        }
         __nv_bfloat16* dst = p.out + (int64_t(it.q_start) + q_idx) * p.o_stride_n + int64_t(head) * p.o_stride_h;
         ptx::bulk_store(dst, src + uint32_t(j) * kHeadDim * 2, kHeadDim * 2);
       }

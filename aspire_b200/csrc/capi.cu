@@ -165,7 +165,7 @@ size_t aspire_status_offset(void) { return kStatusBytes; }
 
 const char* aspire_kernel_names(void) {
   return "aspire_attn_gather_kernel\naspire_attn_tc_kernel\naspire_attn_merge_kernel\naspire_append_kv_kernel\n"
-         "aspire_select_pages_kernel\naspire_page_scores_kernel\naspire_build_indices_kernel\naspire_qkv_prologue_kernel\n";
+         "aspire_select_pages_kernel\naspire_page_scores_kernel\naspire_build_indices_kernel\naspire_qkv_prologue_kernel\naspire_plan_device_kernel\n";
 }
 
 int aspire_plan_host_only(const int32_t* qo_indptr, const int32_t* kv_indptr,
@@ -177,6 +177,66 @@ int aspire_plan_host_only(const int32_t* qo_indptr, const int32_t* kv_indptr,
   return plan_impl(qo_indptr, kv_indptr, kv_len, batch_size, num_qo_heads, num_kv_heads, head_dim,
                    page_size, causal, num_ctas, tc_kernel_available() && tc_env_enabled(), tc_min_rows(),
                    tc_min_kv(), host_buf, host_buf_bytes, float_ws_bytes, info);
+}
+
+int aspire_plan_device(const int32_t* qo_indptr, const int32_t* kv_indptr, const int32_t* last_page_len,
+                       int32_t batch_size, int32_t num_qo_heads, int32_t num_kv_heads, int32_t head_dim,
+                       int32_t page_size, int32_t causal, int32_t num_ctas, void* dev_int_ws,
+                       size_t dev_int_ws_bytes, size_t float_ws_bytes, void* stream, AspirePlanInfo* info) {
+  clear_error();
+  if (!qo_indptr || !kv_indptr || !last_page_len || !dev_int_ws || !info)
+    return set_error(ASPIRE_ERR_INVALID, "aspire_plan_device: null pointer argument");
+  if (batch_size < 0) return set_error(ASPIRE_ERR_INVALID, "aspire_plan_device: batch_size < 0");
+  if (head_dim != kHeadDim || page_size != kPageSize)
+    return set_error(ASPIRE_ERR_INVALID, "aspire_plan_device: head_dim must be 128 and page_size 16");
+  if (num_kv_heads <= 0 || num_qo_heads <= 0 || num_qo_heads % num_kv_heads != 0)
+    return set_error(ASPIRE_ERR_INVALID,
+                     "aspire_plan_device: num_qo_heads must be a positive multiple of num_kv_heads");
+  const int group = num_qo_heads / num_kv_heads;
+  if (group > kTcQTile || !(tc_kernel_available() && tc_env_enabled()) || tc_min_rows() > 1)
+    return set_error(ASPIRE_ERR_INVALID,
+                     "aspire_plan_device: device planning routes every row to the tcgen05 kernel "
+                     "(group <= 48, default routing)");
+  if (dev_int_ws_bytes <= kStatusBytes + kHdrWords * 4)
+    return set_error(ASPIRE_ERR_CAPACITY, "aspire_plan_device: int workspace too small");
+  if (num_ctas <= 0) {
+    int rc = current_sm_count(&num_ctas);
+    if (rc) return rc;
+  }
+  DevPlanParams p;
+  p.qo_indptr = qo_indptr;
+  p.kv_indptr = kv_indptr;
+  p.last_page_len = last_page_len;
+  p.batch = batch_size;
+  p.group = group;
+  p.num_kv_heads = num_kv_heads;
+  p.causal = causal;
+  p.num_sms = num_ctas;
+  p.plan = reinterpret_cast<int32_t*>(static_cast<char*>(dev_int_ws) + kStatusBytes);
+  p.plan_words = int64_t((dev_int_ws_bytes - kStatusBytes) / 4);
+  p.float_ws_bytes = int64_t(float_ws_bytes);
+  p.status = static_cast<uint32_t*>(dev_int_ws);
+  int rc = launch(aspire_plan_device_kernel, dim3(1), dim3(kDevPlanThreads), 0, static_cast<cudaStream_t>(stream),
+                  "aspire_plan_device_kernel launch", p);
+  if (rc) return rc;
+  std::memset(info, 0, sizeof(*info));
+  info->num_items = -1;
+  info->num_items_gather = 0;
+  info->num_items_tc = -1;
+  info->num_ctas = num_ctas;
+  info->num_merge = 1;  // may split: the float workspace is required
+  info->chunk_tokens = -1;
+  info->partial_rows = -1;
+  info->int_bytes = int64_t(dev_int_ws_bytes) - kStatusBytes;
+  info->float_bytes = int64_t(float_ws_bytes);
+  info->num_qo_heads = num_qo_heads;
+  info->num_kv_heads = num_kv_heads;
+  info->causal = causal ? 1 : 0;
+  info->batch_size = batch_size;
+  info->max_q_len = -1;
+  info->tc_enabled = 1;
+  info->on_device = 1;
+  return ASPIRE_OK;
 }
 
 int aspire_plan(const int32_t* qo_indptr, const int32_t* kv_indptr, const int32_t* kv_len,
@@ -268,6 +328,7 @@ int aspire_mixed_attention(const AspireAttnArgs* a, const AspirePlanInfo* plan, 
   p.num_kv_heads = a->num_kv_heads;
   p.group = group;
   p.q_box_tokens = static_cast<int32_t>(std::min<int64_t>(kTcQTile / group, a->q_rows));
+  p.q_rows = a->q_rows;
   p.plan = reinterpret_cast<const int32_t*>(static_cast<const char*>(a->int_ws) + kStatusBytes);
   p.status = static_cast<uint32_t*>(a->int_ws);
   p.partial_o = static_cast<float*>(a->float_ws);

@@ -55,6 +55,19 @@ struct PrologueParams {
 };
 __global__ void aspire_qkv_prologue_kernel(PrologueParams p);
 
+struct DevPlanParams {
+  const int32_t* qo_indptr;     // device [batch + 1]
+  const int32_t* kv_indptr;     // device [batch + 1] page offsets
+  const int32_t* last_page_len; // device [batch]
+  int32_t batch, group, num_kv_heads, causal, num_sms;
+  int32_t* plan;                // int workspace + kStatusBytes
+  int64_t plan_words;           // capacity of the plan area in int32 words
+  int64_t float_ws_bytes;
+  uint32_t* status;
+};
+constexpr int kDevPlanThreads = 1024;
+__global__ void aspire_plan_device_kernel(DevPlanParams p);
+
 struct SelectParams {
   const __half* dump;
   int64_t kv_stride, max_seq_len;

@@ -1,0 +1,229 @@
+// Device-side planner: renders the work list of the mixed attention from
+// device arrays, with no host round trip, so planning can live inside a CUDA
+// graph (the reference plans on the host every step: HolisticAttentionWrapper.
+// plan / plan_host, aspire/attention/holistic_wrapper.py:200-342, fed by
+// HostPlanState, aspire/backends/host_plan.py:154-306).
+//
+// It produces the same items as the host planner (planner.cpp): every
+// (row, KV head, packed-query tile) is cut into chunks of one common length
+// (a multiple of 128 tokens, at least 512, sized for ~4 items per SM), with
+// merge descriptors for the split groups.  All rows go to the tcgen05 kernel
+// (the default routing); items are stored longest first through a counting
+// sort on their length in 128-token tiles, the order in which the persistent
+// CTAs claim them.  One CTA of 1024 threads; each thread owns a contiguous run
+// of rows.  An invalid input row or a plan larger than the workspaces sets
+// ASPIRE_STATUS_BAD_PLAN and leaves a plan with no magic, which every kernel
+// skips.
+#include "kernels.cuh"
+
+namespace aspire {
+
+namespace {
+
+constexpr int kCostBuckets = 1024;
+
+// Exclusive block scan of one int64 per thread; returns the thread's offset
+// and writes the total to *total.
+__device__ int64_t block_exclusive_scan(int64_t v, int64_t* warp_sums, int64_t* total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+  int64_t x = v;
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const int64_t y = __shfl_up_sync(0xffffffffu, x, off);
+    if (lane >= off) x += y;
+  }
+  if (lane == 31) warp_sums[warp] = x;
+  __syncthreads();
+  if (warp == 0) {
+    int64_t w = lane < nwarps ? warp_sums[lane] : 0;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const int64_t y = __shfl_up_sync(0xffffffffu, w, off);
+      if (lane >= off) w += y;
+    }
+    if (lane < nwarps) warp_sums[lane] = w;  // inclusive
+  }
+  __syncthreads();
+  const int64_t before = (warp > 0 ? warp_sums[warp - 1] : 0) + x - v;
+  *total = warp_sums[nwarps - 1];
+  __syncthreads();
+  return before;
+}
+
+struct RowShape {
+  int32_t ql, kl, nq, ntq, nchunks;
+  bool valid;
+};
+
+__device__ __forceinline__ RowShape row_shape(const DevPlanParams& p, int b, int tile, int64_t chunk) {
+  RowShape r{};
+  const int32_t ql = p.qo_indptr[b + 1] - p.qo_indptr[b];
+  const int32_t pages = p.kv_indptr[b + 1] - p.kv_indptr[b];
+  const int32_t last = p.last_page_len[b];
+  const int32_t kl = (pages > 1 ? pages - 1 : 0) * kPageSize + last;
+  r.valid = ql >= 0 && pages >= 0 && last >= 0 && !(kl > 0 && int64_t(kl) > int64_t(pages) * kPageSize);
+  r.ql = r.valid ? ql : 0;
+  r.kl = r.valid ? kl : 0;
+  r.nq = r.ql * p.group;
+  r.ntq = (r.nq + tile - 1) / tile;
+  r.nchunks = chunk > 0 ? (r.kl > 0 ? int32_t((r.kl + chunk - 1) / chunk) : 1) : 0;
+  return r;
+}
+
+__device__ __forceinline__ int cost_bucket(int64_t tokens) {
+  const int64_t tiles = (tokens + 127) / 128;
+  return int(tiles < kCostBuckets - 1 ? tiles : kCostBuckets - 1);
+}
+
+}  // namespace
+
+__global__ void __launch_bounds__(kDevPlanThreads) aspire_plan_device_kernel(DevPlanParams p) {
+  pdl_begin();
+  __shared__ int64_t warp_sums[32];
+  __shared__ int32_t bucket[kCostBuckets];
+  __shared__ int bad;
+  const int tid = threadIdx.x, nthreads = blockDim.x;
+  if (tid == 0) bad = 0;
+  for (int i = tid; i < kCostBuckets; i += nthreads) bucket[i] = 0;
+  __syncthreads();
+  const int tile = (kTcQTile / p.group) * p.group;
+  const int rpt = (p.batch + nthreads - 1) / nthreads;  // rows per thread
+  const int r0 = min(tid * rpt, p.batch), r1 = min(r0 + rpt, p.batch);
+
+  // Total tokens over (row, head, q-tile) groups -> the common chunk length.
+  int64_t tokens = 0;
+  for (int b = r0; b < r1; ++b) {
+    const RowShape s = row_shape(p, b, tile, 0);
+    if (!s.valid) bad = 1;
+    if (s.ql > 0) tokens += int64_t(p.num_kv_heads) * s.ntq * (s.kl > 1 ? s.kl : 1);
+  }
+  int64_t total_tokens;
+  block_exclusive_scan(tokens, warp_sums, &total_tokens);
+  const int64_t target = int64_t(p.num_sms) * 4;
+  int64_t chunk = (total_tokens + target - 1) / target;
+  chunk = chunk < 512 ? 512 : chunk;
+  chunk = (chunk + 127) / 128 * 128;
+
+  // Per-thread counts; item lengths into the cost histogram.
+  int64_t n_items = 0, n_merge = 0, n_prow = 0, n_units = 0;
+  for (int b = r0; b < r1; ++b) {
+    const RowShape s = row_shape(p, b, tile, chunk);
+    if (s.ql <= 0) continue;
+    const int32_t groups = p.num_kv_heads * s.ntq;
+    n_items += int64_t(groups) * s.nchunks;
+    if (s.nchunks > 1) {
+      n_merge += groups;
+      n_prow += int64_t(p.num_kv_heads) * s.nq * s.nchunks;
+      n_units += int64_t(p.num_kv_heads) * s.nq;
+      atomicAdd(&bucket[cost_bucket(chunk)], groups * (s.nchunks - 1));
+    }
+    const int64_t last_len = s.kl - int64_t(s.nchunks - 1) * chunk;
+    atomicAdd(&bucket[cost_bucket(last_len)], groups);
+  }
+  int64_t tot_items, tot_merge, tot_prow, tot_units;
+  int64_t off_item = block_exclusive_scan(n_items, warp_sums, &tot_items);
+  (void)off_item;
+  int64_t off_merge = block_exclusive_scan(n_merge, warp_sums, &tot_merge);
+  int64_t off_prow = block_exclusive_scan(n_prow, warp_sums, &tot_prow);
+  int64_t off_unit = block_exclusive_scan(n_units, warp_sums, &tot_units);
+  // Bucket starts, longest first: start[k] = items in buckets above k.
+  {
+    int64_t mine = 0, tot;
+    const int k = kCostBuckets - 1 - tid;
+    if (tid < kCostBuckets) mine = bucket[k];
+    __syncthreads();
+    const int64_t start = block_exclusive_scan(mine, warp_sums, &tot);
+    if (tid < kCostBuckets) bucket[k] = int32_t(start);
+    __syncthreads();
+  }
+
+  // Layout (int32 words): header | gather indptr | items | merges | merge units.
+  const int gather_ctas = p.num_sms * kGatherCtasPerSm;
+  const int64_t off_gather = kHdrWords;
+  const int64_t off_items = (off_gather + gather_ctas + 1 + 15) / 16 * 16;
+  const int64_t off_merges = off_items + tot_items * kItemWords;
+  const int64_t off_units = off_merges + tot_merge * kMergeWords;
+  const int64_t words = off_units + tot_units;
+  if (tid == 0 && (words > p.plan_words || tot_prow * (kHeadDim + 1) * 4 > p.float_ws_bytes ||
+                   tot_items > INT32_MAX || tot_merge >= (int64_t(1) << 23)))
+    bad = 1;
+  __syncthreads();
+  int32_t* w = p.plan;
+  if (bad) {
+    if (tid == 0) {
+      w[kHdrMagic] = 0;
+      if (p.status) atomicOr(p.status, ASPIRE_STATUS_BAD_PLAN);
+    }
+    return;
+  }
+
+  WorkItem* items = reinterpret_cast<WorkItem*>(w + off_items);
+  MergeDesc* merges = reinterpret_cast<MergeDesc*>(w + off_merges);
+  int32_t* units = w + off_units;
+  for (int b = r0; b < r1; ++b) {
+    const RowShape s = row_shape(p, b, tile, chunk);
+    if (s.ql <= 0) continue;
+    for (int h = 0; h < p.num_kv_heads; ++h) {
+      for (int qt = 0; qt < s.ntq; ++qt) {
+        const int32_t pq0 = qt * tile, pq1 = min(s.nq, pq0 + tile), rows = pq1 - pq0;
+        int32_t merge_id = -1, pbase = 0;
+        if (s.nchunks > 1) {
+          merge_id = int32_t(off_merge++);
+          pbase = int32_t(off_prow);
+          off_prow += int64_t(s.nchunks) * rows;
+          MergeDesc md{};
+          md.q_start = p.qo_indptr[b];
+          md.pq_begin = pq0;
+          md.nrows = rows;
+          md.kv_head = h;
+          md.partial_base = pbase;
+          md.n_chunks = s.nchunks;
+          merges[merge_id] = md;
+          for (int j = 0; j < rows; ++j) units[off_unit++] = (merge_id << 8) | j;
+        }
+        for (int c = 0; c < s.nchunks; ++c) {
+          WorkItem it{};
+          it.row = b;
+          it.kv_head = h;
+          it.q_start = p.qo_indptr[b];
+          it.q_len = s.ql;
+          it.kv_page_base = p.kv_indptr[b];
+          it.kv_len = s.kl;
+          it.tok_begin = int32_t(min(int64_t(c) * chunk, int64_t(s.kl)));
+          it.tok_end = int32_t(min(int64_t(c + 1) * chunk, int64_t(s.kl)));
+          it.pq_begin = pq0;
+          it.pq_end = pq1;
+          it.chunk = c;
+          it.n_chunks = s.nchunks;
+          it.partial_base = pbase;
+          it.merge_id = merge_id;
+          it.kind = 1;
+          const int slot = atomicAdd(&bucket[cost_bucket(it.tok_end - it.tok_begin)], 1);
+          items[slot] = it;
+        }
+      }
+    }
+  }
+  for (int64_t i = off_gather + tid; i < off_items; i += nthreads) w[i] = 0;  // empty CUDA-core list
+  if (tid == 0) {
+    for (int i = 0; i < kHdrWords; ++i) w[i] = 0;
+    w[kHdrNumItems] = int32_t(tot_items);
+    w[kHdrNumGatherCtas] = gather_ctas;
+    w[kHdrNumTcCtas] = p.num_sms * kTcCtasPerSm;
+    w[kHdrCausal] = p.causal ? 1 : 0;
+    w[kHdrOffGatherIndptr] = int32_t(off_gather);
+    w[kHdrTcFirst] = 0;
+    w[kHdrOffItems] = int32_t(off_items);
+    w[kHdrOffMerge] = int32_t(off_merges);
+    w[kHdrNumMerge] = int32_t(tot_merge);
+    w[kHdrOffMergeUnits] = int32_t(off_units);
+    w[kHdrNumMergeUnits] = int32_t(tot_units);
+    const int64_t lse_off = tot_prow * kHeadDim;
+    w[kHdrPartialLseLo] = int32_t(lse_off & 0xffffffff);
+    w[kHdrPartialLseHi] = int32_t(lse_off >> 32);
+    w[kHdrTcClaim] = 0;
+    w[kHdrMagic] = kPlanMagic;
+  }
+}
+
+}  // namespace aspire

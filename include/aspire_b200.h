@@ -83,6 +83,9 @@ typedef struct AspirePlanInfo {
   int32_t batch_size;       /* rows planned (including padding rows)          */
   int32_t max_q_len;
   int32_t tc_enabled;       /* 1 when wide query tiles use the tcgen05 kernel */
+  int32_t on_device;        /* 1 when aspire_plan_device rendered the plan: the
+                               counts above are then upper bounds (int_bytes and
+                               float_bytes the workspace capacities) or -1      */
 } AspirePlanInfo;
 
 /*
@@ -284,6 +287,25 @@ typedef struct AspireSelectArgs {
  * (aspire/backends/base.py:1421-1471).
  */
 ASPIRE_API int aspire_select_pages(const AspireSelectArgs* args, void* stream);
+
+/*
+ * Renders the same work list as aspire_plan on the device, from device
+ * arrays, with no host round trip or synchronisation, so that planning can be
+ * captured in a CUDA graph together with the step.  Replaces the per-step host
+ * planning of HolisticAttentionWrapper.plan / plan_host
+ * (aspire/attention/holistic_wrapper.py:200-342) and the HostPlanState upload
+ * (aspire/backends/host_plan.py:154-306).  kv_len of row b is
+ * max(pages_b - 1, 0) * 16 + last_page_len[b], as in plan().  Every row goes
+ * to the tcgen05 kernel (the default routing; other routing thresholds are
+ * rejected).  A malformed row or a plan beyond the workspaces is reported as
+ * ASPIRE_STATUS_BAD_PLAN on the device (the kernels then skip the plan).
+ * `info` receives the grid, the heads and the workspace capacities.
+ */
+ASPIRE_API int aspire_plan_device(const int32_t* qo_indptr, const int32_t* kv_indptr,
+                                  const int32_t* last_page_len, int32_t batch_size, int32_t num_qo_heads,
+                                  int32_t num_kv_heads, int32_t head_dim, int32_t page_size, int32_t causal,
+                                  int32_t num_ctas, void* dev_int_ws, size_t dev_int_ws_bytes,
+                                  size_t float_ws_bytes, void* stream, AspirePlanInfo* info);
 
 /* ------------------------------------------------------------------------ */
 /* Fused attention prologue: q/k norm + RoPE + paged append (device).       */
