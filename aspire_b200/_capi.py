@@ -144,6 +144,7 @@ class AspireSelectArgs(ctypes.Structure):
         ("scores_out", ctypes.c_void_p),
         ("status", ctypes.c_void_p),
         ("scores_ws", ctypes.c_void_p),
+        ("order_by_page", ctypes.c_int32),
     ]
 
 

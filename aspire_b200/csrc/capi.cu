@@ -585,6 +585,9 @@ int aspire_select_pages(const AspireSelectArgs* a, void* stream) {
   p.counts_out = a->counts_out;
   p.scores_out = a->scores_out;
   p.status = a->status;
+  p.order_by_page = a->order_by_page ? 1 : 0;
+  if (p.order_by_page && !a->scores_in)
+    return set_error(ASPIRE_ERR_INVALID, "aspire_select_pages: order_by_page needs scores_in");
   int cap = 1;
   while (cap < std::min(a->pages_per_slot, a->subset_cache_size)) cap <<= 1;
   p.sort_cap = cap;

@@ -90,6 +90,7 @@ struct SelectParams {
   float* scores_out;
   uint32_t* status;
   int32_t sort_cap;  // power of two >= pages_per_slot
+  int32_t order_by_page;  // sort the selection by page index and write block ids in that order
 };
 
 struct IndicesParams {

@@ -51,11 +51,26 @@ __device__ int64_t block_exclusive_scan(int64_t v, int64_t* warp_sums, int64_t* 
 }
 
 struct RowShape {
-  int32_t ql, kl, nq, ntq, nchunks;
+  int32_t ql, kl, nq, ntq;
   bool valid;
 };
 
-__device__ __forceinline__ RowShape row_shape(const DevPlanParams& p, int b, int tile, int64_t chunk) {
+// KV tokens a query tile [pq_begin, pq_end) can see (the host planner's
+// visible_span): all of kv_len, or under the causal mask up to the tile's last
+// query, except for the tile holding query 0 (the dump needs all its logits).
+__device__ __forceinline__ int32_t tile_span(const DevPlanParams& p, const RowShape& s, int32_t pq_begin,
+                                             int32_t pq_end) {
+  if (!p.causal || pq_begin == 0) return s.kl;
+  const int64_t q_last = (pq_end - 1) / p.group;
+  const int64_t lim = int64_t(s.kl) - s.ql + q_last + 1;
+  return int32_t(max(int64_t(0), min(int64_t(s.kl), lim)));
+}
+
+__device__ __forceinline__ int32_t span_chunks(int32_t span, int64_t chunk) {
+  return span > 0 ? int32_t((span + chunk - 1) / chunk) : 1;
+}
+
+__device__ __forceinline__ RowShape row_shape(const DevPlanParams& p, int b, int tile) {
   RowShape r{};
   const int32_t ql = p.qo_indptr[b + 1] - p.qo_indptr[b];
   const int32_t pages = p.kv_indptr[b + 1] - p.kv_indptr[b];
@@ -66,7 +81,6 @@ __device__ __forceinline__ RowShape row_shape(const DevPlanParams& p, int b, int
   r.kl = r.valid ? kl : 0;
   r.nq = r.ql * p.group;
   r.ntq = (r.nq + tile - 1) / tile;
-  r.nchunks = chunk > 0 ? (r.kl > 0 ? int32_t((r.kl + chunk - 1) / chunk) : 1) : 0;
   return r;
 }
 
@@ -93,9 +107,13 @@ __global__ void __launch_bounds__(kDevPlanThreads) aspire_plan_device_kernel(Dev
   // Total tokens over (row, head, q-tile) groups -> the common chunk length.
   int64_t tokens = 0;
   for (int b = r0; b < r1; ++b) {
-    const RowShape s = row_shape(p, b, tile, 0);
+    const RowShape s = row_shape(p, b, tile);
     if (!s.valid) bad = 1;
-    if (s.ql > 0) tokens += int64_t(p.num_kv_heads) * s.ntq * (s.kl > 1 ? s.kl : 1);
+    if (s.ql <= 0) continue;
+    for (int qt = 0; qt < s.ntq; ++qt) {
+      const int32_t span = tile_span(p, s, qt * tile, min(s.nq, (qt + 1) * tile));
+      tokens += int64_t(p.num_kv_heads) * (span > 1 ? span : 1);
+    }
   }
   int64_t total_tokens;
   block_exclusive_scan(tokens, warp_sums, &total_tokens);
@@ -107,18 +125,23 @@ __global__ void __launch_bounds__(kDevPlanThreads) aspire_plan_device_kernel(Dev
   // Per-thread counts; item lengths into the cost histogram.
   int64_t n_items = 0, n_merge = 0, n_prow = 0, n_units = 0;
   for (int b = r0; b < r1; ++b) {
-    const RowShape s = row_shape(p, b, tile, chunk);
+    const RowShape s = row_shape(p, b, tile);
     if (s.ql <= 0) continue;
-    const int32_t groups = p.num_kv_heads * s.ntq;
-    n_items += int64_t(groups) * s.nchunks;
-    if (s.nchunks > 1) {
-      n_merge += groups;
-      n_prow += int64_t(p.num_kv_heads) * s.nq * s.nchunks;
-      n_units += int64_t(p.num_kv_heads) * s.nq;
-      atomicAdd(&bucket[cost_bucket(chunk)], groups * (s.nchunks - 1));
+    for (int qt = 0; qt < s.ntq; ++qt) {
+      const int32_t pq1 = min(s.nq, (qt + 1) * tile), rows = pq1 - qt * tile;
+      const int32_t span = tile_span(p, s, qt * tile, pq1);
+      const int32_t nch = span_chunks(span, chunk);
+      const int32_t heads = p.num_kv_heads;
+      n_items += int64_t(heads) * nch;
+      if (nch > 1) {
+        n_merge += heads;
+        n_prow += int64_t(heads) * rows * nch;
+        n_units += int64_t(heads) * rows;
+        atomicAdd(&bucket[cost_bucket(chunk)], heads * (nch - 1));
+      }
+      const int64_t last_len = span - int64_t(nch - 1) * chunk;
+      atomicAdd(&bucket[cost_bucket(last_len)], heads);
     }
-    const int64_t last_len = s.kl - int64_t(s.nchunks - 1) * chunk;
-    atomicAdd(&bucket[cost_bucket(last_len)], groups);
   }
   int64_t tot_items, tot_merge, tot_prow, tot_units;
   int64_t off_item = block_exclusive_scan(n_items, warp_sums, &tot_items);
@@ -161,27 +184,29 @@ __global__ void __launch_bounds__(kDevPlanThreads) aspire_plan_device_kernel(Dev
   MergeDesc* merges = reinterpret_cast<MergeDesc*>(w + off_merges);
   int32_t* units = w + off_units;
   for (int b = r0; b < r1; ++b) {
-    const RowShape s = row_shape(p, b, tile, chunk);
+    const RowShape s = row_shape(p, b, tile);
     if (s.ql <= 0) continue;
     for (int h = 0; h < p.num_kv_heads; ++h) {
       for (int qt = 0; qt < s.ntq; ++qt) {
         const int32_t pq0 = qt * tile, pq1 = min(s.nq, pq0 + tile), rows = pq1 - pq0;
+        const int32_t span = tile_span(p, s, pq0, pq1);
+        const int32_t nch = span_chunks(span, chunk);
         int32_t merge_id = -1, pbase = 0;
-        if (s.nchunks > 1) {
+        if (nch > 1) {
           merge_id = int32_t(off_merge++);
           pbase = int32_t(off_prow);
-          off_prow += int64_t(s.nchunks) * rows;
+          off_prow += int64_t(nch) * rows;
           MergeDesc md{};
           md.q_start = p.qo_indptr[b];
           md.pq_begin = pq0;
           md.nrows = rows;
           md.kv_head = h;
           md.partial_base = pbase;
-          md.n_chunks = s.nchunks;
+          md.n_chunks = nch;
           merges[merge_id] = md;
           for (int j = 0; j < rows; ++j) units[off_unit++] = (merge_id << 8) | j;
         }
-        for (int c = 0; c < s.nchunks; ++c) {
+        for (int c = 0; c < nch; ++c) {
           WorkItem it{};
           it.row = b;
           it.kv_head = h;
@@ -189,12 +214,12 @@ __global__ void __launch_bounds__(kDevPlanThreads) aspire_plan_device_kernel(Dev
           it.q_len = s.ql;
           it.kv_page_base = p.kv_indptr[b];
           it.kv_len = s.kl;
-          it.tok_begin = int32_t(min(int64_t(c) * chunk, int64_t(s.kl)));
-          it.tok_end = int32_t(min(int64_t(c + 1) * chunk, int64_t(s.kl)));
+          it.tok_begin = int32_t(min(int64_t(c) * chunk, int64_t(span)));
+          it.tok_end = int32_t(min(int64_t(c + 1) * chunk, int64_t(span)));
           it.pq_begin = pq0;
           it.pq_end = pq1;
           it.chunk = c;
-          it.n_chunks = s.nchunks;
+          it.n_chunks = nch;
           it.partial_base = pbase;
           it.merge_id = merge_id;
           it.kind = 1;

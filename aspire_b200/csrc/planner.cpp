@@ -25,7 +25,23 @@ namespace {
 
 struct GroupDesc {
   int32_t row, kv_head, q_start, q_len, kv_page_base, kv_len, pq_begin, pq_end, kind;
+  int32_t span;  // KV tokens the tile can see: kv_len, or under the causal mask up to its last query
 };
+
+// Under the bottom-right causal mask the tile's last query (packed row
+// pq_end - 1) sees keys [0, kv_len - q_len + q_idx + 1); later keys are
+// masked for every query of the tile, so the tile's work stops there.  For a
+// decode row (one tile holding all queries) this is kv_len itself; for
+// long-query rows (prefill chunks) it skips the fully masked tiles.  The tile
+// holding query 0 keeps the whole range: the first/last logit dump records
+// query 0's raw logits at every key, masked or not.
+inline int32_t visible_span(int32_t kv_len, int32_t q_len, int32_t pq_begin, int32_t pq_end, int group,
+                            bool causal) {
+  if (!causal || pq_begin == 0) return kv_len;
+  const int64_t q_last = (pq_end - 1) / group;
+  const int64_t lim = int64_t(kv_len) - q_len + q_last + 1;
+  return static_cast<int32_t>(std::max<int64_t>(0, std::min<int64_t>(kv_len, lim)));
+}
 
 // Item cost in "tokens": the KV tokens streamed plus a fixed per-item
 // overhead covering setup, the first tile's reduction and the epilogue.
@@ -124,9 +140,11 @@ int plan_impl(const int32_t* qo_indptr, const int32_t* kv_indptr, const int32_t*
     const int tile = wide ? (kTcQTile / group) * group : kGatherQTile;
     for (int h = 0; h < num_kv_heads; ++h) {
       for (int p0 = 0; p0 < nq; p0 += tile) {
-        GroupDesc g{b, h, q0, ql, kv_indptr[b], kl, p0, std::min(nq, p0 + tile), wide ? 1 : 0};
+        const int32_t p1 = std::min(nq, p0 + tile);
+        GroupDesc g{b, h, q0, ql, kv_indptr[b], kl, p0, p1, wide ? 1 : 0,
+                    visible_span(kl, ql, p0, p1, group, causal != 0)};
         groups.push_back(g);
-        total_tokens += std::max<int32_t>(kl, 1);
+        total_tokens += std::max<int32_t>(g.span, 1);
       }
     }
   }
@@ -145,7 +163,7 @@ int plan_impl(const int32_t* qo_indptr, const int32_t* kv_indptr, const int32_t*
   int64_t partial_rows = 0;
   for (const GroupDesc& g : groups) {
     const int32_t n_chunks =
-        g.kv_len > 0 ? static_cast<int32_t>((g.kv_len + chunk - 1) / chunk) : 1;
+        g.span > 0 ? static_cast<int32_t>((g.span + chunk - 1) / chunk) : 1;
     const int32_t rows = g.pq_end - g.pq_begin;
     int32_t merge_id = -1, partial_base = 0;
     if (n_chunks > 1) {
@@ -172,8 +190,8 @@ int plan_impl(const int32_t* qo_indptr, const int32_t* kv_indptr, const int32_t*
       it.q_len = g.q_len;
       it.kv_page_base = g.kv_page_base;
       it.kv_len = g.kv_len;
-      it.tok_begin = static_cast<int32_t>(std::min<int64_t>(int64_t(c) * chunk, g.kv_len));
-      it.tok_end = static_cast<int32_t>(std::min<int64_t>(int64_t(c + 1) * chunk, g.kv_len));
+      it.tok_begin = static_cast<int32_t>(std::min<int64_t>(int64_t(c) * chunk, g.span));
+      it.tok_end = static_cast<int32_t>(std::min<int64_t>(int64_t(c + 1) * chunk, g.span));
       it.pq_begin = g.pq_begin;
       it.pq_end = g.pq_end;
       it.chunk = c;

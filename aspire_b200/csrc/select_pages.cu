@@ -16,7 +16,10 @@
 // then an index-ordered pick among the threshold ties).  The selected
 // block-table ids are sorted ascending and written in place with a zero tail,
 // as LMBackendBase._store_draft_rows (aspire/backends/base.py:1421-1471)
-// leaves the draft table.
+// leaves the draft table.  With order_by_page (given scores only) the last L
+// pages are not forced and the pages are listed in page order: with page-index
+// scores that is the recent-page seeding of
+// LMBackendBase._build_recent_draft_rows (base.py:1522-1537).
 #include "kernels.cuh"
 
 namespace aspire {
@@ -129,91 +132,25 @@ __global__ void __launch_bounds__(kSelThreads) aspire_select_pages_kernel(Select
   uint32_t* keys = reinterpret_cast<uint32_t*>(smem_raw);         // [pps]
   int32_t* sortbuf = reinterpret_cast<int32_t*>(keys + pps);      // [sort_cap]
   __shared__ uint32_t hist[256];
-  __shared__ float lse_s[2][kMaxSelHeads];
   __shared__ uint32_t sh_prefix, sh_remaining;
   __shared__ int sh_count;
   __shared__ int scan_buf[kSelThreads];
 
-  const int b = blockIdx.x;                              // output row
-  const int src_row = p.row_ids ? p.row_ids[b] : b;      // dump / qo_indptr row
+  const int b = blockIdx.x;  // output row
   const int tid = threadIdx.x;
   const int np = p.num_pages[b];
 
-  // ---------------- Phase 1: page scores ----------------
-  if (p.scores_in == nullptr) {
-    const int64_t max_q = p.lse_rows > 0 ? p.lse_rows - 1 : 0;
-    int64_t q_first = p.qo_indptr[src_row];
-    int64_t q_last = int64_t(p.qo_indptr[src_row + 1]) - 1;
-    q_first = q_first < 0 ? 0 : (q_first > max_q ? max_q : q_first);
-    q_last = q_last < 0 ? 0 : (q_last > max_q ? max_q : q_last);
-    for (int h = tid; h < p.num_heads; h += blockDim.x) {
-      lse_s[0][h] = p.lse[q_first * p.num_heads + h];
-      lse_s[1][h] = p.lse[q_last * p.num_heads + h];
-    }
-    __syncthreads();
-    for (int pg = tid; pg < pps; pg += blockDim.x) {
-      float tok[kPageSize];
-#pragma unroll
-      for (int i = 0; i < kPageSize; ++i) tok[i] = 0.f;
-      const int64_t t0 = int64_t(pg) * kPageSize;
-      if (t0 < p.max_seq_len) {
-        float mx[2][kPageSize];
-#pragma unroll
-        for (int s = 0; s < 2; ++s)
-#pragma unroll
-          for (int i = 0; i < kPageSize; ++i) mx[s][i] = -INFINITY;
-        const bool full = t0 + kPageSize <= p.max_seq_len;
-        for (int h = 0; h < p.num_heads; ++h) {
-#pragma unroll
-          for (int s = 0; s < 2; ++s) {
-            const __half* src = p.dump + ((int64_t(src_row) * p.num_heads + h) * 2 + s) * p.kv_stride + t0;
-            const float ls = lse_s[s][h];
-            __half vals[kPageSize];
-            if (full && (reinterpret_cast<uintptr_t>(src) & 15) == 0) {
-              *reinterpret_cast<uint4*>(vals) = reinterpret_cast<const uint4*>(src)[0];
-              *reinterpret_cast<uint4*>(vals + 8) = reinterpret_cast<const uint4*>(src)[1];
-            } else {
-#pragma unroll
-              for (int i = 0; i < kPageSize; ++i)
-                vals[i] = (t0 + i < p.max_seq_len) ? src[i] : __float2half_rn(-INFINITY);
-            }
-#pragma unroll
-            for (int i = 0; i < kPageSize; ++i) {
-              // fp16 * scalar is computed in fp32 and rounded back to fp16.
-              const float scaled = __half2float(__float2half_rn(__half2float(vals[i]) * p.scale_log2));
-              float n = scaled - ls;
-              if (isnan(n)) n = -INFINITY;
-              mx[s][i] = fmaxf(mx[s][i], exp2f(n));
-            }
-          }
-        }
-#pragma unroll
-        for (int i = 0; i < kPageSize; ++i)
-          tok[i] = (t0 + i < p.max_seq_len) ? (mx[0][i] + mx[1][i]) : 0.f;
-      }
-      // Pairwise sum of the 16 token scores.
-#pragma unroll
-      for (int w = kPageSize / 2; w >= 1; w >>= 1)
-#pragma unroll
-        for (int i = 0; i < w; ++i) tok[i] = tok[i] + tok[i + w];
-      const float bias = -(float(pg) * 1e-7f);
-      const float score = tok[0] + bias;
-      if (p.scores_out) p.scores_out[int64_t(b) * pps + pg] = score;
-      float forced = score;
-      const int last_start = max(np - p.L, 0);
-      if (pg >= last_start && pg < np) forced = INFINITY;
-      if (pg >= np) forced = -INFINITY;
-      keys[pg] = order_key(forced);
-    }
-  } else {
-    const int last_start = max(np - p.L, 0);
-    for (int pg = tid; pg < pps; pg += blockDim.x) {
-      float score = p.scores_in[int64_t(b) * pps + pg];
-      if (p.scores_out) p.scores_out[int64_t(b) * pps + pg] = score;
-      if (pg >= last_start && pg < np) score = INFINITY;
-      if (pg >= np) score = -INFINITY;
-      keys[pg] = order_key(score);
-    }
+  // ---------------- Phase 1: the row's page scores (from aspire_page_scores_kernel
+  // or the caller), forced and turned into order-preserving keys ----------------
+  // Recent-page seeding (order_by_page) ranks pages by the given scores
+  // alone: no forced trailing pages.
+  const int last_start = p.order_by_page ? np : max(np - p.L, 0);
+  for (int pg = tid; pg < pps; pg += blockDim.x) {
+    float score = p.scores_in[int64_t(b) * pps + pg];
+    if (p.scores_out) p.scores_out[int64_t(b) * pps + pg] = score;
+    if (pg >= last_start && pg < np) score = INFINITY;
+    if (pg >= np) score = -INFINITY;
+    keys[pg] = order_key(score);
   }
   __syncthreads();
 
@@ -309,7 +246,7 @@ __global__ void __launch_bounds__(kSelThreads) aspire_select_pages_kernel(Select
       }
       if (take) {
         const int slot = atomicAdd(&sh_count, 1);
-        if (slot < p.sort_cap) sortbuf[slot] = bt[min(i, p.block_table_cols - 1)];
+        if (slot < p.sort_cap) sortbuf[slot] = p.order_by_page ? i : bt[min(i, p.block_table_cols - 1)];
       }
     }
   }
@@ -339,8 +276,12 @@ __global__ void __launch_bounds__(kSelThreads) aspire_select_pages_kernel(Select
     }
   }
   int32_t* row_out = p.table_out + int64_t(b) * p.table_stride;
-  for (int c = tid; c < p.table_width; c += blockDim.x)
-    row_out[c] = (c < count && c < p.subset_cache_size) ? sortbuf[c] : 0;
+  for (int c = tid; c < p.table_width; c += blockDim.x) {
+    int32_t v = 0;
+    if (c < count && c < p.subset_cache_size)
+      v = p.order_by_page ? bt[min(sortbuf[c], p.block_table_cols - 1)] : sortbuf[c];
+    row_out[c] = v;
+  }
   if (tid == 0) p.counts_out[b] = reported;
 }
 

@@ -66,7 +66,7 @@ class PageSelectorFirstLastAvg:
         return torch.clamp(target, lo, hi)
 
     def _launch(self, *, dump, lse, qo_indptr, row_ids, scores_in, num_pages, block_table, batch,
-                table_out, table_width, counts_out, scores_out=None, status=None):
+                table_out, table_width, counts_out, scores_out=None, status=None, order_by_page=False):
         def ptr(t):
             return t.data_ptr() if t is not None else None
 
@@ -119,6 +119,7 @@ class PageSelectorFirstLastAvg:
         a.scores_out = ptr(scores_out)
         a.scores_ws = self._scores.data_ptr()
         a.status = ptr(status)
+        a.order_by_page = 1 if order_by_page else 0
         stream = torch.cuda.current_stream(self.device).cuda_stream
         _capi.check(self._lib.aspire_select_pages(ctypes.byref(a), ctypes.c_void_p(stream)),
                     "aspire_select_pages")
@@ -166,6 +167,37 @@ class PageSelectorFirstLastAvg:
                      num_pages=self._contig_i32(num_pages[ids]), block_table=self._contig_i32(block_table[ids]),
                      batch=n, table_out=sel, table_width=self.subset_cache_size, counts_out=counts)
         return sel, counts
+
+    def _index_scores(self) -> torch.Tensor:
+        """Page-index scores [max_batch, pages_per_slot] (static, built once)."""
+        if getattr(self, "_recent_scores", None) is None:
+            idx = torch.arange(self.pages_per_slot, dtype=torch.float32, device=self.device)
+            self._recent_scores = idx.expand(self._scores.shape[0], -1).contiguous()
+        return self._recent_scores
+
+    def seed_recent(self, num_pages: torch.Tensor, block_table: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
+        """Recent-page draft rows for rows with no verify signal yet: the last
+        ``compute_valid_counts(num_pages)`` pages of each row's block table in
+        page order, zero tail (``LMBackendBase._build_recent_draft_rows``,
+        aspire/backends/base.py:1522-1537).  One launch of the selection kernel
+        on page-index scores; returns ``(rows [n, k], valid_counts [n])``."""
+        n = num_pages.shape[0]
+        rows = torch.zeros(n, self.subset_cache_size, dtype=torch.int32, device=self.device)
+        counts = torch.zeros(n, dtype=torch.int32, device=self.device)
+        if n:
+            self.seed_recent_into(rows, counts, num_pages, block_table)
+        return rows, counts
+
+    def seed_recent_into(self, table: torch.Tensor, count_buffer: torch.Tensor, num_pages: torch.Tensor,
+                         block_table: torch.Tensor) -> None:
+        """``seed_recent`` written in place into rows [0, n) of ``table`` and
+        ``count_buffer`` (static buffers, so the call can be captured)."""
+        n = num_pages.shape[0]
+        if n > self._scores.shape[0]:
+            raise ValueError("more rows than max_batch_size")
+        self._launch(dump=None, lse=None, qo_indptr=None, row_ids=None, scores_in=self._index_scores(),
+                     num_pages=self._contig_i32(num_pages), block_table=block_table, batch=n, table_out=table,
+                     table_width=table.shape[1], counts_out=count_buffer, order_by_page=True)
 
     def finalize_scores(self, scores: torch.Tensor, num_pages: torch.Tensor,
                         block_table: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:

@@ -276,6 +276,12 @@ typedef struct AspireSelectArgs {
   float* scores_ws;         /* fp32 [batch, pages_per_slot] scratch for the page
                                scores; required when scores_in and scores_out are
                                both NULL                                           */
+  int32_t order_by_page;    /* 1 (with scores_in): the last L pages are not forced
+                               and a row lists its selected pages in page order;
+                               with page-index scores this is the recent-page
+                               seeding of LMBackendBase._build_recent_draft_rows
+                               (aspire/backends/base.py:1522-1537).  0: ascending
+                               block ids, as the replan path stores them          */
 } AspireSelectArgs;
 
 /*

@@ -121,3 +121,18 @@ def store_draft_rows(table: torch.Tensor, count_buffer: torch.Tensor, selected: 
         keep = torch.arange(n_cols)[None, :] < valid[:, None]
         staged[:, :n_cols] = torch.where(keep, selected[:, :n_cols].to(table.dtype), staged[:, :n_cols])
     table[:rows] = staged
+
+
+def recent_rows(num_pages, block_table, k, L, draft_percent=None, min_draft_pages=None):
+    """Recent-page draft rows (LMBackendBase._build_recent_draft_rows,
+    aspire/backends/base.py:1522-1537): valid = compute_valid_counts(num_pages);
+    row b lists block_table[b, num_pages[b] - valid[b] + j] for j < valid[b]
+    and zeros after, over k = max_draft_pages columns."""
+    num_pages = torch.as_tensor(num_pages).to(torch.int64)
+    valid = valid_counts(num_pages, k, L, draft_percent, min_draft_pages).to(torch.int64)
+    offsets = torch.arange(k, dtype=torch.int64)
+    start = (num_pages - valid).clamp(min=0)
+    pos = start[:, None] + offsets[None, :]
+    rows = torch.as_tensor(block_table).gather(1, pos.clamp(max=block_table.shape[1] - 1))
+    rows = torch.where(offsets[None, :] < valid[:, None], rows, torch.zeros_like(rows))
+    return rows.to(torch.int32), valid.to(torch.int32)

@@ -9,6 +9,8 @@ $ASPIRE_REFERENCE):
   aspire.backends.page_selector.PageSelectorFirstLastAvg.select (imported
   unchanged from the reference tree, run on CPU), including its page-score
   buffer before the +/-inf forcing; tie cases run its _finalize_scores.
+* recent_rows.pt : the reference's LMBackendBase._build_recent_draft_rows
+  (recent-page seeding of the draft table) on CPU.
 * unified_indices.pt : the reference's build_unified_indices
   (aspire/models/sparse_draft_runner.py, with its Triton _copy_indices_kernel)
   under the Triton CPU interpreter.
@@ -193,6 +195,42 @@ def indices_case():
                    check=True, env=env)
 
 
+def recent_case():
+    """Recent-page seeding: the reference's LMBackendBase._build_recent_draft_rows
+    (imported unchanged) on a scattered block table; the bound instance carries
+    the attributes the method reads, with _get_num_pages the documented
+    ceil(seq_len / page_size) (aspire/models/mixed_runner.py:114-120)."""
+    import types
+
+    sys.path.insert(0, str(REF))
+    from aspire.backends.base import LMBackendBase  # noqa: E402
+
+    sel_cls = _ref_selector_cls()
+    out = {}
+    for name, (k, L, pct, mdp) in {"budget": (16, 4, None, None), "pct": (32, 8, 7.0, None),
+                                    "floor": (32, 8, None, 12)}.items():
+        B, pps, page = 9, 64, 16
+        g = torch.Generator().manual_seed(len(name) * 7)
+        cachelens = torch.tensor([0, 1, 16, 17, 100, 400, 1000, 1024, 555], dtype=torch.int64)
+        # The engine's tables are wider than the longest row (the method gathers
+        # k columns from the first recent page), so give the table that headroom.
+        width = pps + k
+        block_table = torch.stack([torch.randperm(width, generator=g) + r * width for r in range(B)]).to(torch.int32)
+        selector = sel_cls(max_batch_size=B, pages_per_slot=pps, subset_cache_size=k, L=L, n_heads=2, page_size=page,
+                           max_seq_length=pps * page, device="cpu", bsz=B, dec_len=1, draft_percent=pct,
+                           min_draft_pages=mdp)
+        fake = types.SimpleNamespace(device=torch.device("cpu"), cachelens=cachelens, page_selector=selector,
+                                     max_draft_pages=k, target_block_table=block_table,
+                                     _get_num_pages=lambda s: (s + page - 1) // page)
+        slots = torch.arange(B)
+        rows, valid = LMBackendBase._build_recent_draft_rows(fake, slots)
+        out[name] = {"params": dict(k=k, L=L, draft_percent=pct, min_draft_pages=mdp, pps=pps, B=B),
+                     "num_pages": ((cachelens + page - 1) // page).to(torch.int32), "block_table": block_table,
+                     "rows": rows.to(torch.int32), "valid": valid.to(torch.int32)}
+        print("recent", name, valid.tolist())
+    torch.save(out, HERE / "recent_rows.pt")
+
+
 def main():
     if not REF.exists():
         raise SystemExit(f"reference tree {REF} not found")
@@ -211,6 +249,7 @@ def main():
     tie_case()
     append_case()
     indices_case()
+    recent_case()
 
 
 if __name__ == "__main__":

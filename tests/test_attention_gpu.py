@@ -31,6 +31,19 @@ def test_config1_refresh_dump(cuda_device):
     assert_dump_close(dump, ref_dump, lay, stride)
 
 
+def test_refresh_dump_multi_tile_rows(cuda_device):
+    """The dump of rows whose packed queries span several tiles (q_len 20 and
+    30 at group 4): query 0's logits are recorded at every key, also in
+    planners that stop later tiles at their causal span."""
+    lay = _custom_layout(q_lens=[20, 1, 30], kv_lens=[700, 300, 1030], hq=32, hkv=8, seed=9)
+    q, kv = make_inputs(lay, cuda_device, seed=9)
+    stride = 1040
+    out, lse, dump, _ = run_attention(lay, q, kv, dump=True, dump_stride=stride)
+    ref_out, ref_lse, ref_dump = oracle_attention(lay, q, kv, dump_stride=stride)
+    assert_attention_close(out, lse, ref_out, ref_lse)
+    assert_dump_close(dump, ref_dump, lay, stride)
+
+
 @pytest.mark.parametrize("hq,hkv", [(32, 8), (16, 8), (8, 1), (4, 2)])
 @pytest.mark.parametrize("draft_fraction", [0.0, 0.5, 1.0])
 def test_mixed_ragged_split_kv(cuda_device, hq, hkv, draft_fraction):
@@ -75,6 +88,18 @@ def test_edge_rows(cuda_device):
     r0, r1 = int(lay.qo_indptr[1]), int(lay.qo_indptr[2])
     assert out[r0:r1].abs().max().item() == 0.0
     assert torch.isinf(lse[r0:r1]).all()
+
+
+@pytest.mark.parametrize("hq,hkv", [(32, 8), (16, 8), (40, 8)])
+def test_prefill_rows(cuda_device, hq, hkv):
+    """Long-query causal rows (prefill chunks, with and without a cached
+    prefix, and one shorter than its chunk): each query tile of a row stops at
+    its causal span, and the tiles of one row are planned independently."""
+    lay = _custom_layout(q_lens=[200, 77, 300, 1, 13], kv_lens=[200, 1077, 350, 900, 9], hq=hq, hkv=hkv, seed=7)
+    q, kv = make_inputs(lay, cuda_device, seed=7)
+    out, lse, _, _ = run_attention(lay, q, kv)
+    ref_out, ref_lse, _ = oracle_attention(lay, q, kv)
+    assert_attention_close(out, lse, ref_out, ref_lse)
 
 
 def test_long_context_rows(cuda_device):

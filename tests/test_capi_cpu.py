@@ -121,3 +121,20 @@ def test_plan_handles_empty_and_padding_rows(built_library):
     rows = {it["row"] for it in items}
     assert rows == {1, 2}
     assert all(it["tok_begin"] == it["tok_end"] == 0 for it in items if it["row"] == 1)
+
+
+def test_plan_clips_causal_tiles_to_their_span(built_library):
+    """A prefill row (q_len 600 over 600 keys, 12 queries per tile at group 4):
+    tile i > 0 covers keys [0, 12 * (i + 1)); the tile holding query 0 keeps
+    all keys (the dump records its raw logits everywhere)."""
+    rc, info, buf = _plan(built_library, [0, 600], [0, 38], [600], 32, 8, num_sms=148)
+    assert rc == 0, built_library.aspire_last_error()
+    _, items = _decode(buf, info)
+    span = {}
+    for it in items:
+        key = (it["kv_head"], it["pq_begin"])
+        span[key] = max(span.get(key, 0), it["tok_end"])
+        assert it["tok_begin"] <= it["tok_end"]
+    for (h, pq0), end in span.items():
+        q_last = (min(pq0 + 48, 600 * 4) - 1) // 4
+        assert end == (600 if pq0 == 0 else q_last + 1), (h, pq0, end)

@@ -185,3 +185,15 @@ def test_prologue_oracle_matches_flashinfer_rope_golden(golden_dir):
             # Tokens outside the rows are not rotated.
             tail = int(indptr[-1])
             assert torch.equal(got[tail:], x[tail:]) and torch.equal(ref[tail:], x[tail:])
+
+
+def test_recent_rows_oracle_matches_reference_golden(golden_dir):
+    """Recent-page seeding restated against the reference's own
+    _build_recent_draft_rows (budget, draft_percent and floor variants)."""
+    g = _load(golden_dir, "recent_rows.pt")
+    for name, c in g.items():
+        p = c["params"]
+        rows, valid = oracle_sel.recent_rows(c["num_pages"], c["block_table"], p["k"], p["L"], p["draft_percent"],
+                                             p["min_draft_pages"])
+        assert torch.equal(valid, c["valid"]), name
+        assert torch.equal(rows, c["rows"]), name

@@ -55,11 +55,31 @@ def _host_plan(lay, num_sms):
     return buf.view(np.int32)
 
 
-@pytest.mark.parametrize("hq,hkv,draft_fraction", [(32, 8, 0.5), (16, 8, 0.0), (32, 4, 1.0), (40, 8, 0.5)])
+def _prefill_layout(hq, hkv):
+    """Prefill chunks: long queries over a cached prefix (several query tiles
+    per row, each clipped to its causal span)."""
+    q_lens = [600, 77, 1300, 1, 40]
+    kv_lens = [600, 2077, 1400, 500, 40]
+    lay = make_layout(batch=len(q_lens), ctx=2100, num_qo_heads=hq, num_kv_heads=hkv, draft_fraction=0.0,
+                      budget_pages=8, seed=44)
+    lay.q_lens = np.array(q_lens, np.int32)
+    lay.kv_lens = np.array(kv_lens, np.int32)
+    lay.qo_indptr = np.concatenate([[0], np.cumsum(q_lens)]).astype(np.int32)
+    pages = [(k + 15) // 16 for k in kv_lens]
+    lay.kv_indptr = np.concatenate([[0], np.cumsum(pages)]).astype(np.int32)
+    lay.kv_indices = np.concatenate([lay.block_table[r, :pages[r]] for r in range(len(q_lens))]).astype(np.int32)
+    return lay
+
+
+@pytest.mark.parametrize("hq,hkv,draft_fraction", [(32, 8, 0.5), (16, 8, 0.0), (32, 4, 1.0), (40, 8, 0.5),
+                                                   (32, 8, "prefill"), (40, 8, "prefill")])
 def test_device_plan_matches_host_plan(cuda_device, hq, hkv, draft_fraction):
     dev = cuda_device
-    lay = make_layout(batch=23, ctx=9000, num_qo_heads=hq, num_kv_heads=hkv, draft_fraction=draft_fraction,
-                      budget_pages=48, seed=41)
+    if draft_fraction == "prefill":
+        lay = _prefill_layout(hq, hkv)
+    else:
+        lay = make_layout(batch=23, ctx=9000, num_qo_heads=hq, num_kv_heads=hkv, draft_fraction=draft_fraction,
+                          budget_pages=48, seed=41)
     num_sms = torch.cuda.get_device_properties(dev).multi_processor_count
     w = HolisticAttentionWrapper(torch.empty(1, device=dev))
     t = lambda a: torch.from_numpy(np.ascontiguousarray(a, dtype=np.int32)).to(dev)  # noqa: E731

@@ -111,3 +111,19 @@ def test_select_subset_rows(cuda_device, golden_dir):
                                            g["block_table"].to(dev), g["qo_indptr"].to(dev))
     assert torch.equal(got_sel.cpu(), g["selected"][[2, 0]])
     assert torch.equal(got_valid.cpu(), g["valid"][[2, 0]])
+
+
+@pytest.mark.parametrize("case", ["budget", "pct", "floor"])
+def test_seed_recent_matches_reference_golden(cuda_device, golden_dir, case):
+    """Recent-page seeding through the selection kernel (page-index scores,
+    page-order rows) against the reference's _build_recent_draft_rows."""
+    c = torch.load(golden_dir / "recent_rows.pt", weights_only=False)[case]
+    p = c["params"]
+    sel = PageSelectorFirstLastAvg(max_batch_size=p["B"], pages_per_slot=p["pps"], subset_cache_size=p["k"],
+                                   L=p["L"], n_heads=2, page_size=16, max_seq_length=p["pps"] * 16,
+                                   device=cuda_device, bsz=p["B"], dec_len=1, draft_percent=p["draft_percent"],
+                                   min_draft_pages=p["min_draft_pages"])
+    rows, valid = sel.seed_recent(c["num_pages"].to(cuda_device), c["block_table"].to(cuda_device))
+    torch.cuda.synchronize()
+    assert torch.equal(valid.cpu(), c["valid"])
+    assert torch.equal(rows.cpu(), c["rows"])
