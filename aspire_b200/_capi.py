@@ -49,6 +49,7 @@ class AspirePlanInfo(ctypes.Structure):
         ("max_q_len", ctypes.c_int32),
         ("tc_enabled", ctypes.c_int32),
         ("on_device", ctypes.c_int32),
+        ("num_items_prefill", ctypes.c_int32),
     ]
 
 
@@ -249,7 +250,7 @@ _SIGNATURES = {
     "aspire_kernel_names": (ctypes.c_char_p, []),
 }
 
-EXPECTED_ABI_VERSION = 2
+EXPECTED_ABI_VERSION = 3
 
 _lib = None
 _lock = threading.Lock()

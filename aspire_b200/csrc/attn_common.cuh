@@ -24,7 +24,8 @@ struct AttnParams {
   int64_t dump_num_heads, dump_kv_stride;
   float scale_log2;          // sm_scale * log2(e)
   int32_t num_qo_heads, num_kv_heads, group;
-  int32_t q_box_tokens;      // tokens per query-tile TMA box (tcgen05 kernel)
+  int32_t q_box_tokens;      // tokens per query-tile TMA box (tcgen05 kernel, decode phase)
+  int32_t pf_box_tokens;     // the same for the prefill phase
   int64_t q_rows;            // rows of q and out: plan rows past them are skipped (BAD_ROW)
   const int32_t* plan;       // int workspace + kStatusBytes
   uint32_t* status;          // int workspace (first word)

@@ -188,6 +188,12 @@ __global__ void __launch_bounds__(kThreads, kGatherCtasPerSm) aspire_attn_gather
           for (int j = 0; j < kQT; ++j) s[j] += __shfl_xor_sync(0xffffffffu, s[j], off);
         }
         const bool in_chunk = tok >= it.tok_begin && tok < it.tok_end;
+        // A page's slots past the row's last token may hold anything (NaN
+        // included); their weight is zero and so must be their values.
+        if (!in_chunk) {
+#pragma unroll
+          for (int d = 0; d < 8; ++d) vf[u][d] = 0.f;
+        }
         if (p.dump != nullptr && in_chunk && tok < p.dump_kv_stride) {
 #pragma unroll
           for (int j = 0; j < kQT; ++j) {

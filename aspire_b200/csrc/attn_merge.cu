@@ -11,7 +11,7 @@
 // chunks are always combined in chunk order, so the result is deterministic.
 // The grid is fixed and the work list comes from the device plan, so a
 // captured graph stays valid across re-plans.  It also rearms the tcgen05
-// kernel's item counter.
+// kernel's item counters.
 #include "kernels.cuh"
 
 namespace aspire {
@@ -20,9 +20,12 @@ __global__ void __launch_bounds__(kMergeThreads) aspire_attn_merge_kernel(AttnPa
   pdl_begin();
   const int32_t* plan = p.plan;
   if (plan[kHdrMagic] != kPlanMagic) return;
-  // The tcgen05 kernel of this call has finished: rearm its item counter for
+  // The tcgen05 kernel of this call has finished: rearm its item counters for
   // the next launch of the same plan (graph replays upload no new plan).
-  if (blockIdx.x == 0 && threadIdx.x == 0) const_cast<int32_t*>(plan)[kHdrTcClaim] = 0;
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    const_cast<int32_t*>(plan)[kHdrTcClaim] = 0;
+    const_cast<int32_t*>(plan)[kHdrPfClaim] = 0;
+  }
   const int num_units = plan[kHdrNumMergeUnits];
   if (num_units == 0) return;
   const MergeDesc* descs = reinterpret_cast<const MergeDesc*>(plan + plan[kHdrOffMerge]);

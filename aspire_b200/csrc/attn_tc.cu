@@ -35,34 +35,39 @@
 // ASPIRE_STATUS_TIMEOUT, stops, drains its own TMA loads and MMAs, frees
 // TMEM and returns.
 //
+// The same launch then serves the plan's prefill list (long-query rows; see
+// attn_prefill.cuh): a CTA that finds the decode list exhausted waits for its
+// own decode work to drain and switches roles in place (same warps, same
+// item-sequence ring, prefill buffers over the decode buffers, 512 TMEM
+// columns allocated once), so batches without prefill rows pay no extra
+// launch and mixed batches need no second grid.
+//
 // Semantics are those of the gather kernel (FlashInfer's persistent paged
 // attention as ASPIRE drives it): bottom-right causal mask, base-2 LSE of the
 // scaled logits, fp16 first/last logit dump of the raw q.k.
 #include <cuda.h>
 
+#include "attn_prefill.cuh"
 #include "kernels.cuh"
+#include "tc_pipeline.cuh"
 #include "tc_ptx.cuh"
 
 namespace aspire {
 
 namespace {
 
+using namespace pipe;
+
 constexpr int kTcThreads = 352;
 constexpr int kFirstSoftmaxWarp = 2;  // warps 2-5: softmax group 0, warps 6-9: group 1
 constexpr int kVProducerWarp = 10;
-constexpr int kSeqDepth = 8;          // item-sequence ring (claimed items in flight per CTA)
 constexpr int kSeqReaders = 10;       // V producer, MMA warp and the 8 softmax warps
-constexpr int kTile = 128;
-constexpr int kPagesPerTile = kTile / kPageSize;
 constexpr int kKStages = 2;
 constexpr int kVStages = 3;
 constexpr int kNMax = kTcQTile;
-constexpr uint32_t kTmemCols = 256;
-constexpr uint32_t kHalfBytes = kTile * 128;       // 128 rows x 128 B (64 dims)
-constexpr uint32_t kSlotBytes = 2 * kHalfBytes;    // one K or V tile: two 64-dim halves
+constexpr uint32_t kTmemCols = pf::kTmemCols;  // the decode phase uses [0, 256)
 constexpr uint32_t kQHalfBytes = kNMax * 128;
 constexpr uint32_t kPBufBytes = (kNMax / 8) * kTile * 16;
-constexpr uint64_t kWaitLimitNs = 1000000000ull;   // 1 s: far above any legitimate wait
 constexpr float kLazyLog2 = 8.0f;                  // max growth tolerated before a rescale
 
 __host__ __device__ constexpr uint32_t col_s(int b) { return uint32_t(b) * 64u; }
@@ -85,45 +90,16 @@ struct TcShared {
   uint64_t v_full[kVStages], v_empty[kVStages];
   uint64_t s_full[2], s_empty[2], p_full[2], p_empty[2];
   uint64_t o_free, q_full, q_empty, done, grp[2];
+  pf::Barriers pf;  // prefill phase
   uint64_t seq_full[kSeqDepth], seq_empty[kSeqDepth];
   int seq[kSeqDepth];
   uint32_t tmem_base;
   int abort_flag;
 };
 static_assert(sizeof(TcShared) + 1024 <= 227 * 1024, "tcgen05 kernel shared memory too large");
+// The prefill phase's buffers overlay the decode phase's data buffers only.
+static_assert(sizeof(pf::Buffers) <= offsetof(TcShared, red), "prefill buffers overlap decode state");
 static_assert(kNMax % 16 == 0 && kNMax <= 64, "N tile must be a multiple of 16 and fit a 64-column buffer");
-
-__device__ __forceinline__ uint64_t global_ns() {
-  uint64_t t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
-
-// Bounded wait on an mbarrier phase.  Returns false (and stops the CTA) when
-// the phase does not complete within kWaitLimitNs or another role aborted.
-__device__ __forceinline__ bool wait_bar(TcShared& sm, uint64_t& bar, uint32_t parity, uint32_t* status) {
-  const uint32_t a = ptx::smem_addr(&bar);
-  if (ptx::mbar_try_wait(a, parity)) return true;
-  const uint64_t t0 = global_ns();
-  for (uint32_t i = 1;; ++i) {
-    if (ptx::mbar_try_wait(a, parity)) return true;
-    if (*reinterpret_cast<volatile int*>(&sm.abort_flag)) return false;
-    if ((i & 255) == 0 && global_ns() - t0 > kWaitLimitNs) break;
-  }
-  *reinterpret_cast<volatile int*>(&sm.abort_flag) = 1;
-  if (status) atomicOr(status, ASPIRE_STATUS_TIMEOUT);
-  return false;
-}
-
-// Wait used while draining after an abort: ignores the abort flag, still bounded.
-__device__ __forceinline__ void drain_bar(uint64_t& bar, uint32_t parity) {
-  const uint32_t a = ptx::smem_addr(&bar);
-  const uint64_t t0 = global_ns();
-  for (uint32_t i = 1;; ++i) {
-    if (ptx::mbar_try_wait(a, parity)) return;
-    if ((i & 255) == 0 && global_ns() - t0 > kWaitLimitNs) return;
-  }
-}
 
 // Barrier of one softmax warpgroup's 128 threads on an mbarrier (bounded, so that a thread
 // that stopped on a timeout cannot leave the others blocked).
@@ -134,153 +110,10 @@ __device__ __forceinline__ bool group_sync(TcShared& sm, uint64_t& grp, uint32_t
   return wait_bar(sm, grp, parity, status);
 }
 
-__device__ __forceinline__ int n_tiles_of(const WorkItem& it) {
-  return it.tok_end > it.tok_begin ? (it.tok_end - it.tok_begin + kTile - 1) / kTile : 0;
-}
-
-// Items every role skips identically (the planner never emits them).
-__device__ __forceinline__ bool item_valid(const AttnParams& p, const WorkItem& it) {
-  const int nrows = it.pq_end - it.pq_begin;
-  return nrows > 0 && nrows <= kNMax && it.kv_head >= 0 && it.kv_head < p.num_kv_heads &&
-         it.tok_begin >= 0 && it.tok_begin % kTile == 0 && it.tok_end <= it.kv_len;
-}
-
-__device__ __forceinline__ bool aborted(TcShared& sm) {
-  return *reinterpret_cast<volatile int*>(&sm.abort_flag) != 0;
-}
-
-// ------------------------------------------------------------------ item sequence
-// The CTAs share the plan's tcgen05 item list and claim items from it at run
-// time, longest first (a global counter in the plan header).  In each CTA the
-// K producer claims an item when it is ready to load it and publishes the
-// index (-1 once the list is exhausted) in a small ring; the other roles read
-// the same sequence in order.  Every warp reads through its lane 0, which
-// returns -2 when a wait times out.
-__device__ __forceinline__ int seq_claim(const AttnParams& p, TcShared& sm, uint32_t& k, int lane, int tc_first,
-                                         int n_tc) {
-  int item = -2;
-  if (lane == 0) {
-    const int s = int(k % kSeqDepth);
-    if (wait_bar(sm, sm.seq_empty[s], ((k / kSeqDepth) & 1) ^ 1, p.status)) {
-      const int c = atomicAdd(const_cast<int32_t*>(p.plan) + kHdrTcClaim, 1);
-      item = c < n_tc ? tc_first + c : -1;
-      *reinterpret_cast<volatile int*>(&sm.seq[s]) = item;
-      ptx::mbar_arrive(ptx::smem_addr(&sm.seq_full[s]));
-    }
-  }
-  ++k;
-  return __shfl_sync(0xffffffffu, item, 0);
-}
-
-__device__ __forceinline__ int seq_read(TcShared& sm, uint32_t& k, int lane, uint32_t* status) {
-  int item = -2;
-  if (lane == 0) {
-    const int s = int(k % kSeqDepth);
-    if (wait_bar(sm, sm.seq_full[s], (k / kSeqDepth) & 1, status)) {
-      item = *reinterpret_cast<volatile int*>(&sm.seq[s]);
-      ptx::mbar_arrive(ptx::smem_addr(&sm.seq_empty[s]));
-    }
-  }
-  ++k;
-  return __shfl_sync(0xffffffffu, item, 0);
-}
-
-// ------------------------------------------------------------------ producers
-// Lane pg (< 8) owns page pg of every tile: it reads the page id one tile
-// ahead (the read overlaps the wait for a free slot) and issues the page's two
-// 64-dim boxes of K (kv_sel 0) or V (kv_sel 1) into the ring slot.
-template <int STAGES>
-__device__ void run_producer(const AttnParams& p, const CUtensorMap* tmap, TcShared& sm,
-                             uint8_t (*ring)[kSlotBytes], uint64_t* full, uint64_t* empty, int kv_sel,
-                             bool leader, int tc_first, int n_tc, int lane) {
-  uint32_t g = 0, k = 0;
-  int64_t last_issue[STAGES];
-#pragma unroll
-  for (int s = 0; s < STAGES; ++s) last_issue[s] = -1;
-  bool ok = true;
-  while (ok) {
-    const int ii = leader ? seq_claim(p, sm, k, lane, tc_first, n_tc) : seq_read(sm, k, lane, p.status);
-    if (ii == -2) ok = false;
-    if (ii < 0) break;
-    const WorkItem it = load_item(p.plan, ii);
-    if (!item_valid(p, it)) continue;
-    const int nt = n_tiles_of(it);
-    const int first_page = it.tok_begin / kPageSize;
-    const int end_page = (it.tok_end + kPageSize - 1) / kPageSize;
-    auto page_id = [&](int t) -> int32_t {
-      const int lp = first_page + t * kPagesPerTile + lane;
-      if (lane >= kPagesPerTile || lp >= end_page) return -1;
-      return row_page(p.kv_indices, it.kv_page_base, p.mode_flags, p.draft_table, p.draft_stride, p.block_table,
-                      p.block_table_stride, it.row, lp);
-    };
-    int32_t next_id = nt > 0 ? page_id(0) : -1;
-    for (int t = 0; t < nt; ++t, ++g) {
-      const int32_t id = next_id;
-      if (t + 1 < nt) next_id = page_id(t + 1);
-      const int s = g % STAGES;
-      const uint32_t ph = (g / STAGES) & 1;
-      if (!wait_bar(sm, empty[s], ph ^ 1, p.status)) {
-        ok = false;
-        break;
-      }
-      const uint32_t fb = ptx::smem_addr(&full[s]);
-      if (lane == 0) ptx::mbar_arrive_expect_tx(fb, kSlotBytes);
-      __syncwarp();
-      if (lane < kPagesPerTile) {
-        int page = static_cast<int>(p.num_pages_total);  // out of range: TMA fills zeros
-        const int lp = first_page + t * kPagesPerTile + lane;
-        if (lp < end_page) {
-          if (id < 0 || int64_t(id) >= p.num_pages_total)
-            record_status(p.status, ASPIRE_STATUS_BAD_PAGE);
-          else
-            page = id;
-        }
-        const uint32_t base = ptx::smem_addr(ring[s]) + uint32_t(lane) * kPageSize * 128;
-        ptx::tma_load_5d(base, tmap, fb, 0, it.kv_head, 0, kv_sel, page);
-        ptx::tma_load_5d(base + kHalfBytes, tmap, fb, 64, it.kv_head, 0, kv_sel, page);
-      }
-      last_issue[s] = g;
-      __syncwarp();
-    }
-  }
-  if (!ok || aborted(sm)) {
-    // Let this CTA's own copies land before the CTA releases its shared memory.
-#pragma unroll
-    for (int s = 0; s < STAGES; ++s)
-      if (last_issue[s] >= 0) drain_bar(full[s], uint32_t(last_issue[s] / STAGES) & 1);
-  }
-}
-
 // ------------------------------------------------------------------ MMA issuer
-// Next item of the sequence that has KV tiles (the roles skip the same items);
-// -1 at the end of the sequence, -2 on a timeout.
-__device__ __forceinline__ int next_tc_item(const AttnParams& p, TcShared& sm, uint32_t& k, int lane) {
-  for (;;) {
-    const int ii = seq_read(sm, k, lane, p.status);
-    if (ii < 0) return ii;
-    const WorkItem it = load_item(p.plan, ii);
-    if (item_valid(p, it) && n_tiles_of(it) > 0) return ii;
-  }
-}
-
-// Requests item `idx`'s query tile: one box of (64 dims x group heads x
-// q_box_tokens tokens, at most kNMax rows) per 64-dim half, starting at the
-// item's first query.
-// Rows past the item's queries are other queries or zero fill; they only feed
-// ignored columns.
-__device__ __forceinline__ void issue_q(const AttnParams& p, const CUtensorMap* qmap, TcShared& sm, int idx) {
-  const WorkItem it = load_item(p.plan, idx);
-  const int q_idx0 = it.pq_begin / p.group;
-  const uint32_t bytes = 2u * 128u * uint32_t(p.group) * uint32_t(p.q_box_tokens);
-  const uint32_t bar = ptx::smem_addr(&sm.q_full);
-  ptx::mbar_arrive_expect_tx(bar, bytes);
-  ptx::tma_load_3d(ptx::smem_addr(sm.q[0]), qmap, bar, 0, it.kv_head * p.group, it.q_start + q_idx0);
-  ptx::tma_load_3d(ptx::smem_addr(sm.q[1]), qmap, bar, 64, it.kv_head * p.group, it.q_start + q_idx0);
-}
-
-__device__ void run_mma(const AttnParams& p, const CUtensorMap* qmap, TcShared& sm, int lane) {
+__device__ void run_mma(const AttnParams& p, const CUtensorMap* qmap, TcShared& sm, int lane, uint32_t& k) {
   const uint32_t tmem = sm.tmem_base;
-  uint32_t g = 0, items_done = 0, k = 0;
+  uint32_t g = 0, items_done = 0;
   bool ok = true;
   const uint32_t k0 = ptx::smem_addr(sm.k[0]);
   const uint32_t v0 = ptx::smem_addr(sm.v[0]);
@@ -288,10 +121,13 @@ __device__ void run_mma(const AttnParams& p, const CUtensorMap* qmap, TcShared& 
   const uint32_t p0 = ptx::smem_addr(sm.p[0]);
   bool q_pending = false;  // a query-tile load is in flight
 
-  // PV of global tile u; `first` marks the item's first tile (fresh accumulator).
-  auto issue_pv = [&](uint32_t u, bool first, uint32_t idesc_pv) -> bool {
+  // PV of global tile u; `first` marks the item's first tile (fresh
+  // accumulator), `valid` is the count of the tile's tokens in the item.
+  auto issue_pv = [&](uint32_t u, bool first, int valid, uint32_t idesc_pv) -> bool {
     if (first && !wait_bar(sm, sm.o_free, (items_done & 1) ^ 1, p.status)) return false;
     if (!wait_bar(sm, sm.v_full[u % kVStages], (u / kVStages) & 1, p.status)) return false;
+    clear_v_tail(sm.v[u % kVStages], valid, lane);
+    __syncwarp();
     if (!wait_bar(sm, sm.p_full[u % 2], (u / 2) & 1, p.status)) return false;
     ptx::tc_fence_after();
     if (lane == 0) {
@@ -310,10 +146,10 @@ __device__ void run_mma(const AttnParams& p, const CUtensorMap* qmap, TcShared& 
     return true;
   };
 
-  int ii = next_tc_item(p, sm, k, lane);
+  int ii = next_item_with_tiles(p, sm, k, lane, kNMax);
   if (ii == -2) ok = false;
   if (ii >= 0) {
-    if (lane == 0) issue_q(p, qmap, sm, ii);
+    if (lane == 0) issue_q(p, qmap, sm, ii, p.q_box_tokens);
     q_pending = true;
   }
   while (ii >= 0 && ok) {
@@ -352,11 +188,12 @@ __device__ void run_mma(const AttnParams& p, const CUtensorMap* qmap, TcShared& 
         if (t == nt - 1) ptx::mma_commit(ptx::smem_addr(&sm.q_empty));
       }
       __syncwarp();
-      if (t > 0 && !issue_pv(g - 1, g - 1 == g0, idesc_pv)) ok = false;
+      if (t > 0 && !issue_pv(g - 1, g - 1 == g0, it.tok_end - (it.tok_begin + (t - 1) * kTile), idesc_pv))
+        ok = false;
     }
     if (!ok) break;
     // The next item's query tile loads while this item's last PV and epilogue run.
-    const int nxt = next_tc_item(p, sm, k, lane);
+    const int nxt = next_item_with_tiles(p, sm, k, lane, kNMax);
     if (nxt == -2) {
       ok = false;
       break;
@@ -366,11 +203,11 @@ __device__ void run_mma(const AttnParams& p, const CUtensorMap* qmap, TcShared& 
         ok = false;
         break;
       }
-      if (lane == 0) issue_q(p, qmap, sm, nxt);
+      if (lane == 0) issue_q(p, qmap, sm, nxt, p.q_box_tokens);
       q_pending = true;
       __syncwarp();
     }
-    if (!issue_pv(g - 1, g - 1 == g0, idesc_pv)) ok = false;
+    if (!issue_pv(g - 1, g - 1 == g0, it.tok_end - (it.tok_begin + (nt - 1) * kTile), idesc_pv)) ok = false;
     ++items_done;
     ii = nxt;
   }
@@ -742,19 +579,19 @@ __device__ bool consume_item(const AttnParams& p, TcShared& sm, const WorkItem& 
   return true;
 }
 
-__device__ void consume_items(const AttnParams& p, TcShared& sm, bool causal, int warp, int lane) {
+__device__ void consume_items(const AttnParams& p, TcShared& sm, bool causal, int warp, int lane, uint32_t& k) {
   const int wq = warp & 3;
   const int wg = (warp - kFirstSoftmaxWarp) / 4;  // softmax warpgroup 0 or 1
   const int r = wq * 32 + lane;                    // TMEM lane = S-tile token = O-tile dim
   const int ctid = (warp - kFirstSoftmaxWarp - 4 * wg) * 32 + lane;  // 0..127 within the group
-  uint32_t g = 0, grp_uses = 0, k = 0;
+  uint32_t g = 0, grp_uses = 0;
   for (;;) {
     if (aborted(sm)) return;
     const int ii = seq_read(sm, k, lane, p.status);
     if (ii < 0) return;
     const WorkItem it = load_item(p.plan, ii);
     const int nrows = it.pq_end - it.pq_begin;
-    if (!item_valid(p, it)) {
+    if (!item_valid(p, it, kNMax)) {
       if (ctid == 0 && wg == 0) record_status(p.status, ASPIRE_STATUS_BAD_PLAN);
       continue;
     }
@@ -775,8 +612,8 @@ __device__ void consume_items(const AttnParams& p, TcShared& sm, bool causal, in
   }
 }
 
-__device__ void run_consumer(const AttnParams& p, TcShared& sm, bool causal, int warp, int lane) {
-  consume_items(p, sm, causal, warp, lane);
+__device__ void run_consumer(const AttnParams& p, TcShared& sm, bool causal, int warp, int lane, uint32_t& k) {
+  consume_items(p, sm, causal, warp, lane, k);
   // The bulk stores of each group's last item (issued by its thread 0) finish
   // before the CTA exits.
   if (lane == 0 && (warp - kFirstSoftmaxWarp) % 4 == 0) ptx::bulk_wait_all();
@@ -786,17 +623,20 @@ __device__ void run_consumer(const AttnParams& p, TcShared& sm, bool causal, int
 
 __global__ void __launch_bounds__(kTcThreads, 1)
     aspire_attn_tc_kernel(AttnParams p, const __grid_constant__ CUtensorMap tmap,
-                          const __grid_constant__ CUtensorMap qmap) {
+                          const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap qmap_pf) {
   pdl_begin();
   extern __shared__ __align__(1024) uint8_t tc_smem_raw[];
   const uint32_t raw = ptx::smem_addr(tc_smem_raw);
   TcShared& sm = *reinterpret_cast<TcShared*>(tc_smem_raw + ((1024 - (raw & 1023)) & 1023));
+  pf::Buffers& pbuf = *reinterpret_cast<pf::Buffers*>(&sm);
   const int32_t* plan = p.plan;
   if (plan[kHdrMagic] != kPlanMagic) return;
   if (int(blockIdx.x) >= plan[kHdrNumTcCtas]) return;
   const int tc_first = plan[kHdrTcFirst];
-  const int n_tc = plan[kHdrNumItems] - tc_first;
-  if (n_tc <= 0) return;
+  const int pf_first = plan[kHdrPfFirst];
+  const int n_tc = pf_first - tc_first;
+  const int n_pf = plan[kHdrNumItems] - pf_first;
+  if (n_tc <= 0 && n_pf <= 0) return;
   const bool causal = plan[kHdrCausal] != 0;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
@@ -821,6 +661,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     ptx::mbar_init(ptx::smem_addr(&sm.done), 1);
     ptx::mbar_init(ptx::smem_addr(&sm.grp[0]), 128);
     ptx::mbar_init(ptx::smem_addr(&sm.grp[1]), 128);
+    pf::init_barriers(sm.pf);
     for (int s = 0; s < kSeqDepth; ++s) {
       ptx::mbar_init(ptx::smem_addr(&sm.seq_full[s]), 1);
       ptx::mbar_init(ptx::smem_addr(&sm.seq_empty[s]), kSeqReaders);
@@ -833,7 +674,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     ptx::tmem_relinquish();
   }
   if (warp == 0 && lane == 0) ptx::prefetch_tmap(&tmap);
-  if (warp == 1 && lane == 0) ptx::prefetch_tmap(&qmap);
+  if (warp == 1 && lane == 0) {
+    ptx::prefetch_tmap(&qmap);
+    ptx::prefetch_tmap(&qmap_pf);
+  }
   // Query rows that no load writes (when kNMax is not a multiple of the group)
   // stay zero.
   for (int i = threadIdx.x; i < int(sizeof(sm.q) / 16); i += blockDim.x)
@@ -843,14 +687,44 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   __syncthreads();
   ptx::tc_fence_after();
 
-  if (warp == 0) {
-    run_producer<kKStages>(p, &tmap, sm, sm.k, sm.k_full, sm.k_empty, 0, true, tc_first, n_tc, lane);
-  } else if (warp == kVProducerWarp) {
-    run_producer<kVStages>(p, &tmap, sm, sm.v, sm.v_full, sm.v_empty, 1, false, tc_first, n_tc, lane);
-  } else if (warp == 1) {
-    run_mma(p, &qmap, sm, lane);
-  } else {
-    run_consumer(p, sm, causal, warp, lane);
+  // Both phases read one item sequence (the ring of claimed item indices);
+  // each warp keeps its position across the phase change.
+  uint32_t k = 0;
+  // Phase 1: the decode list.
+  if (n_tc > 0) {
+    if (warp == 0) {
+      run_producer<kKStages>(p, &tmap, sm, sm.k, sm.k_full, sm.k_empty, 0, true, tc_first, n_tc, kHdrTcClaim, kNMax,
+                             lane, k);
+    } else if (warp == kVProducerWarp) {
+      run_producer<kVStages>(p, &tmap, sm, sm.v, sm.v_full, sm.v_empty, 1, false, tc_first, n_tc, kHdrTcClaim,
+                             kNMax, lane, k);
+    } else if (warp == 1) {
+      run_mma(p, &qmap, sm, lane, k);
+    } else {
+      run_consumer(p, sm, causal, warp, lane, k);
+    }
+  }
+  // Phase 2: the prefill list, in the same shared memory and TMEM.  Every
+  // copy, MMA and bulk store of phase 1 has completed (each role drained its
+  // own) before any role passes this barrier.
+  if (n_pf > 0) {
+    ptx::fence_proxy_async_smem();
+    ptx::tc_fence_before();
+    __syncthreads();
+    ptx::tc_fence_after();
+    if (!aborted(sm)) {
+      if (warp == 0) {
+        run_producer<pf::kKStages>(p, &tmap, sm, pbuf.k, sm.pf.k_full, sm.pf.k_empty, 0, true, pf_first, n_pf,
+                                   kHdrPfClaim, kPfMaxRows, lane, k);
+      } else if (warp == kVProducerWarp) {
+        run_producer<pf::kVStages>(p, &tmap, sm, pbuf.v, sm.pf.v_full, sm.pf.v_empty, 1, false, pf_first, n_pf,
+                                   kHdrPfClaim, kPfMaxRows, lane, k);
+      } else if (warp == 1) {
+        pf::run_mma(p, &qmap_pf, sm, pbuf, lane, k);
+      } else {
+        pf::consume_items(p, sm, causal, (warp - kFirstSoftmaxWarp) / 4, warp & 3, lane, k);
+      }
+    }
   }
 
   ptx::tc_fence_before();

@@ -236,6 +236,7 @@ int aspire_plan_device(const int32_t* qo_indptr, const int32_t* kv_indptr, const
   info->max_q_len = -1;
   info->tc_enabled = 1;
   info->on_device = 1;
+  info->num_items_prefill = -1;
   return ASPIRE_OK;
 }
 
@@ -328,6 +329,7 @@ int aspire_mixed_attention(const AspireAttnArgs* a, const AspirePlanInfo* plan, 
   p.num_kv_heads = a->num_kv_heads;
   p.group = group;
   p.q_box_tokens = static_cast<int32_t>(std::min<int64_t>(kTcQTile / group, a->q_rows));
+  p.pf_box_tokens = static_cast<int32_t>(std::min<int64_t>(kPfQTile / group, a->q_rows));
   p.q_rows = a->q_rows;
   p.plan = reinterpret_cast<const int32_t*>(static_cast<const char*>(a->int_ws) + kStatusBytes);
   p.status = static_cast<uint32_t*>(a->int_ws);
@@ -365,8 +367,12 @@ int aspire_mixed_attention(const AspireAttnArgs* a, const AspirePlanInfo* plan, 
     rc = encode_q_tensor_map(&qmap, a->q, a->q_rows, a->num_qo_heads, a->q_stride_n, a->q_stride_h, group,
                              p.q_box_tokens);
     if (rc) return rc;
+    alignas(64) CUtensorMap qmap_pf;
+    rc = encode_q_tensor_map(&qmap_pf, a->q, a->q_rows, a->num_qo_heads, a->q_stride_n, a->q_stride_h, group,
+                             p.pf_box_tokens);
+    if (rc) return rc;
     rc = launch(aspire_attn_tc_kernel, dim3(plan->num_ctas * kTcCtasPerSm), dim3(tc_threads()), smem, st,
-                "aspire_attn_tc_kernel launch", p, tmap, qmap);
+                "aspire_attn_tc_kernel launch", p, tmap, qmap, qmap_pf);
     if (rc) return rc;
   }
   // Split-KV merge (exits at once when the current plan split nothing).

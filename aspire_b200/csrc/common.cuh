@@ -25,7 +25,7 @@ enum PlanHeader : int {
   kHdrNumItems = 1,
   kHdrNumGatherCtas = 2,     // grid of the gather kernel the list was built for
   kHdrOffGatherIndptr = 3,   // int32 index of gather CTA indptr [num_ctas + 1]
-  kHdrTcFirst = 4,           // index of the first tcgen05 item; they run to kHdrNumItems
+  kHdrTcFirst = 4,           // index of the first tcgen05 decode item; they run to kHdrPfFirst
   kHdrOffItems = 5,          // int32 index of the item array
   kHdrOffMerge = 6,          // int32 index of the merge descriptors [num_merge]
   kHdrNumMerge = 7,
@@ -36,7 +36,9 @@ enum PlanHeader : int {
   kHdrOffMergeUnits = 12,    // int32 index of the merge units [num_merge_units]
   kHdrNumMergeUnits = 13,    // (merge group, packed row) pairs, one warp each
   kHdrTcClaim = 14,          // tcgen05 items claimed so far (0 at upload; the merge kernel resets it)
-  kHdrWords = 16,
+  kHdrPfFirst = 15,          // index of the first prefill item; they run to kHdrNumItems
+  kHdrPfClaim = 16,          // prefill items claimed so far (same rule as kHdrTcClaim)
+  kHdrWords = 32,
 };
 constexpr int32_t kPlanMagic = 0x41535042;  // "ASPB"
 
@@ -56,7 +58,7 @@ struct WorkItem {
   int32_t n_chunks;
   int32_t partial_base;  // partial row of chunk 0 of the merge group
   int32_t merge_id;      // merge descriptor index, -1 when n_chunks == 1
-  int32_t kind;          // 0 = CUDA-core gather kernel, 1 = tcgen05 kernel
+  int32_t kind;          // 0 = CUDA-core gather kernel, 1 = tcgen05 decode kernel, 2 = prefill kernel
   int32_t reserved;
 };
 static_assert(sizeof(WorkItem) == 64, "WorkItem must stay 64 bytes");
@@ -87,5 +89,14 @@ constexpr int kTcCtasPerSm = 1;
 constexpr int kGatherQTile = 4;
 // Packed query rows handled by one tcgen05 item (N of the MMA after padding).
 constexpr int kTcQTile = 48;
+// Prefill items: two halves of up to kPfQTile packed query rows (the M of
+// the MMA), whole query positions per half, sharing every K/V tile.  Rows
+// with at least kPfMinRows packed query rows (long queries: prefill chunks)
+// go to the prefill phase of the tcgen05 kernel.
+constexpr int kPfQTile = 128;
+constexpr int kPfMinRows = 128;
+constexpr int kPfMaxRows = 2 * kPfQTile;
+__host__ __device__ constexpr int pf_half_rows(int group) { return (kPfQTile / group) * group; }
+__host__ __device__ constexpr int pf_item_rows(int group) { return 2 * pf_half_rows(group); }
 
 }  // namespace aspire

@@ -118,7 +118,8 @@ constexpr int kMaxSelHeads = 128;
 
 __global__ void aspire_attn_gather_kernel(AttnParams p);
 __global__ void aspire_attn_tc_kernel(AttnParams p, const __grid_constant__ CUtensorMap tmap,
-                                      const __grid_constant__ CUtensorMap qmap);
+                                      const __grid_constant__ CUtensorMap qmap,
+                                      const __grid_constant__ CUtensorMap qmap_pf);
 constexpr int kMergeThreads = 128;
 constexpr int kMergeCtasPerSm = 4;
 __global__ void aspire_attn_merge_kernel(AttnParams p);

@@ -7,10 +7,11 @@
 // It produces the same items as the host planner (planner.cpp): every
 // (row, KV head, packed-query tile) is cut into chunks of one common length
 // (a multiple of 128 tokens, at least 512, sized for ~4 items per SM), with
-// merge descriptors for the split groups.  All rows go to the tcgen05 kernel
-// (the default routing); items are stored longest first through a counting
-// sort on their length in 128-token tiles, the order in which the persistent
-// CTAs claim them.  One CTA of 1024 threads; each thread owns a contiguous run
+// merge descriptors for the split groups.  Rows go to the tcgen05 decode
+// kernel, or to the prefill kernel when their packed queries reach
+// kPfMinRows (the default routing); each list is stored longest first through
+// a counting sort on item length in 128-token tiles, the order in which the
+// persistent CTAs claim them.  One CTA of 1024 threads; each thread owns a contiguous run
 // of rows.  An invalid input row or a plan larger than the workspaces sets
 // ASPIRE_STATUS_BAD_PLAN and leaves a plan with no magic, which every kernel
 // skips.
@@ -51,7 +52,7 @@ __device__ int64_t block_exclusive_scan(int64_t v, int64_t* warp_sums, int64_t* 
 }
 
 struct RowShape {
-  int32_t ql, kl, nq, ntq;
+  int32_t ql, kl, nq, ntq, tile, kind;  // kind 1: tcgen05 decode kernel, 2: prefill kernel
   bool valid;
 };
 
@@ -70,7 +71,7 @@ __device__ __forceinline__ int32_t span_chunks(int32_t span, int64_t chunk) {
   return span > 0 ? int32_t((span + chunk - 1) / chunk) : 1;
 }
 
-__device__ __forceinline__ RowShape row_shape(const DevPlanParams& p, int b, int tile) {
+__device__ __forceinline__ RowShape row_shape(const DevPlanParams& p, int b) {
   RowShape r{};
   const int32_t ql = p.qo_indptr[b + 1] - p.qo_indptr[b];
   const int32_t pages = p.kv_indptr[b + 1] - p.kv_indptr[b];
@@ -80,7 +81,9 @@ __device__ __forceinline__ RowShape row_shape(const DevPlanParams& p, int b, int
   r.ql = r.valid ? ql : 0;
   r.kl = r.valid ? kl : 0;
   r.nq = r.ql * p.group;
-  r.ntq = (r.nq + tile - 1) / tile;
+  r.kind = r.nq >= kPfMinRows ? 2 : 1;
+  r.tile = r.kind == 2 ? pf_item_rows(p.group) : (kTcQTile / p.group) * p.group;
+  r.ntq = (r.nq + r.tile - 1) / r.tile;
   return r;
 }
 
@@ -94,24 +97,23 @@ __device__ __forceinline__ int cost_bucket(int64_t tokens) {
 __global__ void __launch_bounds__(kDevPlanThreads) aspire_plan_device_kernel(DevPlanParams p) {
   pdl_begin();
   __shared__ int64_t warp_sums[32];
-  __shared__ int32_t bucket[kCostBuckets];
+  __shared__ int32_t bucket[2][kCostBuckets];  // per kernel list: decode (1), prefill (2)
   __shared__ int bad;
   const int tid = threadIdx.x, nthreads = blockDim.x;
   if (tid == 0) bad = 0;
-  for (int i = tid; i < kCostBuckets; i += nthreads) bucket[i] = 0;
+  for (int i = tid; i < 2 * kCostBuckets; i += nthreads) bucket[i / kCostBuckets][i % kCostBuckets] = 0;
   __syncthreads();
-  const int tile = (kTcQTile / p.group) * p.group;
   const int rpt = (p.batch + nthreads - 1) / nthreads;  // rows per thread
   const int r0 = min(tid * rpt, p.batch), r1 = min(r0 + rpt, p.batch);
 
   // Total tokens over (row, head, q-tile) groups -> the common chunk length.
   int64_t tokens = 0;
   for (int b = r0; b < r1; ++b) {
-    const RowShape s = row_shape(p, b, tile);
+    const RowShape s = row_shape(p, b);
     if (!s.valid) bad = 1;
     if (s.ql <= 0) continue;
     for (int qt = 0; qt < s.ntq; ++qt) {
-      const int32_t span = tile_span(p, s, qt * tile, min(s.nq, (qt + 1) * tile));
+      const int32_t span = tile_span(p, s, qt * s.tile, min(s.nq, (qt + 1) * s.tile));
       tokens += int64_t(p.num_kv_heads) * (span > 1 ? span : 1);
     }
   }
@@ -125,11 +127,12 @@ __global__ void __launch_bounds__(kDevPlanThreads) aspire_plan_device_kernel(Dev
   // Per-thread counts; item lengths into the cost histogram.
   int64_t n_items = 0, n_merge = 0, n_prow = 0, n_units = 0;
   for (int b = r0; b < r1; ++b) {
-    const RowShape s = row_shape(p, b, tile);
+    const RowShape s = row_shape(p, b);
     if (s.ql <= 0) continue;
+    int32_t* hist = bucket[s.kind - 1];
     for (int qt = 0; qt < s.ntq; ++qt) {
-      const int32_t pq1 = min(s.nq, (qt + 1) * tile), rows = pq1 - qt * tile;
-      const int32_t span = tile_span(p, s, qt * tile, pq1);
+      const int32_t pq1 = min(s.nq, (qt + 1) * s.tile), rows = pq1 - qt * s.tile;
+      const int32_t span = tile_span(p, s, qt * s.tile, pq1);
       const int32_t nch = span_chunks(span, chunk);
       const int32_t heads = p.num_kv_heads;
       n_items += int64_t(heads) * nch;
@@ -137,10 +140,10 @@ __global__ void __launch_bounds__(kDevPlanThreads) aspire_plan_device_kernel(Dev
         n_merge += heads;
         n_prow += int64_t(heads) * rows * nch;
         n_units += int64_t(heads) * rows;
-        atomicAdd(&bucket[cost_bucket(chunk)], heads * (nch - 1));
+        atomicAdd(&hist[cost_bucket(chunk)], heads * (nch - 1));
       }
       const int64_t last_len = span - int64_t(nch - 1) * chunk;
-      atomicAdd(&bucket[cost_bucket(last_len)], heads);
+      atomicAdd(&hist[cost_bucket(last_len)], heads);
     }
   }
   int64_t tot_items, tot_merge, tot_prow, tot_units;
@@ -149,14 +152,17 @@ __global__ void __launch_bounds__(kDevPlanThreads) aspire_plan_device_kernel(Dev
   int64_t off_merge = block_exclusive_scan(n_merge, warp_sums, &tot_merge);
   int64_t off_prow = block_exclusive_scan(n_prow, warp_sums, &tot_prow);
   int64_t off_unit = block_exclusive_scan(n_units, warp_sums, &tot_units);
-  // Bucket starts, longest first: start[k] = items in buckets above k.
-  {
+  // Bucket starts, longest first within each list; the decode list comes
+  // first, the prefill list after it: start[k] = items in buckets above k.
+  int64_t n_decode = 0;
+  for (int list = 0; list < 2; ++list) {
     int64_t mine = 0, tot;
     const int k = kCostBuckets - 1 - tid;
-    if (tid < kCostBuckets) mine = bucket[k];
+    if (tid < kCostBuckets) mine = bucket[list][k];
     __syncthreads();
     const int64_t start = block_exclusive_scan(mine, warp_sums, &tot);
-    if (tid < kCostBuckets) bucket[k] = int32_t(start);
+    if (tid < kCostBuckets) bucket[list][k] = int32_t(start + (list == 1 ? n_decode : 0));
+    if (list == 0) n_decode = tot;
     __syncthreads();
   }
 
@@ -184,11 +190,12 @@ __global__ void __launch_bounds__(kDevPlanThreads) aspire_plan_device_kernel(Dev
   MergeDesc* merges = reinterpret_cast<MergeDesc*>(w + off_merges);
   int32_t* units = w + off_units;
   for (int b = r0; b < r1; ++b) {
-    const RowShape s = row_shape(p, b, tile);
+    const RowShape s = row_shape(p, b);
     if (s.ql <= 0) continue;
+    int32_t* slots = bucket[s.kind - 1];
     for (int h = 0; h < p.num_kv_heads; ++h) {
       for (int qt = 0; qt < s.ntq; ++qt) {
-        const int32_t pq0 = qt * tile, pq1 = min(s.nq, pq0 + tile), rows = pq1 - pq0;
+        const int32_t pq0 = qt * s.tile, pq1 = min(s.nq, pq0 + s.tile), rows = pq1 - pq0;
         const int32_t span = tile_span(p, s, pq0, pq1);
         const int32_t nch = span_chunks(span, chunk);
         int32_t merge_id = -1, pbase = 0;
@@ -222,8 +229,8 @@ __global__ void __launch_bounds__(kDevPlanThreads) aspire_plan_device_kernel(Dev
           it.n_chunks = nch;
           it.partial_base = pbase;
           it.merge_id = merge_id;
-          it.kind = 1;
-          const int slot = atomicAdd(&bucket[cost_bucket(it.tok_end - it.tok_begin)], 1);
+          it.kind = s.kind;
+          const int slot = atomicAdd(&slots[cost_bucket(it.tok_end - it.tok_begin)], 1);
           items[slot] = it;
         }
       }
@@ -247,6 +254,8 @@ __global__ void __launch_bounds__(kDevPlanThreads) aspire_plan_device_kernel(Dev
     w[kHdrPartialLseLo] = int32_t(lse_off & 0xffffffff);
     w[kHdrPartialLseHi] = int32_t(lse_off >> 32);
     w[kHdrTcClaim] = 0;
+    w[kHdrPfFirst] = int32_t(n_decode);
+    w[kHdrPfClaim] = 0;
     w[kHdrMagic] = kPlanMagic;
   }
 }

@@ -137,11 +137,15 @@ int plan_impl(const int32_t* qo_indptr, const int32_t* kv_indptr, const int32_t*
     // so that one TMA box loads it.
     const bool wide = tc_enabled && group <= kTcQTile &&
                       (nq > kGatherQTile || nq >= tc_min_rows || kl >= tc_min_kv);
-    const int tile = wide ? (kTcQTile / group) * group : kGatherQTile;
+    // Long queries (prefill chunks) go to the prefill phase: items of two
+    // 128-row halves (whole query positions each) that share every K/V tile.
+    const bool prefill = wide && nq >= kPfMinRows;
+    const int tile = prefill ? pf_item_rows(group) : wide ? (kTcQTile / group) * group : kGatherQTile;
+    const int kind = prefill ? 2 : (wide ? 1 : 0);
     for (int h = 0; h < num_kv_heads; ++h) {
       for (int p0 = 0; p0 < nq; p0 += tile) {
         const int32_t p1 = std::min(nq, p0 + tile);
-        GroupDesc g{b, h, q0, ql, kv_indptr[b], kl, p0, p1, wide ? 1 : 0,
+        GroupDesc g{b, h, q0, ql, kv_indptr[b], kl, p0, p1, kind,
                     visible_span(kl, ql, p0, p1, group, causal != 0)};
         groups.push_back(g);
         total_tokens += std::max<int32_t>(g.span, 1);
@@ -156,7 +160,7 @@ int plan_impl(const int32_t* qo_indptr, const int32_t* kv_indptr, const int32_t*
   chunk = std::max<int64_t>(chunk, 512);
   chunk = (chunk + 127) / 128 * 128;
 
-  std::vector<WorkItem> gather_items, tc_items;
+  std::vector<WorkItem> gather_items, tc_items, pf_items;
   std::vector<MergeDesc> merges;
   std::vector<int32_t> merge_units;  // (merge index << 8) | packed row within the tile
   int32_t num_merge = 0;
@@ -199,7 +203,7 @@ int plan_impl(const int32_t* qo_indptr, const int32_t* kv_indptr, const int32_t*
       it.partial_base = partial_base;
       it.merge_id = merge_id;
       it.kind = g.kind;
-      (g.kind ? tc_items : gather_items).push_back(it);
+      (g.kind == 2 ? pf_items : g.kind == 1 ? tc_items : gather_items).push_back(it);
     }
   }
 
@@ -209,9 +213,12 @@ int plan_impl(const int32_t* qo_indptr, const int32_t* kv_indptr, const int32_t*
   std::vector<WorkItem> gather_ordered;
   assign_lpt(gather_items, gather_ctas, gather_indptr, gather_ordered);
   order_by_cost(tc_items);
-  const std::vector<WorkItem>& tc_ordered = tc_items;
-  // The tcgen05 list is stored after the gather list in one item array.
+  order_by_cost(pf_items);
+  std::vector<WorkItem> tc_ordered = tc_items;
+  tc_ordered.insert(tc_ordered.end(), pf_items.begin(), pf_items.end());
+  // One item array: gather list | tcgen05 decode list | prefill list.
   const int32_t n_gather = static_cast<int32_t>(gather_ordered.size());
+  const int32_t n_decode_tc = static_cast<int32_t>(tc_items.size());
   const int32_t num_items = n_gather + static_cast<int32_t>(tc_ordered.size());
 
   // Layout (int32 words): header | gather indptr | items | merges | merge units.
@@ -243,6 +250,8 @@ int plan_impl(const int32_t* qo_indptr, const int32_t* kv_indptr, const int32_t*
   w[kHdrOffGatherIndptr] = static_cast<int32_t>(off_gather);
   w[kHdrTcFirst] = n_gather;
   w[kHdrTcClaim] = 0;
+  w[kHdrPfFirst] = n_gather + n_decode_tc;
+  w[kHdrPfClaim] = 0;
   w[kHdrOffItems] = static_cast<int32_t>(off_items);
   w[kHdrOffMerge] = static_cast<int32_t>(off_merge);
   w[kHdrNumMerge] = num_merge;
@@ -263,7 +272,8 @@ int plan_impl(const int32_t* qo_indptr, const int32_t* kv_indptr, const int32_t*
   std::memset(info, 0, sizeof(*info));
   info->num_items = num_items;
   info->num_items_gather = n_gather;
-  info->num_items_tc = num_items - n_gather;
+  info->num_items_tc = n_decode_tc;
+  info->num_items_prefill = static_cast<int32_t>(pf_items.size());
   info->num_ctas = num_sms;
   info->num_merge = num_merge;
   info->chunk_tokens = static_cast<int32_t>(chunk);

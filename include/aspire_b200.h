@@ -41,7 +41,7 @@
 extern "C" {
 #endif
 
-#define ASPIRE_B200_ABI_VERSION 2
+#define ASPIRE_B200_ABI_VERSION 3
 
 #define ASPIRE_OK 0
 #define ASPIRE_ERR_INVALID (-1)  /* bad argument (shape, size, alignment)       */
@@ -70,7 +70,7 @@ extern "C" {
 typedef struct AspirePlanInfo {
   int32_t num_items;        /* work items over all kernel classes            */
   int32_t num_items_gather; /* items for the CUDA-core gather kernel         */
-  int32_t num_items_tc;     /* items for the tcgen05 kernel                  */
+  int32_t num_items_tc;     /* decode items for the tcgen05 kernel           */
   int32_t num_ctas;         /* persistent grid of each kernel class          */
   int32_t num_merge;        /* (row, kv-head, q-tile) groups split over chunks */
   int32_t chunk_tokens;     /* KV tokens per split-KV chunk                   */
@@ -86,6 +86,9 @@ typedef struct AspirePlanInfo {
   int32_t on_device;        /* 1 when aspire_plan_device rendered the plan: the
                                counts above are then upper bounds (int_bytes and
                                float_bytes the workspace capacities) or -1      */
+  int32_t num_items_prefill;/* prefill items for the tcgen05 kernel (rows of
+                               at least 128 packed query rows: prefill chunks,
+                               up to 256 packed rows per item)                 */
 } AspirePlanInfo;
 
 /*
@@ -302,7 +305,8 @@ ASPIRE_API int aspire_select_pages(const AspireSelectArgs* args, void* stream);
  * (aspire/attention/holistic_wrapper.py:200-342) and the HostPlanState upload
  * (aspire/backends/host_plan.py:154-306).  kv_len of row b is
  * max(pages_b - 1, 0) * 16 + last_page_len[b], as in plan().  Every row goes
- * to the tcgen05 kernel (the default routing; other routing thresholds are
+ * to the tcgen05 kernel, as a decode item or, with 128 or more packed query
+ * rows, a prefill item (the default routing; other routing thresholds are
  * rejected).  A malformed row or a plan beyond the workspaces is reported as
  * ASPIRE_STATUS_BAD_PLAN on the device (the kernels then skip the plan).
  * `info` receives the grid, the heads and the workspace capacities.

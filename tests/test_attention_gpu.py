@@ -102,6 +102,50 @@ def test_prefill_rows(cuda_device, hq, hkv):
     assert_attention_close(out, lse, ref_out, ref_lse)
 
 
+@pytest.mark.parametrize("hq,hkv", [(32, 8), (8, 8), (48, 8), (64, 8)])
+def test_prefill_items_halves_chunks_and_dump(cuda_device, hq, hkv):
+    """Prefill items (rows of >= 128 packed query rows) next to decode items
+    in one launch: two-half items, single-half tail items, a long cached
+    prefix split into KV chunks merged on device, groups that do not divide
+    128 (group 6: halves of 126 rows), and the first/last logit dump."""
+    lay = _custom_layout(q_lens=[700, 150, 40, 1, 260], kv_lens=[5000, 150, 2100, 3000, 900], hq=hq, hkv=hkv,
+                         seed=21)
+    q, kv = make_inputs(lay, cuda_device, seed=21)
+    stride = 5008
+    out, lse, dump, w = run_attention(lay, q, kv, dump=True, dump_stride=stride)
+    assert w.plan_info.num_items_prefill > 0 or not w.plan_info.tc_enabled
+    ref_out, ref_lse, ref_dump = oracle_attention(lay, q, kv, dump_stride=stride)
+    assert_attention_close(out, lse, ref_out, ref_lse)
+    assert_dump_close(dump, ref_dump, lay, stride)
+
+
+@pytest.mark.parametrize("causal", [True, False])
+def test_prefill_rows_mask_modes(cuda_device, causal):
+    """Prefill rows with and without the causal mask (a chunk of 300 queries
+    after a 500-token prefix, and a row whose keys are fewer than its queries)."""
+    lay = _custom_layout(q_lens=[300, 64, 200], kv_lens=[800, 64, 130], hq=32, hkv=8, seed=13)
+    q, kv = make_inputs(lay, cuda_device, seed=13)
+    out, lse, _, _ = run_attention(lay, q, kv, causal=causal)
+    ref_out, ref_lse, _ = oracle_attention(lay, q, kv, causal=causal)
+    assert_attention_close(out, lse, ref_out, ref_lse)
+
+
+def test_nan_in_unused_page_slots(cuda_device):
+    """A page's slots past a row's last token may hold anything: NaN there
+    (zero weight) must not reach the output, on the decode and prefill paths."""
+    lay = _custom_layout(q_lens=[1, 5, 300, 2, 40], kv_lens=[17, 1000, 333, 130, 77], hq=32, hkv=8, seed=4)
+    q, kv = make_inputs(lay, cuda_device, seed=4)
+    for r in range(lay.batch):
+        n = int(lay.kv_lens[r])
+        if n % 16:
+            page = int(lay.kv_indices[int(lay.kv_indptr[r + 1]) - 1])
+            kv[page, :, n % 16:] = float("nan")
+    out, lse, _, _ = run_attention(lay, q, kv)
+    ref_out, ref_lse, _ = oracle_attention(lay, q, kv)
+    assert torch.isfinite(out.float()).all()
+    assert_attention_close(out, lse, ref_out, ref_lse)
+
+
 def test_long_context_rows(cuda_device):
     lay = make_layout(batch=3, ctx=32768 + 7, num_qo_heads=32, num_kv_heads=8, draft_fraction=0.34,
                       budget_pages=128, seed=11)

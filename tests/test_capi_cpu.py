@@ -27,7 +27,7 @@ def test_library_exports_every_declared_symbol(built_library):
     for name in declared:
         assert hasattr(built_library, name), name
     assert set(declared) == set(_capi.exported_symbols())
-    assert built_library.aspire_abi_version() == _capi.EXPECTED_ABI_VERSION == 2
+    assert built_library.aspire_abi_version() == _capi.EXPECTED_ABI_VERSION == 3
     assert built_library.aspire_status_offset() == 256
 
 
@@ -78,11 +78,15 @@ def test_plan_covers_every_token_once(built_library, draft_fraction):
                 assert ranges[0][0] == 0 and ranges[-1][1] == int(lay.kv_lens[b])
                 for (a0, a1), (b0, b1) in zip(ranges, ranges[1:]):
                     assert a1 == b0
-    # tcgen05 items follow the CUDA-core items, longest first (claimed in that
-    # order at run time); the claim counter starts at zero.
-    assert w[4] == info.num_items_gather and w[14] == 0
-    tc_cost = [it["tok_end"] - it["tok_begin"] for it in items[info.num_items_gather:]]
-    assert all(a >= b for a, b in zip(tc_cost, tc_cost[1:]))
+    # tcgen05 decode items follow the CUDA-core items, then the prefill items;
+    # each list longest first (claimed in that order at run time); the claim
+    # counters start at zero.
+    assert w[4] == info.num_items_gather and w[14] == 0 and w[16] == 0
+    assert w[15] == info.num_items_gather + info.num_items_tc
+    assert w[1] == w[15] + info.num_items_prefill
+    for lo, hi in ((w[4], w[15]), (w[15], w[1])):
+        cost = [it["tok_end"] - it["tok_begin"] for it in items[lo:hi]]
+        assert all(a >= b for a, b in zip(cost, cost[1:]))
     # CTA indptrs partition the CUDA-core item list.
     g_ctas = w[2]
     g_indptr = w[w[3]: w[3] + g_ctas + 1]
@@ -123,18 +127,28 @@ def test_plan_handles_empty_and_padding_rows(built_library):
     assert all(it["tok_begin"] == it["tok_end"] == 0 for it in items if it["row"] == 1)
 
 
-def test_plan_clips_causal_tiles_to_their_span(built_library):
-    """A prefill row (q_len 600 over 600 keys, 12 queries per tile at group 4):
-    tile i > 0 covers keys [0, 12 * (i + 1)); the tile holding query 0 keeps
-    all keys (the dump records its raw logits everywhere)."""
-    rc, info, buf = _plan(built_library, [0, 600], [0, 38], [600], 32, 8, num_sms=148)
+@pytest.mark.parametrize("q_len,group", [(600, 4), (130, 1), (45, 3), (17, 8)])
+def test_plan_clips_causal_tiles_to_their_span(built_library, q_len, group):
+    """A prefill row (q_len queries over as many keys): prefill items of two
+    halves of (128 // group) query positions each; item i > 0 covers keys up
+    to its last query's; the item holding query 0 keeps all keys (the dump
+    records its raw logits everywhere)."""
+    kvh = 2
+    pages = (q_len + 15) // 16
+    rc, info, buf = _plan(built_library, [0, q_len], [0, pages], [q_len], kvh * group, kvh, num_sms=148)
     assert rc == 0, built_library.aspire_last_error()
-    _, items = _decode(buf, info)
+    w, items = _decode(buf, info)
+    nq = q_len * group
+    item_rows = 2 * (128 // group) * group
+    assert info.num_items_tc == 0 and info.num_items_prefill == len(items) and w[15] == 0
     span = {}
     for it in items:
+        assert it["kind"] == 2 and it["pq_begin"] % item_rows == 0
+        assert it["pq_end"] == min(it["pq_begin"] + item_rows, nq)
         key = (it["kv_head"], it["pq_begin"])
         span[key] = max(span.get(key, 0), it["tok_end"])
         assert it["tok_begin"] <= it["tok_end"]
+    assert len(span) == kvh * ((nq + item_rows - 1) // item_rows)
     for (h, pq0), end in span.items():
-        q_last = (min(pq0 + 48, 600 * 4) - 1) // 4
-        assert end == (600 if pq0 == 0 else q_last + 1), (h, pq0, end)
+        q_last = (min(pq0 + item_rows, nq) - 1) // group
+        assert end == (q_len if pq0 == 0 else q_last + 1), (h, pq0, end)
