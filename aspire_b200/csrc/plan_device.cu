@@ -58,10 +58,11 @@ struct RowShape {
 
 // KV tokens a query tile [pq_begin, pq_end) can see (the host planner's
 // visible_span): all of kv_len, or under the causal mask up to the tile's last
-// query, except for the tile holding query 0 (the dump needs all its logits).
+// query, except for the tiles holding rows of query 0 (the dump needs all its
+// logits).
 __device__ __forceinline__ int32_t tile_span(const DevPlanParams& p, const RowShape& s, int32_t pq_begin,
                                              int32_t pq_end) {
-  if (!p.causal || pq_begin == 0) return s.kl;
+  if (!p.causal || pq_begin < p.group) return s.kl;
   const int64_t q_last = (pq_end - 1) / p.group;
   const int64_t lim = int64_t(s.kl) - s.ql + q_last + 1;
   return int32_t(max(int64_t(0), min(int64_t(s.kl), lim)));

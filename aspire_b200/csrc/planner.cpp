@@ -32,12 +32,13 @@ struct GroupDesc {
 // pq_end - 1) sees keys [0, kv_len - q_len + q_idx + 1); later keys are
 // masked for every query of the tile, so the tile's work stops there.  For a
 // decode row (one tile holding all queries) this is kv_len itself; for
-// long-query rows (prefill chunks) it skips the fully masked tiles.  The tile
-// holding query 0 keeps the whole range: the first/last logit dump records
-// query 0's raw logits at every key, masked or not.
+// long-query rows (prefill chunks) it skips the fully masked tiles.  Tiles
+// holding any row of query 0 (more than one when the group is wider than the
+// tile) keep the whole range: the first/last logit dump records query 0's raw
+// logits at every key, masked or not.
 inline int32_t visible_span(int32_t kv_len, int32_t q_len, int32_t pq_begin, int32_t pq_end, int group,
                             bool causal) {
-  if (!causal || pq_begin == 0) return kv_len;
+  if (!causal || pq_begin < group) return kv_len;
   const int64_t q_last = (pq_end - 1) / group;
   const int64_t lim = int64_t(kv_len) - q_len + q_last + 1;
   return static_cast<int32_t>(std::max<int64_t>(0, std::min<int64_t>(kv_len, lim)));

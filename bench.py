@@ -18,6 +18,12 @@ each rank holds its tensor-parallel share of the heads (KV-head ranges, as
 the reference's aspire/tp.py shards them) for the same batch.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl aspire_b200|reference]
+
+`--workload prefill` measures the prefill phase instead (long-query causal
+rows through the same wrapper, the reference's chunked `encode_slots`
+attention): TFLOP/s of the attention over the visible (query, key) pairs,
+beside FlashInfer's BatchPrefillWithPagedKVCacheWrapper (the library the
+reference runs prefill through) on the same inputs when it is installed.
 """
 
 from __future__ import annotations
@@ -61,6 +67,9 @@ def parse_args():
     ap.add_argument("--layers", type=int, default=None)
     ap.add_argument("--block-table", default="arange", choices=["arange", "random"],
                     help="arange: the reference engine's contiguous per-row pages; random: scattered pages")
+    ap.add_argument("--workload", default="step", choices=["step", "prefill"])
+    ap.add_argument("--prefill-cases", default="1x8192+0,4x2048+16384,8x1024+4096,2x4096+0",
+                    help="comma-separated ROWSxQLEN+PREFIX prefill chunks (Qwen3-8B heads, causal)")
     args = ap.parse_args()
     if args.batch is not None:
         CFG["batch"] = args.batch
@@ -293,8 +302,9 @@ def kernel_roofline(hp: HotPath, steps: int, peak: float, peak_kind: str):
         hp.mixed.run(q, hp.kv, out=out)
     torch.cuda.synchronize()
     # A CUDA graph of back-to-back launches timed between two events on the
-    # launching stream: device time only, under the sustained load of a step.
-    ms = graph_time(lambda: hp.mixed.run(q, hp.kv, out=out), max(steps, 30))
+    # launching stream: device time only, under the sustained load of a step;
+    # the average over three replays (90+ launches).
+    ms = graph_time(lambda: hp.mixed.run(q, hp.kv, out=out), max(steps, 30), replays=3)
     bytes_ = hp.lay.algorithmic_bytes()
     achieved = bytes_ / (ms * 1e-3) / 1e9
     # DRAM bytes (read + write) per algorithmic byte of the mixed layer-call,
@@ -313,9 +323,9 @@ def kernel_roofline(hp: HotPath, steps: int, peak: float, peak_kind: str):
             "algorithmic_bytes_per_launch": int(bytes_)}
 
 
-def graph_time(fn, reps: int) -> float:
-    """Device milliseconds per call of `fn`, from one replay of a CUDA graph that
-    holds `reps` back-to-back calls (no host time in the interval)."""
+def graph_time(fn, reps: int, replays: int = 1) -> float:
+    """Device milliseconds per call of `fn`, from `replays` replays of a CUDA
+    graph that holds `reps` back-to-back calls (no host time in the interval)."""
     fn()
     torch.cuda.synchronize()
     s = torch.cuda.Stream()
@@ -332,10 +342,11 @@ def graph_time(fn, reps: int) -> float:
     torch.cuda.synchronize()
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a.record()
-    g.replay()
+    for _ in range(replays):
+        g.replay()
     b.record()
     torch.cuda.synchronize()
-    ms = a.elapsed_time(b) / reps
+    ms = a.elapsed_time(b) / (reps * replays)
     del g
     return ms
 
@@ -485,6 +496,81 @@ def reference_arm(args, rank, world):
 
 
 # ----------------------------------------------------------------------------- main
+def prefill_bench(args):
+    """Prefill chunks through HolisticAttentionWrapper (prefill phase of the
+    tcgen05 kernel): device time per call from CUDA-graph replays, TFLOP/s over
+    the visible causal (query, key) pairs, and the same inputs through
+    FlashInfer's prefill wrapper when it is installed (library code: the
+    comparison the reference's own prefill path would give)."""
+    from aspire_b200.attention import HolisticAttentionWrapper
+    dev = torch.device("cuda", 0)
+    hq, hkv, d = CFG["num_qo_heads"], CFG["num_kv_heads"], 128
+    try:
+        import flashinfer
+    except Exception:  # noqa: BLE001
+        flashinfer = None
+    peak = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())["bf16_tflops"] \
+        if (ROOT / "MEASURED_PEAKS.json").exists() else 1590.0
+    cases = []
+    for spec in args.prefill_cases.split(","):
+        rows_s, rest = spec.split("x")
+        qlen_s, prefix_s = rest.split("+")
+        rows, qlen, prefix = int(rows_s), int(qlen_s), int(prefix_s)
+        kvl = prefix + qlen
+        pages = (kvl + 15) // 16
+        qo = np.arange(rows + 1, dtype=np.int32) * qlen
+        kvp = np.arange(rows + 1, dtype=np.int32) * pages
+        idx = np.arange(rows * pages, dtype=np.int32)
+        g = torch.Generator(device=dev)
+        g.manual_seed(CFG["seed"])
+        q = torch.randn(rows * qlen, hq, d, generator=g, device=dev).to(torch.bfloat16)
+        kv = torch.randn(rows * pages, 2, 16, hkv, d, generator=g, device=dev).to(torch.bfloat16)
+        t = lambda a: torch.from_numpy(a).to(dev)  # noqa: E731
+        w = HolisticAttentionWrapper(torch.empty(1, device=dev))
+        w.plan_host(torch.from_numpy(qo), torch.from_numpy(kvp), torch.from_numpy(np.full(rows, kvl, np.int32)),
+                    t(idx), hq, hkv, d, 16, causal=True)
+        out = torch.empty_like(q)
+        for _ in range(max(args.warmup, 1)):
+            w.run(q, kv, out=out)
+        torch.cuda.synchronize()
+        ms = graph_time(lambda: w.run(q, kv, out=out), max(args.steps, 1), replays=3)
+        # causal (bottom-right): query i of a row sees prefix + i + 1 keys; QK^T and PV, 2 flops per MAC
+        pairs = rows * (qlen * prefix + qlen * (qlen + 1) / 2)
+        flops = pairs * hq * d * 2 * 2
+        case = {"case": spec, "ms": round(ms, 4), "tflops": round(flops / (ms * 1e-3) / 1e12, 1),
+                "frac_of_bf16_peak": round(flops / (ms * 1e-3) / 1e12 / peak, 4),
+                "items": int(w.plan_info.num_items_prefill), "status": int(w.device_status())}
+        if flashinfer is not None:
+            ws = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+            fw = flashinfer.BatchPrefillWithPagedKVCacheWrapper(ws, "NHD")
+            last = np.full(rows, (kvl - 1) % 16 + 1, np.int32)
+            fw.plan(t(qo), t(kvp), t(idx), t(last), hq, hkv, d, 16, causal=True, q_data_type=torch.bfloat16,
+                    kv_data_type=torch.bfloat16)
+            fo = fw.run(q, kv)
+            torch.cuda.synchronize()
+            try:
+                ms_fi = graph_time(lambda: fw.run(q, kv), max(args.steps, 1), replays=3)
+            except Exception:  # noqa: BLE001  (a library call that cannot be captured: time it eagerly)
+                torch.cuda.synchronize()
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record()
+                for _ in range(max(args.steps, 1)):
+                    fw.run(q, kv)
+                b.record()
+                torch.cuda.synchronize()
+                ms_fi = a.elapsed_time(b) / max(args.steps, 1)
+            case.update({"flashinfer_ms": round(ms_fi, 4),
+                         "flashinfer_tflops": round(flops / (ms_fi * 1e-3) / 1e12, 1),
+                         "max_abs_diff_vs_flashinfer": float((fo.float() - out.float()).abs().max().item())})
+            del ws, fw
+        cases.append(case)
+        del q, kv, out, w
+        torch.cuda.empty_cache()
+    print(json.dumps({"workload": "prefill", "metric": "prefill attention TFLOP/s (causal visible pairs)",
+                      "unit": "TFLOP/s", "dtype": "bf16", "data": "synthetic", "heads": [hq, hkv, d],
+                      "peak_bf16_tflops": peak, "cases": cases}), flush=True)
+
+
 def main():
     args = parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -492,6 +578,11 @@ def main():
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         reference_arm(args, rank, world)
+        return
+    if args.workload == "prefill":
+        from aspire_b200 import load_library
+        load_library()
+        prefill_bench(args)
         return
     dist_on = world > 1
     torch.cuda.set_device(local_rank)

@@ -152,3 +152,18 @@ def test_plan_clips_causal_tiles_to_their_span(built_library, q_len, group):
     for (h, pq0), end in span.items():
         q_last = (min(pq0 + item_rows, nq) - 1) // group
         assert end == (q_len if pq0 == 0 else q_last + 1), (h, pq0, end)
+
+
+def test_plan_keeps_every_query0_tile_whole(built_library, monkeypatch):
+    """With the group wider than the CUDA-core tile (4 packed rows), query 0's
+    heads span several tiles; all of them keep every key for the dump."""
+    monkeypatch.setenv("ASPIRE_B200_DISABLE_TC", "1")  # every row on 4-row CUDA-core tiles
+    rc, info, buf = _plan(built_library, [0, 20], [0, 63], [1000], 64, 8)  # group 8
+    assert rc == 0, built_library.aspire_last_error()
+    _, items = _decode(buf, info)
+    assert info.num_items_gather == len(items)
+    assert {it["pq_begin"] for it in items if it["pq_begin"] < 8} == {0, 4}
+    for it in items:
+        if it["pq_begin"] < 8:
+            assert max(i["tok_end"] for i in items
+                       if i["pq_begin"] == it["pq_begin"] and i["kv_head"] == it["kv_head"]) == 1000
