@@ -10,16 +10,16 @@
 //   S^T[128 tok x N]  = K[128 tok x 128 d]  . Q^T      (A: K, K-major SW128)
 //   O^T[128 d   x N] += V^T[128 d x 128 tok] . P^T     (A: V, MN-major SW128)
 //
-// Warp roles (352 threads):
+// Warp roles (384 threads):
 //   warp 0     K producer: TMA-gathers the tile's 8 pages (2 KiB boxes of 16
 //              tokens x 64 dims, 128-byte swizzle, through a 5-D tensor map
 //              over the paged cache) into a 2-stage K ring.
 //   warp 10    V producer: the same into a 3-stage V ring.
-//   warp 1     MMA issuer (one thread) and TMEM owner (256 columns: two S
-//              tiles and the O accumulator).  A K stage is released as soon
-//              as its QK^T completes, a V stage when its PV completes.  It
-//              also TMA-loads each item's query tile while the previous item
-//              finishes.
+//   warp 1     QK^T issuer (one thread) and TMEM owner (two S tiles and the
+//              O accumulator).  A K stage is released as soon as its QK^T
+//              completes.  It also TMA-loads each item's query tile while the
+//              previous item finishes.
+//   warp 11    P.V issuer: a V stage is released when its PV completes.
 //   warps 2-9  softmax / epilogue in two warpgroups that split the item's N
 //              columns in halves: thread r of a group owns TMEM lane r, i.e.
 //              token r of the S tile and dim r of the O tile, for the group's
@@ -58,10 +58,11 @@ namespace {
 
 using namespace pipe;
 
-constexpr int kTcThreads = 352;
+constexpr int kTcThreads = 384;
 constexpr int kFirstSoftmaxWarp = 2;  // warps 2-5: softmax group 0, warps 6-9: group 1
 constexpr int kVProducerWarp = 10;
-constexpr int kSeqReaders = 10;       // V producer, MMA warp and the 8 softmax warps
+constexpr int kPvWarp = 11;           // decode phase: the P.V issuer
+constexpr int kSeqReaders = 11;       // V producer, the two MMA warps and the 8 softmax warps
 constexpr int kKStages = 2;
 constexpr int kVStages = 3;
 constexpr int kNMax = kTcQTile;
@@ -89,7 +90,7 @@ struct TcShared {
   uint64_t k_full[kKStages], k_empty[kKStages];
   uint64_t v_full[kVStages], v_empty[kVStages];
   uint64_t s_full[2], s_empty[2], p_full[2], p_empty[2];
-  uint64_t o_free, q_full, q_empty, done, grp[2];
+  uint64_t o_free, q_full, q_empty, done, done_pv, grp[2];
   pf::Barriers pf;  // prefill phase
   uint64_t seq_full[kSeqDepth], seq_empty[kSeqDepth];
   int seq[kSeqDepth];
@@ -110,41 +111,27 @@ __device__ __forceinline__ bool group_sync(TcShared& sm, uint64_t& grp, uint32_t
   return wait_bar(sm, grp, parity, status);
 }
 
-// ------------------------------------------------------------------ MMA issuer
-__device__ void run_mma(const AttnParams& p, const CUtensorMap* qmap, TcShared& sm, int lane, uint32_t& k) {
+// ------------------------------------------------------------------ MMA issuers
+// A tcgen05.mma issue proceeds at about the rate the tensor core takes the
+// instruction (~90 cycles for these small-N products), so one thread issuing
+// both products of a tile (16 instructions) plus its barrier traffic would
+// take about as long as the tile's 64 KiB take to arrive from HBM at a
+// power-capped clock.  The two products share no data (S buffers vs the O
+// accumulator), so each has its own issuing warp.
+//
+// Shared-memory descriptors of consecutive K steps differ only in their
+// start-address field (address >> 4, 14 bits, no carry for addresses inside
+// the CTA's shared memory), so each loop adds offsets to a base descriptor.
+
+// QK^T of every tile, and the query-tile loads (warp 1).
+__device__ void run_qk(const AttnParams& p, const CUtensorMap* qmap, TcShared& sm, int lane, uint32_t& k) {
   const uint32_t tmem = sm.tmem_base;
   uint32_t g = 0, items_done = 0;
   bool ok = true;
   const uint32_t k0 = ptx::smem_addr(sm.k[0]);
-  const uint32_t v0 = ptx::smem_addr(sm.v[0]);
   const uint32_t q0 = ptx::smem_addr(sm.q[0]);
-  const uint32_t p0 = ptx::smem_addr(sm.p[0]);
+  const uint64_t qdesc0 = ptx::smem_desc(q0, 16, 1024, ptx::kLayoutSw128);
   bool q_pending = false;  // a query-tile load is in flight
-
-  // PV of global tile u; `first` marks the item's first tile (fresh
-  // accumulator), `valid` is the count of the tile's tokens in the item.
-  auto issue_pv = [&](uint32_t u, bool first, int valid, uint32_t idesc_pv) -> bool {
-    if (first && !wait_bar(sm, sm.o_free, (items_done & 1) ^ 1, p.status)) return false;
-    if (!wait_bar(sm, sm.v_full[u % kVStages], (u / kVStages) & 1, p.status)) return false;
-    clear_v_tail(sm.v[u % kVStages], valid, lane);
-    __syncwarp();
-    if (!wait_bar(sm, sm.p_full[u % 2], (u / 2) & 1, p.status)) return false;
-    ptx::tc_fence_after();
-    if (lane == 0) {
-      const uint32_t vbase = v0 + (u % kVStages) * kSlotBytes;
-      const uint32_t pbase = p0 + (u % 2) * kPBufBytes;
-#pragma unroll
-      for (int kk = 0; kk < kTile / 16; ++kk) {
-        const uint64_t a = ptx::smem_desc(vbase + kk * 2048, kHalfBytes, 1024, ptx::kLayoutSw128);
-        const uint64_t bd = ptx::smem_desc(pbase + kk * 256, 128, kTile * 16, ptx::kLayoutNone);
-        ptx::mma_bf16(tmem + kColO, a, bd, idesc_pv, (!first || kk > 0) ? 1u : 0u);
-      }
-      ptx::mma_commit(ptx::smem_addr(&sm.v_empty[u % kVStages]));
-      ptx::mma_commit(ptx::smem_addr(&sm.p_empty[u % 2]));
-    }
-    __syncwarp();
-    return true;
-  };
 
   int ii = next_item_with_tiles(p, sm, k, lane, kNMax);
   if (ii == -2) ok = false;
@@ -158,13 +145,11 @@ __device__ void run_mma(const AttnParams& p, const CUtensorMap* qmap, TcShared& 
     const int nrows = it.pq_end - it.pq_begin;
     const uint32_t N = uint32_t((nrows + 15) / 16 * 16);
     const uint32_t idesc_qk = ptx::idesc_bf16(128, N, false, false);
-    const uint32_t idesc_pv = ptx::idesc_bf16(128, N, true, true);
     if (!wait_bar(sm, sm.q_full, items_done & 1, p.status)) {
       ok = false;
       break;
     }
     q_pending = false;
-    const uint32_t g0 = g;
     for (int t = 0; t < nt && ok; ++t, ++g) {
       const int ks = g % kKStages, sb = g % 2;
       if (!wait_bar(sm, sm.k_full[ks], (g / kKStages) & 1, p.status) ||
@@ -174,22 +159,18 @@ __device__ void run_mma(const AttnParams& p, const CUtensorMap* qmap, TcShared& 
       }
       ptx::tc_fence_after();
       if (lane == 0) {
-        const uint32_t kbase = k0 + uint32_t(ks) * kSlotBytes;
+        const uint64_t kdesc0 = ptx::smem_desc(k0 + uint32_t(ks) * kSlotBytes, 16, 1024, ptx::kLayoutSw128);
 #pragma unroll
         for (int kk = 0; kk < 128 / 16; ++kk) {
           const uint32_t koff = uint32_t(kk / 4) * kHalfBytes + uint32_t(kk % 4) * 32;
           const uint32_t qoff = uint32_t(kk / 4) * kQHalfBytes + uint32_t(kk % 4) * 32;
-          const uint64_t a = ptx::smem_desc(kbase + koff, 16, 1024, ptx::kLayoutSw128);
-          const uint64_t bd = ptx::smem_desc(q0 + qoff, 16, 1024, ptx::kLayoutSw128);
-          ptx::mma_bf16(tmem + col_s(sb), a, bd, idesc_qk, kk > 0 ? 1u : 0u);
+          ptx::mma_bf16(tmem + col_s(sb), kdesc0 + (koff >> 4), qdesc0 + (qoff >> 4), idesc_qk, kk > 0 ? 1u : 0u);
         }
         ptx::mma_commit(ptx::smem_addr(&sm.s_full[sb]));
         ptx::mma_commit(ptx::smem_addr(&sm.k_empty[ks]));
         if (t == nt - 1) ptx::mma_commit(ptx::smem_addr(&sm.q_empty));
       }
       __syncwarp();
-      if (t > 0 && !issue_pv(g - 1, g - 1 == g0, it.tok_end - (it.tok_begin + (t - 1) * kTile), idesc_pv))
-        ok = false;
     }
     if (!ok) break;
     // The next item's query tile loads while this item's last PV and epilogue run.
@@ -207,7 +188,6 @@ __device__ void run_mma(const AttnParams& p, const CUtensorMap* qmap, TcShared& 
       q_pending = true;
       __syncwarp();
     }
-    if (!issue_pv(g - 1, g - 1 == g0, it.tok_end - (it.tok_begin + (nt - 1) * kTile), idesc_pv)) ok = false;
     ++items_done;
     ii = nxt;
   }
@@ -217,6 +197,58 @@ __device__ void run_mma(const AttnParams& p, const CUtensorMap* qmap, TcShared& 
   if (lane == 0) ptx::mma_commit(ptx::smem_addr(&sm.done));
   __syncwarp();
   drain_bar(sm.done, 0);
+}
+
+// P.V of every tile into the O accumulator (warp 11).
+__device__ void run_pv(const AttnParams& p, TcShared& sm, int lane, uint32_t& k) {
+  const uint32_t tmem = sm.tmem_base;
+  uint32_t g = 0, items_done = 0;
+  bool ok = true;
+  const uint32_t v0 = ptx::smem_addr(sm.v[0]);
+  const uint32_t p0 = ptx::smem_addr(sm.p[0]);
+  int ii = next_item_with_tiles(p, sm, k, lane, kNMax);
+  if (ii == -2) ok = false;
+  while (ii >= 0 && ok) {
+    const WorkItem it = load_item(p.plan, ii);
+    const int nt = n_tiles_of(it);
+    const int nrows = it.pq_end - it.pq_begin;
+    const uint32_t N = uint32_t((nrows + 15) / 16 * 16);
+    const uint32_t idesc_pv = ptx::idesc_bf16(128, N, true, true);
+    for (int t = 0; t < nt && ok; ++t, ++g) {
+      const uint32_t vs = g % kVStages, pb = g % 2;
+      // The item's first PV overwrites O: the previous item's epilogue has read it.
+      if ((t == 0 && !wait_bar(sm, sm.o_free, (items_done & 1) ^ 1, p.status)) ||
+          !wait_bar(sm, sm.v_full[vs], (g / kVStages) & 1, p.status)) {
+        ok = false;
+        break;
+      }
+      clear_v_tail(sm.v[vs], it.tok_end - (it.tok_begin + t * kTile), lane);
+      __syncwarp();
+      if (!wait_bar(sm, sm.p_full[pb], (g / 2) & 1, p.status)) {
+        ok = false;
+        break;
+      }
+      ptx::tc_fence_after();
+      if (lane == 0) {
+        const uint64_t vdesc0 = ptx::smem_desc(v0 + vs * kSlotBytes, kHalfBytes, 1024, ptx::kLayoutSw128);
+        const uint64_t pdesc0 = ptx::smem_desc(p0 + pb * kPBufBytes, 128, kTile * 16, ptx::kLayoutNone);
+#pragma unroll
+        for (int kk = 0; kk < kTile / 16; ++kk)
+          ptx::mma_bf16(tmem + kColO, vdesc0 + uint64_t(kk * 2048 >> 4), pdesc0 + uint64_t(kk * 256 >> 4), idesc_pv,
+                        (t > 0 || kk > 0) ? 1u : 0u);
+        ptx::mma_commit(ptx::smem_addr(&sm.v_empty[vs]));
+        ptx::mma_commit(ptx::smem_addr(&sm.p_empty[pb]));
+      }
+      __syncwarp();
+    }
+    if (!ok) break;
+    ++items_done;
+    ii = next_item_with_tiles(p, sm, k, lane, kNMax);
+    if (ii == -2) ok = false;
+  }
+  if (lane == 0) ptx::mma_commit(ptx::smem_addr(&sm.done_pv));
+  __syncwarp();
+  drain_bar(sm.done_pv, 0);
 }
 
 // ------------------------------------------------------------------ warp reductions
@@ -301,6 +333,29 @@ __device__ __forceinline__ void tmem_load_cols(uint32_t taddr, float* v) {
 }
 
 // ------------------------------------------------------------------ softmax / epilogue
+// Writes dump columns [lo, hi) of one token (raw logits, fp16); the first 8
+// are in dv, further pieces are read from the S tile at s_addr.  Kept out of
+// line: the three column-count instantiations of the consumer loop share it,
+// which keeps their hot loops small.
+__device__ __noinline__ void dump_columns(int lo, int hi, __half* base, int base_col, int64_t col_stride, int tok,
+                                          bool store, uint32_t s_addr, const float* dv_in) {
+  float dv[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) dv[i] = dv_in[i];
+  for (int c = lo; c < hi; c += 8) {
+    if (c > lo) {
+      ptx::tmem_ld8(s_addr + c, dv);
+      ptx::tmem_wait_ld();
+    }
+    if (store) {
+      __half* dst = base + int64_t(c - base_col) * col_stride + tok;
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        if (c + i < hi) dst[int64_t(i) * col_stride] = __float2half_rn(dv[i]);
+    }
+  }
+}
+
 // The item's N packed columns are split between the two softmax warpgroups:
 // warpgroup wg owns columns [c0, c0 + NH) with c0 = wg * NH, NH = N / 2.  A
 // column's running statistics (reference max, sum, rescale factor) live with
@@ -391,24 +446,22 @@ __device__ bool consume_item(const AttnParams& p, TcShared& sm, const WorkItem& 
       }
     };
     float sv[NH];
-    load_s(sv);
     if (dumping) {
-      // Raw logits before scale and mask.  tcgen05.ld is warp-collective:
-      // every lane loads, in-chunk lanes store.
-      auto dump_run = [&](int lo, int hi, __half* base, int base_col) {
-        float dv[8];
-        for (int c = lo; c < hi; c += 8) {
-          ptx::tmem_ld8(tmem_lane + col_s(b) + c, dv);
-          ptx::tmem_wait_ld();
-          if (in_chunk && tok < p.dump_kv_stride) {
-#pragma unroll
-            for (int i = 0; i < 8; ++i)
-              if (c + i < hi) base[(c + i - base_col) * dump_col_stride + tok] = __float2half_rn(dv[i]);
-          }
-        }
-      };
-      dump_run(d0_lo, d0_hi, dump_base0, 0);
-      dump_run(d1_lo, d1_hi, dump_base1, dump_c1);
+      // Raw logits before scale and mask of the dump columns: each slot's
+      // columns are a run [lo, hi) of this group's columns; the first 8 of
+      // each run load with the tile (one wait), longer runs in more pieces.
+      float dv0[8], dv1[8];
+      tmem_load_cols<NH>(s_cols, sv);
+      if (d0_lo < d0_hi) ptx::tmem_ld8(tmem_lane + col_s(b) + d0_lo, dv0);
+      if (d1_lo < d1_hi) ptx::tmem_ld8(tmem_lane + col_s(b) + d1_lo, dv1);
+      ptx::tmem_wait_ld();
+      const bool store = in_chunk && tok < p.dump_kv_stride;
+      if (d0_lo < d0_hi)
+        dump_columns(d0_lo, d0_hi, dump_base0, 0, dump_col_stride, tok, store, tmem_lane + col_s(b), dv0);
+      if (d1_lo < d1_hi)
+        dump_columns(d1_lo, d1_hi, dump_base1, dump_c1, dump_col_stride, tok, store, tmem_lane + col_s(b), dv1);
+    } else {
+      load_s(sv);
     }
     mask_s(sv);
 
@@ -659,6 +712,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     ptx::mbar_init(ptx::smem_addr(&sm.q_full), 1);
     ptx::mbar_init(ptx::smem_addr(&sm.q_empty), 1);
     ptx::mbar_init(ptx::smem_addr(&sm.done), 1);
+    ptx::mbar_init(ptx::smem_addr(&sm.done_pv), 1);
     ptx::mbar_init(ptx::smem_addr(&sm.grp[0]), 128);
     ptx::mbar_init(ptx::smem_addr(&sm.grp[1]), 128);
     pf::init_barriers(sm.pf);
@@ -699,7 +753,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       run_producer<kVStages>(p, &tmap, sm, sm.v, sm.v_full, sm.v_empty, 1, false, tc_first, n_tc, kHdrTcClaim,
                              kNMax, lane, k);
     } else if (warp == 1) {
-      run_mma(p, &qmap, sm, lane, k);
+      run_qk(p, &qmap, sm, lane, k);
+    } else if (warp == kPvWarp) {
+      run_pv(p, sm, lane, k);
     } else {
       run_consumer(p, sm, causal, warp, lane, k);
     }
@@ -721,6 +777,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                                    kHdrPfClaim, kPfMaxRows, lane, k);
       } else if (warp == 1) {
         pf::run_mma(p, &qmap_pf, sm, pbuf, lane, k);
+      } else if (warp == kPvWarp) {
+        // No prefill role: follow the item sequence to its end.
+        while (seq_read(sm, k, lane, p.status) >= 0) {
+        }
       } else {
         pf::consume_items(p, sm, causal, (warp - kFirstSoftmaxWarp) / 4, warp & 3, lane, k);
       }

@@ -104,3 +104,36 @@ def test_page_tables_require_a_page_source(cuda_device):
     w = HolisticAttentionWrapper(torch.empty(1, device=cuda_device))
     with pytest.raises(ValueError):
         w.plan_host(torch.tensor([0, 1]), torch.tensor([0, 1]), torch.tensor([5]), None, 32, 8, 128, 16)
+
+
+def test_prefill_rows_page_tables_match_flat_list(cuda_device):
+    """Prefill rows (the prefill phase's producers) read the block table the
+    same way: a prefill chunk after a prefix, a short prefill row and a draft
+    row in one batch."""
+    from aspire_b200.workloads import MixedLayout
+    dev = cuda_device
+    rng = np.random.default_rng(21)
+    q_lens, kv_lens, modes = [300, 40, 1], [800, 40, 500], [1, 1, 0]
+    B = len(q_lens)
+    pages = [(k + 15) // 16 for k in kv_lens]
+    ppr = max(pages) + 3
+    bt = rng.permutation(B * ppr).reshape(B, ppr).astype(np.int32)
+    kv_indptr = np.concatenate([[0], np.cumsum(pages)]).astype(np.int32)
+    kv_indices = np.concatenate([bt[r, :pages[r]] for r in range(B)]).astype(np.int32)
+    qo = np.concatenate([[0], np.cumsum(q_lens)]).astype(np.int32)
+    lay = MixedLayout(num_qo_heads=32, num_kv_heads=8, modes=np.array(modes), q_lens=np.array(q_lens, np.int32),
+                      kv_lens=np.array(kv_lens, np.int32), qo_indptr=qo, kv_indptr=kv_indptr, kv_indices=kv_indices,
+                      block_table=bt, ctx_lens=np.array(kv_lens, np.int32), pages_per_row=ppr,
+                      num_pages_total=B * ppr)
+    q, kv = fill_tensors(lay, device=dev, seed=22)
+    flat = HolisticAttentionWrapper(torch.empty(1, device=dev))
+    _plan(flat, lay, dev, torch.from_numpy(lay.kv_indices).to(dev))
+    assert flat.plan_info.num_items_prefill > 0 or not flat.plan_info.tc_enabled
+    out_flat, lse_flat = flat.run(q, kv, return_lse=True)
+    tab = HolisticAttentionWrapper(torch.empty(1, device=dev))
+    tab.set_page_tables(*_tables(lay, dev))
+    _plan(tab, lay, dev, None)
+    out_tab, lse_tab = tab.run(q, kv, return_lse=True)
+    torch.cuda.synchronize()
+    assert torch.equal(out_flat, out_tab)
+    assert torch.equal(lse_flat, lse_tab)
