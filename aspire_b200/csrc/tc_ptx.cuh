@@ -53,8 +53,8 @@ __device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t count) {
 }
 
 // ---------------------------------------------------------------- TMA
-// 5-D tiled load into this CTA's shared memory, completion counted on `bar`
-// in bytes.  No multicast.
+// 5-D tiled load into this CTA's own shared memory only, completion counted
+// on `bar` in bytes.
 __device__ __forceinline__ void tma_load_5d(uint32_t dst, const void* tmap, uint32_t bar, int c0, int c1,
                                             int c2, int c3, int c4) {
   asm volatile(
@@ -63,7 +63,8 @@ __device__ __forceinline__ void tma_load_5d(uint32_t dst, const void* tmap, uint
       "l"(tmap), "r"(bar), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4)
       : "memory");
 }
-// 3-D tiled load (the query tile), same completion rule.  No multicast.
+// 3-D tiled load (the query tile) into this CTA's own shared memory, same
+// completion rule.
 __device__ __forceinline__ void tma_load_3d(uint32_t dst, const void* tmap, uint32_t bar, int c0, int c1,
                                             int c2) {
   asm volatile(
