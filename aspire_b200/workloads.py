@@ -159,6 +159,28 @@ def full_context_layout(layout: MixedLayout) -> MixedLayout:
                        num_pages_total=layout.num_pages_total)
 
 
+def rows_layout(q_lens, kv_lens, num_qo_heads: int, num_kv_heads: int, seed: int = 0) -> MixedLayout:
+    """A batch of explicit rows (q_len, kv_len each), e.g. prefill chunks: rows
+    with one query are draft rows, the others verify / prefill rows; each row
+    owns a shuffled run of whole pages of one pool."""
+    rng = np.random.default_rng(seed)
+    B = len(q_lens)
+    q_lens = np.asarray(q_lens, np.int32)
+    kv_lens = np.asarray(kv_lens, np.int32)
+    pages = (kv_lens + PAGE - 1) // PAGE
+    ppr = max(int(pages.max()) if B else 1, 1)
+    bt = np.stack([r * ppr + rng.permutation(ppr) for r in range(B)]).astype(np.int32)
+    kv_indptr = np.zeros(B + 1, np.int32)
+    kv_indptr[1:] = np.cumsum(pages)
+    idx = np.concatenate([bt[r, :pages[r]] for r in range(B)]).astype(np.int32)
+    qo = np.zeros(B + 1, np.int32)
+    qo[1:] = np.cumsum(q_lens)
+    return MixedLayout(num_qo_heads=num_qo_heads, num_kv_heads=num_kv_heads,
+                       modes=(q_lens > 1).astype(np.int32), q_lens=q_lens, kv_lens=kv_lens, qo_indptr=qo,
+                       kv_indptr=kv_indptr, kv_indices=idx, block_table=bt, ctx_lens=kv_lens.copy(),
+                       pages_per_row=ppr, num_pages_total=B * ppr)
+
+
 def last_page_lens(layout: MixedLayout) -> np.ndarray:
     """Tokens in each row's last attended page: (kv_len - 1) % 16 + 1, 0 when empty."""
     k = layout.kv_lens.astype(np.int64)

@@ -218,3 +218,19 @@ def test_matches_flashinfer_golden(cuda_device, golden_dir, case):
     err = (out.float().cpu() - g["out"].float()).abs()
     assert err.max().item() <= 2e-2 and err.mean().item() <= 2e-3, err.max().item()
     assert (lse.cpu() - g["lse"]).abs().max().item() <= 2e-3
+
+
+@pytest.mark.parametrize("case", ["prefill_g4", "prefill_g1"])
+def test_prefill_matches_flashinfer_golden(cuda_device, golden_dir, case):
+    """The prefill phase against FlashInfer's prefill wrapper on the same seeded
+    chunks (fixture from tests/golden/make_flashinfer_golden.py --prefill)."""
+    from aspire_b200.workloads import fill_tensors
+
+    g = torch.load(golden_dir / "flashinfer_prefill.pt", weights_only=False)["cases"][case]
+    lay = MixedLayout(**g["layout"])
+    q, kv = fill_tensors(lay, device="cpu", dtype=torch.bfloat16, seed=g["seed"])
+    out, lse, _, w = run_attention(lay, q.to(cuda_device), kv.to(cuda_device))
+    assert w.plan_info.num_items_prefill > 0 or not w.plan_info.tc_enabled
+    err = (out.float().cpu() - g["out"].float()).abs()
+    assert err.max().item() <= 2e-2 and err.mean().item() <= 2e-3, err.max().item()
+    assert (lse.cpu() - g["lse"]).abs().max().item() <= 2e-3

@@ -142,6 +142,24 @@ def test_attention_oracle_matches_flashinfer(golden_dir, case):
     assert (lse - g["lse"]).abs().max().item() <= 2e-3
 
 
+@pytest.mark.parametrize("case", ["prefill_g4", "prefill_g1"])
+def test_attention_oracle_matches_flashinfer_prefill(golden_dir, case):
+    """The oracle against FlashInfer's BatchPrefillWithPagedKVCacheWrapper (the
+    library the reference runs its prefill chunks through), on seeded prefill
+    chunks (tests/golden/make_flashinfer_golden.py --prefill)."""
+    from aspire_b200.workloads import MixedLayout, fill_tensors
+    from oracle import attention as oracle_attn
+
+    g = _load(golden_dir, "flashinfer_prefill.pt")["cases"][case]
+    lay = MixedLayout(**g["layout"])
+    q, kv = fill_tensors(lay, device="cpu", dtype=torch.bfloat16, seed=g["seed"])
+    out, lse = oracle_attn.paged_attention(q.float(), kv, lay.qo_indptr, lay.kv_indptr, lay.kv_indices,
+                                           lay.kv_lens)
+    err = (out - g["out"].float()).abs()
+    assert err.max().item() <= 2e-2 and err.mean().item() <= 2e-3
+    assert (lse - g["lse"]).abs().max().item() <= 2e-3
+
+
 def test_unified_indices_oracle_matches_reference_golden(golden_dir):
     """The restatement of build_unified_indices reproduces the reference's
     output (Triton interpreter) bit for bit, untouched entries included."""
