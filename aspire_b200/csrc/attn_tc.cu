@@ -361,7 +361,7 @@ __device__ __noinline__ void dump_columns(int lo, int hi, __half* base, int base
 // column's running statistics (reference max, sum, rescale factor) live with
 // its owner, so the two groups never wait for each other; they meet only on
 // the S / P / O barriers shared with the MMA warp.
-template <int NH>
+template <int NH, bool kDump>
 __device__ bool consume_item(const AttnParams& p, TcShared& sm, const WorkItem& it, bool causal, int r,
                              int ctid, int wg, int wq, int lane, uint32_t& g, uint32_t& grp_uses) {
   constexpr int N = 2 * NH;
@@ -383,7 +383,7 @@ __device__ bool consume_item(const AttnParams& p, TcShared& sm, const WorkItem& 
   __half* dump_base0 = nullptr;
   __half* dump_base1 = nullptr;
   const int64_t dump_col_stride = 2 * p.dump_kv_stride;  // between heads
-  if (p.dump != nullptr) {
+  if (kDump) {
     const int last_lo = (it.q_len - 1) * group;  // first packed row of the last query
     const int64_t head0 = int64_t(it.row) * p.dump_num_heads + int64_t(it.kv_head) * group;
     if (it.pq_begin < group) {
@@ -399,7 +399,7 @@ __device__ bool consume_item(const AttnParams& p, TcShared& sm, const WorkItem& 
       dump_base1 = p.dump + (head0 + it.pq_begin + dump_c1 - last_lo) * dump_col_stride + p.dump_kv_stride;
     }
   }
-  const bool dumping = d0_lo < d0_hi || d1_lo < d1_hi;
+  const bool dumping = kDump && (d0_lo < d0_hi || d1_lo < d1_hi);
   // The column reference max (times scale) is uniform across the group's
   // threads and lives in shared memory (mref[cur]); the first tile of an item
   // always sets it.
@@ -654,13 +654,25 @@ __device__ void consume_items(const AttnParams& p, TcShared& sm, bool causal, in
       continue;
     }
     const int N = (nrows + 15) / 16 * 16;
+    // Items whose columns include dump rows (query 0 or the last query, with a
+    // dump buffer) take the instantiation that carries the dump path.
+    const bool dump_item = p.dump != nullptr && (it.pq_begin < p.group || (it.q_len > 1 && (it.q_len - 1) * p.group < it.pq_end));
     bool ok;
-    if (N == 16)
-      ok = consume_item<8>(p, sm, it, causal, r, ctid, wg, wq, lane, g, grp_uses);
-    else if (N == 32)
-      ok = consume_item<16>(p, sm, it, causal, r, ctid, wg, wq, lane, g, grp_uses);
-    else
-      ok = consume_item<24>(p, sm, it, causal, r, ctid, wg, wq, lane, g, grp_uses);
+    if (dump_item) {
+      if (N == 16)
+        ok = consume_item<8, true>(p, sm, it, causal, r, ctid, wg, wq, lane, g, grp_uses);
+      else if (N == 32)
+        ok = consume_item<16, true>(p, sm, it, causal, r, ctid, wg, wq, lane, g, grp_uses);
+      else
+        ok = consume_item<24, true>(p, sm, it, causal, r, ctid, wg, wq, lane, g, grp_uses);
+    } else {
+      if (N == 16)
+        ok = consume_item<8, false>(p, sm, it, causal, r, ctid, wg, wq, lane, g, grp_uses);
+      else if (N == 32)
+        ok = consume_item<16, false>(p, sm, it, causal, r, ctid, wg, wq, lane, g, grp_uses);
+      else
+        ok = consume_item<24, false>(p, sm, it, causal, r, ctid, wg, wq, lane, g, grp_uses);
+    }
     if (!ok) return;
   }
 }
