@@ -18,7 +18,7 @@ import torch
 
 from aspire_b200 import _capi
 from aspire_b200.attention import HolisticAttentionWrapper
-from aspire_b200.workloads import fill_tensors, make_layout
+from aspire_b200.workloads import fill_tensors, make_layout, rows_layout
 
 pytestmark = pytest.mark.gpu
 
@@ -54,6 +54,8 @@ def test_noalloc_matches_regular_entry_point_twice(cuda_device):
                     seed=21),
         make_layout(batch=4, ctx=3000, num_qo_heads=16, num_kv_heads=8, draft_fraction=0.25, budget_pages=24,
                     seed=22),
+        # Prefill chunks beside decode rows (the prefill phase of the same launch).
+        rows_layout([150, 1, 5, 64], [1000, 1500, 800, 64], 32, 8, seed=23),
     ]
     for call, lay in enumerate(layouts):
         q, kv = fill_tensors(lay, device=dev, seed=30 + call)
