@@ -93,10 +93,12 @@ def test_device_plan_matches_host_plan(cuda_device, hq, hkv, draft_fraction):
     hw, hitems, hmerges = _decode(host_words)
     assert len(ditems) == len(hitems) and len(dmerges) == len(hmerges)
     assert _canon(dw, ditems, dmerges) == _canon(hw, hitems, hmerges)
-    # Longest first, and the claim counter armed.
-    lens = ditems[:, 7] - ditems[:, 6]
-    assert np.all((lens[:-1] + 127) // 128 >= (lens[1:] + 127) // 128)
-    assert dw[14] == 0 and dw[4] == 0
+    # Each list (decode items, then prefill items from word 15 on) longest
+    # first, and the claim counters armed.
+    lens = (ditems[:, 7] - ditems[:, 6] + 127) // 128
+    for lo, hi in ((0, dw[15]), (dw[15], len(ditems))):
+        assert np.all(lens[lo:hi - 1] >= lens[lo + 1:hi])
+    assert dw[14] == 0 and dw[16] == 0 and dw[4] == 0
     assert w.device_status() == 0
 
 
