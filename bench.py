@@ -237,20 +237,26 @@ class HotPath:
         self.refresh.plan_host(t(full.qo_indptr), t(full.kv_indptr), t(full.kv_lens), None,
                                full.num_qo_heads, full.num_kv_heads, 128, 16, causal=True)
 
-    def step_eager(self):
-        n_layer = CFG["n_layer"]
-        for layer in range(n_layer):
-            if layer == CFG["refresh_layer"]:
-                self.append_kv(self.k_new[layer], self.v_new[layer], self.qo_indptr, self.kv, None,
-                               self.full_indptr, self.full_last, 16, page_tables=self.full_tables)
-                self.refresh.run(self.q[layer], self.kv, self.dump, self.lay.num_qo_heads, self.kv_stride,
-                                 out=self.out[layer], lse=self.lse)
-            else:
-                self.append_kv(self.k_new[layer], self.v_new[layer], self.qo_indptr, self.kv, None,
-                               self.mixed_indptr, self.mixed_last, 16, page_tables=self.mixed_tables)
-                self.mixed.run(self.q[layer], self.kv, out=self.out[layer])
+    def layer(self, layer: int):
+        """Append + attention of one layer (the refresh layer with the dump)."""
+        if layer == CFG["refresh_layer"]:
+            self.append_kv(self.k_new[layer], self.v_new[layer], self.qo_indptr, self.kv, None,
+                           self.full_indptr, self.full_last, 16, page_tables=self.full_tables)
+            self.refresh.run(self.q[layer], self.kv, self.dump, self.lay.num_qo_heads, self.kv_stride,
+                             out=self.out[layer], lse=self.lse)
+        else:
+            self.append_kv(self.k_new[layer], self.v_new[layer], self.qo_indptr, self.kv, None,
+                           self.mixed_indptr, self.mixed_last, 16, page_tables=self.mixed_tables)
+            self.mixed.run(self.q[layer], self.kv, out=self.out[layer])
+
+    def select(self):
         self.selector.select_into(self.draft_table, self.draft_counts, self.dump, self.lse, self.num_pages,
                                   self.block_table, self.qo_indptr)
+
+    def step_eager(self):
+        for layer in range(CFG["n_layer"]):
+            self.layer(layer)
+        self.select()
 
     def capture(self):
         self.step_eager()
@@ -396,24 +402,65 @@ def breakdown(hp: HotPath) -> dict:
 
 
 def e2e_measure(hp: HotPath, steps: int, warmup: int, bytes_per_step: int):
-    """Through the public API with host buffers: H2D of the step's q / new K,V, host
-    planning of both attention programs, the step, D2H of outputs and tables."""
+    """Through the public API with host buffers, every step: host planning of
+    both attention programs (plan upload included), H2D of every layer's q and
+    new K/V from pinned memory, the step, D2H of every layer's attention output
+    and of the new draft table and counts, then a host synchronisation.  The
+    copies stream per layer on a second stream, as a serving loop would issue
+    them: layer L's inputs land while earlier layers compute (the layer waits
+    for its own copy), and its output leaves once the layer is done; the
+    timed region ends when the last copy of the step has reached the host."""
     q_h = hp.q.cpu().pin_memory()
     k_h = hp.k_new.cpu().pin_memory()
     v_h = hp.v_new.cpu().pin_memory()
     out_h = torch.empty(hp.out.shape, dtype=hp.out.dtype, pin_memory=True)
     tab_h = torch.empty(hp.draft_table.shape, dtype=torch.int32, pin_memory=True)
     cnt_h = torch.empty(hp.draft_counts.shape, dtype=torch.int32, pin_memory=True)
+    n_layer = CFG["n_layer"]
+    copy = torch.cuda.Stream()
 
-    def one():
-        hp.q.copy_(q_h, non_blocking=True)
-        hp.k_new.copy_(k_h, non_blocking=True)
-        hp.v_new.copy_(v_h, non_blocking=True)
-        hp.plan()
-        hp.graph.replay()
-        out_h.copy_(hp.out, non_blocking=True)
+    def streamed_step():
+        main = torch.cuda.current_stream()
+        ev_in = [torch.cuda.Event() for _ in range(n_layer)]
+        ev_out = [torch.cuda.Event() for _ in range(n_layer)]
+        copy.wait_stream(main)
+        with torch.cuda.stream(copy):
+            for layer in range(n_layer):
+                hp.q[layer].copy_(q_h[layer], non_blocking=True)
+                hp.k_new[layer].copy_(k_h[layer], non_blocking=True)
+                hp.v_new[layer].copy_(v_h[layer], non_blocking=True)
+                ev_in[layer].record(copy)
+        for layer in range(n_layer):
+            main.wait_event(ev_in[layer])
+            hp.layer(layer)
+            ev_out[layer].record(main)
+        with torch.cuda.stream(copy):
+            for layer in range(n_layer):
+                copy.wait_event(ev_out[layer])
+                out_h[layer].copy_(hp.out[layer], non_blocking=True)
+        hp.select()
         tab_h.copy_(hp.draft_table, non_blocking=True)
         cnt_h.copy_(hp.draft_counts, non_blocking=True)
+        main.wait_stream(copy)
+
+    # One CUDA graph of the streamed step (copies included); the host plans
+    # both programs before every replay.
+    streamed_step()
+    torch.cuda.synchronize()
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        streamed_step()
+    torch.cuda.current_stream().wait_stream(side)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        streamed_step()
+    torch.cuda.synchronize()
+
+    def one():
+        hp.plan()
+        g.replay()
         torch.cuda.current_stream().synchronize()
 
     for _ in range(warmup):
@@ -422,6 +469,7 @@ def e2e_measure(hp: HotPath, steps: int, warmup: int, bytes_per_step: int):
     for _ in range(steps):
         one()
     dt = (time.perf_counter() - t0) / steps
+    del g
     h2d = q_h.numel() * 2 + k_h.numel() * 2 + v_h.numel() * 2
     d2h = out_h.numel() * 2 + tab_h.numel() * 4 + cnt_h.numel() * 4
     return dt, h2d, d2h
