@@ -689,21 +689,15 @@ __device__ void run_consumer(const AttnParams& p, TcShared& sm, bool causal, int
 __global__ void __launch_bounds__(kTcThreads, 1)
     aspire_attn_tc_kernel(AttnParams p, const __grid_constant__ CUtensorMap tmap,
                           const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap qmap_pf) {
-  pdl_begin();
+  pdl_launch_dependents();
   extern __shared__ __align__(1024) uint8_t tc_smem_raw[];
   const uint32_t raw = ptx::smem_addr(tc_smem_raw);
   TcShared& sm = *reinterpret_cast<TcShared*>(tc_smem_raw + ((1024 - (raw & 1023)) & 1023));
   pf::Buffers& pbuf = *reinterpret_cast<pf::Buffers*>(&sm);
-  const int32_t* plan = p.plan;
-  if (plan[kHdrMagic] != kPlanMagic) return;
-  if (int(blockIdx.x) >= plan[kHdrNumTcCtas]) return;
-  const int tc_first = plan[kHdrTcFirst];
-  const int pf_first = plan[kHdrPfFirst];
-  const int n_tc = pf_first - tc_first;
-  const int n_pf = plan[kHdrNumItems] - pf_first;
-  if (n_tc <= 0 && n_pf <= 0) return;
-  const bool causal = plan[kHdrCausal] != 0;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  // Prologue: shared memory, TMEM and the tensor maps only (no global memory
+  // written by earlier kernels), so it overlaps the preceding kernel's tail.
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kKStages; ++s) {
@@ -752,6 +746,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   ptx::tc_fence_before();
   __syncthreads();
   ptx::tc_fence_after();
+
+  // The plan and every input are outputs of earlier kernels (or copies).
+  pdl_wait();
+  const int32_t* plan = p.plan;
+  const bool live = plan[kHdrMagic] == kPlanMagic && int(blockIdx.x) < plan[kHdrNumTcCtas];
+  const int tc_first = live ? plan[kHdrTcFirst] : 0;
+  const int pf_first = live ? plan[kHdrPfFirst] : 0;
+  const int n_tc = live ? pf_first - tc_first : 0;
+  const int n_pf = live ? plan[kHdrNumItems] - pf_first : 0;
+  const bool causal = live && plan[kHdrCausal] != 0;
 
   // Both phases read one item sequence (the ring of claimed item indices);
   // each warp keeps its position across the phase change.

@@ -13,9 +13,15 @@ namespace aspire {
 // one runs (its launch latency hides under this kernel's tail), and wait
 // blocks until the preceding kernel has completed and its writes are visible.
 // Without such a dependency both are no-ops.
-__device__ __forceinline__ void pdl_begin() {
+__device__ __forceinline__ void pdl_launch_dependents() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+// Waits until the preceding kernels of the stream have completed and their
+// memory is visible; nothing that reads their outputs may run before it.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_begin() {
+  pdl_launch_dependents();
+  pdl_wait();
 }
 
 
