@@ -52,7 +52,8 @@ extern "C" {
 /* Device status word bits (written by kernels instead of faulting). */
 #define ASPIRE_STATUS_BAD_PAGE 1u  /* a page id >= num_pages_total was skipped */
 #define ASPIRE_STATUS_BAD_PLAN 2u  /* a work item was inconsistent and skipped */
-#define ASPIRE_STATUS_BAD_ROW 4u   /* selection row/argument out of range      */
+#define ASPIRE_STATUS_BAD_ROW 4u   /* attention row past q_rows, or selection
+                                      row/argument out of range               */
 #define ASPIRE_STATUS_TIMEOUT 8u   /* a bounded device wait expired; the CTA stopped */
 
 /* ------------------------------------------------------------------------ */
