@@ -791,12 +791,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       } else if (warp == kVProducerWarp) {
         run_producer<pf::kVStages>(p, &tmap, sm, pbuf.v, sm.pf.v_full, sm.pf.v_empty, 1, false, pf_first, n_pf,
                                    kHdrPfClaim, kPfMaxRows, lane, k);
-      } else if (warp == 1) {
-        pf::run_mma(p, &qmap_pf, sm, pbuf, lane, k);
-      } else if (warp == kPvWarp) {
-        // No prefill role: follow the item sequence to its end.
-        while (seq_read(sm, k, lane, p.status) >= 0) {
-        }
+      } else if (warp == 1 || warp == kPvWarp) {
+        // One MMA-issuing warp per item half.
+        pf::run_mma(p, &qmap_pf, sm, pbuf, warp == 1 ? 0 : 1, lane, k);
       } else {
         pf::consume_items(p, sm, causal, (warp - kFirstSoftmaxWarp) / 4, warp & 3, lane, k);
       }
