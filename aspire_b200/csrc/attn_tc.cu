@@ -20,6 +20,8 @@
 //              completes.  It also TMA-loads each item's query tile while the
 //              previous item finishes.
 //   warp 11    P.V issuer: a V stage is released when its PV completes.
+//              (In the prefill phase warps 1 and 11 issue the products of
+//              the item's two halves.)
 //   warps 2-9  softmax / epilogue in two warpgroups that split the item's N
 //              columns in halves: thread r of a group owns TMEM lane r, i.e.
 //              token r of the S tile and dim r of the O tile, for the group's
