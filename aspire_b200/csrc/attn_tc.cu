@@ -104,6 +104,21 @@ static_assert(sizeof(TcShared) + 1024 <= 227 * 1024, "tcgen05 kernel shared memo
 static_assert(sizeof(pf::Buffers) <= offsetof(TcShared, red), "prefill buffers overlap decode state");
 static_assert(kNMax % 16 == 0 && kNMax <= 64, "N tile must be a multiple of 16 and fit a 64-column buffer");
 
+// Columns N of an item's products: its packed rows padded to 16, or kNMax for
+// every item of a launch with short items.  Each width has its own softmax
+// loop (consume_item<N / 2>), and a CTA alternates between widths from item
+// to item; with items of a few tiles (split-KV chunks of <= 2048 tokens, as in
+// a TP-8 rank's share of the heads) the switches, whose code must come back
+// into the instruction cache under full HBM load, cost more than the padded
+// columns, so such launches run one width.  Measured per mixed layer-call
+// (B=64, 32k, Qwen3-8B heads): -7.5 % at a TP-8 share (1920-token chunks),
+// -1.5 % at TP-4 (3840), +2 % at TP-2 (7680); launches with the dump keep the
+// exact widths (their dump path is longer per column).
+constexpr int kUniformColumnsMaxChunk = 2048;
+__device__ __forceinline__ int item_columns(int nrows, bool uniform) {
+  return uniform ? kNMax : (nrows + 15) / 16 * 16;
+}
+
 // Barrier of one softmax warpgroup's 128 threads on an mbarrier (bounded, so that a thread
 // that stopped on a timeout cannot leave the others blocked).
 __device__ __forceinline__ bool group_sync(TcShared& sm, uint64_t& grp, uint32_t& uses, uint32_t* status) {
@@ -126,7 +141,8 @@ __device__ __forceinline__ bool group_sync(TcShared& sm, uint64_t& grp, uint32_t
 // the CTA's shared memory), so each loop adds offsets to a base descriptor.
 
 // QK^T of every tile, and the query-tile loads (warp 1).
-__device__ void run_qk(const AttnParams& p, const CUtensorMap* qmap, TcShared& sm, int lane, uint32_t& k) {
+__device__ void run_qk(const AttnParams& p, const CUtensorMap* qmap, TcShared& sm, int lane, uint32_t& k,
+                       bool uniform) {
   const uint32_t tmem = sm.tmem_base;
   uint32_t g = 0, items_done = 0;
   bool ok = true;
@@ -145,7 +161,7 @@ __device__ void run_qk(const AttnParams& p, const CUtensorMap* qmap, TcShared& s
     const WorkItem it = load_item(p.plan, ii);
     const int nt = n_tiles_of(it);
     const int nrows = it.pq_end - it.pq_begin;
-    const uint32_t N = uint32_t((nrows + 15) / 16 * 16);
+    const uint32_t N = uint32_t(item_columns(nrows, uniform));
     const uint32_t idesc_qk = ptx::idesc_bf16(128, N, false, false);
     if (!wait_bar(sm, sm.q_full, items_done & 1, p.status)) {
       ok = false;
@@ -202,7 +218,7 @@ __device__ void run_qk(const AttnParams& p, const CUtensorMap* qmap, TcShared& s
 }
 
 // P.V of every tile into the O accumulator (warp 11).
-__device__ void run_pv(const AttnParams& p, TcShared& sm, int lane, uint32_t& k) {
+__device__ void run_pv(const AttnParams& p, TcShared& sm, int lane, uint32_t& k, bool uniform) {
   const uint32_t tmem = sm.tmem_base;
   uint32_t g = 0, items_done = 0;
   bool ok = true;
@@ -214,7 +230,7 @@ __device__ void run_pv(const AttnParams& p, TcShared& sm, int lane, uint32_t& k)
     const WorkItem it = load_item(p.plan, ii);
     const int nt = n_tiles_of(it);
     const int nrows = it.pq_end - it.pq_begin;
-    const uint32_t N = uint32_t((nrows + 15) / 16 * 16);
+    const uint32_t N = uint32_t(item_columns(nrows, uniform));
     const uint32_t idesc_pv = ptx::idesc_bf16(128, N, true, true);
     for (int t = 0; t < nt && ok; ++t, ++g) {
       const uint32_t vs = g % kVStages, pb = g % 2;
@@ -634,7 +650,8 @@ __device__ bool consume_item(const AttnParams& p, TcShared& sm, const WorkItem& 
   return true;
 }
 
-__device__ void consume_items(const AttnParams& p, TcShared& sm, bool causal, int warp, int lane, uint32_t& k) {
+__device__ void consume_items(const AttnParams& p, TcShared& sm, bool causal, int warp, int lane, uint32_t& k,
+                              bool uniform) {
   const int wq = warp & 3;
   const int wg = (warp - kFirstSoftmaxWarp) / 4;  // softmax warpgroup 0 or 1
   const int r = wq * 32 + lane;                    // TMEM lane = S-tile token = O-tile dim
@@ -655,7 +672,7 @@ __device__ void consume_items(const AttnParams& p, TcShared& sm, bool causal, in
       for (int j = wg; j < nrows; j += 2) store_final(p, it, it.pq_begin + j, r, 0.f, -INFINITY);
       continue;
     }
-    const int N = (nrows + 15) / 16 * 16;
+    const int N = item_columns(nrows, uniform);
     // Items whose columns include dump rows (query 0 or the last query, with a
     // dump buffer) take the instantiation that carries the dump path.
     const bool dump_item = p.dump != nullptr && (it.pq_begin < p.group || (it.q_len > 1 && (it.q_len - 1) * p.group < it.pq_end));
@@ -679,8 +696,9 @@ __device__ void consume_items(const AttnParams& p, TcShared& sm, bool causal, in
   }
 }
 
-__device__ void run_consumer(const AttnParams& p, TcShared& sm, bool causal, int warp, int lane, uint32_t& k) {
-  consume_items(p, sm, causal, warp, lane, k);
+__device__ void run_consumer(const AttnParams& p, TcShared& sm, bool causal, int warp, int lane, uint32_t& k,
+                             bool uniform) {
+  consume_items(p, sm, causal, warp, lane, k, uniform);
   // The bulk stores of each group's last item (issued by its thread 0) finish
   // before the CTA exits.
   if (lane == 0 && (warp - kFirstSoftmaxWarp) % 4 == 0) ptx::bulk_wait_all();
@@ -758,6 +776,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const int n_tc = live ? pf_first - tc_first : 0;
   const int n_pf = live ? plan[kHdrNumItems] - pf_first : 0;
   const bool causal = live && plan[kHdrCausal] != 0;
+  const int chunk_tokens = live ? plan[kHdrChunkTokens] : 0;
+  const bool uniform = p.dump == nullptr && chunk_tokens > 0 && chunk_tokens <= kUniformColumnsMaxChunk;
 
   // Both phases read one item sequence (the ring of claimed item indices);
   // each warp keeps its position across the phase change.
@@ -771,11 +791,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       run_producer<kVStages>(p, &tmap, sm, sm.v, sm.v_full, sm.v_empty, 1, false, tc_first, n_tc, kHdrTcClaim,
                              kNMax, lane, k);
     } else if (warp == 1) {
-      run_qk(p, &qmap, sm, lane, k);
+      run_qk(p, &qmap, sm, lane, k, uniform);
     } else if (warp == kPvWarp) {
-      run_pv(p, sm, lane, k);
+      run_pv(p, sm, lane, k, uniform);
     } else {
-      run_consumer(p, sm, causal, warp, lane, k);
+      run_consumer(p, sm, causal, warp, lane, k, uniform);
     }
   }
   // Phase 2: the prefill list, in the same shared memory and TMEM.  Every

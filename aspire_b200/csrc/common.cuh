@@ -38,6 +38,7 @@ enum PlanHeader : int {
   kHdrTcClaim = 14,          // tcgen05 items claimed so far (0 at upload; the merge kernel resets it)
   kHdrPfFirst = 15,          // index of the first prefill item; they run to kHdrNumItems
   kHdrPfClaim = 16,          // prefill items claimed so far (same rule as kHdrTcClaim)
+  kHdrChunkTokens = 17,      // the plan's common split-KV chunk length (tokens)
   kHdrWords = 32,
 };
 constexpr int32_t kPlanMagic = 0x41535042;  // "ASPB"

@@ -257,6 +257,7 @@ __global__ void __launch_bounds__(kDevPlanThreads) aspire_plan_device_kernel(Dev
     w[kHdrTcClaim] = 0;
     w[kHdrPfFirst] = int32_t(n_decode);
     w[kHdrPfClaim] = 0;
+    w[kHdrChunkTokens] = int32_t(chunk);
     w[kHdrMagic] = kPlanMagic;
   }
 }

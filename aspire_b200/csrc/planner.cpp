@@ -253,6 +253,7 @@ int plan_impl(const int32_t* qo_indptr, const int32_t* kv_indptr, const int32_t*
   w[kHdrTcClaim] = 0;
   w[kHdrPfFirst] = n_gather + n_decode_tc;
   w[kHdrPfClaim] = 0;
+  w[kHdrChunkTokens] = static_cast<int32_t>(chunk);
   w[kHdrOffItems] = static_cast<int32_t>(off_items);
   w[kHdrOffMerge] = static_cast<int32_t>(off_merge);
   w[kHdrNumMerge] = num_merge;

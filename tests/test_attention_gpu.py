@@ -57,6 +57,20 @@ def test_mixed_ragged_split_kv(cuda_device, hq, hkv, draft_fraction):
     assert_attention_close(out, lse, ref_out, ref_lse)
 
 
+def test_exact_widths_with_long_chunks(cuda_device):
+    """A plan whose split-KV chunks exceed 2048 tokens: the kernel runs every
+    item at its own padded width (16/32/48 columns) instead of one common width
+    (the mode every smaller test above runs in)."""
+    lay = make_layout(batch=16, ctx=20000, num_qo_heads=32, num_kv_heads=8, draft_fraction=0.5, budget_pages=40,
+                      seed=21)
+    q, kv = make_inputs(lay, cuda_device, seed=21)
+    out, lse, _, w = run_attention(lay, q, kv)
+    assert w.plan_info.chunk_tokens > 2048 and w.plan_info.num_merge > 0
+    assert len(set(((lay.q_lens * 4 + 15) // 16).tolist())) > 1, "the case must mix item widths"
+    ref_out, ref_lse, _ = oracle_attention(lay, q, kv)
+    assert_attention_close(out, lse, ref_out, ref_lse)
+
+
 def _custom_layout(q_lens, kv_lens, hq=16, hkv=8, seed=0):
     rng = np.random.default_rng(seed)
     B = len(q_lens)

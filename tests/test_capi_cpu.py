@@ -58,6 +58,7 @@ def test_plan_covers_every_token_once(built_library, draft_fraction):
     assert rc == 0, built_library.aspire_last_error()
     w, items = _decode(buf, info)
     assert w[0] == 0x41535042
+    assert int(w[17]) == info.chunk_tokens  # the chunk length the kernel reads to pick its column widths
     group = 4
     cover = {}
     for it in items:
