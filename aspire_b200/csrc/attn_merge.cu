@@ -9,6 +9,9 @@
 // One warp per (merge group, packed row): lanes split the chunks for the LSE
 // reduction and the 128 dims (4 each, 16-byte loads) for the weighted sum;
 // chunks are always combined in chunk order, so the result is deterministic.
+// The pass waits on few memory round trips (the unit, its descriptor, then the
+// LSEs and the first chunks' rows together), since a warp merges about one
+// row and the kernel sits between two attention launches.
 // The grid is fixed and the work list comes from the device plan, so a
 // captured graph stays valid across re-plans.  It also rearms the tcgen05
 // kernel's item counters.
@@ -43,14 +46,48 @@ __global__ void __launch_bounds__(kMergeThreads) aspire_attn_merge_kernel(AttnPa
     const int n = md.n_chunks;
     const int64_t row0 = int64_t(md.partial_base) + j;  // partial row of chunk c: row0 + c * nrows
 
-    float m = -INFINITY;
-    for (int c = lane; c < n; c += 32) m = fmaxf(m, __ldcg(plse + row0 + int64_t(c) * md.nrows));
-#pragma unroll
-    for (int off = 16; off >= 1; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
-
+    const float4* orow = reinterpret_cast<const float4*>(p.partial_o + row0 * kHeadDim) + lane;
+    const int64_t ostep = int64_t(md.nrows) * (kHeadDim / 4);  // float4s between chunks of the row
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
     float wsum = 0.f;
-    if (m != -INFINITY) {
+    float m = -INFINITY;
+    if (n <= 32) {
+      // One memory round trip for the LSEs (one per lane) and the first eight
+      // chunks' rows together, since the rows' loads do not need the weights.
+      const float lse_lane = lane < n ? __ldcg(plse + row0 + int64_t(lane) * md.nrows) : -INFINITY;
+      float4 ov[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) ov[i] = i < n ? __ldcg(orow + i * ostep) : make_float4(0.f, 0.f, 0.f, 0.f);
+      m = lse_lane;
+#pragma unroll
+      for (int off = 16; off >= 1; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+      if (m != -INFINITY) {
+        const float w_lane = lane < n ? ex2(lse_lane - m) : 0.f;
+        for (int c0 = 0; c0 < n; c0 += 8) {
+          if (c0 > 0) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+              ov[i] = c0 + i < n ? __ldcg(orow + (c0 + i) * ostep) : make_float4(0.f, 0.f, 0.f, 0.f);
+          }
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const float w = __shfl_sync(0xffffffffu, w_lane, (c0 + i) & 31);
+            if (c0 + i < n) {  // chunk order, as in the general path below
+              wsum += w;
+              acc.x = fmaf(w, ov[i].x, acc.x);
+              acc.y = fmaf(w, ov[i].y, acc.y);
+              acc.z = fmaf(w, ov[i].z, acc.z);
+              acc.w = fmaf(w, ov[i].w, acc.w);
+            }
+          }
+        }
+      }
+    } else {
+      for (int c = lane; c < n; c += 32) m = fmaxf(m, __ldcg(plse + row0 + int64_t(c) * md.nrows));
+#pragma unroll
+      for (int off = 16; off >= 1; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+    }
+    if (n > 32 && m != -INFINITY) {
       for (int c0 = 0; c0 < n; c0 += 32) {
         const int cl = c0 + lane;
         const float w_lane = cl < n ? ex2(__ldcg(plse + row0 + int64_t(cl) * md.nrows) - m) : 0.f;
