@@ -111,9 +111,10 @@ static_assert(kNMax % 16 == 0 && kNMax <= 64, "N tile must be a multiple of 16 a
 // a TP-8 rank's share of the heads) the switches, whose code must come back
 // into the instruction cache under full HBM load, cost more than the padded
 // columns, so such launches run one width.  Measured per mixed layer-call
-// (B=64, 32k, Qwen3-8B heads): -7.5 % at a TP-8 share (1920-token chunks),
-// -1.5 % at TP-4 (3840), +2 % at TP-2 (7680); launches with the dump keep the
-// exact widths (their dump path is longer per column).
+// (B=64, 32k, Qwen3-8B heads): -5 % at a TP-8 share (1920-token chunks); one
+// width everywhere was -1.5 % at TP-4 (3840) and +2 % at TP-2 (7680).
+// Launches with the dump keep the exact widths (their dump path is longer
+// per column).
 constexpr int kUniformColumnsMaxChunk = 2048;
 __device__ __forceinline__ int item_columns(int nrows, bool uniform) {
   return uniform ? kNMax : (nrows + 15) / 16 * 16;

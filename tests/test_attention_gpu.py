@@ -71,6 +71,20 @@ def test_exact_widths_with_long_chunks(cuda_device):
     assert_attention_close(out, lse, ref_out, ref_lse)
 
 
+@pytest.mark.parametrize("hq,hkv", [(40, 8), (56, 8), (24, 1)])
+def test_common_width_groups_not_dividing_the_tile(cuda_device, hq, hkv):
+    """Short chunks (every item at the common 48-column width) with GQA groups
+    of 5, 7 and 24: the query tile holds 45, 42 and 48 rows, the rest of its
+    columns stay zero."""
+    lay = make_layout(batch=7, ctx=1900, num_qo_heads=hq, num_kv_heads=hkv, draft_fraction=0.4, budget_pages=23,
+                      seed=hq)
+    q, kv = make_inputs(lay, cuda_device, seed=hq)
+    out, lse, _, w = run_attention(lay, q, kv)
+    assert w.plan_info.chunk_tokens <= 2048
+    ref_out, ref_lse, _ = oracle_attention(lay, q, kv)
+    assert_attention_close(out, lse, ref_out, ref_lse)
+
+
 def _custom_layout(q_lens, kv_lens, hq=16, hkv=8, seed=0):
     rng = np.random.default_rng(seed)
     B = len(q_lens)
