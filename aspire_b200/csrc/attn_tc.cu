@@ -107,15 +107,15 @@ static_assert(kNMax % 16 == 0 && kNMax <= 64, "N tile must be a multiple of 16 a
 // Columns N of an item's products: its packed rows padded to 16, or kNMax for
 // every item of a launch with short items.  Each width has its own softmax
 // loop (consume_item<N / 2>), and a CTA alternates between widths from item
-// to item; with items of a few tiles (split-KV chunks of <= 2048 tokens, as in
-// a TP-8 rank's share of the heads) the switches, whose code must come back
-// into the instruction cache under full HBM load, cost more than the padded
-// columns, so such launches run one width.  Measured per mixed layer-call
-// (B=64, 32k, Qwen3-8B heads): -5 % at a TP-8 share (1920-token chunks); one
-// width everywhere was -1.5 % at TP-4 (3840) and +2 % at TP-2 (7680).
-// Launches with the dump keep the exact widths (their dump path is longer
-// per column).
-constexpr int kUniformColumnsMaxChunk = 2048;
+// to item; with items of a few tiles (split-KV chunks of <= 4096 tokens, as in
+// a TP-4 or TP-8 rank's share of the heads) the switches, whose code must come
+// back into the instruction cache under full HBM load, cost more than the
+// padded columns, so such launches run one width.  Measured per mixed
+// layer-call (B=64, 32k, Qwen3-8B heads): -5 % at a TP-8 share with 1920-token
+// chunks, -2.5 % with 3840-token chunks; one width everywhere was +2 % at TP-2
+// (7680-token chunks).  Launches with the dump keep the exact widths (their
+// dump path is longer per column).
+constexpr int kUniformColumnsMaxChunk = 4096;
 __device__ __forceinline__ int item_columns(int nrows, bool uniform) {
   return uniform ? kNMax : (nrows + 15) / 16 * 16;
 }

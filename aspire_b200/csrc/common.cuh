@@ -82,6 +82,10 @@ struct MergeDesc {
 static_assert(sizeof(MergeDesc) == 32, "MergeDesc must stay 32 bytes");
 constexpr int kMergeWords = sizeof(MergeDesc) / 4;
 
+// Split-KV chunk length = total KV tokens / (SMs x kItemsPerCta), at least
+// 512, rounded up to 128 (both planners).
+constexpr int kItemsPerCta = 2;
+
 // Resident CTAs per SM of each kernel class (sets the persistent grids).
 constexpr int kGatherCtasPerSm = 4;
 constexpr int kTcCtasPerSm = 1;

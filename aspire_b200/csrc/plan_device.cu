@@ -120,7 +120,7 @@ __global__ void __launch_bounds__(kDevPlanThreads) aspire_plan_device_kernel(Dev
   }
   int64_t total_tokens;
   block_exclusive_scan(tokens, warp_sums, &total_tokens);
-  const int64_t target = int64_t(p.num_sms) * 4;
+  const int64_t target = int64_t(p.num_sms) * kItemsPerCta;
   int64_t chunk = (total_tokens + target - 1) / target;
   chunk = chunk < 512 ? 512 : chunk;
   chunk = (chunk + 127) / 128 * 128;

@@ -154,9 +154,11 @@ int plan_impl(const int32_t* qo_indptr, const int32_t* kv_indptr, const int32_t*
     }
   }
 
-  // Common chunk length: several items per CTA, never below 512 tokens,
-  // a multiple of 128 tokens (one tcgen05 KV tile = 8 pages).
-  const int64_t target_items = int64_t(num_sms) * 4;
+  // Common chunk length: about two items per CTA (each item boundary costs
+  // a few microseconds of claim, query reload and epilogue latency; run-time
+  // claiming longest first balances the rest), never below 512 tokens, a
+  // multiple of 128 tokens (one tcgen05 KV tile = 8 pages).
+  const int64_t target_items = int64_t(num_sms) * kItemsPerCta;
   int64_t chunk = (total_tokens + target_items - 1) / std::max<int64_t>(target_items, 1);
   chunk = std::max<int64_t>(chunk, 512);
   chunk = (chunk + 127) / 128 * 128;
