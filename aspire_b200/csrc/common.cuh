@@ -83,8 +83,18 @@ static_assert(sizeof(MergeDesc) == 32, "MergeDesc must stay 32 bytes");
 constexpr int kMergeWords = sizeof(MergeDesc) / 4;
 
 // Split-KV chunk length = total KV tokens / (SMs x kItemsPerCta), at least
-// 512, rounded up to 128 (both planners).
+// 512, rounded up to 128 (both planners).  When that length would split no
+// (row, KV head, query-tile) group, the items are whole groups of similar
+// size, which balance poorly at two per CTA: the length then targets
+// kItemsPerCtaUnsplit per CTA (a full-context refresh layer at TP 1).
 constexpr int kItemsPerCta = 2;
+constexpr int kItemsPerCtaUnsplit = 4;
+__host__ __device__ inline int64_t chunk_for(int64_t total_tokens, int64_t num_sms, int64_t per_cta) {
+  const int64_t target = num_sms * per_cta;
+  int64_t chunk = (total_tokens + target - 1) / (target > 0 ? target : 1);
+  chunk = chunk < 512 ? 512 : chunk;
+  return (chunk + 127) / 128 * 128;
+}
 
 // Resident CTAs per SM of each kernel class (sets the persistent grids).
 constexpr int kGatherCtasPerSm = 4;

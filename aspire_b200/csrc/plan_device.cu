@@ -99,16 +99,21 @@ __global__ void __launch_bounds__(kDevPlanThreads) aspire_plan_device_kernel(Dev
   pdl_begin();
   __shared__ int64_t warp_sums[32];
   __shared__ int32_t bucket[2][kCostBuckets];  // per kernel list: decode (1), prefill (2)
-  __shared__ int bad;
+  __shared__ int bad, max_span;
   const int tid = threadIdx.x, nthreads = blockDim.x;
-  if (tid == 0) bad = 0;
+  if (tid == 0) {
+    bad = 0;
+    max_span = 0;
+  }
   for (int i = tid; i < 2 * kCostBuckets; i += nthreads) bucket[i / kCostBuckets][i % kCostBuckets] = 0;
   __syncthreads();
   const int rpt = (p.batch + nthreads - 1) / nthreads;  // rows per thread
   const int r0 = min(tid * rpt, p.batch), r1 = min(r0 + rpt, p.batch);
 
-  // Total tokens over (row, head, q-tile) groups -> the common chunk length.
+  // Total tokens over (row, head, q-tile) groups and the longest group span
+  // -> the common chunk length.
   int64_t tokens = 0;
+  int my_max_span = 0;
   for (int b = r0; b < r1; ++b) {
     const RowShape s = row_shape(p, b);
     if (!s.valid) bad = 1;
@@ -116,14 +121,14 @@ __global__ void __launch_bounds__(kDevPlanThreads) aspire_plan_device_kernel(Dev
     for (int qt = 0; qt < s.ntq; ++qt) {
       const int32_t span = tile_span(p, s, qt * s.tile, min(s.nq, (qt + 1) * s.tile));
       tokens += int64_t(p.num_kv_heads) * (span > 1 ? span : 1);
+      my_max_span = max(my_max_span, int(span));
     }
   }
+  atomicMax(&max_span, my_max_span);
   int64_t total_tokens;
-  block_exclusive_scan(tokens, warp_sums, &total_tokens);
-  const int64_t target = int64_t(p.num_sms) * kItemsPerCta;
-  int64_t chunk = (total_tokens + target - 1) / target;
-  chunk = chunk < 512 ? 512 : chunk;
-  chunk = (chunk + 127) / 128 * 128;
+  block_exclusive_scan(tokens, warp_sums, &total_tokens);  // (its barriers publish max_span)
+  int64_t chunk = chunk_for(total_tokens, p.num_sms, kItemsPerCta);
+  if (chunk >= max_span) chunk = chunk_for(total_tokens, p.num_sms, kItemsPerCtaUnsplit);
 
   // Per-thread counts; item lengths into the cost histogram.
   int64_t n_items = 0, n_merge = 0, n_prow = 0, n_units = 0;

@@ -158,10 +158,10 @@ int plan_impl(const int32_t* qo_indptr, const int32_t* kv_indptr, const int32_t*
   // a few microseconds of claim, query reload and epilogue latency; run-time
   // claiming longest first balances the rest), never below 512 tokens, a
   // multiple of 128 tokens (one tcgen05 KV tile = 8 pages).
-  const int64_t target_items = int64_t(num_sms) * kItemsPerCta;
-  int64_t chunk = (total_tokens + target_items - 1) / std::max<int64_t>(target_items, 1);
-  chunk = std::max<int64_t>(chunk, 512);
-  chunk = (chunk + 127) / 128 * 128;
+  int32_t max_span = 0;
+  for (const GroupDesc& g : groups) max_span = std::max(max_span, g.span);
+  int64_t chunk = chunk_for(total_tokens, num_sms, kItemsPerCta);
+  if (chunk >= max_span) chunk = chunk_for(total_tokens, num_sms, kItemsPerCtaUnsplit);
 
   std::vector<WorkItem> gather_items, tc_items, pf_items;
   std::vector<MergeDesc> merges;
