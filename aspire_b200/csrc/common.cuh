@@ -84,9 +84,11 @@ constexpr int kMergeWords = sizeof(MergeDesc) / 4;
 
 // Split-KV chunk length = total KV tokens / (SMs x kItemsPerCta), at least
 // 512, rounded up to 128 (both planners).  When that length would split no
-// (row, KV head, query-tile) group, the items are whole groups of similar
-// size, which balance poorly at two per CTA: the length then targets
-// kItemsPerCtaUnsplit per CTA (a full-context refresh layer at TP 1).
+// (row, KV head, query-tile) group and the groups' spans are within a factor
+// of two of each other, the items are whole groups of similar size, which
+// balance poorly at two per CTA: the length then targets kItemsPerCtaUnsplit
+// per CTA (a full-context refresh layer at TP 1).  Groups of spread-out sizes
+// (the query tiles of a causal prefill chunk) balance well whole.
 constexpr int kItemsPerCta = 2;
 constexpr int kItemsPerCtaUnsplit = 4;
 __host__ __device__ inline int64_t chunk_for(int64_t total_tokens, int64_t num_sms, int64_t per_cta) {

@@ -99,11 +99,12 @@ __global__ void __launch_bounds__(kDevPlanThreads) aspire_plan_device_kernel(Dev
   pdl_begin();
   __shared__ int64_t warp_sums[32];
   __shared__ int32_t bucket[2][kCostBuckets];  // per kernel list: decode (1), prefill (2)
-  __shared__ int bad, max_span;
+  __shared__ int bad, max_span, min_span;
   const int tid = threadIdx.x, nthreads = blockDim.x;
   if (tid == 0) {
     bad = 0;
     max_span = 0;
+    min_span = INT_MAX;
   }
   for (int i = tid; i < 2 * kCostBuckets; i += nthreads) bucket[i / kCostBuckets][i % kCostBuckets] = 0;
   __syncthreads();
@@ -113,7 +114,7 @@ __global__ void __launch_bounds__(kDevPlanThreads) aspire_plan_device_kernel(Dev
   // Total tokens over (row, head, q-tile) groups and the longest group span
   // -> the common chunk length.
   int64_t tokens = 0;
-  int my_max_span = 0;
+  int my_max_span = 0, my_min_span = INT_MAX;
   for (int b = r0; b < r1; ++b) {
     const RowShape s = row_shape(p, b);
     if (!s.valid) bad = 1;
@@ -122,13 +123,16 @@ __global__ void __launch_bounds__(kDevPlanThreads) aspire_plan_device_kernel(Dev
       const int32_t span = tile_span(p, s, qt * s.tile, min(s.nq, (qt + 1) * s.tile));
       tokens += int64_t(p.num_kv_heads) * (span > 1 ? span : 1);
       my_max_span = max(my_max_span, int(span));
+      my_min_span = min(my_min_span, int(span));
     }
   }
   atomicMax(&max_span, my_max_span);
+  atomicMin(&min_span, my_min_span);
   int64_t total_tokens;
   block_exclusive_scan(tokens, warp_sums, &total_tokens);  // (its barriers publish max_span)
   int64_t chunk = chunk_for(total_tokens, p.num_sms, kItemsPerCta);
-  if (chunk >= max_span) chunk = chunk_for(total_tokens, p.num_sms, kItemsPerCtaUnsplit);
+  if (chunk >= max_span && 2 * int64_t(min_span) >= max_span)
+    chunk = chunk_for(total_tokens, p.num_sms, kItemsPerCtaUnsplit);
 
   // Per-thread counts; item lengths into the cost histogram.
   int64_t n_items = 0, n_merge = 0, n_prow = 0, n_units = 0;
