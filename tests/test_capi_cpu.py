@@ -108,6 +108,53 @@ def test_plan_balances_ctas(built_library):
     assert info.float_bytes < 128 * 1024 * 1024
 
 
+def _expected_chunk(spans, hkv, num_sms):
+    """The planner's chunk rule, restated: about two items per SM, or four when
+    two per SM would split no group and the groups' spans are within 2x."""
+    total = sum(max(s, 1) for s in spans) * hkv
+
+    def chunk_for(per_cta):
+        target = num_sms * per_cta
+        c = max(-(-total // target), 512)
+        return -(-c // 128) * 128
+
+    c = chunk_for(2)
+    if c >= max(spans) and 2 * min(spans) >= max(spans):
+        c = chunk_for(4)
+    return c
+
+
+@pytest.mark.parametrize("case", ["mixed", "full_context", "prefill_spread"])
+def test_plan_chunk_rule(built_library, case):
+    """Decode batches (long verify rows beside short draft rows) get about two
+    items per SM; whole-context rows of equal length, four; the spread-out
+    query tiles of a causal prefill chunk stay whole at two per SM."""
+    num_sms = 148
+    if case == "mixed":
+        lay = make_layout(batch=64, ctx=32768, num_qo_heads=32, num_kv_heads=8, draft_fraction=0.5,
+                          budget_pages=128, seed=0)
+        qo, kvp, kvl = lay.qo_indptr, lay.kv_indptr, lay.kv_lens
+        spans = [int(k) for k in kvl]
+    elif case == "full_context":
+        kvl = np.full(64, 32773, np.int32)
+        qo = np.arange(65, dtype=np.int32)
+        kvp = np.concatenate([[0], np.cumsum((kvl + 15) // 16)]).astype(np.int32)
+        spans = [int(k) for k in kvl]
+    else:  # one 8192-token prefill chunk: 128 query tiles of 64 positions (group 4), each
+        # stopping at its causal span except the tile holding query 0 (all keys)
+        kvl = np.array([8192], np.int32)
+        qo = np.array([0, 8192], np.int32)
+        kvp = np.array([0, 512], np.int32)
+        spans = [8192] + [64 * (t + 1) for t in range(1, 128)]
+    rc, info, _ = _plan(built_library, qo, kvp, kvl, 32, 8, num_sms=num_sms)
+    assert rc == 0, built_library.aspire_last_error()
+    assert info.chunk_tokens == _expected_chunk(spans, 8, num_sms)
+    if case == "mixed":
+        assert info.num_items_tc == 768  # verify rows in two chunks, draft rows whole
+    if case == "prefill_spread":
+        assert info.num_merge == 0 and info.num_items_prefill == 128 * 8
+
+
 def test_plan_rejects_bad_input(built_library):
     rc, _, _ = _plan(built_library, [0, 1], [0, 1], [17], 32, 8)  # 17 tokens need 2 pages
     assert rc == _capi.ASPIRE_ERR_INVALID
