@@ -82,15 +82,16 @@ struct MergeDesc {
 static_assert(sizeof(MergeDesc) == 32, "MergeDesc must stay 32 bytes");
 constexpr int kMergeWords = sizeof(MergeDesc) / 4;
 
-// Split-KV chunk length = total KV tokens / (SMs x kItemsPerCta), at least
-// 512, rounded up to 128 (both planners).  When that length would split no
-// (row, KV head, query-tile) group and the groups' spans are within a factor
-// of two of each other, the items are whole groups of similar size, which
-// balance poorly at two per CTA: the length then targets kItemsPerCtaUnsplit
-// per CTA (a full-context refresh layer at TP 1).  Groups of spread-out sizes
-// (the query tiles of a causal prefill chunk) balance well whole.
-constexpr int kItemsPerCta = 2;
-constexpr int kItemsPerCtaUnsplit = 4;
+// Split-KV chunk length = total KV tokens / (SMs x items per CTA), at least
+// 512, rounded up to 128 (both planners).  Batches whose (row, KV head,
+// query-tile) groups differ in span by more than 2x (long verify rows beside
+// short draft rows, or the query tiles of a causal prefill chunk) take about
+// kItemsPerCtaMixed items per CTA: every item boundary costs a few
+// microseconds, and the spread of item sizes balances the CTAs.  Groups of
+// similar span (a full-context refresh layer) are cut into about
+// kItemsPerCtaUniform per CTA, since fewer equal items balance poorly.
+constexpr int kItemsPerCtaMixed = 2;
+constexpr int kItemsPerCtaUniform = 4;
 __host__ __device__ inline int64_t chunk_for(int64_t total_tokens, int64_t num_sms, int64_t per_cta) {
   const int64_t target = num_sms * per_cta;
   int64_t chunk = (total_tokens + target - 1) / (target > 0 ? target : 1);

@@ -6,7 +6,8 @@
 //
 // It produces the same items as the host planner (planner.cpp): every
 // (row, KV head, packed-query tile) is cut into chunks of one common length
-// (a multiple of 128 tokens, at least 512, sized for ~4 items per SM), with
+// (chunk_for: a multiple of 128 tokens, at least 512, sized for about two
+// or four items per SM by the spread of the groups' spans), with
 // merge descriptors for the split groups.  Rows go to the tcgen05 decode
 // kernel, or to the prefill kernel when their packed queries reach
 // kPfMinRows (the default routing); each list is stored longest first through
@@ -130,9 +131,8 @@ __global__ void __launch_bounds__(kDevPlanThreads) aspire_plan_device_kernel(Dev
   atomicMin(&min_span, my_min_span);
   int64_t total_tokens;
   block_exclusive_scan(tokens, warp_sums, &total_tokens);  // (its barriers publish max_span)
-  int64_t chunk = chunk_for(total_tokens, p.num_sms, kItemsPerCta);
-  if (chunk >= max_span && 2 * int64_t(min_span) >= max_span)
-    chunk = chunk_for(total_tokens, p.num_sms, kItemsPerCtaUnsplit);
+  const bool similar = 2 * int64_t(min_span) >= max_span;
+  const int64_t chunk = chunk_for(total_tokens, p.num_sms, similar ? kItemsPerCtaUniform : kItemsPerCtaMixed);
 
   // Per-thread counts; item lengths into the cost histogram.
   int64_t n_items = 0, n_merge = 0, n_prow = 0, n_units = 0;

@@ -154,18 +154,16 @@ int plan_impl(const int32_t* qo_indptr, const int32_t* kv_indptr, const int32_t*
     }
   }
 
-  // Common chunk length: about two items per CTA (each item boundary costs
-  // a few microseconds of claim, query reload and epilogue latency; run-time
-  // claiming longest first balances the rest), never below 512 tokens, a
-  // multiple of 128 tokens (one tcgen05 KV tile = 8 pages).
+  // Common chunk length (chunk_for): a multiple of 128 tokens (one tcgen05 KV
+  // tile = 8 pages), never below 512; two or four items per CTA by the spread
+  // of the groups' spans.
   int32_t max_span = 0, min_span = INT32_MAX;
   for (const GroupDesc& g : groups) {
     max_span = std::max(max_span, g.span);
     min_span = std::min(min_span, g.span);
   }
-  int64_t chunk = chunk_for(total_tokens, num_sms, kItemsPerCta);
-  if (chunk >= max_span && 2 * int64_t(min_span) >= max_span)
-    chunk = chunk_for(total_tokens, num_sms, kItemsPerCtaUnsplit);
+  const bool similar = 2 * int64_t(min_span) >= max_span;
+  const int64_t chunk = chunk_for(total_tokens, num_sms, similar ? kItemsPerCtaUniform : kItemsPerCtaMixed);
 
   std::vector<WorkItem> gather_items, tc_items, pf_items;
   std::vector<MergeDesc> merges;

@@ -109,8 +109,8 @@ def test_plan_balances_ctas(built_library):
 
 
 def _expected_chunk(spans, hkv, num_sms):
-    """The planner's chunk rule, restated: about two items per SM, or four when
-    two per SM would split no group and the groups' spans are within 2x."""
+    """The planner's chunk rule, restated: about four items per SM when the
+    groups' spans are within 2x of each other, else about two."""
     total = sum(max(s, 1) for s in spans) * hkv
 
     def chunk_for(per_cta):
@@ -118,10 +118,7 @@ def _expected_chunk(spans, hkv, num_sms):
         c = max(-(-total // target), 512)
         return -(-c // 128) * 128
 
-    c = chunk_for(2)
-    if c >= max(spans) and 2 * min(spans) >= max(spans):
-        c = chunk_for(4)
-    return c
+    return chunk_for(4 if 2 * min(spans) >= max(spans) else 2)
 
 
 @pytest.mark.parametrize("case", ["mixed", "full_context", "prefill_spread"])
