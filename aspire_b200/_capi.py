@@ -27,6 +27,7 @@ NOALLOC_FLOAT_BYTES = 8 * 1024 * 1024
 STATUS_BAD_PAGE = 1
 STATUS_BAD_PLAN = 2
 STATUS_BAD_ROW = 4
+STATUS_TIMEOUT = 8
 
 c_int32_p = ctypes.POINTER(ctypes.c_int32)
 
@@ -234,6 +235,8 @@ _SIGNATURES = {
         ctypes.c_int,
         [ctypes.POINTER(AspireAttnArgs), ctypes.POINTER(AspirePlanInfo), ctypes.c_void_p, ctypes.c_void_p],
     ),
+    "aspire_noalloc_status": (ctypes.c_int, [ctypes.POINTER(ctypes.c_uint32), ctypes.c_int32, ctypes.c_void_p]),
+    "aspire_set_wait_limit_ns": (ctypes.c_int, [ctypes.c_uint64]),
     "aspire_append_kv": (ctypes.c_int, [ctypes.POINTER(AspireAppendArgs), ctypes.c_void_p]),
     "aspire_select_pages": (ctypes.c_int, [ctypes.POINTER(AspireSelectArgs), ctypes.c_void_p]),
     "aspire_build_unified_indices": (ctypes.c_int, [ctypes.POINTER(AspireIndicesArgs), ctypes.c_void_p]),
@@ -250,7 +253,7 @@ _SIGNATURES = {
     "aspire_kernel_names": (ctypes.c_char_p, []),
 }
 
-EXPECTED_ABI_VERSION = 3
+EXPECTED_ABI_VERSION = 4
 
 _lib = None
 _lock = threading.Lock()

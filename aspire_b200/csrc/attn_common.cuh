@@ -30,6 +30,7 @@ struct AttnParams {
   const int32_t* plan;       // int workspace + kStatusBytes
   uint32_t* status;          // int workspace (first word)
   float* partial_o;          // float workspace
+  uint64_t wait_ns;          // bound of one pipeline wait of the tcgen05 kernel (ns)
 };
 
 // Page id of logical page lp of a row: from the flat page list at the row's

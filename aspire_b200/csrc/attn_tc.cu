@@ -33,9 +33,10 @@
 //              one 128-thread barrier per group.  P^T is written as bf16
 //              (no-swizzle MN-major), O accumulates in TMEM, finished rows
 //              leave through shared memory by bulk stores.
-// Every mbarrier wait is time-bounded: on timeout the CTA records
-// ASPIRE_STATUS_TIMEOUT, stops, drains its own TMA loads and MMAs, frees
-// TMEM and returns.
+// Every mbarrier wait is time-bounded (1 s unless aspire_set_wait_limit_ns
+// sets another bound): on timeout the CTA records ASPIRE_STATUS_TIMEOUT,
+// stops, drains its own TMA loads and MMAs (those waits keep a fixed 1 s
+// bound), frees TMEM and returns.
 //
 // The same launch then serves the plan's prefill list (long-query rows; see
 // attn_prefill.cuh): a CTA that finds the decode list exhausted waits for its
@@ -96,6 +97,7 @@ struct TcShared {
   pf::Barriers pf;  // prefill phase
   uint64_t seq_full[kSeqDepth], seq_empty[kSeqDepth];
   int seq[kSeqDepth];
+  uint64_t wait_ns;  // bound of one pipeline wait (launch parameter)
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -748,6 +750,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       ptx::mbar_init(ptx::smem_addr(&sm.seq_empty[s]), kSeqReaders);
     }
     sm.abort_flag = 0;
+    sm.wait_ns = p.wait_ns;
     ptx::mbar_fence_init();
   }
   if (warp == 1) {

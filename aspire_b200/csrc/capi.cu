@@ -1,6 +1,7 @@
 // extern "C" entry points of libaspire_b200.so (declared in
 // include/aspire_b200.h): argument checking, launch configuration and
 // error reporting.  No entry point allocates memory or synchronises.
+#include <atomic>
 #include <cmath>
 #include <cstdlib>
 #include <algorithm>
@@ -68,15 +69,40 @@ int current_sm_count(int* out) {
                     "cudaDeviceGetAttribute(SM count)");
 }
 
+// Dynamic shared memory a kernel has been opted in to, per device: the
+// attribute set by cudaFuncSetAttribute applies to the current device only,
+// so a host thread that drives several GPUs sets it once on each.
+constexpr int kMaxDevices = 64;
+struct SmemOptIn {
+  std::atomic<int> bytes[kMaxDevices];
+  SmemOptIn() {
+    for (auto& b : bytes) b.store(48 * 1024);
+  }
+};
+
 // Opt-in to large dynamic shared memory once per (kernel, device, size).
-int ensure_smem(const void* func, size_t bytes, int* configured_bytes) {
-  if (int(bytes) <= *configured_bytes) return ASPIRE_OK;
-  int rc = check_cuda(cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           static_cast<int>(bytes)),
-                      "cudaFuncSetAttribute(max dynamic smem)");
-  if (rc == ASPIRE_OK) *configured_bytes = static_cast<int>(bytes);
+int ensure_smem(const void* func, size_t bytes, SmemOptIn& cache) {
+  int dev = 0;
+  int rc = check_cuda(cudaGetDevice(&dev), "cudaGetDevice");
+  if (rc) return rc;
+  const bool cached = dev >= 0 && dev < kMaxDevices;
+  if (cached && int(bytes) <= cache.bytes[dev].load(std::memory_order_relaxed)) return ASPIRE_OK;
+  rc = check_cuda(cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes)),
+                  "cudaFuncSetAttribute(max dynamic smem)");
+  if (rc == ASPIRE_OK && cached) {
+    int cur = cache.bytes[dev].load(std::memory_order_relaxed);
+    while (cur < int(bytes) && !cache.bytes[dev].compare_exchange_weak(cur, int(bytes))) {
+    }
+  }
   return rc;
 }
+
+SmemOptIn g_gather_smem, g_tc_smem, g_sel_smem;
+
+// Bound of one pipeline wait of the tcgen05 kernel (aspire_set_wait_limit_ns);
+// 0 selects the default.
+constexpr uint64_t kDefaultWaitNs = 1000000000ull;
+std::atomic<uint64_t> g_wait_limit_ns{0};
 
 // cuTensorMapEncodeTiled through the runtime's driver entry point (no libcuda link).
 PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
@@ -151,6 +177,36 @@ bool tc_env_enabled() {
 }
 
 }  // namespace
+
+int check_attention_args(const AspireAttnArgs* a, const AspirePlanInfo* plan, const char* who) {
+  const std::string w(who);
+  if (!a || !plan) return set_error(ASPIRE_ERR_INVALID, w + ": null argument");
+  if (a->head_dim != kHeadDim) return set_error(ASPIRE_ERR_INVALID, w + ": head_dim must be 128");
+  if (a->page_size != kPageSize) return set_error(ASPIRE_ERR_INVALID, w + ": page_size must be 16");
+  if (a->num_kv_heads <= 0 || a->num_qo_heads % a->num_kv_heads != 0)
+    return set_error(ASPIRE_ERR_INVALID, w + ": bad head counts");
+  if (a->num_qo_heads != plan->num_qo_heads || a->num_kv_heads != plan->num_kv_heads)
+    return set_error(ASPIRE_ERR_INVALID, w + ": head counts differ from the plan's");
+  if (!a->q || !a->kv_cache || !a->out) return set_error(ASPIRE_ERR_INVALID, w + ": null tensor pointer");
+  if (!a->kv_indices && (!a->mode_flags || !a->draft_table || !a->block_table))
+    return set_error(ASPIRE_ERR_INVALID, w + ": kv_indices or the three page tables are required");
+  if ((reinterpret_cast<uintptr_t>(a->q) | reinterpret_cast<uintptr_t>(a->kv_cache)) & 15)
+    return set_error(ASPIRE_ERR_INVALID, w + ": q / kv_cache not 16-byte aligned");
+  if ((a->q_stride_n | a->q_stride_h) & 7)
+    return set_error(ASPIRE_ERR_INVALID, w + ": q strides must be multiples of 8 elements");
+  if (a->dump && (a->dump_num_heads < a->num_qo_heads || a->dump_kv_stride <= 0))
+    return set_error(ASPIRE_ERR_INVALID, w + ": bad dump geometry");
+  if (a->q_rows <= 0 || a->q_rows > INT32_MAX)
+    return set_error(ASPIRE_ERR_INVALID, w + ": q_rows (rows of q) must be set");
+  const int group = a->num_qo_heads / a->num_kv_heads;
+  const bool run_tc = plan->tc_enabled && group <= kTcQTile;
+  if (run_tc && ((reinterpret_cast<uintptr_t>(a->out) & 15) || ((a->o_stride_n | a->o_stride_h) & 7)))
+    return set_error(ASPIRE_ERR_INVALID, w + ": out must be 16-byte aligned with strides in multiples of 8");
+  if (run_tc && (a->num_pages_total <= 0 || a->num_pages_total > INT32_MAX))
+    return set_error(ASPIRE_ERR_INVALID, w + ": num_pages_total out of range");
+  return ASPIRE_OK;
+}
+
 }  // namespace aspire
 
 using namespace aspire;
@@ -162,6 +218,12 @@ int aspire_abi_version(void) { return ASPIRE_B200_ABI_VERSION; }
 const char* aspire_last_error(void) { return aspire::last_error(); }
 
 size_t aspire_status_offset(void) { return kStatusBytes; }
+
+int aspire_set_wait_limit_ns(uint64_t ns) {
+  clear_error();
+  g_wait_limit_ns.store(ns, std::memory_order_relaxed);
+  return ASPIRE_OK;
+}
 
 const char* aspire_kernel_names(void) {
   return "aspire_attn_gather_kernel\naspire_attn_tc_kernel\naspire_attn_merge_kernel\naspire_append_kv_kernel\n"
@@ -268,41 +330,18 @@ int aspire_plan(const int32_t* qo_indptr, const int32_t* kv_indptr, const int32_
 
 int aspire_mixed_attention(const AspireAttnArgs* a, const AspirePlanInfo* plan, void* stream) {
   clear_error();
-  if (!a || !plan) return set_error(ASPIRE_ERR_INVALID, "aspire_mixed_attention: null argument");
-  if (a->head_dim != kHeadDim)
-    return set_error(ASPIRE_ERR_INVALID, "aspire_mixed_attention: head_dim must be 128");
-  if (a->page_size != kPageSize)
-    return set_error(ASPIRE_ERR_INVALID, "aspire_mixed_attention: page_size must be 16");
-  if (a->num_kv_heads <= 0 || a->num_qo_heads % a->num_kv_heads != 0)
-    return set_error(ASPIRE_ERR_INVALID, "aspire_mixed_attention: bad head counts");
-  if (a->num_qo_heads != plan->num_qo_heads || a->num_kv_heads != plan->num_kv_heads)
-    return set_error(ASPIRE_ERR_INVALID,
-                     "aspire_mixed_attention: head counts differ from the plan's");
-  if (!a->q || !a->kv_cache || !a->out || !a->int_ws)
-    return set_error(ASPIRE_ERR_INVALID, "aspire_mixed_attention: null tensor pointer");
-  if (!a->kv_indices && (!a->mode_flags || !a->draft_table || !a->block_table))
-    return set_error(ASPIRE_ERR_INVALID, "aspire_mixed_attention: kv_indices or the three page tables are required");
-  if ((reinterpret_cast<uintptr_t>(a->q) | reinterpret_cast<uintptr_t>(a->kv_cache)) & 15)
-    return set_error(ASPIRE_ERR_INVALID, "aspire_mixed_attention: q / kv_cache not 16-byte aligned");
-  if ((a->q_stride_n | a->q_stride_h) & 7)
-    return set_error(ASPIRE_ERR_INVALID,
-                     "aspire_mixed_attention: q strides must be multiples of 8 elements");
-  if (a->dump && (a->dump_num_heads < a->num_qo_heads || a->dump_kv_stride <= 0))
-    return set_error(ASPIRE_ERR_INVALID, "aspire_mixed_attention: bad dump geometry");
+  int rc = check_attention_args(a, plan, "aspire_mixed_attention");
+  if (rc) return rc;
+  if (!a->int_ws) return set_error(ASPIRE_ERR_INVALID, "aspire_mixed_attention: null int workspace");
   if (size_t(plan->int_bytes) + kStatusBytes > a->int_ws_bytes)
     return set_error(ASPIRE_ERR_CAPACITY, "aspire_mixed_attention: int workspace smaller than plan");
   if (size_t(plan->float_bytes) > a->float_ws_bytes)
     return set_error(ASPIRE_ERR_CAPACITY, "aspire_mixed_attention: float workspace smaller than plan");
   if (plan->num_merge > 0 && !a->float_ws)
     return set_error(ASPIRE_ERR_INVALID, "aspire_mixed_attention: split-KV needs a float workspace");
-  if (a->q_rows <= 0 || a->q_rows > INT32_MAX)
-    return set_error(ASPIRE_ERR_INVALID, "aspire_mixed_attention: q_rows (rows of q) must be set");
   const int group = a->num_qo_heads / a->num_kv_heads;
   // The tcgen05 kernel takes rows only when a whole query position fits its tile.
   const bool run_tc = plan->tc_enabled && group <= kTcQTile;
-  if (run_tc && ((reinterpret_cast<uintptr_t>(a->out) & 15) || ((a->o_stride_n | a->o_stride_h) & 7)))
-    return set_error(ASPIRE_ERR_INVALID,
-                     "aspire_mixed_attention: out must be 16-byte aligned with strides in multiples of 8");
 
   AttnParams p;
   p.q = static_cast<const __nv_bfloat16*>(a->q);
@@ -334,32 +373,28 @@ int aspire_mixed_attention(const AspireAttnArgs* a, const AspirePlanInfo* plan, 
   p.plan = reinterpret_cast<const int32_t*>(static_cast<const char*>(a->int_ws) + kStatusBytes);
   p.status = static_cast<uint32_t*>(a->int_ws);
   p.partial_o = static_cast<float*>(a->float_ws);
+  const uint64_t wait_ns = g_wait_limit_ns.load(std::memory_order_relaxed);
+  p.wait_ns = wait_ns ? wait_ns : kDefaultWaitNs;
 
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  int rc;
   // Kernels are launched with plan-independent grids: items live in device
   // memory, so a captured graph stays valid across re-plans.  The CUDA-core
   // kernel is left out only when the routing thresholds send every row to
   // the tcgen05 kernel (no plan can then hold a CUDA-core item); the
   // thresholds are read from the environment once per process.
-  static thread_local int gather_smem_cfg = 48 * 1024;
   static const bool all_rows_tc = tc_min_rows() <= 1;
   if (!(run_tc && all_rows_tc)) {
     const size_t smem = gather_smem_bytes();
-    rc = ensure_smem(reinterpret_cast<const void*>(&aspire_attn_gather_kernel), smem,
-                     &gather_smem_cfg);
+    rc = ensure_smem(reinterpret_cast<const void*>(&aspire_attn_gather_kernel), smem, g_gather_smem);
     if (rc) return rc;
     rc = launch(aspire_attn_gather_kernel, dim3(plan->num_ctas * kGatherCtasPerSm), dim3(128), smem, st,
                 "aspire_attn_gather_kernel launch", p);
     if (rc) return rc;
   }
   if (run_tc) {
-    static thread_local int tc_smem_cfg = 48 * 1024;
     const size_t smem = tc_smem_bytes();
-    rc = ensure_smem(reinterpret_cast<const void*>(&aspire_attn_tc_kernel), smem, &tc_smem_cfg);
+    rc = ensure_smem(reinterpret_cast<const void*>(&aspire_attn_tc_kernel), smem, g_tc_smem);
     if (rc) return rc;
-    if (a->num_pages_total <= 0 || a->num_pages_total > INT32_MAX)
-      return set_error(ASPIRE_ERR_INVALID, "aspire_mixed_attention: num_pages_total out of range");
     alignas(64) CUtensorMap tmap;
     rc = encode_kv_tensor_map(&tmap, a->kv_cache, a->num_pages_total, a->num_kv_heads);
     if (rc) return rc;
@@ -600,8 +635,7 @@ int aspire_select_pages(const AspireSelectArgs* a, void* stream) {
   const size_t smem = select_smem_bytes(a->pages_per_slot, cap);
   if (smem > 200 * 1024)
     return set_error(ASPIRE_ERR_CAPACITY, "aspire_select_pages: pages_per_slot too large");
-  static thread_local int sel_smem_cfg = 48 * 1024;
-  int rc = ensure_smem(reinterpret_cast<const void*>(&aspire_select_pages_kernel), smem, &sel_smem_cfg);
+  int rc = ensure_smem(reinterpret_cast<const void*>(&aspire_select_pages_kernel), smem, g_sel_smem);
   if (rc) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (!a->scores_in) {

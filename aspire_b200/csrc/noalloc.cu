@@ -16,8 +16,8 @@
 // current, and caches them.  Make that first call before any stream capture.
 //
 // All calls share the arrays and the arrays keep the last call's contents.
-// The status word is cleared on every call; the plan and the partials are
-// always written before they are read.  Calls that overlap on the GPU (two
+// The status word is cleared on every call (aspire_noalloc_status reads it
+// back); the plan and the partials are always written before they are read.  Calls that overlap on the GPU (two
 // streams, two host threads) race on the arrays: serialise them.
 #include <cstring>
 #include <mutex>
@@ -78,18 +78,26 @@ extern "C" int aspire_mixed_attention_noalloc(const AspireAttnArgs* args, const 
   clear_error();
   if (!args || !plan || !host_plan)
     return set_error(ASPIRE_ERR_INVALID, "aspire_mixed_attention_noalloc: null argument");
+  if (plan->on_device)
+    return set_error(ASPIRE_ERR_INVALID,
+                     "aspire_mixed_attention_noalloc: the plan must be rendered on the host with "
+                     "aspire_plan_host_only (an aspire_plan_device plan has no host copy to upload)");
+  // Every argument is checked before the shared arrays are touched, so a
+  // rejected call leaves the previous call's plan and status in place.
+  int rc = check_attention_args(args, plan, "aspire_mixed_attention_noalloc");
+  if (rc) return rc;
   if (plan->int_bytes <= 0 || size_t(plan->int_bytes) + kStatusBytes > kNoAllocIntBytes)
     return set_error(ASPIRE_ERR_CAPACITY,
                      "aspire_mixed_attention_noalloc: the plan needs " +
                          std::to_string(plan->int_bytes + kStatusBytes) +
                          " bytes, the built-in plan scratch holds " + std::to_string(kNoAllocIntBytes));
-  if (size_t(plan->float_bytes) > kNoAllocFloatBytes)
+  if (plan->float_bytes < 0 || size_t(plan->float_bytes) > kNoAllocFloatBytes)
     return set_error(ASPIRE_ERR_CAPACITY,
                      "aspire_mixed_attention_noalloc: split-KV partials need " +
                          std::to_string(plan->float_bytes) + " bytes, the built-in scratch holds " +
                          std::to_string(kNoAllocFloatBytes) + " (fewer, longer chunks: a smaller batch)");
   DeviceScratch s;
-  int rc = scratch_for_current_device(&s);
+  rc = scratch_for_current_device(&s);
   if (rc) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   // The status word must start at zero; the plan follows the control block.
@@ -106,4 +114,17 @@ extern "C" int aspire_mixed_attention_noalloc(const AspireAttnArgs* args, const 
   a.float_ws = s.float_ws;
   a.float_ws_bytes = kNoAllocFloatBytes;
   return aspire_mixed_attention(&a, plan, stream);
+}
+
+extern "C" int aspire_noalloc_status(uint32_t* host_out, int32_t clear, void* stream) {
+  clear_error();
+  if (!host_out) return set_error(ASPIRE_ERR_INVALID, "aspire_noalloc_status: null host_out");
+  DeviceScratch s;
+  int rc = scratch_for_current_device(&s);
+  if (rc) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  rc = check_cuda(cudaMemcpyAsync(host_out, s.int_ws, sizeof(uint32_t), cudaMemcpyDeviceToHost, st),
+                  "aspire_noalloc_status: status copy");
+  if (rc || !clear) return rc;
+  return check_cuda(cudaMemsetAsync(s.int_ws, 0, sizeof(uint32_t), st), "aspire_noalloc_status: clearing");
 }

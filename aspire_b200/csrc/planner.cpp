@@ -6,9 +6,11 @@
 // design: every (request row, KV head, packed-query tile) is cut into
 // split-KV chunks of a common length chosen so that the persistent grid
 // gets several items per CTA, and items are placed on CTAs longest-first
-// onto the least-loaded CTA (LPT).  Rows whose packed query tile is wide
-// (verify rows) go to the tcgen05 kernel; narrow rows (draft / decode
-// rows) go to the CUDA-core gather kernel.
+// onto the least-loaded CTA (LPT).  By default every row goes to the
+// tcgen05 kernel (decode items, or prefill items for rows of at least 128
+// packed query rows); the CUDA-core gather kernel takes narrow rows only when
+// the routing thresholds (ASPIRE_B200_TC_MIN_ROWS / ASPIRE_B200_TC_MIN_KV)
+// send them there.
 #include <algorithm>
 #include <cstring>
 #include <numeric>

@@ -2,7 +2,8 @@
 // bounded mbarrier waits, the run-time item sequence, the paged K/V TMA
 // producers and the query-tile load.  A kernel's shared-memory struct
 // provides the fields these templates name: abort_flag, the seq ring
-// (seq, seq_full, seq_empty), q_full and the two 64-dim query halves q[0..1].
+// (seq, seq_full, seq_empty), q_full, the two 64-dim query halves q[0..1]
+// and wait_ns (the bound of one pipeline wait, from the launch parameters).
 #pragma once
 
 #include <cuda.h>
@@ -17,7 +18,7 @@ constexpr int kTile = 128;                          // KV tokens per tile
 constexpr int kPagesPerTile = kTile / kPageSize;
 constexpr uint32_t kHalfBytes = kTile * 128;        // 128 rows x 128 B (64 dims)
 constexpr uint32_t kSlotBytes = 2 * kHalfBytes;     // one K or V tile: two 64-dim halves
-constexpr uint64_t kWaitLimitNs = 1000000000ull;    // 1 s: far above any legitimate wait
+constexpr uint64_t kDrainLimitNs = 1000000000ull;   // 1 s: bound of the waits of a stopping CTA
 constexpr int kSeqDepth = 8;                        // item-sequence ring (claimed items in flight per CTA)
 
 __device__ __forceinline__ uint64_t global_ns() {
@@ -32,7 +33,8 @@ __device__ __forceinline__ bool aborted(Sh& sm) {
 }
 
 // Bounded wait on an mbarrier phase.  Returns false (and stops the CTA) when
-// the phase does not complete within kWaitLimitNs or another role aborted.
+// the phase does not complete within sm.wait_ns (the launch's wait limit: 1 s
+// unless aspire_set_wait_limit_ns set another) or another role aborted.
 template <class Sh>
 __device__ __forceinline__ bool wait_bar(Sh& sm, uint64_t& bar, uint32_t parity, uint32_t* status) {
   const uint32_t a = ptx::smem_addr(&bar);
@@ -41,20 +43,23 @@ __device__ __forceinline__ bool wait_bar(Sh& sm, uint64_t& bar, uint32_t parity,
   for (uint32_t i = 1;; ++i) {
     if (ptx::mbar_try_wait(a, parity)) return true;
     if (*reinterpret_cast<volatile int*>(&sm.abort_flag)) return false;
-    if ((i & 255) == 0 && global_ns() - t0 > kWaitLimitNs) break;
+    if ((i & 255) == 0 && global_ns() - t0 > sm.wait_ns) break;
   }
   *reinterpret_cast<volatile int*>(&sm.abort_flag) = 1;
   if (status) atomicOr(status, ASPIRE_STATUS_TIMEOUT);
   return false;
 }
 
-// Wait used while draining after an abort: ignores the abort flag, still bounded.
+// Wait used while draining after an abort: ignores the abort flag and keeps
+// the fixed 1 s bound whatever the launch's wait limit, so that copies and
+// MMAs already issued (which always complete) land before the CTA releases
+// its shared memory and TMEM.
 __device__ __forceinline__ void drain_bar(uint64_t& bar, uint32_t parity) {
   const uint32_t a = ptx::smem_addr(&bar);
   const uint64_t t0 = global_ns();
   for (uint32_t i = 1;; ++i) {
     if (ptx::mbar_try_wait(a, parity)) return;
-    if ((i & 255) == 0 && global_ns() - t0 > kWaitLimitNs) return;
+    if ((i & 255) == 0 && global_ns() - t0 > kDrainLimitNs) return;
   }
 }
 

@@ -207,7 +207,16 @@ class PageSelectorFirstLastAvg:
             raise ValueError("scores must be contiguous fp32 [batch, pages_per_slot]")
         sel = torch.zeros(n, self.subset_cache_size, dtype=torch.int32, device=self.device)
         counts = torch.zeros(n, dtype=torch.int32, device=self.device)
+        self.finalize_scores_into(sel, counts, scores, num_pages, block_table)
+        return sel, counts
+
+    def finalize_scores_into(self, table: torch.Tensor, count_buffer: torch.Tensor, scores: torch.Tensor,
+                             num_pages: torch.Tensor, block_table: torch.Tensor) -> None:
+        """``finalize_scores`` written in place into rows [0, n) of ``table`` /
+        ``count_buffer`` (zero tail); allocates nothing, so it can be captured."""
+        n = scores.shape[0]
+        if scores.dtype != torch.float32 or not scores.is_contiguous() or scores.shape[1] != self.pages_per_slot:
+            raise ValueError("scores must be contiguous fp32 [batch, pages_per_slot]")
         self._launch(dump=None, lse=None, qo_indptr=None, row_ids=None, scores_in=scores,
                      num_pages=self._contig_i32(num_pages), block_table=self._contig_i32(block_table),
-                     batch=n, table_out=sel, table_width=self.subset_cache_size, counts_out=counts)
-        return sel, counts
+                     batch=n, table_out=table, table_width=table.shape[1], counts_out=count_buffer)

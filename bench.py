@@ -1,4 +1,4 @@
-"""Benchmark of the unified mixed forward hot path on B200 (see DESIGN.md).
+"""Benchmark of the unified mixed forward hot path on B200.
 
 One step = one decode step's hot path of a Qwen3-8B-shaped model (config 3 of
 the reference's benchmark list: 36 layers, 32 q / 8 KV heads, head_dim 128,
@@ -24,12 +24,24 @@ rows through the same wrapper, the reference's chunked `encode_slots`
 attention): TFLOP/s of the attention over the visible (query, key) pairs,
 beside FlashInfer's BatchPrefillWithPagedKVCacheWrapper (the library the
 reference runs prefill through) on the same inputs when it is installed.
+
+`--workload sweep` runs the reference's config-5 kernel sweep: the mixed
+attention plus the top-k page selection alone at Qwen3-8B heads over context
+lengths 4k/16k/32k/80k, batch 1 to 128, drafting fraction 0/0.5/1, verify
+q_len 1/5/9 and budgets of 64 and 512 pages, HBM GB/s against the measured
+peak per point.
+
+After the timed region the step's outputs are checked (outside the timing):
+two rows of a mixed layer and of the refresh layer against a plain torch
+fp32 attention on the GPU, and the new draft table against the properties
+the selection guarantees; a failed check ends the run with an error.
 """
 
 from __future__ import annotations
 
 import argparse
 import json
+import math
 import os
 import statistics
 import subprocess
@@ -67,7 +79,9 @@ def parse_args():
     ap.add_argument("--layers", type=int, default=None)
     ap.add_argument("--block-table", default="arange", choices=["arange", "random"],
                     help="arange: the reference engine's contiguous per-row pages; random: scattered pages")
-    ap.add_argument("--workload", default="step", choices=["step", "prefill"])
+    ap.add_argument("--workload", default="step", choices=["step", "prefill", "sweep"])
+    ap.add_argument("--sweep-ctx", default="4096,16384,32768,81920")
+    ap.add_argument("--sweep-batch", default="1,4,16,64,128")
     ap.add_argument("--prefill-cases", default="1x8192+0,4x2048+16384,8x1024+4096,2x4096+0",
                     help="comma-separated ROWSxQLEN+PREFIX prefill chunks (Qwen3-8B heads, causal)")
     args = ap.parse_args()
@@ -381,6 +395,36 @@ def breakdown(hp: HotPath) -> dict:
         q_rot = torch.empty_like(hp.q[0])
         hp.prologue_args = (qkv_prologue, w, offs, q_rot)
     qkv_prologue, w, offs, q_rot = hp.prologue_args
+    if not hasattr(hp, "mixed_random"):
+        # The same batch with scattered physical pages (each row's pages a
+        # random permutation of its own range of the same cache), as the draft
+        # tables look after re-selection and block tables after reuse.
+        from aspire_b200.attention import HolisticAttentionWrapper, first_last_dump_jit_args
+        from aspire_b200.workloads import make_layout
+        lay = hp.lay
+        lay_r = make_layout(batch=lay.batch, ctx=CFG["ctx"], num_qo_heads=lay.num_qo_heads,
+                            num_kv_heads=lay.num_kv_heads, draft_fraction=CFG["draft_fraction"],
+                            budget_pages=CFG["budget_pages"], pages_per_row=CFG["pages_per_row"], seed=CFG["seed"],
+                            block_table="random")
+        assert np.array_equal(lay_r.kv_lens, lay.kv_lens) and np.array_equal(lay_r.q_lens, lay.q_lens)
+        i32 = lambda a: torch.from_numpy(np.ascontiguousarray(a, dtype=np.int32)).to(hp.device)  # noqa: E731
+        counts = np.diff(lay_r.kv_indptr)
+        draft_tab = np.zeros((lay.batch, max(1, int(counts.max()))), np.int32)
+        for b in range(lay.batch):
+            if lay_r.modes[b] == 0:
+                draft_tab[b, :counts[b]] = lay_r.kv_indices[lay_r.kv_indptr[b]:lay_r.kv_indptr[b + 1]]
+        hp.random_tables = (i32(draft_tab), i32(lay_r.block_table))
+        t = lambda a: torch.from_numpy(np.ascontiguousarray(a, dtype=np.int32))  # noqa: E731
+        hp.mixed_random = HolisticAttentionWrapper(torch.empty(1, device=hp.device))
+        hp.mixed_random.set_page_tables(hp.mode_flags, *hp.random_tables)
+        hp.mixed_random.plan_host(t(lay.qo_indptr), t(lay.kv_indptr), t(lay.kv_lens), None, lay.num_qo_heads,
+                                  lay.num_kv_heads, 128, 16, causal=True)
+        full = hp.full
+        hp.refresh_random = HolisticAttentionWrapper(torch.empty(1, device=hp.device),
+                                                     jit_args=first_last_dump_jit_args())
+        hp.refresh_random.set_page_tables(hp.full_modes, *hp.random_tables)
+        hp.refresh_random.plan_host(t(full.qo_indptr), t(full.kv_indptr), t(full.kv_lens), None,
+                                    full.num_qo_heads, full.num_kv_heads, 128, 16, causal=True)
     calls = {
         "prologue": (lambda: qkv_prologue(hp.q[0], hp.k_new[0], hp.v_new[0], hp.qo_indptr, offs, hp.kv, None,
                                           hp.mixed_indptr, hp.mixed_last, 16, q_norm_weight=w[0],
@@ -394,11 +438,80 @@ def breakdown(hp: HotPath) -> dict:
         "refresh_nodump": (lambda: hp.refresh_nodump.run(hp.q[L - 2], hp.kv, out=hp.out[L - 2], lse=hp.lse), 15),
         "select_pages": (lambda: hp.selector.select_into(hp.draft_table, hp.draft_counts, hp.dump, hp.lse,
                                                          hp.num_pages, hp.block_table, hp.qo_indptr), 100),
+        "mixed_attention_random_tables": (lambda: hp.mixed_random.run(hp.q[0], hp.kv, out=hp.out[0]), 30),
+        "refresh_attention_random_tables": (lambda: hp.refresh_random.run(hp.q[L - 2], hp.kv, hp.dump,
+                                                                          hp.lay.num_qo_heads, hp.kv_stride,
+                                                                          out=hp.out[L - 2], lse=hp.lse), 15),
     }
     res = {}
     for name, (fn, reps) in calls.items():
         res[name + "_ms"] = round(graph_time(fn, reps), 4)
     return res
+
+
+def _torch_attention_row(q, kv, pages, kv_len: int, causal: bool = True):
+    """Plain torch fp32 attention of one request row on the GPU (no library
+    code): q [q_len, Hq, 128], pages the row's page ids; bottom-right causal
+    mask, GQA head h -> KV head h // group.  Returns (out [q_len, Hq, 128],
+    base-2 LSE [q_len, Hq])."""
+    ql, hq, d = q.shape
+    hkv = kv.shape[3]
+    g = hq // hkv
+    k = kv[pages, 0].reshape(-1, hkv, d)[:kv_len].float()
+    v = kv[pages, 1].reshape(-1, hkv, d)[:kv_len].float()
+    qg = q.float().view(ql, hkv, g, d)
+    s = torch.einsum("qkgd,skd->kgqs", qg, k) / math.sqrt(d)
+    if causal:
+        i = torch.arange(ql, device=q.device)[:, None]
+        j = torch.arange(kv_len, device=q.device)[None, :]
+        s = s.masked_fill((j > kv_len - ql + i)[None, None], float("-inf"))
+    lse = torch.logsumexp(s, dim=-1) / math.log(2.0)
+    o = torch.einsum("kgqs,skd->qkgd", torch.softmax(s, dim=-1), v)
+    return o.reshape(ql, hq, d), lse.permute(2, 0, 1).reshape(ql, hq)
+
+
+def check_step(hp: HotPath) -> dict:
+    """Outside the timed region: recomputes a mixed layer and the refresh
+    layer eagerly and compares one draft and one verify row of each with
+    _torch_attention_row (max-abs <= 2e-2, mean-abs <= 2e-3, LSE <= 2e-3),
+    then checks the new draft table: counts = min(pages, budget); each row's
+    ids ascending, from its own block-table prefix, including its last L
+    pages; zeros past the count.  Returns a summary; raises on a mismatch."""
+    lay, full = hp.lay, hp.full
+    rows = [int(np.flatnonzero(lay.modes == 0)[0]), int(np.flatnonzero(lay.modes == 1)[0])]
+    worst = {"max_abs": 0.0, "mean_abs": 0.0, "lse_abs": 0.0}
+    R = CFG["refresh_layer"]
+    for layer, src, want_lse in ((0, lay, False), (R, full, True)):
+        hp.layer(layer)
+        torch.cuda.synchronize()
+        for r in rows:
+            t0, t1 = int(src.qo_indptr[r]), int(src.qo_indptr[r + 1])
+            pages = torch.from_numpy(src.kv_indices[src.kv_indptr[r]:src.kv_indptr[r + 1]].astype(np.int64))
+            ref, ref_lse = _torch_attention_row(hp.q[layer][t0:t1], hp.kv, pages.to(hp.device), int(src.kv_lens[r]))
+            err = (hp.out[layer][t0:t1].float() - ref).abs()
+            worst["max_abs"] = max(worst["max_abs"], float(err.max().item()))
+            worst["mean_abs"] = max(worst["mean_abs"], float(err.mean().item()))
+            if want_lse:
+                worst["lse_abs"] = max(worst["lse_abs"], float((hp.lse[t0:t1] - ref_lse).abs().max().item()))
+    hp.select()
+    torch.cuda.synchronize()
+    tab, cnt = hp.draft_table.cpu().numpy(), hp.draft_counts.cpu().numpy()
+    num_pages = hp.num_pages.cpu().numpy()
+    k, L = hp.k_sel, CFG["L"]
+    table_ok = bool(np.array_equal(cnt, np.minimum(num_pages, k)))
+    for b in range(lay.batch):
+        n = int(cnt[b])
+        ids = tab[b, :n]
+        own = lay.block_table[b, :num_pages[b]]
+        table_ok &= bool(np.all(np.diff(ids) > 0)) and bool(np.all(tab[b, n:] == 0))
+        table_ok &= bool(np.isin(ids, own).all()) and bool(np.isin(own[max(0, num_pages[b] - L):], ids).all())
+    ok = worst["max_abs"] <= 2e-2 and worst["mean_abs"] <= 2e-3 and worst["lse_abs"] <= 2e-3 and table_ok
+    summary = {"rows": rows, "layers": [0, R], **{k_: round(v, 6) for k_, v in worst.items()},
+               "draft_table_ok": table_ok, "ok": ok,
+               "reference": "plain torch fp32 attention on the GPU (mixed layer 0 and the refresh layer)"}
+    if not ok:
+        raise SystemExit(f"bench output check failed: {json.dumps(summary)}")
+    return summary
 
 
 def e2e_measure(hp: HotPath, steps: int, warmup: int, bytes_per_step: int):
@@ -619,6 +732,141 @@ def prefill_bench(args):
                       "peak_bf16_tflops": peak, "cases": cases}), flush=True)
 
 
+def sweep_bench(args):
+    """The reference's config-5 sweep: mixed attention
+    plus top-k page selection alone at Qwen3-8B heads (32 / 8 / 128).
+
+    Grid: context in --sweep-ctx x batch in --sweep-batch x drafting fraction
+    {0, 0.5, 1} x verify q_len {1, 5, 9} (when some rows verify) x budget
+    {64, 512} pages (when some rows draft; capped at the context's pages).
+    Every point plans its batch, then times a CUDA graph of back-to-back
+    attention calls in page-table mode (arange block tables as the reference
+    engine lays them out; draft rows' selected pages scattered over their
+    context).  A point whose KV bytes are below 256 MB cycles through copies
+    of its page tables shifted to disjoint page ranges of one large cache, so
+    that consecutive calls read different memory and nothing is served from
+    L2.  The selection is the top-k stage (aspire_select_pages on fp32 page
+    scores) over the same batch, with page scores from mean-pooled keys:
+    score[b, p] = max_h q_last[b, h] . mean_t K[b, p, t, kv(h)] (fp32,
+    computed once per point outside the timing).  Reported per point:
+    attention ms and GB/s (algorithmic bytes: KV read once, Q in, O out, page
+    ids), selection ms, attention + selection GB/s, fraction of the measured
+    HBM peak."""
+    from aspire_b200.attention import HolisticAttentionWrapper
+    from aspire_b200.page_selector import PageSelectorFirstLastAvg
+    from aspire_b200.workloads import make_layout
+
+    dev = torch.device("cuda", 0)
+    hq, hkv = CFG["num_qo_heads"], CFG["num_kv_heads"]
+    peak, peak_kind = measured_peaks()
+    ctxs = [int(x) for x in args.sweep_ctx.split(",")]
+    batches = [int(x) for x in args.sweep_batch.split(",")]
+    ppr_of = lambda ctx: (ctx + 512 + 15) // 16  # noqa: E731  (context plus generation headroom)
+    max_pages = max(b * ppr_of(c) for b in batches for c in ctxs)
+    target = 256 << 20  # bytes cycled per call at least (2x the L2)
+    page_bytes = 2 * 16 * hkv * 128 * 2
+    total_pages = max(max_pages, (2 * target) // page_bytes + 1)
+    kv = torch.empty(total_pages, 2, 16, hkv, 128, dtype=torch.bfloat16, device=dev)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(CFG["seed"])
+    step = 1 << 14
+    for p0 in range(0, total_pages, step):
+        p1 = min(total_pages, p0 + step)
+        kv[p0:p1] = torch.randn(p1 - p0, 2, 16, hkv, 128, generator=gen, device=dev).to(torch.bfloat16)
+    ws = torch.empty(1, device=dev)
+    w = HolisticAttentionWrapper(ws)
+    points = []
+    t_start = time.perf_counter()
+    for ctx in ctxs:
+        ppr = ppr_of(ctx)
+        ctx_pages = (ctx + 15) // 16
+        budgets = sorted({min(b, ctx_pages) for b in (64, 512)})
+        for B in batches:
+            for frac in (0.0, 0.5, 1.0):
+                qls = (1, 5, 9) if frac < 1.0 else (None,)
+                buds = budgets if frac > 0.0 else (None,)
+                for ql in qls:
+                    for bud in buds:
+                        lay = make_layout(batch=B, ctx=ctx, num_qo_heads=hq, num_kv_heads=hkv, draft_fraction=frac,
+                                          verify_q_len=ql if ql is not None else 1,
+                                          budget_pages=bud if bud is not None else 64, pages_per_row=ppr,
+                                          seed=CFG["seed"], block_table="arange")
+                        points.append(_sweep_point(w, kv, lay, ctx, B, frac, ql, bud, total_pages, target, peak,
+                                                   PageSelectorFirstLastAvg, args))
+    worst = sorted(points, key=lambda p: p["attn_frac"])[:8]
+    fr = [p["attn_frac"] for p in points]
+    print(json.dumps({"workload": "sweep", "metric": "mixed attention + page selection HBM GB/s per point",
+                      "unit": "GB/s", "peak": peak, "peak_source": peak_kind, "dtype": "bf16", "data": "synthetic",
+                      "heads": [hq, hkv, 128], "n_points": len(points),
+                      "attn_frac_median": round(statistics.median(fr), 4), "attn_frac_min": round(min(fr), 4),
+                      "wall_s": round(time.perf_counter() - t_start, 1), "worst": worst, "points": points}),
+          flush=True)
+
+
+def _sweep_point(w, kv, lay, ctx, B, frac, ql, bud, total_pages, target, peak, selector_cls, args):
+    dev = kv.device
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a, dtype=np.int32))  # noqa: E731
+    nbytes = lay.algorithmic_bytes()
+    span = lay.batch * lay.pages_per_row  # pages one copy of the tables addresses
+    copies = int(max(1, min(math.ceil(target / max(nbytes, 1)), total_pages // span, 64)))
+    counts = np.diff(lay.kv_indptr)
+    draft_tab = np.zeros((lay.batch, max(1, int(counts.max()))), np.int32)
+    for b in range(lay.batch):
+        if lay.modes[b] == 0:
+            draft_tab[b, :counts[b]] = lay.kv_indices[lay.kv_indptr[b]:lay.kv_indptr[b + 1]]
+    modes = t(lay.modes).to(dev)
+    tables = [(modes, (t(draft_tab) + c * span).to(dev), (t(lay.block_table) + c * span).to(dev))
+              for c in range(copies)]
+    q = torch.randn(lay.total_q, lay.num_qo_heads, 128, device=dev).to(torch.bfloat16)
+    out = torch.empty_like(q)
+    w.set_page_tables(*tables[0])
+    w.plan_host(t(lay.qo_indptr), t(lay.kv_indptr), t(lay.kv_lens), None, lay.num_qo_heads, lay.num_kv_heads, 128, 16,
+                causal=True)
+    # Page scores from mean-pooled keys (fp32), then the top-k stage alone.
+    pages = torch.from_numpy(lay.block_table.astype(np.int64)).to(dev)          # [B, ppr]
+    last_q = q[torch.from_numpy(lay.qo_indptr[1:] - 1).long().to(dev)].float()  # [B, Hq, 128]
+    g = lay.num_qo_heads // lay.num_kv_heads
+    scores = torch.empty(lay.batch, lay.pages_per_row, dtype=torch.float32, device=dev)
+    for b in range(lay.batch):  # one row at a time keeps the fp32 temporary small
+        kmean = kv[pages[b], 0].float().mean(dim=1)                             # [ppr, Hkv, 128]
+        sc = torch.einsum("kgd,pkd->kgp", last_q[b].view(lay.num_kv_heads, g, 128), kmean)
+        scores[b] = sc.amax(dim=(0, 1))
+    del kmean, sc
+    k_sel = int(bud) if bud is not None else 64
+    sel = selector_cls(max_batch_size=lay.batch, pages_per_slot=lay.pages_per_row, subset_cache_size=k_sel,
+                       L=CFG["L"], n_heads=lay.num_qo_heads, page_size=16, max_seq_length=lay.pages_per_row * 16,
+                       device=dev, bsz=lay.batch, dec_len=9, kv_stride=lay.pages_per_row * 16, draft_percent=None,
+                       min_draft_pages=k_sel)
+    num_pages = t((lay.ctx_lens + 15) // 16).to(dev)
+    table_out = torch.zeros(lay.batch, k_sel, dtype=torch.int32, device=dev)
+    counts_out = torch.zeros(lay.batch, dtype=torch.int32, device=dev)
+    bt = t(lay.block_table).to(dev)
+    state = {"i": 0}
+
+    def attn():
+        i = state["i"] % copies
+        state["i"] += 1
+        w.set_page_tables(*tables[i])
+        w.run(q, kv, out=out)
+
+    def select():
+        sel.finalize_scores_into(table_out, counts_out, scores, num_pages, bt)
+
+    reps = int(max(copies, min(200, math.ceil(2.0e9 / max(nbytes, 1)))))
+    reps = (reps + copies - 1) // copies * copies
+    attn_ms = graph_time(attn, reps, replays=2)
+    sel_ms = graph_time(select, 100, replays=2)
+    status = int(w.device_status())
+    sel_bytes = lay.batch * lay.pages_per_row * 4 + lay.batch * k_sel * 4 * 2
+    gbps = nbytes / (attn_ms * 1e-3) / 1e9
+    both = (nbytes + sel_bytes) / ((attn_ms + sel_ms) * 1e-3) / 1e9
+    return {"ctx": ctx, "batch": B, "draft_fraction": frac, "verify_q_len": ql, "budget_pages": bud,
+            "attn_bytes": int(nbytes), "attn_ms": round(attn_ms, 5), "attn_GBps": round(gbps, 1),
+            "attn_frac": round(gbps / peak, 4), "select_ms": round(sel_ms, 5), "attn_select_GBps": round(both, 1),
+            "attn_select_frac": round(both / peak, 4), "items": int(w.plan_info.num_items_tc),
+            "chunk": int(w.plan_info.chunk_tokens), "copies": copies, "status": status}
+
+
 def main():
     args = parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -627,10 +875,11 @@ def main():
     if args.impl == "reference":
         reference_arm(args, rank, world)
         return
-    if args.workload == "prefill":
+    if args.workload in ("prefill", "sweep"):
         from aspire_b200 import load_library
         load_library()
-        prefill_bench(args)
+        torch.cuda.set_device(0)
+        (prefill_bench if args.workload == "prefill" else sweep_bench)(args)
         return
     dist_on = world > 1
     torch.cuda.set_device(local_rank)
@@ -662,8 +911,13 @@ def main():
     parts = breakdown(hp)
     parts["refresh_attention_GBps"] = round(sb["refresh"] / (parts["refresh_attention_ms"] * 1e-3) / 1e9, 1)
     parts["mixed_attention_GBps"] = round(sb["mixed"] / (parts["mixed_attention_ms"] * 1e-3) / 1e9, 1)
+    parts["mixed_attention_random_tables_GBps"] = round(
+        sb["mixed"] / (parts["mixed_attention_random_tables_ms"] * 1e-3) / 1e9, 1)
+    parts["refresh_attention_random_tables_GBps"] = round(
+        sb["refresh"] / (parts["refresh_attention_random_tables_ms"] * 1e-3) / 1e9, 1)
     parts["tc_items"] = [hp.mixed.plan_info.num_items_tc, hp.refresh.plan_info.num_items_tc]
     parts["gather_items"] = [hp.mixed.plan_info.num_items_gather, hp.refresh.plan_info.num_items_gather]
+    check = check_step(hp)
     e2e = None
     if not args.no_e2e:
         dt, h2d, d2h = e2e_measure(hp, max(2, args.steps // 2), 1, sb["total"])
@@ -688,7 +942,7 @@ def main():
                                    "straight from the draft / block tables (page-list build absorbed)",
                        "batch": CFG["batch"], "ctx": CFG["ctx"], "tp": world, "heads_per_rank": [lay.num_qo_heads, lay.num_kv_heads],
                        "l2": "inputs larger than L2 (8.7 GB cache at TP1)", "bytes_per_step": sb},
-            "roofline": roof, "breakdown": parts, "clocks": clocks.summary(), "e2e": e2e,
+            "roofline": roof, "breakdown": parts, "clocks": clocks.summary(), "e2e": e2e, "check": check,
             "gpu_launches": hp.launches_per_step() * args.steps,
             "cpu_baseline": cb,
         }

@@ -41,7 +41,7 @@
 extern "C" {
 #endif
 
-#define ASPIRE_B200_ABI_VERSION 3
+#define ASPIRE_B200_ABI_VERSION 4
 
 #define ASPIRE_OK 0
 #define ASPIRE_ERR_INVALID (-1)  /* bad argument (shape, size, alignment)       */
@@ -195,16 +195,33 @@ ASPIRE_API int aspire_mixed_attention(const AspireAttnArgs* args, const AspirePl
  * The caller renders the plan on the host with aspire_plan_host_only (its
  * num_ctas = the device's SM count) into `host_plan` and passes the returned
  * info; the call uploads that plan into the library's built-in plan array on
- * `stream` (pinned host memory keeps the copy asynchronous) and runs the
+ * `stream` (pinned host memory keeps the copy asynchronous: `host_plan` must
+ * then stay unchanged until the stream has reached that copy) and runs the
  * attention with the built-in partials array.  The int_ws / float_ws fields
- * of `args` are ignored.  Plans larger than ASPIRE_NOALLOC_INT_BYTES or
- * needing more than ASPIRE_NOALLOC_FLOAT_BYTES of partials are rejected with
- * ASPIRE_ERR_CAPACITY.  The first call on a device looks up the arrays'
- * device addresses (make it before any stream capture).  All calls share
- * the arrays: calls that overlap on the GPU race and must be serialised.
+ * of `args` are ignored.  A plan rendered by aspire_plan_device (on_device
+ * set) is rejected with ASPIRE_ERR_INVALID.  Plans larger than
+ * ASPIRE_NOALLOC_INT_BYTES or needing more than ASPIRE_NOALLOC_FLOAT_BYTES of
+ * partials are rejected with ASPIRE_ERR_CAPACITY.  Every argument is checked
+ * before the built-in arrays are touched: a rejected call changes nothing on
+ * the device.  The first call on a device looks up the arrays' device
+ * addresses (make it before any stream capture).  All calls share the
+ * arrays: calls that overlap on the GPU race and must be serialised.  The
+ * kernels' status word (ASPIRE_STATUS_* bits) lives in the built-in plan
+ * array; it is cleared by every call and read by aspire_noalloc_status.
  */
 ASPIRE_API int aspire_mixed_attention_noalloc(const AspireAttnArgs* args, const AspirePlanInfo* plan,
                                               const void* host_plan, void* stream);
+
+/*
+ * Enqueues on `stream` a copy of the status word of the calls above (the
+ * ASPIRE_STATUS_* bits their kernels set instead of faulting: a bad page id,
+ * an inconsistent plan, a row past q_rows, a wait that timed out) into
+ * *host_out, and with `clear` != 0 a reset of the word to zero after it.
+ * *host_out holds the value once the stream has reached the copy
+ * (synchronise the stream before reading it).  Allocates nothing.  Companion
+ * of aspire_mixed_attention_noalloc; no counterpart in the reference.
+ */
+ASPIRE_API int aspire_noalloc_status(uint32_t* host_out, int32_t clear, void* stream);
 
 /* ------------------------------------------------------------------------ */
 /* Paged KV append (device).                                                */
@@ -417,6 +434,15 @@ ASPIRE_API int aspire_abi_version(void);
 /* Bytes of the int workspace reserved ahead of the plan for the status word;
  * the status word is the first uint32 of the int workspace. */
 ASPIRE_API size_t aspire_status_offset(void);
+
+/* Bound of one pipeline wait inside the tcgen05 attention kernel, in
+ * nanoseconds, for launches made after the call (0 restores the default of
+ * 1 s).  A wait that runs past it stops its CTA, which sets
+ * ASPIRE_STATUS_TIMEOUT, waits (with a fixed 1 s bound) for its own copies and
+ * MMAs in flight, frees its tensor memory and returns; the device stays
+ * usable.  Process-wide.  No counterpart in the reference, whose waits are
+ * unbounded. */
+ASPIRE_API int aspire_set_wait_limit_ns(uint64_t ns);
 
 /* Names of the kernels the library launches, one per line (diagnostics). */
 ASPIRE_API const char* aspire_kernel_names(void);

@@ -1,9 +1,9 @@
 """Generates the golden fixtures of tests/golden/ from the reference's own code.
 
-Run in a container that has the reference tree (default /root/reference, or
-$ASPIRE_REFERENCE):
+Run where the reference tree is checked out, with $ASPIRE_REFERENCE naming
+its root:
 
-    python tests/golden/make_golden.py
+    ASPIRE_REFERENCE=<path to the ASPIRE checkout> python tests/golden/make_golden.py
 
 * page_selector_*.pt : inputs and outputs of the reference's
   aspire.backends.page_selector.PageSelectorFirstLastAvg.select (imported
@@ -34,7 +34,7 @@ from pathlib import Path
 import torch
 
 HERE = Path(__file__).resolve().parent
-REF = Path(os.environ.get("ASPIRE_REFERENCE", "/root/reference"))
+REF = Path(os.environ.get("ASPIRE_REFERENCE", ""))
 
 
 def _ref_selector_cls():
@@ -232,8 +232,8 @@ def recent_case():
 
 
 def main():
-    if not REF.exists():
-        raise SystemExit(f"reference tree {REF} not found")
+    if not os.environ.get("ASPIRE_REFERENCE") or not REF.exists():
+        raise SystemExit("set ASPIRE_REFERENCE to the root of the reference (ASPIRE) checkout")
     # BASELINE config 1 geometry: 16 heads, 1024-token cache, 8 selected pages.
     selector_case("cfg1", B=4, H=16, max_seq_len=1024, kv_stride=1024, top_k_pages=8, L=2,
                   draft_percent=None, seed=0, q_lens=[1, 1, 5, 5], lens=[1000, 1024, 1021, 1024],

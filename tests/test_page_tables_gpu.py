@@ -1,7 +1,8 @@
 """Page-table mode: the attention and the append read each row's pages from
 the draft table / block table by mode flag (build_unified_indices absorbed,
 the reference's aspire/models/sparse_draft_runner.py:126-153).  Results must
-be bit-identical to the flat page-list mode on the same pages."""
+be bit-identical to the flat page-list mode on the same pages, and agree with
+the oracle (attention within the bf16 tolerance, append bit-exact)."""
 
 import numpy as np
 import pytest
@@ -10,6 +11,8 @@ import torch
 from aspire_b200.attention import HolisticAttentionWrapper, first_last_dump_jit_args
 from aspire_b200.kv_ops import append_kv
 from aspire_b200.workloads import fill_tensors, full_context_layout, last_page_lens, make_layout
+from gpu_helpers import assert_attention_close, assert_dump_close, oracle_attention
+from oracle import kv_append as oracle_append
 
 pytestmark = pytest.mark.gpu
 
@@ -52,6 +55,8 @@ def test_attention_page_tables_match_flat_list(cuda_device, hq, hkv):
     torch.cuda.synchronize()
     assert torch.equal(out_flat, out_tab)
     assert torch.equal(lse_flat, lse_tab)
+    ref_out, ref_lse, _ = oracle_attention(lay, q, kv)
+    assert_attention_close(out_tab, lse_tab, ref_out, ref_lse)
 
 
 def test_refresh_dump_page_tables_match_flat_list(cuda_device):
@@ -76,6 +81,9 @@ def test_refresh_dump_page_tables_match_flat_list(cuda_device):
     torch.cuda.synchronize()
     for a, b in zip(outs[0], outs[1]):
         assert torch.equal(a, b)
+    ref_out, ref_lse, ref_dump = oracle_attention(full, q, kv, dump_stride=stride)
+    assert_attention_close(outs[1][0], outs[1][1], ref_out, ref_lse)
+    assert_dump_close(outs[1][2], ref_dump, full, stride)
 
 
 def test_append_page_tables_match_flat_list(cuda_device):
@@ -98,6 +106,11 @@ def test_append_page_tables_match_flat_list(cuda_device):
     torch.cuda.synchronize()
     assert torch.equal(flat, tab)
     assert not torch.equal(flat, kv0)
+    ref = kv0.cpu()
+    i32 = lambda a: torch.from_numpy(np.ascontiguousarray(a, dtype=np.int32))  # noqa: E731
+    oracle_append.update_kv_padded(k.cpu(), v.cpu(), i32(lay.qo_indptr), ref, i32(lay.kv_indices),
+                                   i32(lay.kv_indptr), i32(last_page_lens(lay)))
+    assert torch.equal(tab.cpu(), ref)
 
 
 def test_page_tables_require_a_page_source(cuda_device):
@@ -137,3 +150,5 @@ def test_prefill_rows_page_tables_match_flat_list(cuda_device):
     torch.cuda.synchronize()
     assert torch.equal(out_flat, out_tab)
     assert torch.equal(lse_flat, lse_tab)
+    ref_out, ref_lse, _ = oracle_attention(lay, q, kv)
+    assert_attention_close(out_tab, lse_tab, ref_out, ref_lse)

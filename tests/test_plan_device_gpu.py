@@ -11,6 +11,7 @@ import torch
 from aspire_b200 import _capi
 from aspire_b200.attention import HolisticAttentionWrapper, first_last_dump_jit_args
 from aspire_b200.workloads import fill_tensors, full_context_layout, last_page_lens, make_layout
+from gpu_helpers import MAX_ABS, MEAN_ABS, assert_attention_close, oracle_attention
 
 pytestmark = pytest.mark.gpu
 
@@ -119,6 +120,8 @@ def test_device_plan_gives_identical_attention(cuda_device):
     o2, l2 = devw.run(q, kv, return_lse=True)
     torch.cuda.synchronize()
     assert torch.equal(o1, o2) and torch.equal(l1, l2)
+    ref_out, ref_lse, _ = oracle_attention(lay, q, kv)
+    assert_attention_close(o2, l2, ref_out, ref_lse)
 
 
 def test_device_plan_replans_inside_a_graph(cuda_device):
@@ -169,6 +172,9 @@ def test_device_plan_replans_inside_a_graph(cuda_device):
         expect = ref.run(q[:n], kv)
         torch.cuda.synchronize()
         assert torch.equal(out[:n], expect)
+        o_ref, _, _ = oracle_attention(lay, q[:n], kv)
+        err = (out[:n].float().cpu() - o_ref).abs()
+        assert err.max().item() <= MAX_ABS and err.mean().item() <= MEAN_ABS
     del graph
 
 
