@@ -212,6 +212,24 @@ class AspirePrologueArgs(ctypes.Structure):
     ]
 
 
+class AspireSpillArgs(ctypes.Structure):
+    _fields_ = [
+        ("mode_flags", ctypes.c_void_p),
+        ("dec_lens", ctypes.c_void_p),
+        ("draft_cachelens", ctypes.c_void_p),
+        ("draft_indices", ctypes.c_void_p),
+        ("draft_stride", ctypes.c_int64),
+        ("draft_cols", ctypes.c_int32),
+        ("draft_num_pages", ctypes.c_void_p),
+        ("block_table", ctypes.c_void_p),
+        ("block_table_stride", ctypes.c_int64),
+        ("block_table_cols", ctypes.c_int32),
+        ("batch", ctypes.c_int32),
+        ("page_size", ctypes.c_int32),
+        ("status", ctypes.c_void_p),
+    ]
+
+
 # Exported symbols and their signatures (must match include/aspire_b200.h).
 _SIGNATURES = {
     "aspire_plan": (
@@ -241,6 +259,7 @@ _SIGNATURES = {
     "aspire_select_pages": (ctypes.c_int, [ctypes.POINTER(AspireSelectArgs), ctypes.c_void_p]),
     "aspire_build_unified_indices": (ctypes.c_int, [ctypes.POINTER(AspireIndicesArgs), ctypes.c_void_p]),
     "aspire_qkv_prologue": (ctypes.c_int, [ctypes.POINTER(AspirePrologueArgs), ctypes.c_void_p]),
+    "aspire_draft_page_spill": (ctypes.c_int, [ctypes.POINTER(AspireSpillArgs), ctypes.c_void_p]),
     "aspire_plan_device": (
         ctypes.c_int,
         [c_int32_p, c_int32_p, c_int32_p, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,

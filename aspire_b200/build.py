@@ -31,6 +31,7 @@ SOURCES = [
     "qkv_prologue.cu",
     "plan_device.cu",
     "noalloc.cu",
+    "draft_spill.cu",
 ]
 
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]

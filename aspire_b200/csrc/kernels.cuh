@@ -114,6 +114,22 @@ struct IndicesParams {
   uint32_t* status;
 };
 
+struct SpillParams {
+  const int32_t* mode_flags;
+  const int32_t* dec_lens;
+  const int32_t* draft_cachelens;
+  int32_t* draft_indices;
+  int64_t draft_stride;
+  int32_t draft_cols;
+  int32_t* draft_num_pages;
+  const int32_t* block_table;
+  int64_t block_table_stride;
+  int32_t block_table_cols;
+  int32_t batch;
+  uint32_t* status;
+};
+__global__ void aspire_draft_spill_kernel(SpillParams p);
+
 constexpr int kIndicesThreads = 128;
 __global__ void aspire_build_indices_kernel(IndicesParams p);
 

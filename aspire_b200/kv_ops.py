@@ -161,6 +161,53 @@ def build_unified_indices(mode_flags: torch.Tensor, draft_indices: torch.Tensor,
     _capi.check(rc, "aspire_build_unified_indices")
 
 
+def draft_page_spill(mode_flags: torch.Tensor, dec_lens: torch.Tensor, draft_cachelens: torch.Tensor,
+                     draft_indices: torch.Tensor, draft_num_pages: torch.Tensor, block_table: torch.Tensor,
+                     page_size: int = 16, status: torch.Tensor | None = None) -> None:
+    """Draft-page spill insert, in place (C ABI ``aspire_draft_page_spill``):
+    a draft row whose newest token opened a new page gets that page
+    (``block_table[b, ceil(draft_cachelens[b] / page_size) - 1]``) appended to
+    its draft table, unless the table already ends there or is full.  Replaces
+    the spill check of LMBackendBase.prepare_forward_inputs
+    (aspire/backends/base.py:1222-1236) with _handle_draft_page_spill
+    (:718-742): one launch, no host synchronisation, capturable.  All tensors
+    are int32 on the GPU; ``dec_lens`` are the step's decode lengths (0 for
+    finished rows) and ``draft_cachelens`` count this step's token."""
+    batch = mode_flags.shape[0]
+    tensors = {"mode_flags": mode_flags, "dec_lens": dec_lens, "draft_cachelens": draft_cachelens,
+               "draft_indices": draft_indices, "draft_num_pages": draft_num_pages, "block_table": block_table}
+    for name, t in tensors.items():
+        if t.dtype != torch.int32:
+            raise ValueError(f"{name} must be int32, got {t.dtype}")
+        if t.device.type != "cuda":
+            raise ValueError(f"{name} must be a CUDA tensor")
+    if draft_indices.dim() != 2 or block_table.dim() != 2 or draft_indices.stride(1) != 1 or block_table.stride(1) != 1:
+        raise ValueError("draft_indices / block_table must be 2-D with contiguous rows")
+    for name in ("mode_flags", "dec_lens", "draft_cachelens", "draft_num_pages"):
+        t = tensors[name]
+        if not t.is_contiguous() or t.shape[0] < batch:
+            raise ValueError(f"{name} must be contiguous with at least batch entries")
+    if draft_indices.shape[0] < batch or block_table.shape[0] < batch:
+        raise ValueError("tables have fewer rows than mode_flags")
+    a = _capi.AspireSpillArgs()
+    a.mode_flags = mode_flags.data_ptr()
+    a.dec_lens = dec_lens.data_ptr()
+    a.draft_cachelens = draft_cachelens.data_ptr()
+    a.draft_indices = draft_indices.data_ptr()
+    a.draft_stride = draft_indices.stride(0)
+    a.draft_cols = draft_indices.shape[1]
+    a.draft_num_pages = draft_num_pages.data_ptr()
+    a.block_table = block_table.data_ptr()
+    a.block_table_stride = block_table.stride(0)
+    a.block_table_cols = block_table.shape[1]
+    a.batch = batch
+    a.page_size = int(page_size)
+    a.status = status.data_ptr() if status is not None else None
+    stream = torch.cuda.current_stream(mode_flags.device).cuda_stream
+    rc = _capi.load_library().aspire_draft_page_spill(ctypes.byref(a), ctypes.c_void_p(stream))
+    _capi.check(rc, "aspire_draft_page_spill")
+
+
 def qkv_prologue(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, kv_append_indptr: torch.Tensor,
                  rope_offsets: torch.Tensor, kv_cache: torch.Tensor, kv_page_indices: torch.Tensor | None,
                  kv_page_indptr: torch.Tensor, kv_last_page_len: torch.Tensor, page_size: int = 16, *,

@@ -422,6 +422,42 @@ typedef struct AspireIndicesArgs {
 ASPIRE_API int aspire_build_unified_indices(const AspireIndicesArgs* args, void* stream);
 
 /* ------------------------------------------------------------------------ */
+/* Draft-page spill insert (device).                                        */
+/* ------------------------------------------------------------------------ */
+
+typedef struct AspireSpillArgs {
+  const int32_t* mode_flags;      /* int32 [batch]: 0 = draft row                          */
+  const int32_t* dec_lens;        /* int32 [batch]: the step's decode lengths (0 = finished) */
+  const int32_t* draft_cachelens; /* int32 [batch]: draft cache lengths, this step's token
+                                     counted                                                */
+  int32_t* draft_indices;         /* int32 [batch, draft_stride] draft tables (in place)    */
+  int64_t draft_stride;
+  int32_t draft_cols;             /* usable columns of a draft table row                    */
+  int32_t* draft_num_pages;       /* int32 [batch] draft page counts (in place)             */
+  const int32_t* block_table;     /* int32 [batch, block_table_stride]                      */
+  int64_t block_table_stride;
+  int32_t block_table_cols;
+  int32_t batch;
+  int32_t page_size;              /* must be 16                                             */
+  uint32_t* status;               /* optional device status word                            */
+} AspireSpillArgs;
+
+/*
+ * Adds the page of a draft row's newest token to its draft table when that
+ * token opened a new page: for a draft row with dec_len > 0 whose
+ * (draft_cachelen - 1) is a multiple of the page size, the page
+ * block_table[b, ceil(draft_cachelen / 16) - 1] is appended at column
+ * draft_num_pages[b] (and the count incremented) unless the table's last
+ * listed page already is that page or the row has no free column.  Replaces
+ * the spill check and insert of LMBackendBase.prepare_forward_inputs
+ * (aspire/backends/base.py:1222-1236) with _handle_draft_page_spill
+ * (:718-742) and its host-identified variant _handle_draft_page_spill_ids
+ * (:744-759): one launch, no host synchronisation, capturable.  A page index
+ * past block_table_cols sets ASPIRE_STATUS_BAD_ROW and skips the row.
+ */
+ASPIRE_API int aspire_draft_page_spill(const AspireSpillArgs* args, void* stream);
+
+/* ------------------------------------------------------------------------ */
 /* Utilities.                                                               */
 /* ------------------------------------------------------------------------ */
 

@@ -231,6 +231,68 @@ def recent_case():
     torch.save(out, HERE / "recent_rows.pt")
 
 
+def spill_case():
+    """Draft-page spill insert: the reference's LMBackendBase._handle_draft_page_spill
+    (aspire/backends/base.py:718-742, imported unchanged) applied to the spill
+    mask that prepare_forward_inputs computes (:1222-1236, whose statements
+    are evaluated here on the fixture's tensors), and its host-identified
+    variant _handle_draft_page_spill_ids (:744-759) on the rows of that mask
+    that have a free column; both must give the same tables.  Rows cover: a
+    token opening a new page (spill), the table already ending at that page,
+    a full table, no crossing, verify and finished rows, an empty row."""
+    import types
+
+    sys.path.insert(0, str(REF))
+    from aspire.backends.base import LMBackendBase  # noqa: E402
+
+    page, width, pps = 16, 6, 20
+    g = torch.Generator().manual_seed(99)
+    B = 12
+    block_table = torch.stack([torch.randperm(pps, generator=g) + r * pps for r in range(B)]).to(torch.int32)
+    # mode 0 = draft; dec_lens 0 = finished
+    mode = torch.tensor([0, 0, 0, 0, 0, 0, 1, 0, 0, 0, 0, 1], dtype=torch.int32)
+    dec = torch.tensor([1, 1, 1, 1, 0, 1, 5, 1, 1, 1, 1, 3], dtype=torch.int32)
+    dcl = torch.tensor([33, 17, 49, 20, 33, 1, 33, 0, 65, 16, 97, 48], dtype=torch.int32)
+    counts = torch.tensor([3, 2, 6, 2, 3, 0, 4, 0, 4, 1, 5, 2], dtype=torch.int32)
+    draft = torch.randint(0, B * pps, (B, width), generator=g, dtype=torch.int32)
+    # Row 1: the table already ends at the new page (no insert).
+    draft[1, 1] = block_table[1, 1]
+    # Row 5 (empty table, first token): column 0 holds another page.
+    draft[5, 0] = block_table[5, 0] + 1
+    before = (draft.clone(), counts.clone())
+
+    def mask(draft_indices, draft_num_pages):
+        # aspire/backends/base.py:1222-1236, on this fixture's tensors
+        is_draft = mode == 0
+        draft_pages_needed = ((dcl + page - 1) // page).to(torch.int32)
+        just_crossed = ((dcl - 1) % page == 0) & is_draft & (dec > 0)
+        tail_index = (draft_num_pages.to(torch.long) - 1).clamp(min=0)
+        tail_page = draft_indices.gather(1, tail_index.unsqueeze(1)).squeeze(1)
+        new_page_index = (draft_pages_needed.to(torch.long) - 1).clamp(min=0)
+        new_page = block_table.gather(1, new_page_index.unsqueeze(1)).squeeze(1).to(tail_page.dtype)
+        return just_crossed & (tail_page != new_page), draft_pages_needed
+
+    fake = types.SimpleNamespace(_draft_indices=draft, target_block_table=block_table,
+                                 _draft_num_pages_per_request=counts, draft_cachelens=dcl,
+                                 _get_num_pages=lambda s: (s + page - 1) // page)
+    need, needed = mask(draft, counts)
+    LMBackendBase._handle_draft_page_spill(fake, need, needed, counts)
+    # Host-identified path on a fresh copy: the rows of the mask with room.
+    d2, c2 = before[0].clone(), before[1].clone()
+    fake2 = types.SimpleNamespace(_draft_indices=d2, target_block_table=block_table,
+                                  _draft_num_pages_per_request=c2, draft_cachelens=dcl,
+                                  _get_num_pages=lambda s: (s + page - 1) // page)
+    need2, _ = mask(d2, c2)
+    ids = torch.nonzero(need2 & (c2 < width), as_tuple=True)[0]
+    LMBackendBase._handle_draft_page_spill_ids(fake2, ids, B)
+    assert torch.equal(d2, draft) and torch.equal(c2, counts), "mask and id spill paths differ"
+    out = {"mode_flags": mode, "dec_lens": dec, "draft_cachelens": dcl, "block_table": block_table,
+           "draft_before": before[0], "counts_before": before[1], "draft_after": draft, "counts_after": counts,
+           "spill_rows": ids}
+    print("spill rows", ids.tolist(), "counts", counts.tolist())
+    torch.save(out, HERE / "draft_spill.pt")
+
+
 def main():
     if not os.environ.get("ASPIRE_REFERENCE") or not REF.exists():
         raise SystemExit("set ASPIRE_REFERENCE to the root of the reference (ASPIRE) checkout")
@@ -250,6 +312,7 @@ def main():
     append_case()
     indices_case()
     recent_case()
+    spill_case()
 
 
 if __name__ == "__main__":

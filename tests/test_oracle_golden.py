@@ -215,3 +215,17 @@ def test_recent_rows_oracle_matches_reference_golden(golden_dir):
                                              p["min_draft_pages"])
         assert torch.equal(valid, c["valid"]), name
         assert torch.equal(rows, c["rows"]), name
+
+
+def test_draft_spill_oracle_matches_reference_golden(golden_dir):
+    """Draft-page spill restated against the reference's own
+    _handle_draft_page_spill / _handle_draft_page_spill_ids."""
+    from oracle import draft_spill as oracle_spill
+
+    g = _load(golden_dir, "draft_spill.pt")
+    draft, counts = g["draft_before"].clone(), g["counts_before"].clone()
+    oracle_spill.draft_page_spill(g["mode_flags"], g["dec_lens"], g["draft_cachelens"], draft, counts,
+                                  g["block_table"])
+    assert torch.equal(draft, g["draft_after"])
+    assert torch.equal(counts, g["counts_after"])
+    assert not torch.equal(counts, g["counts_before"])  # the fixture has rows that spill
