@@ -39,11 +39,14 @@ template <class Sh>
 __device__ __forceinline__ bool wait_bar(Sh& sm, uint64_t& bar, uint32_t parity, uint32_t* status) {
   const uint32_t a = ptx::smem_addr(&bar);
   if (ptx::mbar_try_wait(a, parity)) return true;
+  // Each failed try_wait has already suspended the thread for a while, so the
+  // clock is read after every poll (a check every few hundred polls would
+  // only fire for waits far longer than any short bound).
   const uint64_t t0 = global_ns();
-  for (uint32_t i = 1;; ++i) {
+  for (;;) {
     if (ptx::mbar_try_wait(a, parity)) return true;
     if (*reinterpret_cast<volatile int*>(&sm.abort_flag)) return false;
-    if ((i & 255) == 0 && global_ns() - t0 > sm.wait_ns) break;
+    if (global_ns() - t0 > sm.wait_ns) break;
   }
   *reinterpret_cast<volatile int*>(&sm.abort_flag) = 1;
   if (status) atomicOr(status, ASPIRE_STATUS_TIMEOUT);
