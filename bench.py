@@ -79,7 +79,11 @@ def parse_args():
     ap.add_argument("--layers", type=int, default=None)
     ap.add_argument("--block-table", default="arange", choices=["arange", "random"],
                     help="arange: the reference engine's contiguous per-row pages; random: scattered pages")
-    ap.add_argument("--workload", default="step", choices=["step", "prefill", "sweep"])
+    ap.add_argument("--workload", default="step", choices=["step", "prefill", "sweep", "decode"])
+    ap.add_argument("--no-decode", action="store_true", help="skip the end-to-end decode leg of the step run")
+    ap.add_argument("--decode-batch", type=int, default=32)
+    ap.add_argument("--decode-prompt", type=int, default=16384)
+    ap.add_argument("--decode-new", type=int, default=256)
     ap.add_argument("--sweep-ctx", default="4096,16384,32768,81920")
     ap.add_argument("--sweep-batch", default="1,4,16,64,128")
     ap.add_argument("--prefill-cases", default="1x8192+0,4x2048+16384,8x1024+4096,2x4096+0",
@@ -732,6 +736,58 @@ def prefill_bench(args):
                       "peak_bf16_tflops": peak, "cases": cases}), flush=True)
 
 
+DECODE_CFG = dict(model="qwen3-1.7b", draft_len=4, budget_pages=128, recent_pages=8, refresh_layer=2, seed=0)
+
+
+def decode_bench(args, device, world: int, dist_on: bool) -> dict:
+    """End-to-end accepted tokens/s (the metric's second half) on the
+    reference's config 2: Qwen3-1.7B shapes with random-init bf16 weights,
+    batch 32, synthetic 16384-token prompts, 256 generated tokens per
+    request, fixed draft length 4, sparse budget 128 pages + 8 recent pages,
+    refresh layer 2, TP = the number of ranks (aspire_b200.spec_decode).  The
+    prompts are prefilled, one decode run warms up (and captures the CUDA
+    graphs of the step shapes), then a second run from the same prefill
+    state is timed: tokens produced by the decode loop / its wall time with
+    the device synchronised at both ends, max over ranks.  The 4 sink pages
+    of the config have no counterpart in ASPIRE's selector and are left out."""
+    from aspire_b200.spec_decode import PRESETS, DenseModel, SpecDecoder, synthetic_prompts, token_sha256
+    c = DECODE_CFG
+    cfg = PRESETS[c["model"]]
+    model = DenseModel(cfg, device, seed=c["seed"])
+    prompts = synthetic_prompts(args.decode_batch, args.decode_prompt, cfg.vocab, seed=c["seed"])
+    dec = SpecDecoder(model, batch=args.decode_batch, prompt_len=args.decode_prompt, max_new=args.decode_new,
+                      draft_len=c["draft_len"], budget_pages=c["budget_pages"], recent_pages=c["recent_pages"],
+                      refresh_layer=c["refresh_layer"])
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    g0 = dec.prefill(prompts)
+    torch.cuda.synchronize()
+    prefill_s = time.perf_counter() - t0
+    warm = dec.generate()
+    dec.restart(g0)
+    r = dec.generate()
+    same = bool(np.array_equal(warm["tokens"], r["tokens"]))
+    secs = torch.tensor([r["seconds"], prefill_s], device=device)
+    if dist_on:
+        torch.distributed.all_reduce(secs, op=torch.distributed.ReduceOp.MAX)
+    dec_s, pre_s = float(secs[0].item()), float(secs[1].item())
+    steps = sum(r["steps"].values())
+    out = {"model": c["model"] + " shapes, random-init bf16 weights", "batch": args.decode_batch,
+           "prompt_tokens": args.decode_prompt, "new_tokens": args.decode_new, "draft_len": c["draft_len"],
+           "budget_pages": c["budget_pages"], "recent_pages": c["recent_pages"], "refresh_layer": c["refresh_layer"],
+           "tp": world, "accepted_tokens_per_s": round(r["decoded_tokens"] / dec_s, 1),
+           "decode_s": round(dec_s, 3), "prefill_s": round(pre_s, 2),
+           "prefill_tokens_per_s": round(args.decode_batch * args.decode_prompt / pre_s, 1),
+           "steps": r["steps"], "ms_per_step": round(1e3 * dec_s / max(steps, 1), 3),
+           "mean_accepted_drafts_per_verify": round(r["accepted_drafts"] / max(r["verify_rows"], 1), 3),
+           "tokens_per_row_per_step": round(r["decoded_tokens"] / max(steps, 1) / args.decode_batch, 3),
+           "repeat_identical": same, "token_sha256": token_sha256(r["tokens"]),
+           "cuda_graphs": dec.use_graphs, "data": "synthetic uniform tokens in [100, vocab), no EOS"}
+    del dec, model
+    torch.cuda.empty_cache()
+    return out
+
+
 def sweep_bench(args):
     """The reference's config-5 sweep: mixed attention
     plus top-k page selection alone at Qwen3-8B heads (32 / 8 / 128).
@@ -875,6 +931,22 @@ def main():
     if args.impl == "reference":
         reference_arm(args, rank, world)
         return
+    if args.workload == "decode":
+        dist_on = world > 1
+        torch.cuda.set_device(local_rank)
+        device = torch.device("cuda", local_rank)
+        if dist_on:
+            import datetime
+            torch.distributed.init_process_group("nccl", device_id=device, timeout=datetime.timedelta(seconds=300))
+        from aspire_b200 import load_library
+        load_library()
+        res = decode_bench(args, device, world, dist_on)
+        if rank == 0:
+            print(json.dumps({"workload": "decode", "metric": "accepted tokens/s per box", **res}), flush=True)
+        if dist_on:
+            torch.distributed.barrier()
+            torch.distributed.destroy_process_group()
+        return
     if args.workload in ("prefill", "sweep"):
         from aspire_b200 import load_library
         load_library()
@@ -929,6 +1001,13 @@ def main():
     cb = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cb = cpu_baseline(lay, full, budget_s=12.0)
+    launches = hp.launches_per_step() * args.steps
+    decode = None
+    if not args.no_decode:
+        hp.graph = None
+        del hp
+        torch.cuda.empty_cache()
+        decode = decode_bench(args, device, world, dist_on)
 
     if rank == 0:
         line = {
@@ -943,12 +1022,13 @@ def main():
                        "batch": CFG["batch"], "ctx": CFG["ctx"], "tp": world, "heads_per_rank": [lay.num_qo_heads, lay.num_kv_heads],
                        "l2": "inputs larger than L2 (8.7 GB cache at TP1)", "bytes_per_step": sb},
             "roofline": roof, "breakdown": parts, "clocks": clocks.summary(), "e2e": e2e, "check": check,
-            "gpu_launches": hp.launches_per_step() * args.steps,
-            "cpu_baseline": cb,
+            "gpu_launches": launches,
+            "cpu_baseline": cb, "decode": decode,
         }
         print(json.dumps(line), flush=True)
     if dist_on:
-        hp.graph = None
+        if args.no_decode:
+            hp.graph = None
         torch.distributed.barrier()
         torch.distributed.destroy_process_group()
 
