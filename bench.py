@@ -779,6 +779,7 @@ def decode_bench(args, device, world: int, dist_on: bool) -> dict:
            "decode_s": round(dec_s, 3), "prefill_s": round(pre_s, 2),
            "prefill_tokens_per_s": round(args.decode_batch * args.decode_prompt / pre_s, 1),
            "steps": r["steps"], "ms_per_step": round(1e3 * dec_s / max(steps, 1), 3),
+           "device_ms_per_step": r["device_ms_per_step"],
            "mean_accepted_drafts_per_verify": round(r["accepted_drafts"] / max(r["verify_rows"], 1), 3),
            "tokens_per_row_per_step": round(r["decoded_tokens"] / max(steps, 1) / args.decode_batch, 3),
            "repeat_identical": same, "token_sha256": token_sha256(r["tokens"]),
