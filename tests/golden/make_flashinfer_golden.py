@@ -13,6 +13,20 @@ Needs a CUDA GPU (FlashInfer JIT-compiles its kernel on first use):
 
     python tests/golden/make_flashinfer_golden.py [out.pt]
     python tests/golden/make_flashinfer_golden.py --prefill [out.pt]
+    python tests/golden/make_flashinfer_golden.py --dump [out.pt]
+
+`--dump` runs the reference's first/last logit-dump transform inside
+FlashInfer (aspire/backends/jit_kernels.py:188-193, offsets :252-256): a
+custom attention variant of FlashInfer's FA2 paged-prefill kernel, JIT-built
+with the argument layout of the reference's build_dump_jit_args
+(jit_kernels.py:356-390: one fp16 dump tensor, scalars sm_scale, num_heads,
+jit_kv_stride), on the refresh layer's full-context program of seeded mixed
+batches, into flashinfer_dump.pt.  The installed FlashInfer's holistic
+kernel builds its variant with batch index 0 for every request (the request
+index is what the reference's patch adds), so it cannot place a per-request
+dump; the FA2 kernel passes the request index, and in both kernels the
+transform sees the raw q.k (sm_scale is applied afterwards, in the softmax
+update).
 
 `--prefill` runs FlashInfer's BatchPrefillWithPagedKVCacheWrapper, the
 library the reference runs its prefill chunks through
@@ -57,6 +71,97 @@ def prefill_cases():
     yield "prefill_g1", rows_layout([150], [400], 4, 4, seed=12), 12
 
 
+# The first/last dump as a FlashInfer attention variant (FA2 form): for
+# query 0 (slot 0) and the row's last query (slot 1) the raw logit of every
+# key the kernel visits is written as fp16 to
+# dump[row, head, slot, kv_idx]; the logit itself passes through unchanged.
+# Written for this fixture from the transform's description; like the
+# reference's variant it does not test kv_idx < kv_len.
+DUMP_VARIANT = r"""
+struct FirstLastDumpFA2 : AttentionVariantBase {
+  static constexpr bool use_softmax = true;
+  uint32_t window_left, qo_len, kv_len;
+  float sm_scale_log2;
+  half* out_dump;
+  uint64_t slot_stride, head_stride, row_offset;
+
+  template <typename Params>
+  __device__ __host__ FirstLastDumpFA2(const Params& params, uint32_t batch_idx, uint8_t* smem_ptr) {
+    qo_len = params.get_qo_len(batch_idx);
+    kv_len = params.get_kv_len(batch_idx);
+    window_left = kv_len;
+    sm_scale_log2 = params.sm_scale * math::log2e;
+    out_dump = params.attention_weights;
+    slot_stride = (uint64_t)params.jit_kv_stride;
+    head_stride = 2u * slot_stride;
+    row_offset = (uint64_t)batch_idx * (uint64_t)params.num_heads * head_stride;
+  }
+
+  REGISTER_LOGITS_TRANSFORM(params, logits, batch_idx, qo_idx, kv_idx, qo_head_idx, kv_head_idx, {
+    if (qo_idx == 0u || qo_idx + 1u == qo_len) {
+      const uint64_t slot = (qo_idx == 0u) ? 0u : 1u;
+      out_dump[row_offset + (uint64_t)qo_head_idx * head_stride + slot * slot_stride + kv_idx] =
+          __float2half(logits);
+    }
+    return logits;
+  })
+};
+"""
+
+
+def dump_cases():
+    from aspire_b200.workloads import config1_layout as c1
+    yield "cfg1_full", full_context_layout(c1(seed=0)), 0
+    lay = make_layout(batch=4, ctx=2000, num_qo_heads=32, num_kv_heads=8, draft_fraction=0.5, budget_pages=24,
+                      seed=8)
+    yield "qwen8b_full", full_context_layout(lay), 8
+
+
+def dump_main(out_path):
+    import flashinfer
+
+    dev = torch.device("cuda:0")
+    jit_args = ["aspire_golden_first_last_dump", torch.bfloat16, torch.bfloat16, torch.bfloat16, torch.int32,
+                128, 128, ["attention_weights"], ["half"], ["sm_scale", "num_heads", "jit_kv_stride"],
+                ["double", "int64_t", "int64_t"], "FirstLastDumpFA2", DUMP_VARIANT]
+    result = {"flashinfer_version": flashinfer.__version__, "variant": DUMP_VARIANT, "cases": {}}
+    for name, lay, seed in dump_cases():
+        q, kv = fill_tensors(lay, device="cpu", dtype=torch.bfloat16, seed=seed)
+        q, kv = q.to(dev), kv.to(dev)
+        i32 = lambda a: torch.from_numpy(np.ascontiguousarray(a, dtype=np.int32)).to(dev)  # noqa: E731
+        # Padded to a multiple of the kernel's key tile, as the engine pads its
+        # dump stride (compute_max_cta_tile_kv, aspire/attention/flashinfer.py:63-105):
+        # the transform has no kv_idx < kv_len test, so the last tile's
+        # positions past kv_len land in the padding.
+        stride = (lay.pages_per_row * 16 + 127) // 128 * 128
+        H = lay.num_qo_heads
+        dump = torch.full((lay.batch * H * 2 * stride,), float("-inf"), dtype=torch.float16, device=dev)
+        ws = torch.empty(128 * 1024 * 1024, dtype=torch.uint8, device=dev)
+        w = flashinfer.BatchPrefillWithPagedKVCacheWrapper(ws, "NHD", backend="fa2", jit_args=jit_args)
+        # One KV chunk per request: with split-KV chunks the last key tile of
+        # a chunk runs past the chunk's end and, with no kv_idx test in the
+        # transform, overwrites the next chunk's positions with logits of
+        # other keys (seen as windows of wrong values every chunk length).
+        w.plan(i32(lay.qo_indptr), i32(lay.kv_indptr), i32(lay.kv_indices), i32(last_page_lens(lay)), H,
+               lay.num_kv_heads, 128, 16, causal=True, q_data_type=torch.bfloat16, kv_data_type=torch.bfloat16,
+               disable_split_kv=True)
+        sm_scale = 1.0 / 128 ** 0.5
+        out, lse = w.run(q, kv, dump, sm_scale, H, stride, return_lse=True)
+        torch.cuda.synchronize()
+        result["cases"][name] = {
+            "seed": seed, "kv_stride": stride,
+            "layout": {k: getattr(lay, k) for k in ("num_qo_heads", "num_kv_heads", "modes", "q_lens", "kv_lens",
+                                                    "qo_indptr", "kv_indptr", "kv_indices", "block_table",
+                                                    "ctx_lens", "pages_per_row", "num_pages_total")},
+            "dump": dump.view(lay.batch, H, 2, stride).cpu(),
+            "out": out.cpu(),
+            "lse": lse.float().cpu(),
+        }
+        print(name, "dump", (lay.batch, H, 2, stride), "finite", int(torch.isfinite(dump).sum()), flush=True)
+    torch.save(result, out_path)
+    print("saved", out_path)
+
+
 def prefill_main(out_path):
     import flashinfer
 
@@ -89,9 +194,12 @@ def prefill_main(out_path):
 def main():
     import flashinfer
 
-    args = [a for a in sys.argv[1:] if a != "--prefill"]
+    args = [a for a in sys.argv[1:] if a not in ("--prefill", "--dump")]
     if "--prefill" in sys.argv[1:]:
         prefill_main(Path(args[0]) if args else HERE / "flashinfer_prefill.pt")
+        return
+    if "--dump" in sys.argv[1:]:
+        dump_main(Path(args[0]) if args else HERE / "flashinfer_dump.pt")
         return
     out_path = Path(args[0]) if args else HERE / "flashinfer_attention.pt"
     dev = torch.device("cuda:0")

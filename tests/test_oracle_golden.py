@@ -229,3 +229,41 @@ def test_draft_spill_oracle_matches_reference_golden(golden_dir):
     assert torch.equal(draft, g["draft_after"])
     assert torch.equal(counts, g["counts_after"])
     assert not torch.equal(counts, g["counts_before"])  # the fixture has rows that spill
+
+
+def dump_positions_close(got, ref, lay):
+    """fp16 dumps agree within one fp16 rounding step (plus a small absolute
+    slack for the fp32 accumulation order) at every position the first/last
+    transform defines: slot 0 of every row and slot 1 of rows with more than
+    one query, keys [0, kv_len)."""
+    for b in range(lay.batch):
+        L = int(lay.kv_lens[b])
+        for s in [0] + ([1] if int(lay.q_lens[b]) > 1 else []):
+            a, e = got[b, :, s, :L].float(), ref[b, :, s, :L].float()
+            tol = e.abs() * 2.0 ** -10 + 2.0 ** -14 + 2e-3
+            assert bool(torch.isfinite(e).all()), (b, s)
+            assert bool(((a - e).abs() <= tol).all()), (b, s, float((a - e).abs().max()))
+
+
+@pytest.mark.parametrize("case", ["cfg1_full", "qwen8b_full"])
+def test_dump_oracle_matches_flashinfer_variant(golden_dir, case):
+    """The oracle's first/last dump against the reference's dump transform run
+    inside FlashInfer (a custom FA2 attention variant, fixture from
+    tests/golden/make_flashinfer_golden.py --dump): pins that the dump holds
+    the raw q.k before scaling and masking, fp16-rounded, slot 0 for query 0
+    and slot 1 for the last query."""
+    from aspire_b200.workloads import MixedLayout, fill_tensors
+    from oracle import attention as oracle_attn
+
+    g = _load(golden_dir, "flashinfer_dump.pt")["cases"][case]
+    lay = MixedLayout(**g["layout"])
+    S = g["kv_stride"]
+    q, kv = fill_tensors(lay, device="cpu", dtype=torch.bfloat16, seed=g["seed"])
+    dump = torch.full((lay.batch * lay.num_qo_heads * 2 * S,), float("-inf"), dtype=torch.float16)
+    out, lse = oracle_attn.paged_attention(q.float(), kv, lay.qo_indptr, lay.kv_indptr, lay.kv_indices,
+                                           lay.kv_lens, dump=dump, dump_num_heads=lay.num_qo_heads,
+                                           dump_kv_stride=S)
+    dump_positions_close(dump.view(lay.batch, lay.num_qo_heads, 2, S), g["dump"], lay)
+    err = (out - g["out"].float()).abs()
+    assert err.max().item() <= 2e-2 and err.mean().item() <= 2e-3
+    assert (lse - g["lse"]).abs().max().item() <= 2e-3
