@@ -225,11 +225,12 @@ class DenseModel:
         return torch.gather(ids, 1, r)[:, 0], best[:, 0], best[:, 1], e
 
 
-def step_shape(n: np.ndarray, dcnt: np.ndarray, active: np.ndarray, draft_len: int, budget_pages: int) -> dict:
+def step_shape(n: np.ndarray, dcnt: np.ndarray, active: np.ndarray, draft_len, budget_pages: int) -> dict:
     """Per-row shape of one fixed-draft step (host arrays).
 
     n: committed tokens in the cache; dcnt: drafted tokens pending; active:
     rows still generating.  A row verifies when it holds draft_len drafts
+    (one length for every row, or an array of per-row lengths)
     (q_len dcnt + 1 at positions n..), else drafts one token at position
     n + dcnt.  ``end`` is the row's length once this step's tokens are
     appended.  Draft rows attend their draft table: after the step's
@@ -261,16 +262,23 @@ def accept(drafts: np.ndarray, target: np.ndarray) -> int:
 
 
 class SpecDecoder:
-    """Batched self-speculative decoding (fixed draft length) of one batch of
-    equal-length prompts.  ``draft_len == 0`` gives plain greedy decoding
-    (every step a q_len-1 full-attention step through the same ops)."""
+    """Batched self-speculative decoding of one batch of equal-length prompts.
+    ``draft_len`` is the fixed draft length of every row (``0`` gives plain
+    greedy decoding: every step a q_len-1 full-attention step through the
+    same ops), or a ``(lo, hi)`` range: each row draws its next draft length
+    uniformly from it after every verification (seeded by ``draft_seed``), so
+    the rows drift apart and steps mix drafting and verifying rows, as the
+    reference's asynchronous scheduling interleaves them."""
 
-    def __init__(self, model: DenseModel, *, batch: int, prompt_len: int, max_new: int, draft_len: int,
+    def __init__(self, model: DenseModel, *, batch: int, prompt_len: int, max_new: int, draft_len,
                  budget_pages: int, recent_pages: int = 8, refresh_layer: int = -2, use_graphs: bool = True,
-                 prefill_chunk: int = 8192):
+                 prefill_chunk: int = 8192, draft_seed: int = 0):
         cfg = model.cfg
         dev = model.device
         self.model, self.dev = model, dev
+        self.draft_range = tuple(draft_len) if isinstance(draft_len, (tuple, list)) else None
+        self.draft_seed = draft_seed
+        draft_len = self.draft_range[1] if self.draft_range else int(draft_len)
         self.B, self.P, self.G, self.D = batch, prompt_len, max_new, draft_len
         self.pps = (prompt_len + max_new + draft_len + 2 * PAGE - 1) // PAGE
         self.kv_stride = self.pps * PAGE
@@ -383,6 +391,8 @@ class SpecDecoder:
         self.n = np.full(B, self.P, np.int64)      # committed tokens in the cache
         self.dcnt = np.zeros(B, np.int64)          # drafted tokens pending verification
         self.tok0 = np.asarray(g0, np.int64).copy()  # last committed token of each row (not yet in the cache)
+        self._rng = np.random.default_rng(self.draft_seed)
+        self.dtarget = self._draw_targets(B)      # drafts each row makes before verifying
         self.out = [[int(g0[b])] for b in range(B)]
         self.tok_dev.zero_()
         self.step_no = 0
@@ -392,6 +402,12 @@ class SpecDecoder:
         num_pages = torch.from_numpy(((self.n + 1 + PAGE - 1) // PAGE).astype(np.int32)).to(self.dev)
         self.draft_table.zero_()
         self.selector.seed_recent_into(self.draft_table, self.draft_counts, num_pages, self.block_table)
+
+    def _draw_targets(self, n: int) -> np.ndarray:
+        if self.draft_range is None:
+            return np.full(n, self.D, np.int64)
+        lo, hi = self.draft_range
+        return self._rng.integers(lo, hi + 1, size=n).astype(np.int64)
 
     # ------------------------------------------------------------------ steps
     def _attn_step(self, l, q, k, v):
@@ -428,7 +444,7 @@ class SpecDecoder:
         """Host side of one step: modes, lengths, plans and uploads (no sync)."""
         B = self.B
         active = np.array([len(o) < self.G for o in self.out])
-        s = step_shape(self.n, self.dcnt, active, self.D, self.k_sel)
+        s = step_shape(self.n, self.dcnt, active, self.dtarget, self.k_sel)
         verify, draft, qlen, start, end = s["verify"], s["draft"], s["qlen"], s["start"], s["end"]
         full_pages, last, mixed_pages, mixed_len, qo = (s["full_pages"], s["last"], s["mixed_pages"],
                                                         s["mixed_len"], s["qo"])
@@ -533,6 +549,7 @@ class SpecDecoder:
             self.n[b] += acc + 1
             self.tok0[b] = out_b[acc]
             self.dcnt[b] = 0
+            self.dtarget[b] = self._draw_targets(1)[0]
             self.accepted_total += acc
             self.verify_rows += 1
 

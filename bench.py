@@ -81,9 +81,11 @@ def parse_args():
                     help="arange: the reference engine's contiguous per-row pages; random: scattered pages")
     ap.add_argument("--workload", default="step", choices=["step", "prefill", "sweep", "decode"])
     ap.add_argument("--no-decode", action="store_true", help="skip the end-to-end decode leg of the step run")
-    ap.add_argument("--decode-batch", type=int, default=32)
-    ap.add_argument("--decode-prompt", type=int, default=16384)
-    ap.add_argument("--decode-new", type=int, default=256)
+    ap.add_argument("--decode-config", type=int, default=2, choices=[2, 3, 4],
+                    help="the reference's end-to-end config the decode leg runs (2 by default)")
+    ap.add_argument("--decode-batch", type=int, default=None)
+    ap.add_argument("--decode-prompt", type=int, default=None)
+    ap.add_argument("--decode-new", type=int, default=None)
     ap.add_argument("--sweep-ctx", default="4096,16384,32768,81920")
     ap.add_argument("--sweep-batch", default="1,4,16,64,128")
     ap.add_argument("--prefill-cases", default="1x8192+0,4x2048+16384,8x1024+4096,2x4096+0",
@@ -736,28 +738,41 @@ def prefill_bench(args):
                       "peak_bf16_tflops": peak, "cases": cases}), flush=True)
 
 
-DECODE_CFG = dict(model="qwen3-1.7b", draft_len=4, budget_pages=128, recent_pages=8, refresh_layer=2, seed=0)
+# The reference's end-to-end configs (BASELINE configs[1..3]).  Config 3's
+# 4 sink pages (config 2) have no counterpart in ASPIRE's selector and are
+# left out; config 4 names no draft length, so it drafts 4 like config 2.
+DECODE_CFGS = {
+    2: dict(model="qwen3-1.7b", batch=32, prompt=16384, new=256, draft_len=4, budget_pages=128, recent_pages=8,
+            refresh_layer=2, seed=0),
+    3: dict(model="qwen3-8b", batch=64, prompt=32768, new=512, draft_len=(2, 8), budget_pages=128, recent_pages=8,
+            refresh_layer=-2, seed=0),
+    4: dict(model="llama-3.1-8b", batch=16, prompt=81920, new=256, draft_len=4, budget_pages=256, recent_pages=8,
+            refresh_layer=-2, seed=0),
+}
 
 
 def decode_bench(args, device, world: int, dist_on: bool) -> dict:
-    """End-to-end accepted tokens/s (the metric's second half) on the
-    reference's config 2: Qwen3-1.7B shapes with random-init bf16 weights,
-    batch 32, synthetic 16384-token prompts, 256 generated tokens per
-    request, fixed draft length 4, sparse budget 128 pages + 8 recent pages,
-    refresh layer 2, TP = the number of ranks (aspire_b200.spec_decode).  The
-    prompts are prefilled, one decode run warms up (and captures the CUDA
-    graphs of the step shapes), then a second run from the same prefill
-    state is timed: tokens produced by the decode loop / its wall time with
-    the device synchronised at both ends, max over ranks.  The 4 sink pages
-    of the config have no counterpart in ASPIRE's selector and are left out."""
+    """End-to-end accepted tokens/s (the metric's second half) on one of the
+    reference's end-to-end configs (DECODE_CFGS; config 2 by default:
+    Qwen3-1.7B shapes with random-init bf16 weights, batch 32, synthetic
+    16384-token prompts, 256 generated tokens per request, fixed draft length
+    4, sparse budget 128 pages + 8 recent pages, refresh layer 2), TP = the
+    number of ranks (aspire_b200.spec_decode).  The prompts are prefilled,
+    one decode run warms up (and captures the CUDA graphs of the step
+    shapes), then a second run from the same prefill state is timed: tokens
+    produced by the decode loop / its wall time with the device synchronised
+    at both ends, max over ranks."""
     from aspire_b200.spec_decode import PRESETS, DenseModel, SpecDecoder, synthetic_prompts, token_sha256
-    c = DECODE_CFG
+    c = dict(DECODE_CFGS[args.decode_config])
+    for key, arg in (("batch", args.decode_batch), ("prompt", args.decode_prompt), ("new", args.decode_new)):
+        if arg is not None:
+            c[key] = arg
     cfg = PRESETS[c["model"]]
     model = DenseModel(cfg, device, seed=c["seed"])
-    prompts = synthetic_prompts(args.decode_batch, args.decode_prompt, cfg.vocab, seed=c["seed"])
-    dec = SpecDecoder(model, batch=args.decode_batch, prompt_len=args.decode_prompt, max_new=args.decode_new,
+    prompts = synthetic_prompts(c["batch"], c["prompt"], cfg.vocab, seed=c["seed"])
+    dec = SpecDecoder(model, batch=c["batch"], prompt_len=c["prompt"], max_new=c["new"],
                       draft_len=c["draft_len"], budget_pages=c["budget_pages"], recent_pages=c["recent_pages"],
-                      refresh_layer=c["refresh_layer"])
+                      refresh_layer=c["refresh_layer"], draft_seed=c["seed"])
     torch.cuda.synchronize()
     t0 = time.perf_counter()
     g0 = dec.prefill(prompts)
@@ -772,16 +787,17 @@ def decode_bench(args, device, world: int, dist_on: bool) -> dict:
         torch.distributed.all_reduce(secs, op=torch.distributed.ReduceOp.MAX)
     dec_s, pre_s = float(secs[0].item()), float(secs[1].item())
     steps = sum(r["steps"].values())
-    out = {"model": c["model"] + " shapes, random-init bf16 weights", "batch": args.decode_batch,
-           "prompt_tokens": args.decode_prompt, "new_tokens": args.decode_new, "draft_len": c["draft_len"],
+    out = {"config": args.decode_config, "model": c["model"] + " shapes, random-init bf16 weights",
+           "batch": c["batch"], "prompt_tokens": c["prompt"], "new_tokens": c["new"],
+           "draft_len": list(c["draft_len"]) if isinstance(c["draft_len"], tuple) else c["draft_len"],
            "budget_pages": c["budget_pages"], "recent_pages": c["recent_pages"], "refresh_layer": c["refresh_layer"],
            "tp": world, "accepted_tokens_per_s": round(r["decoded_tokens"] / dec_s, 1),
            "decode_s": round(dec_s, 3), "prefill_s": round(pre_s, 2),
-           "prefill_tokens_per_s": round(args.decode_batch * args.decode_prompt / pre_s, 1),
+           "prefill_tokens_per_s": round(c["batch"] * c["prompt"] / pre_s, 1),
            "steps": r["steps"], "ms_per_step": round(1e3 * dec_s / max(steps, 1), 3),
            "device_ms_per_step": r["device_ms_per_step"],
            "mean_accepted_drafts_per_verify": round(r["accepted_drafts"] / max(r["verify_rows"], 1), 3),
-           "tokens_per_row_per_step": round(r["decoded_tokens"] / max(steps, 1) / args.decode_batch, 3),
+           "tokens_per_row_per_step": round(r["decoded_tokens"] / max(steps, 1) / c["batch"], 3),
            "repeat_identical": same, "token_sha256": token_sha256(r["tokens"]),
            "cuda_graphs": dec.use_graphs, "data": "synthetic uniform tokens in [100, vocab), no EOS"}
     del dec, model

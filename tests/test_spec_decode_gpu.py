@@ -88,3 +88,27 @@ def test_full_budget_drafts_are_accepted(model):
     print("full budget:", {k: v for k, v in a.items() if k != "tokens"}, "acceptance", round(rate, 4))
     assert rate >= 0.8, rate
     _check_greedy(dec, a["tokens"], "full budget")
+
+
+def test_random_draft_lengths_mix_steps_and_stay_greedy(model):
+    """Per-row draft lengths drawn from 2..6 after every verification (config
+    3's asynchronous interleaving): the rows drift apart, so most steps hold
+    drafting and verifying rows together, and the output is still the plain
+    greedy decode of the same prompts."""
+    prompts = synthetic_prompts(B, P, model.cfg.vocab, seed=2)
+    dec = SpecDecoder(model, batch=B, prompt_len=P, max_new=G, draft_len=(2, 6), budget_pages=32, recent_pages=8,
+                      draft_seed=3)
+    g0 = dec.prefill(prompts)
+    a = dec.generate()
+    print("random lengths:", {k: v for k, v in a.items() if k != "tokens"})
+    assert a["steps"]["mixed"] > a["steps"]["draft"] + a["steps"]["verify"], a["steps"]
+    dec.restart(g0)
+    b = dec.generate()
+    assert np.array_equal(a["tokens"], b["tokens"])
+    _check_greedy(dec, a["tokens"], "random lengths")
+    ar = SpecDecoder(model, batch=B, prompt_len=P, max_new=G, draft_len=0, budget_pages=32, recent_pages=8)
+    ar.prefill(prompts)
+    r = ar.generate()
+    cmp = compare_sequences(a["tokens"], r["tokens"])
+    print("random lengths vs plain greedy:", cmp)
+    assert cmp["rows_identical"] == B, cmp
