@@ -99,6 +99,36 @@ __host__ __device__ inline int64_t chunk_for(int64_t total_tokens, int64_t num_s
   return (chunk + 127) / 128 * 128;
 }
 
+// Whole (row, KV head, query-tile) groups instead of split-KV chunks, when
+// they would fill the grid about as evenly: a medium draft-only batch (16 to
+// 64 rows over a 64-512 page budget) otherwise pays item boundaries and the
+// merge for balance it does not need.  Both planners compare two makespan
+// estimates in tenths of a 128-token tile (1.5-1.8 us on B200 at any load):
+//   whole = ceil(groups / SMs) x (longest span + item)
+//   split = max(tokens / SMs, chunk) + ceil(chunk items / SMs) x item
+//           + merge (when any group splits)
+// with an item boundary at 2.3 tiles and the merge (its launch and the extra
+// kernel boundary) at 2.5, fitted to timed draft-only batches: 16 rows over
+// 64 pages ran 22.0 us whole against 28.1 us split, one row 19.1 us whole
+// against 15.5 us split (its few SMs gain more from halving the span).
+constexpr int64_t kItemCost10 = 23;
+constexpr int64_t kMergeCost10 = 25;
+__host__ __device__ inline bool whole_groups_cheaper(int64_t n_groups, int64_t max_span, int64_t total_tokens,
+                                                     int64_t chunk, int64_t n_chunk_items, int64_t num_sms) {
+  if (n_groups <= 0 || num_sms <= 0) return false;
+  const int64_t whole = (n_groups + num_sms - 1) / num_sms * ((max_span + 127) / 128 * 10 + kItemCost10);
+  const int64_t avg10 = (total_tokens * 10 + 128 * num_sms - 1) / (128 * num_sms);
+  const int64_t chunk10 = chunk / 128 * 10;
+  const int64_t split = (avg10 > chunk10 ? avg10 : chunk10) + (n_chunk_items + num_sms - 1) / num_sms * kItemCost10 +
+                        (n_chunk_items > n_groups ? kMergeCost10 : 0);
+  return whole <= split;
+}
+// The chunk length that keeps every group whole.
+__host__ __device__ inline int64_t whole_group_chunk(int64_t max_span) {
+  const int64_t c = (max_span + 127) / 128 * 128;
+  return c < 512 ? 512 : c;
+}
+
 // Resident CTAs per SM of each kernel class (sets the persistent grids).
 constexpr int kGatherCtasPerSm = 4;
 constexpr int kTcCtasPerSm = 1;

@@ -132,7 +132,25 @@ __global__ void __launch_bounds__(kDevPlanThreads) aspire_plan_device_kernel(Dev
   int64_t total_tokens;
   block_exclusive_scan(tokens, warp_sums, &total_tokens);  // (its barriers publish max_span)
   const bool similar = 2 * int64_t(min_span) >= max_span;
-  const int64_t chunk = chunk_for(total_tokens, p.num_sms, similar ? kItemsPerCtaUniform : kItemsPerCtaMixed);
+  int64_t chunk = chunk_for(total_tokens, p.num_sms, similar ? kItemsPerCtaUniform : kItemsPerCtaMixed);
+  {
+    // Whole groups when they balance about as well (whole_groups_cheaper).
+    int64_t my_groups = 0, my_chunk_items = 0;
+    for (int b = r0; b < r1; ++b) {
+      const RowShape s = row_shape(p, b);
+      if (s.ql <= 0) continue;
+      for (int qt = 0; qt < s.ntq; ++qt) {
+        const int32_t span = tile_span(p, s, qt * s.tile, min(s.nq, (qt + 1) * s.tile));
+        my_groups += p.num_kv_heads;
+        my_chunk_items += int64_t(p.num_kv_heads) * span_chunks(span, chunk);
+      }
+    }
+    int64_t n_groups, n_chunk_items;
+    block_exclusive_scan(my_groups, warp_sums, &n_groups);
+    block_exclusive_scan(my_chunk_items, warp_sums, &n_chunk_items);
+    if (whole_groups_cheaper(n_groups, max_span, total_tokens, chunk, n_chunk_items, p.num_sms))
+      chunk = whole_group_chunk(max_span);
+  }
 
   // Per-thread counts; item lengths into the cost histogram.
   int64_t n_items = 0, n_merge = 0, n_prow = 0, n_units = 0;

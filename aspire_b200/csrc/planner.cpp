@@ -165,7 +165,13 @@ int plan_impl(const int32_t* qo_indptr, const int32_t* kv_indptr, const int32_t*
     min_span = std::min(min_span, g.span);
   }
   const bool similar = 2 * int64_t(min_span) >= max_span;
-  const int64_t chunk = chunk_for(total_tokens, num_sms, similar ? kItemsPerCtaUniform : kItemsPerCtaMixed);
+  int64_t chunk = chunk_for(total_tokens, num_sms, similar ? kItemsPerCtaUniform : kItemsPerCtaMixed);
+  {
+    int64_t n_chunk_items = 0;
+    for (const GroupDesc& g : groups) n_chunk_items += g.span > 0 ? (g.span + chunk - 1) / chunk : 1;
+    if (whole_groups_cheaper(int64_t(groups.size()), max_span, total_tokens, chunk, n_chunk_items, num_sms))
+      chunk = whole_group_chunk(max_span);
+  }
 
   std::vector<WorkItem> gather_items, tc_items, pf_items;
   std::vector<MergeDesc> merges;

@@ -110,23 +110,51 @@ def test_plan_balances_ctas(built_library):
 
 def _expected_chunk(spans, hkv, num_sms):
     """The planner's chunk rule, restated: about four items per SM when the
-    groups' spans are within 2x of each other, else about two."""
+    groups' spans are within 2x of each other, else about two; but every
+    group whole (chunk = longest span rounded up to 128, at least 512) when
+    the whole-group makespan estimate is no worse than the split one (in
+    tenths of a 128-token tile: an item boundary 2.3 tiles, the merge 2.5)."""
     total = sum(max(s, 1) for s in spans) * hkv
+    cdiv = lambda a, b: -(-a // b)  # noqa: E731
 
     def chunk_for(per_cta):
         target = num_sms * per_cta
-        c = max(-(-total // target), 512)
-        return -(-c // 128) * 128
+        c = max(cdiv(total, target), 512)
+        return cdiv(c, 128) * 128
 
-    return chunk_for(4 if 2 * min(spans) >= max(spans) else 2)
+    chunk = chunk_for(4 if 2 * min(spans) >= max(spans) else 2)
+    n_groups = len(spans) * hkv
+    n_items = sum(cdiv(s, chunk) if s > 0 else 1 for s in spans) * hkv
+    whole = cdiv(n_groups, num_sms) * (cdiv(max(spans), 128) * 10 + 23)
+    split = (max(cdiv(total * 10, 128 * num_sms), chunk // 128 * 10) + cdiv(n_items, num_sms) * 23
+             + (25 if n_items > n_groups else 0))
+    return max(512, cdiv(max(spans), 128) * 128) if whole <= split else chunk
 
 
-@pytest.mark.parametrize("case", ["mixed", "full_context", "prefill_spread"])
+@pytest.mark.parametrize("case", ["mixed", "full_context", "prefill_spread", "draft_b1", "draft_b16", "draft_b32"])
 def test_plan_chunk_rule(built_library, case):
     """Decode batches (long verify rows beside short draft rows) get about two
     items per SM; whole-context rows of equal length, four; the spread-out
-    query tiles of a causal prefill chunk stay whole at two per SM."""
+    query tiles of a causal prefill chunk stay whole at two per SM.  Medium
+    draft-only batches keep every group whole (one item each, no merge): 16
+    rows over 64 pages at 32 / 8 heads, 32 rows over 136 pages at 16 / 8; one
+    row over 64 pages is still split (its 8 groups use 16 SMs)."""
     num_sms = 148
+    if case.startswith("draft_"):
+        B, pages, hq, hkv = {"draft_b1": (1, 64, 32, 8), "draft_b16": (16, 64, 32, 8),
+                             "draft_b32": (32, 136, 16, 8)}[case]
+        kvl = np.full(B, pages * 16, np.int32)
+        qo = np.arange(B + 1, dtype=np.int32)
+        kvp = (np.arange(B + 1) * pages).astype(np.int32)
+        rc, info, _ = _plan(built_library, qo, kvp, kvl, hq, hkv, num_sms=num_sms)
+        assert rc == 0, built_library.aspire_last_error()
+        assert info.chunk_tokens == _expected_chunk([pages * 16] * B, hkv, num_sms)
+        if case == "draft_b1":
+            assert info.chunk_tokens == 512 and info.num_merge == B * hkv
+        else:
+            assert info.chunk_tokens == pages * 16
+            assert info.num_merge == 0 and info.num_items_tc == B * hkv
+        return
     if case == "mixed":
         lay = make_layout(batch=64, ctx=32768, num_qo_heads=32, num_kv_heads=8, draft_fraction=0.5,
                           budget_pages=128, seed=0)
@@ -158,7 +186,8 @@ def test_plan_rejects_bad_input(built_library):
     assert b"exceeds its page list" in built_library.aspire_last_error()
     rc, _, _ = _plan(built_library, [0, 1], [0, 1], [5], 30, 8)  # heads not a multiple
     assert rc == _capi.ASPIRE_ERR_INVALID
-    rc, _, _ = _plan(built_library, [0, 1], [0, 4096], [65536], 32, 8, float_ws=16)
+    # 8 groups of 64k tokens on 148 SMs split into chunks, whose partials need float workspace.
+    rc, _, _ = _plan(built_library, [0, 1], [0, 4096], [65536], 32, 8, num_sms=148, float_ws=16)
     assert rc == _capi.ASPIRE_ERR_CAPACITY
 
 
