@@ -28,6 +28,10 @@ STATUS_BAD_PAGE = 1
 STATUS_BAD_PLAN = 2
 STATUS_BAD_ROW = 4
 STATUS_TIMEOUT = 8
+DUMP_FIRST_LAST = 0
+DUMP_LAST_TOKEN = 1
+DUMP_F16 = 0
+DUMP_F32 = 1
 
 c_int32_p = ctypes.POINTER(ctypes.c_int32)
 
@@ -84,6 +88,9 @@ class AspireAttnArgs(ctypes.Structure):
         ("draft_stride", ctypes.c_int64),
         ("block_table", ctypes.c_void_p),
         ("block_table_stride", ctypes.c_int64),
+        ("dump_kind", ctypes.c_int32),
+        ("dump_dtype", ctypes.c_int32),
+        ("dump_flags", ctypes.c_void_p),
     ]
 
 
@@ -147,6 +154,8 @@ class AspireSelectArgs(ctypes.Structure):
         ("status", ctypes.c_void_p),
         ("scores_ws", ctypes.c_void_p),
         ("order_by_page", ctypes.c_int32),
+        ("dump_kind", ctypes.c_int32),
+        ("dump_dtype", ctypes.c_int32),
     ]
 
 
@@ -272,7 +281,7 @@ _SIGNATURES = {
     "aspire_kernel_names": (ctypes.c_char_p, []),
 }
 
-EXPECTED_ABI_VERSION = 4
+EXPECTED_ABI_VERSION = 5
 
 _lib = None
 _lock = threading.Lock()

@@ -69,16 +69,21 @@ def _unpack_paged_kv_cache(
     return paged_kv_cache
 
 
-def _dump_kind_from_jit_args(jit_args) -> Tuple[str, bool]:
-    """Recovers (dump_kind, uses_mode_flags) from the reference's JIT argument list."""
+def _dump_kind_from_jit_args(jit_args) -> Tuple[str, bool, Optional[torch.dtype]]:
+    """Recovers (dump_kind, uses_mode_flags, dump buffer dtype) from the
+    reference's JIT argument list (build_holistic_dump_jit_args,
+    aspire/attention/holistic_wrapper.py:401-434: tensor names at [7], their
+    C types at [8], the struct source at [12])."""
     tensor_names = list(jit_args[7]) if len(jit_args) > 7 else []
+    tensor_types = list(jit_args[8]) if len(jit_args) > 8 else []
     code = str(jit_args[12]) if len(jit_args) > 12 else ""
     uses_mode_flags = "mode_flags" in tensor_names
+    dtype = {"half": torch.float16, "float": torch.float32}.get(str(tensor_types[0]) if tensor_types else "")
     if "qo_slot" in code:
-        return "first_last_compact", uses_mode_flags
+        return "first_last_compact", uses_mode_flags, dtype
     if "attn_weights[" in code:
-        return "last_token", uses_mode_flags
-    return "noop", uses_mode_flags
+        return "last_token", uses_mode_flags, dtype
+    return "noop", False, None
 
 
 class HolisticAttentionWrapper:
@@ -120,13 +125,9 @@ class HolisticAttentionWrapper:
 
         self._dump_kind = "noop"
         self._dump_mode_flags = False
+        self._dump_dtype: Optional[torch.dtype] = None
         if jit_args is not None:
-            self._dump_kind, self._dump_mode_flags = _dump_kind_from_jit_args(jit_args)
-            if self._dump_kind == "last_token" or self._dump_mode_flags:
-                raise NotImplementedError(
-                    "aspire_b200 implements the first_last_compact dump (the ASPIRE backend); "
-                    f"got dump kind {self._dump_kind!r} with mode flags={self._dump_mode_flags}"
-                )
+            self._dump_kind, self._dump_mode_flags, self._dump_dtype = _dump_kind_from_jit_args(jit_args)
         self._has_jit = jit_args is not None
 
         self._plan_info: Optional[_capi.AspirePlanInfo] = None
@@ -343,21 +344,35 @@ class HolisticAttentionWrapper:
                                 or tuple(lse.shape) != (q.shape[0], q.shape[1])):
             raise ValueError("lse must be a contiguous fp32 [tokens, num_qo_heads] tensor")
 
+        # Dump variants take run(q, kv, dump_buffer, [mode_flags,] num_heads,
+        # kv_stride): the struct's tensors, then its scalars
+        # (holistic_wrapper.py:411-416, base.py:468-473).
         dump = None
+        dump_flags = None
         dump_heads = 0
         dump_stride = 0
-        if self._has_jit and self._dump_kind == "first_last_compact":
-            if len(args) < 3:
-                raise ValueError("dump variant run(q, kv, dump_buffer, num_heads, kv_stride)")
+        if self._has_jit and self._dump_kind != "noop":
+            n_t = 2 if self._dump_mode_flags else 1
+            if len(args) < n_t + 2:
+                raise ValueError("dump variant run(q, kv, dump_buffer, " + ("mode_flags, " if n_t == 2 else "")
+                                 + "num_heads, kv_stride)")
             dump = args[0]
-            dump_heads = int(args[1])
-            dump_stride = int(args[2])
-            if dump.dtype != torch.float16 or not dump.is_contiguous():
-                raise ValueError("dump buffer must be a contiguous float16 tensor")
+            dump_flags = args[1] if n_t == 2 else None
+            dump_heads = int(args[n_t])
+            dump_stride = int(args[n_t + 1])
+            if dump.dtype not in (torch.float16, torch.float32) or not dump.is_contiguous():
+                raise ValueError("dump buffer must be a contiguous float16 or float32 tensor")
+            if self._dump_dtype is not None and dump.dtype != self._dump_dtype:
+                raise ValueError(f"dump buffer is {dump.dtype}, the dump variant writes {self._dump_dtype}")
             if dump_heads < self._num_qo_heads or dump_stride < self._plan_max_kv_len:
                 raise ValueError("dump buffer heads/stride smaller than the planned heads/kv_len")
-            if dump.numel() < self._plan_rows * dump_heads * 2 * dump_stride:
-                raise ValueError("dump buffer smaller than rows * num_heads * 2 * kv_stride")
+            slots = 2 if self._dump_kind == "first_last_compact" else 1
+            if dump.numel() < self._plan_rows * dump_heads * slots * dump_stride:
+                raise ValueError(f"dump buffer smaller than rows * num_heads * {slots} * kv_stride")
+            if dump_flags is not None and (dump_flags.dtype != torch.int32 or not dump_flags.is_contiguous()
+                                           or dump_flags.device != dump.device
+                                           or dump_flags.numel() < self._plan_rows):
+                raise ValueError("mode_flags must be a contiguous int32 tensor with one entry per row")
 
         sm_scale = self._sm_scale if self._sm_scale is not None else 1.0 / math.sqrt(q.shape[2])
         a = _capi.AspireAttnArgs()
@@ -386,6 +401,9 @@ class HolisticAttentionWrapper:
         a.dump = dump.data_ptr() if dump is not None else None
         a.dump_num_heads = dump_heads
         a.dump_kv_stride = dump_stride
+        a.dump_kind = _capi.DUMP_LAST_TOKEN if self._dump_kind == "last_token" else _capi.DUMP_FIRST_LAST
+        a.dump_dtype = _capi.DUMP_F32 if dump is not None and dump.dtype == torch.float32 else _capi.DUMP_F16
+        a.dump_flags = dump_flags.data_ptr() if dump_flags is not None else None
         a.sm_scale = float(sm_scale)
         a.num_qo_heads = self._num_qo_heads
         a.num_kv_heads = self._num_kv_heads
@@ -422,14 +440,31 @@ def wrapper_from_id(wrapper_id: int) -> HolisticAttentionWrapper:
     return _WRAPPER_REGISTRY[wrapper_id]
 
 
-def first_last_dump_jit_args(head_dim: int = 128) -> list:
-    """JIT-argument list equivalent to the reference's
-    ``build_holistic_dump_jit_args(dtype, head_dim, "first_last_compact")``
-    (aspire/attention/holistic_wrapper.py:401-434), for callers that do not
-    import the reference's builder.  Only its shape and the dump kind matter."""
+def dump_jit_args(dump_kind: str = "first_last_compact", head_dim: int = 128, use_mode_flags: bool = False,
+                  dump_buffer_dtype: torch.dtype = torch.float16) -> list:
+    """JIT-argument list with the layout of the reference's
+    ``build_holistic_dump_jit_args(dtype, head_dim, dump_kind, ...,
+    use_mode_flags, dump_buffer_dtype)`` (aspire/attention/holistic_wrapper.py:
+    401-434), for callers that do not import the reference's builder.  Only
+    the tensor names and types and the marker of the dump kind in the source
+    slot are read."""
+    if dump_kind not in ("noop", "last_token", "first_last_compact"):
+        raise ValueError(f"unknown dump_kind {dump_kind!r}")
+    attn_type = {torch.float16: "half", torch.float32: "float"}[dump_buffer_dtype]
+    names, types = ["attention_weights"], [attn_type]
+    if use_mode_flags and dump_kind != "noop":
+        names.append("mode_flags")
+        types.append("int32_t")
+    marker = {"noop": "noop", "last_token": "last_token: attn_weights[...] = logits",
+              "first_last_compact": "first_last_compact: qo_slot = (qo_idx == 0u) ? 0u : 1u"}[dump_kind]
     return [
-        "holistic_batch_dump_attention_weights_firstlastcompact", torch.bfloat16, torch.bfloat16,
-        torch.bfloat16, torch.int32, head_dim, head_dim, ["attention_weights"], ["half"],
-        ["num_heads", "jit_kv_stride"], ["int64_t", "int64_t"], "HolisticDumpAttentionWeightsFirstLastCompact",
-        "first_last_compact: qo_slot = (qo_idx == 0u) ? 0u : 1u",
+        "holistic_batch_dump_attention_weights_" + dump_kind.replace("_", ""), torch.bfloat16, torch.bfloat16,
+        torch.bfloat16, torch.int32, head_dim, head_dim, names, types,
+        ["num_heads", "jit_kv_stride"], ["int64_t", "int64_t"], "HolisticDumpAttentionWeights", marker,
     ]
+
+
+def first_last_dump_jit_args(head_dim: int = 128) -> list:
+    """``dump_jit_args("first_last_compact", head_dim)``: the ASPIRE backend's
+    fp16 first/last dump."""
+    return dump_jit_args("first_last_compact", head_dim)

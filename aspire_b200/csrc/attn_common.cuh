@@ -20,8 +20,11 @@ struct AttnParams {
   __nv_bfloat16* out;
   int64_t o_stride_n, o_stride_h;
   float* lse;                // optional
-  __half* dump;              // optional
+  void* dump;                // optional logit dump (dump_kind, dump_f32)
   int64_t dump_num_heads, dump_kv_stride;
+  int32_t dump_kind;         // ASPIRE_DUMP_FIRST_LAST or ASPIRE_DUMP_LAST_TOKEN
+  int32_t dump_f32;          // 1: fp32 elements holding the fp16-rounded logit
+  const int32_t* dump_flags; // optional per-row enable (row dumps iff flag != 0)
   float scale_log2;          // sm_scale * log2(e)
   int32_t num_qo_heads, num_kv_heads, group;
   int32_t q_box_tokens;      // tokens per query-tile TMA box (tcgen05 kernel, decode phase)
@@ -42,6 +45,37 @@ __device__ __forceinline__ int32_t row_page(const int32_t* kv_indices, int64_t p
   if (kv_indices) return __ldg(kv_indices + page_base + lp);
   return __ldg(mode_flags + row) == 0 ? __ldg(draft_table + row * draft_stride + lp)
                                       : __ldg(block_table + row * block_table_stride + lp);
+}
+
+// Logit dump of the chosen queries (raw q.k before scale and mask, rounded to
+// fp16), the LogitsTransform bodies of aspire/backends/jit_kernels.py:180-203:
+// first/last writes query 0 to slot 0 and query q_len-1 (q_len > 1) to slot 1
+// of [batch, heads, 2, stride]; last-token writes query q_len-1 (q_len >= 1)
+// to [batch, heads, stride].  With dump_flags a row writes only when its flag
+// is set.
+__device__ __forceinline__ bool dump_row_on(const AttnParams& p, int row) {
+  return p.dump != nullptr && (p.dump_flags == nullptr || p.dump_flags[row] != 0);
+}
+__device__ __forceinline__ bool dump_has_first(const AttnParams& p) { return p.dump_kind == ASPIRE_DUMP_FIRST_LAST; }
+__device__ __forceinline__ bool dump_has_last(const AttnParams& p, int q_len) {
+  return p.dump_kind == ASPIRE_DUMP_LAST_TOKEN || q_len > 1;
+}
+// Elements between consecutive heads of the dump.
+__device__ __forceinline__ int64_t dump_head_stride(const AttnParams& p) {
+  return p.dump_kind == ASPIRE_DUMP_LAST_TOKEN ? p.dump_kv_stride : 2 * p.dump_kv_stride;
+}
+// Element index of token 0 of (row, head) for the first (last = false) or the
+// last query.
+__device__ __forceinline__ int64_t dump_index(const AttnParams& p, int row, int64_t head, bool last) {
+  return (int64_t(row) * p.dump_num_heads + head) * dump_head_stride(p) +
+         (last && p.dump_kind == ASPIRE_DUMP_FIRST_LAST ? p.dump_kv_stride : 0);
+}
+__device__ __forceinline__ void dump_store(const AttnParams& p, int64_t idx, float logit) {
+  const __half h = __float2half_rn(logit);
+  if (p.dump_f32)
+    static_cast<float*>(p.dump)[idx] = __half2float(h);
+  else
+    static_cast<__half*>(p.dump)[idx] = h;
 }
 
 __device__ __forceinline__ float ex2(float x) {

@@ -14,9 +14,9 @@
 // prefill.cuh logits_mask):  bottom-right causal mask (query i of a row of
 // q_len sees KV positions < kv_len - q_len + i + 1), base-2 LSE of the
 // scaled logits, GQA kv_head = q_head / group.  With a dump buffer the raw
-// fp32 q.k (before scaling and masking) of query 0 -> slot 0 and of query
-// q_len-1 -> slot 1 is stored rounded to fp16, as the reference's
-// first_last_compact variant does (aspire/backends/jit_kernels.py:188-193).
+// fp32 q.k (before scaling and masking) of the dumped queries is stored
+// rounded to fp16 (dump_index / dump_store: first/last or last-token, as the
+// reference's variants do, aspire/backends/jit_kernels.py:180-193).
 #include "kernels.cuh"
 
 namespace aspire {
@@ -86,16 +86,16 @@ __global__ void __launch_bounds__(kThreads, kGatherCtasPerSm) aspire_attn_gather
     // Query rows of this item (raw bf16 -> fp32, 8 dims per lane).
     float qv[kQT][8];
     int lim[kQT];
-    bool slot0[kQT], slot1[kQT];
-    int qhead[kQT];
+    int64_t dump_at[kQT];  // dump element index of token 0 of row j, -1 when not dumped
+    const bool row_dumps = dump_row_on(p, it.row);
 #pragma unroll
     for (int j = 0; j < kQT; ++j) {
       int q_idx = 0, head = 0;
       if (j < nq) packed_row(p, it, it.pq_begin + j, q_idx, head);
-      qhead[j] = head;
       lim[j] = causal ? (it.kv_len - it.q_len + q_idx + 1) : it.kv_len;
-      slot0[j] = (j < nq) && q_idx == 0;
-      slot1[j] = (j < nq) && q_idx != 0 && q_idx + 1 == it.q_len;
+      const bool first = (j < nq) && row_dumps && dump_has_first(p) && q_idx == 0;
+      const bool last = (j < nq) && row_dumps && !first && dump_has_last(p, it.q_len) && q_idx + 1 == it.q_len;
+      dump_at[j] = (first || last) ? dump_index(p, it.row, head, last) : -1;
       if (j < nq && int64_t(it.q_start) + q_idx < p.q_rows) {
         const uint4 u = *reinterpret_cast<const uint4*>(
             p.q + int64_t(it.q_start + q_idx) * p.q_stride_n + int64_t(head) * p.q_stride_h +
@@ -197,10 +197,8 @@ __global__ void __launch_bounds__(kThreads, kGatherCtasPerSm) aspire_attn_gather
         if (p.dump != nullptr && in_chunk && tok < p.dump_kv_stride) {
 #pragma unroll
           for (int j = 0; j < kQT; ++j) {
-            if (l16 == j && (slot0[j] || slot1[j])) {
-              const int64_t idx = (int64_t(it.row) * p.dump_num_heads + qhead[j]) * 2 * p.dump_kv_stride +
-                                  (slot0[j] ? 0 : p.dump_kv_stride) + tok;
-              p.dump[idx] = __float2half_rn(s[j]);
+            if (l16 == j && dump_at[j] >= 0) {
+              dump_store(p, dump_at[j] + tok, s[j]);
             }
           }
         }

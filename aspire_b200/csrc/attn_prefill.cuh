@@ -374,15 +374,16 @@ __device__ bool consume_item(const AttnParams& p, Sh& sm, const WorkItem& it, bo
   // causal mask); padding rows see none.
   int vis_end = it.tok_begin;
   if (valid) vis_end = causal ? min(it.tok_end, it.kv_len - it.q_len + q_idx + 1) : it.tok_end;
-  // First/last-query logit dump (raw q.k before scale and mask, fp16): query 0
-  // to slot 0, query q_len-1 (q_len > 1) to slot 1.
-  __half* dump_row = nullptr;
-  if (p.dump != nullptr && valid && (q_idx == 0 || q_idx == it.q_len - 1)) {
-    dump_row = p.dump + (int64_t(it.row) * p.dump_num_heads + head) * 2 * p.dump_kv_stride;
-    if (q_idx != 0) dump_row += p.dump_kv_stride;
+  // Logit dump (raw q.k before scale and mask, dump_index): query 0 to the
+  // first slot, query q_len-1 to the last one, as the dump kind has them.
+  int64_t dump_at = -1;
+  if (valid && dump_row_on(p, it.row)) {
+    const bool first = dump_has_first(p) && q_idx == 0;
+    const bool last = !first && dump_has_last(p, it.q_len) && q_idx == it.q_len - 1;
+    if (first || last) dump_at = dump_index(p, it.row, head, last);
   }
   const int dump_end = p.dump_kv_stride < it.tok_end ? int(p.dump_kv_stride) : it.tok_end;
-  const bool warp_dumps = __any_sync(0xffffffffu, dump_row != nullptr);
+  const bool warp_dumps = __any_sync(0xffffffffu, dump_at >= 0);
   const float scale = p.scale_log2;
   const uint64_t scale2 = f2_pack(scale, scale);
   const uint32_t o_addr = tmem_lane + col_o(h);
@@ -400,10 +401,10 @@ __device__ bool consume_item(const AttnParams& p, Sh& sm, const WorkItem& it, bo
     ptx::tmem_ld32(s_addr, s);
     ptx::tmem_ld32(s_addr + 32, s + 32);
     ptx::tmem_wait_ld();
-    if (warp_dumps && dump_row != nullptr) {
+    if (warp_dumps && dump_at >= 0) {
 #pragma unroll
       for (int c = 0; c < kSub; ++c)
-        if (sub0 + c < dump_end) dump_row[sub0 + c] = __float2half_rn(s[c]);
+        if (sub0 + c < dump_end) dump_store(p, dump_at + sub0 + c, s[c]);
     }
     const int nvis = vis_end - sub0;
     if (nvis < kSub) {

@@ -47,7 +47,7 @@
 //
 // Semantics are those of the gather kernel (FlashInfer's persistent paged
 // attention as ASPIRE drives it): bottom-right causal mask, base-2 LSE of the
-// scaled logits, fp16 first/last logit dump of the raw q.k.
+// scaled logits, logit dump of the raw q.k (first/last or last-token).
 #include <cuda.h>
 
 #include "attn_prefill.cuh"
@@ -354,12 +354,14 @@ __device__ __forceinline__ void tmem_load_cols(uint32_t taddr, float* v) {
 }
 
 // ------------------------------------------------------------------ softmax / epilogue
-// Writes dump columns [lo, hi) of one token (raw logits, fp16); the first 8
+// Writes dump columns [lo, hi) of one token (raw logits, dump_store); column
+// c goes to element base + (c - base_col) * col_stride + tok.  The first 8
 // are in dv, further pieces are read from the S tile at s_addr.  Kept out of
 // line: the three column-count instantiations of the consumer loop share it,
 // which keeps their hot loops small.
-__device__ __noinline__ void dump_columns(int lo, int hi, __half* base, int base_col, int64_t col_stride, int tok,
-                                          bool store, uint32_t s_addr, const float* dv_in) {
+__device__ __noinline__ void dump_columns(const AttnParams& p, int lo, int hi, int64_t base, int base_col,
+                                          int64_t col_stride, int tok, bool store, uint32_t s_addr,
+                                          const float* dv_in) {
   float dv[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) dv[i] = dv_in[i];
@@ -369,10 +371,10 @@ __device__ __noinline__ void dump_columns(int lo, int hi, __half* base, int base
       ptx::tmem_wait_ld();
     }
     if (store) {
-      __half* dst = base + int64_t(c - base_col) * col_stride + tok;
+      const int64_t dst = base + int64_t(c - base_col) * col_stride + tok;
 #pragma unroll
       for (int i = 0; i < 8; ++i)
-        if (c + i < hi) dst[int64_t(i) * col_stride] = __float2half_rn(dv[i]);
+        if (c + i < hi) dump_store(p, dst + int64_t(i) * col_stride, dv[i]);
     }
   }
 }
@@ -397,27 +399,27 @@ __device__ bool consume_item(const AttnParams& p, TcShared& sm, const WorkItem& 
   int* grew = sm.grew[wg];
 
   const int q_idx0 = it.pq_begin / group;
-  // First/last-query dump: the item's columns of query 0 (slot 0) and of query
-  // q_len-1 (slot 1, only when q_len > 1) are two runs of at most `group`
-  // consecutive S columns; each tile reads this group's part of those runs.
+  // Logit dump: the item's columns of query 0 (first slot) and of query
+  // q_len-1 (last slot) are two runs of at most `group` consecutive S
+  // columns; each tile reads this group's part of those runs.  Which runs
+  // exist depends on the dump kind and the row's flag (dump_index).
   int d0_lo = 0, d0_hi = 0, d1_lo = 0, d1_hi = 0, dump_c1 = 0;
-  __half* dump_base0 = nullptr;
-  __half* dump_base1 = nullptr;
-  const int64_t dump_col_stride = 2 * p.dump_kv_stride;  // between heads
-  if (kDump) {
+  int64_t dump_base0 = 0, dump_base1 = 0;
+  const int64_t dump_col_stride = dump_head_stride(p);  // between heads
+  if (kDump && dump_row_on(p, it.row)) {
     const int last_lo = (it.q_len - 1) * group;  // first packed row of the last query
-    const int64_t head0 = int64_t(it.row) * p.dump_num_heads + int64_t(it.kv_head) * group;
-    if (it.pq_begin < group) {
+    const int64_t head0 = int64_t(it.kv_head) * group;
+    if (dump_has_first(p) && it.pq_begin < group) {
       const int n0 = min(group - it.pq_begin, nrows);
       d0_lo = c0;
       d0_hi = min(n0, c0 + NH);
-      dump_base0 = p.dump + (head0 + it.pq_begin) * dump_col_stride;
+      dump_base0 = dump_index(p, it.row, head0 + it.pq_begin, false);
     }
-    if (it.q_len > 1 && last_lo < it.pq_end) {
+    if (dump_has_last(p, it.q_len) && last_lo < it.pq_end) {
       dump_c1 = max(last_lo - it.pq_begin, 0);
       d1_lo = max(dump_c1, c0);
       d1_hi = min(nrows, c0 + NH);
-      dump_base1 = p.dump + (head0 + it.pq_begin + dump_c1 - last_lo) * dump_col_stride + p.dump_kv_stride;
+      dump_base1 = dump_index(p, it.row, head0 + it.pq_begin + dump_c1 - last_lo, true);
     }
   }
   const bool dumping = kDump && (d0_lo < d0_hi || d1_lo < d1_hi);
@@ -478,9 +480,9 @@ __device__ bool consume_item(const AttnParams& p, TcShared& sm, const WorkItem& 
       ptx::tmem_wait_ld();
       const bool store = in_chunk && tok < p.dump_kv_stride;
       if (d0_lo < d0_hi)
-        dump_columns(d0_lo, d0_hi, dump_base0, 0, dump_col_stride, tok, store, tmem_lane + col_s(b), dv0);
+        dump_columns(p, d0_lo, d0_hi, dump_base0, 0, dump_col_stride, tok, store, tmem_lane + col_s(b), dv0);
       if (d1_lo < d1_hi)
-        dump_columns(d1_lo, d1_hi, dump_base1, dump_c1, dump_col_stride, tok, store, tmem_lane + col_s(b), dv1);
+        dump_columns(p, d1_lo, d1_hi, dump_base1, dump_c1, dump_col_stride, tok, store, tmem_lane + col_s(b), dv1);
     } else {
       load_s(sv);
     }
@@ -676,9 +678,12 @@ __device__ void consume_items(const AttnParams& p, TcShared& sm, bool causal, in
       continue;
     }
     const int N = item_columns(nrows, uniform);
-    // Items whose columns include dump rows (query 0 or the last query, with a
-    // dump buffer) take the instantiation that carries the dump path.
-    const bool dump_item = p.dump != nullptr && (it.pq_begin < p.group || (it.q_len > 1 && (it.q_len - 1) * p.group < it.pq_end));
+    // Items whose columns include dumped rows (query 0 or the last query, as
+    // the dump kind and the row's flag have it) take the instantiation that
+    // carries the dump path.
+    const bool dump_item = dump_row_on(p, it.row) &&
+                           ((dump_has_first(p) && it.pq_begin < p.group) ||
+                            (dump_has_last(p, it.q_len) && (it.q_len - 1) * p.group < it.pq_end));
     bool ok;
     if (dump_item) {
       if (N == 16)

@@ -196,6 +196,12 @@ int check_attention_args(const AspireAttnArgs* a, const AspirePlanInfo* plan, co
     return set_error(ASPIRE_ERR_INVALID, w + ": q strides must be multiples of 8 elements");
   if (a->dump && (a->dump_num_heads < a->num_qo_heads || a->dump_kv_stride <= 0))
     return set_error(ASPIRE_ERR_INVALID, w + ": bad dump geometry");
+  if (a->dump_kind != ASPIRE_DUMP_FIRST_LAST && a->dump_kind != ASPIRE_DUMP_LAST_TOKEN)
+    return set_error(ASPIRE_ERR_INVALID, w + ": dump_kind must be ASPIRE_DUMP_FIRST_LAST or ASPIRE_DUMP_LAST_TOKEN");
+  if (a->dump_dtype != ASPIRE_DUMP_F16 && a->dump_dtype != ASPIRE_DUMP_F32)
+    return set_error(ASPIRE_ERR_INVALID, w + ": dump_dtype must be ASPIRE_DUMP_F16 or ASPIRE_DUMP_F32");
+  if (a->dump && (reinterpret_cast<uintptr_t>(a->dump) & (a->dump_dtype == ASPIRE_DUMP_F32 ? 3 : 1)))
+    return set_error(ASPIRE_ERR_INVALID, w + ": dump buffer not aligned to its element type");
   if (a->q_rows <= 0 || a->q_rows > INT32_MAX)
     return set_error(ASPIRE_ERR_INVALID, w + ": q_rows (rows of q) must be set");
   const int group = a->num_qo_heads / a->num_kv_heads;
@@ -360,9 +366,12 @@ int aspire_mixed_attention(const AspireAttnArgs* a, const AspirePlanInfo* plan, 
   p.o_stride_n = a->o_stride_n;
   p.o_stride_h = a->o_stride_h;
   p.lse = a->lse;
-  p.dump = static_cast<__half*>(a->dump);
+  p.dump = a->dump;
   p.dump_num_heads = a->dump_num_heads;
   p.dump_kv_stride = a->dump_kv_stride;
+  p.dump_kind = a->dump_kind;
+  p.dump_f32 = a->dump_dtype == ASPIRE_DUMP_F32 ? 1 : 0;
+  p.dump_flags = a->dump_flags;
   const float sm_scale = a->sm_scale > 0.f ? a->sm_scale : 1.0f / std::sqrt(float(kHeadDim));
   p.scale_log2 = sm_scale * 1.44269504088896340736f;
   p.num_qo_heads = a->num_qo_heads;
@@ -597,8 +606,16 @@ int aspire_select_pages(const AspireSelectArgs* a, void* stream) {
     return set_error(ASPIRE_ERR_INVALID, "aspire_select_pages: max_seq_len exceeds kv_stride");
   if (!a->scores_in && int64_t(a->pages_per_slot) * kPageSize < a->max_seq_len)
     return set_error(ASPIRE_ERR_INVALID, "aspire_select_pages: pages_per_slot*16 < max_seq_len");
+  if (a->dump_kind != ASPIRE_DUMP_FIRST_LAST && a->dump_kind != ASPIRE_DUMP_LAST_TOKEN)
+    return set_error(ASPIRE_ERR_INVALID, "aspire_select_pages: bad dump_kind");
+  if (a->dump_dtype != ASPIRE_DUMP_F16 && a->dump_dtype != ASPIRE_DUMP_F32)
+    return set_error(ASPIRE_ERR_INVALID, "aspire_select_pages: bad dump_dtype");
+  if (a->dump && (reinterpret_cast<uintptr_t>(a->dump) & (a->dump_dtype == ASPIRE_DUMP_F32 ? 3 : 1)))
+    return set_error(ASPIRE_ERR_INVALID, "aspire_select_pages: dump buffer not aligned to its element type");
   SelectParams p;
-  p.dump = reinterpret_cast<const __half*>(a->dump);
+  p.dump = a->dump;
+  p.dump_slots = a->dump_kind == ASPIRE_DUMP_LAST_TOKEN ? 1 : 2;
+  p.dump_f32 = a->dump_dtype == ASPIRE_DUMP_F32 ? 1 : 0;
   p.kv_stride = a->kv_stride;
   p.max_seq_len = a->max_seq_len;
   p.lse = a->lse;

@@ -75,7 +75,9 @@ constexpr int kDevPlanThreads = 1024;
 __global__ void aspire_plan_device_kernel(DevPlanParams p);
 
 struct SelectParams {
-  const __half* dump;
+  const void* dump;  // fp16 or fp32 (dump_f32) [rows, num_heads, dump_slots, kv_stride]
+  int32_t dump_slots;  // 2: first/last dump (first + last query), 1: last-token dump
+  int32_t dump_f32;
   int64_t kv_stride, max_seq_len;
   const float* lse;
   int64_t lse_rows;

@@ -1,13 +1,16 @@
 // Refresh-layer page scoring + block radix top-k page re-selection.
 //
-// Phase 1 (its own launch over rows x page splits) turns the first/last logit
-// dump of the refresh layer into fp32 page scores, restating
+// Phase 1 (its own launch over rows x page splits) turns the logit dump of
+// the refresh layer into fp32 page scores, restating
 // PageSelectorFirstLastAvg._select_first_last_impl
-// (aspire/backends/page_selector.py:163-181):
+// (aspire/backends/page_selector.py:163-181) for a first/last dump:
 //   norm  = float(half(float(logit) * sm_scale*log2e)) - lse      (NaN -> -inf)
 //   tok   = max_h exp2(norm[slot 0]) + max_h exp2(norm[slot 1])
 //   score = sum of the 16 token scores of the page + (-page * 1e-7)
-// with tokens past max_seq_len counting as zero.  One CTA per request row
+// and PageSelector._select_impl (:110-130, select :140-146) for a last-token
+// dump (one slot, normalised by the last query's LSE: tok = max_h
+// exp2(norm)); with an fp32 dump the product stays fp32.  Tokens past
+// max_seq_len count as zero.  One CTA per request row
 // then runs phase 2, which restates
 // _finalize_scores (page_selector.py:79-108) and compute_valid_counts
 // (:52-62): the last L valid pages are forced to +inf, pages past num_pages
@@ -47,10 +50,95 @@ __device__ __forceinline__ int valid_count(const SelectParams& p, int np) {
   return min(max(target, lo), hi);
 }
 
+// The 16 raw logits of one page of one (head, slot) dump row, as fp32;
+// positions at or past max_seq_len read -inf.
+__device__ __forceinline__ void load_page_logits(const __half* src, bool vec, int64_t t0, int64_t max_seq_len,
+                                                 float* v) {
+  __half2 h[kPageSize / 2];
+  if (vec) {
+    *reinterpret_cast<uint4*>(h) = __ldcs(reinterpret_cast<const uint4*>(src));
+    *reinterpret_cast<uint4*>(h + 4) = __ldcs(reinterpret_cast<const uint4*>(src) + 1);
+  } else {
+#pragma unroll
+    for (int i = 0; i < kPageSize / 2; ++i) {
+      const __half lo = (t0 + 2 * i < max_seq_len) ? src[2 * i] : __float2half_rn(-INFINITY);
+      const __half hi = (t0 + 2 * i + 1 < max_seq_len) ? src[2 * i + 1] : __float2half_rn(-INFINITY);
+      h[i] = __halves2half2(lo, hi);
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < kPageSize / 2; ++i) {
+    const float2 f = __half22float2(h[i]);
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+__device__ __forceinline__ void load_page_logits(const float* src, bool vec, int64_t t0, int64_t max_seq_len,
+                                                 float* v) {
+  if (vec) {
+#pragma unroll
+    for (int i = 0; i < kPageSize / 4; ++i) *reinterpret_cast<float4*>(v + 4 * i) = __ldcs(reinterpret_cast<const float4*>(src) + i);
+  } else {
+#pragma unroll
+    for (int i = 0; i < kPageSize; ++i) v[i] = (t0 + i < max_seq_len) ? src[i] : -INFINITY;
+  }
+}
+// logit * sm_scale*log2(e) in the dump's own type: an fp16 tensor times a
+// scalar is computed in fp32 and rounded back to fp16; an fp32 one stays fp32.
+__device__ __forceinline__ float scaled_logit(float f, float scale, const __half*) {
+  return __half2float(__float2half_rn(f * scale));
+}
+__device__ __forceinline__ float scaled_logit(float f, float scale, const float*) { return f * scale; }
+
+// Token scores of page pg of one row: tok[t] = sum over the dump's slots of
+// max_h exp2(norm), norm = scaled_logit - lse (NaN -> -inf); zero past
+// max_seq_len.  exp2 is monotonic, so the max over heads is taken on the
+// normalised logits and exponentiated once per (token, slot).
+template <typename T, int kSlots>
+__device__ __forceinline__ void page_token_scores(const SelectParams& p, const float (*lse_s)[kMaxSelHeads],
+                                                  int src_row, int pg, float* tok) {
+#pragma unroll
+  for (int i = 0; i < kPageSize; ++i) tok[i] = 0.f;
+  const int64_t t0 = int64_t(pg) * kPageSize;
+  if (t0 >= p.max_seq_len) return;
+  float mx[kSlots][kPageSize];
+#pragma unroll
+  for (int s = 0; s < kSlots; ++s)
+#pragma unroll
+    for (int i = 0; i < kPageSize; ++i) mx[s][i] = -INFINITY;
+  const bool full = t0 + kPageSize <= p.max_seq_len;
+  const T* row = static_cast<const T*>(p.dump) + int64_t(src_row) * p.num_heads * kSlots * p.kv_stride + t0;
+  const bool vec =
+      full && ((reinterpret_cast<uintptr_t>(row) | uintptr_t(p.kv_stride * int64_t(sizeof(T)))) & 15) == 0;
+  for (int h = 0; h < p.num_heads; ++h) {
+#pragma unroll
+    for (int s = 0; s < kSlots; ++s) {
+      const T* src = row + (int64_t(h) * kSlots + s) * p.kv_stride;
+      // Slot 0 of a first/last dump is normalised by the first query's LSE;
+      // the last-query slot by the last query's.
+      const float ls = lse_s[kSlots == 2 ? s : 1][h];
+      float v[kPageSize];
+      load_page_logits(src, vec, t0, p.max_seq_len, v);
+#pragma unroll
+      for (int i = 0; i < kPageSize; ++i) {
+        float n = scaled_logit(v[i], p.scale_log2, src) - ls;
+        if (isnan(n)) n = -INFINITY;
+        mx[s][i] = fmaxf(mx[s][i], n);
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < kPageSize; ++i) {
+    float t = 0.f;
+#pragma unroll
+    for (int s = 0; s < kSlots; ++s) t = (s == 0) ? exp2f(mx[0][i]) : t + exp2f(mx[s][i]);
+    tok[i] = (t0 + i < p.max_seq_len) ? t : 0.f;
+  }
+}
+
 // Phase 1 on its own grid (rows x page splits), one page per thread: the
 // scores go to p.scores_out, which the selection launch then reads as its
-// scores_in.  exp2 is monotonic, so the max over heads is taken on the
-// normalised logits and exponentiated once per (token, slot).
+// scores_in.
 __global__ void __launch_bounds__(kScoreThreads) aspire_page_scores_kernel(SelectParams p) {
   pdl_begin();
   __shared__ float lse_s[2][kMaxSelHeads];
@@ -71,51 +159,16 @@ __global__ void __launch_bounds__(kScoreThreads) aspire_page_scores_kernel(Selec
   const int pg = blockIdx.y * blockDim.x + tid;
   if (pg >= pps) return;
   float tok[kPageSize];
-#pragma unroll
-  for (int i = 0; i < kPageSize; ++i) tok[i] = 0.f;
-  const int64_t t0 = int64_t(pg) * kPageSize;
-  if (t0 < p.max_seq_len) {
-    float mx[2][kPageSize];
-#pragma unroll
-    for (int s = 0; s < 2; ++s)
-#pragma unroll
-      for (int i = 0; i < kPageSize; ++i) mx[s][i] = -INFINITY;
-    const bool full = t0 + kPageSize <= p.max_seq_len;
-    const __half* row = p.dump + int64_t(src_row) * p.num_heads * 2 * p.kv_stride + t0;
-    const bool vec = full && ((reinterpret_cast<uintptr_t>(row) | uintptr_t(p.kv_stride * 2)) & 15) == 0;
-    for (int h = 0; h < p.num_heads; ++h) {
-#pragma unroll
-      for (int s = 0; s < 2; ++s) {
-        const __half* src = row + (int64_t(h) * 2 + s) * p.kv_stride;
-        const float ls = lse_s[s][h];
-        __half2 vals[kPageSize / 2];
-        if (vec) {
-          *reinterpret_cast<uint4*>(vals) = __ldcs(reinterpret_cast<const uint4*>(src));
-          *reinterpret_cast<uint4*>(vals + 4) = __ldcs(reinterpret_cast<const uint4*>(src) + 1);
-        } else {
-#pragma unroll
-          for (int i = 0; i < kPageSize / 2; ++i) {
-            const __half lo = (t0 + 2 * i < p.max_seq_len) ? src[2 * i] : __float2half_rn(-INFINITY);
-            const __half hi = (t0 + 2 * i + 1 < p.max_seq_len) ? src[2 * i + 1] : __float2half_rn(-INFINITY);
-            vals[i] = __halves2half2(lo, hi);
-          }
-        }
-#pragma unroll
-        for (int i = 0; i < kPageSize / 2; ++i) {
-          // fp16 * scalar is computed in fp32 and rounded back to fp16.
-          const float2 f = __half22float2(vals[i]);
-          const float2 r = __half22float2(__floats2half2_rn(f.x * p.scale_log2, f.y * p.scale_log2));
-          float n0 = r.x - ls, n1 = r.y - ls;
-          if (isnan(n0)) n0 = -INFINITY;
-          if (isnan(n1)) n1 = -INFINITY;
-          mx[s][2 * i] = fmaxf(mx[s][2 * i], n0);
-          mx[s][2 * i + 1] = fmaxf(mx[s][2 * i + 1], n1);
-        }
-      }
-    }
-#pragma unroll
-    for (int i = 0; i < kPageSize; ++i)
-      tok[i] = (t0 + i < p.max_seq_len) ? (exp2f(mx[0][i]) + exp2f(mx[1][i])) : 0.f;
+  if (p.dump_f32) {
+    if (p.dump_slots == 1)
+      page_token_scores<float, 1>(p, lse_s, src_row, pg, tok);
+    else
+      page_token_scores<float, 2>(p, lse_s, src_row, pg, tok);
+  } else {
+    if (p.dump_slots == 1)
+      page_token_scores<__half, 1>(p, lse_s, src_row, pg, tok);
+    else
+      page_token_scores<__half, 2>(p, lse_s, src_row, pg, tok);
   }
   // Pairwise sum of the 16 token scores.
 #pragma unroll

@@ -1,9 +1,14 @@
-"""Page selection on the GPU: drop-in for ``PageSelectorFirstLastAvg``.
+"""Page selection on the GPU: drop-in for ``PageSelector`` and
+``PageSelectorFirstLastAvg``.
 
 Same constructor and ``compute_valid_counts`` / ``select`` /
-``select_subset`` / ``select_from_compact_first_last`` surface as
-``aspire/backends/page_selector.py:9-233``; scoring and top-k run as one
-fused kernel per call (``aspire_select_pages``) instead of ~20 torch ops.
+``select_subset`` surface as ``aspire/backends/page_selector.py:7-233``
+(plus ``select_from_compact_first_last`` and
+``select_layers_from_compact_first_last`` on the first/last class); scoring
+and top-k run as two kernels per call (``aspire_select_pages``) instead of
+~20 torch ops.  ``PageSelector`` scores pages from the last-token dump of
+``LMBackendBase`` (one slot per head), ``PageSelectorFirstLastAvg`` from the
+first/last dump of the ASPIRE backend; either dump may be fp16 or fp32.
 
 ``select`` returns ``(selected[B, k] int32, valid_counts[B] int32)`` with the
 reference's layout: the valid prefix of each row holds the selected
@@ -25,8 +30,14 @@ import torch
 from . import _capi
 
 
-class PageSelectorFirstLastAvg:
-    """First/last verify-token page selector backed by libaspire_b200."""
+class PageSelector:
+    """Last verify-token page selector backed by libaspire_b200
+    (``PageSelector``, aspire/backends/page_selector.py:7-158): a page's
+    score is the sum over its tokens of exp2(max over heads of
+    logit * sm_scale * log2(e) - LSE of the row's last query)."""
+
+    _dump_kind = _capi.DUMP_LAST_TOKEN
+    _dump_slots = 1
 
     def __init__(self, max_batch_size, pages_per_slot, subset_cache_size, L, n_heads, page_size,
                  max_seq_length, device, bsz, dec_len, head_dim=128, kv_stride=None,
@@ -66,7 +77,8 @@ class PageSelectorFirstLastAvg:
         return torch.clamp(target, lo, hi)
 
     def _launch(self, *, dump, lse, qo_indptr, row_ids, scores_in, num_pages, block_table, batch,
-                table_out, table_width, counts_out, scores_out=None, status=None, order_by_page=False):
+                table_out, table_width, counts_out, scores_out=None, status=None, order_by_page=False,
+                kv_stride=None):
         def ptr(t):
             return t.data_ptr() if t is not None else None
 
@@ -79,19 +91,22 @@ class PageSelectorFirstLastAvg:
         if block_table.shape[0] < batch or num_pages.shape[0] < batch or table_out.shape[0] < batch \
                 or counts_out.shape[0] < batch:
             raise ValueError("block_table / num_pages / outputs have fewer rows than the batch")
+        stride = self._kv_stride if kv_stride is None else int(kv_stride)
         if dump is not None:
-            if dump.dtype != torch.float16 or not dump.is_contiguous():
-                raise ValueError("dump buffer must be a contiguous float16 tensor")
+            if dump.dtype not in (torch.float16, torch.float32) or not dump.is_contiguous():
+                raise ValueError("dump buffer must be a contiguous float16 or float32 tensor")
             rows = int(row_ids.max().item()) + 1 if row_ids is not None else batch
-            if dump.numel() < rows * self.n_heads * 2 * self._kv_stride:
-                raise ValueError("dump buffer smaller than rows * n_heads * 2 * kv_stride")
+            if dump.numel() < rows * self.n_heads * self._dump_slots * stride:
+                raise ValueError(f"dump buffer smaller than rows * n_heads * {self._dump_slots} * kv_stride")
             if lse is None or lse.dtype != torch.float32 or not lse.is_contiguous() or lse.shape[1] != self.n_heads:
                 raise ValueError("lse must be a contiguous fp32 [tokens, n_heads] tensor")
             if qo_indptr.shape[0] < rows + 1:
                 raise ValueError("qo_indptr needs rows + 1 entries")
         a = _capi.AspireSelectArgs()
         a.dump = ptr(dump)
-        a.kv_stride = self._kv_stride
+        a.dump_kind = self._dump_kind
+        a.dump_dtype = _capi.DUMP_F32 if dump is not None and dump.dtype == torch.float32 else _capi.DUMP_F16
+        a.kv_stride = stride
         a.max_seq_len = self.max_seq_length
         a.lse = ptr(lse)
         a.lse_rows = lse.shape[0] if lse is not None else 0
@@ -131,7 +146,8 @@ class PageSelectorFirstLastAvg:
     # ------------------------------------------------------------------ API
     def select(self, attention_weights_buffer, lse_buffer, num_pages, block_table, qo_indptr,
                scores_out: Optional[torch.Tensor] = None) -> Tuple[torch.Tensor, torch.Tensor]:
-        """Whole-batch selection (``page_selector.py:206-214``)."""
+        """Whole-batch selection (``page_selector.py:140-146``; first/last:
+        ``:206-214``)."""
         B = self._bsz
         sel = self._selected_buf[:B]
         counts = self._valid_counts_buf[:B]
@@ -154,7 +170,7 @@ class PageSelectorFirstLastAvg:
 
     def select_subset(self, slot_ids, attention_weights_buffer, lse_buffer, num_pages, block_table,
                       qo_indptr) -> Tuple[torch.Tensor, torch.Tensor]:
-        """Selection for a subset of slots (``page_selector.py:216-233``)."""
+        """Selection for a subset of slots (``page_selector.py:148-158``; first/last: ``:216-233``)."""
         if slot_ids.numel() == 0:
             empty = block_table.new_empty((0, self.subset_cache_size), dtype=torch.int32)
             return empty, torch.zeros(0, dtype=torch.int32, device=self.device)
@@ -220,3 +236,55 @@ class PageSelectorFirstLastAvg:
         self._launch(dump=None, lse=None, qo_indptr=None, row_ids=None, scores_in=scores,
                      num_pages=self._contig_i32(num_pages), block_table=self._contig_i32(block_table),
                      batch=n, table_out=table, table_width=table.shape[1], counts_out=count_buffer)
+
+
+class PageSelectorFirstLastAvg(PageSelector):
+    """First/last verify-token page selector backed by libaspire_b200
+    (``PageSelectorFirstLastAvg``, aspire/backends/page_selector.py:160-233):
+    a token's score is the sum over the two dump slots of exp2(max over heads
+    of logit * sm_scale * log2(e) - LSE of the slot's query)."""
+
+    _dump_kind = _capi.DUMP_FIRST_LAST
+    _dump_slots = 2
+
+    def _compact_launch(self, logits, first_lse, last_lse, num_pages, block_table):
+        """Selection from an explicit [rows, n_heads, 2, max_seq_length] logit
+        view (a narrowing of a [rows, n_heads, 2, kv_stride] buffer) and the
+        first / last query LSE of each row [rows, n_heads]: the LSE rows are
+        interleaved so that the kernel's (first, last) query of row b are rows
+        2b and 2b + 1."""
+        n = logits.shape[0]
+        if logits.dim() != 4 or logits.shape[1] != self.n_heads or logits.shape[2] != 2:
+            raise ValueError("logits must be [rows, n_heads, 2, seq_len]")
+        s = logits.stride(2)
+        if logits.stride(3) != 1 or logits.stride(1) != 2 * s or logits.stride(0) != self.n_heads * 2 * s \
+                or logits.shape[3] != self.max_seq_length or s < self.max_seq_length:
+            raise ValueError("logits must be a [rows, n_heads, 2, max_seq_length] view of a contiguous "
+                             "[rows, n_heads, 2, kv_stride] buffer")
+        base = logits.as_strided((n * self.n_heads * 2 * s,), (1,))
+        lse = torch.stack([first_lse.float(), last_lse.float()], dim=1).reshape(2 * n, self.n_heads).contiguous()
+        qo = torch.arange(0, 2 * n + 1, 2, dtype=torch.int32, device=self.device)
+        sel = torch.zeros(n, self.subset_cache_size, dtype=torch.int32, device=self.device)
+        counts = torch.zeros(n, dtype=torch.int32, device=self.device)
+        self._launch(dump=base, lse=lse, qo_indptr=qo, row_ids=None, scores_in=None,
+                     num_pages=self._contig_i32(num_pages), block_table=self._contig_i32(block_table), batch=n,
+                     table_out=sel, table_width=self.subset_cache_size, counts_out=counts, kv_stride=s)
+        return sel, counts
+
+    def select_from_compact_first_last(self, logits, first_lse, last_lse, num_pages, block_table):
+        """``page_selector.py:183-184``: logits [B, n_heads, 2, seq_len],
+        first_lse / last_lse [B, n_heads]."""
+        return self._compact_launch(logits, first_lse, last_lse, num_pages, block_table)
+
+    def select_layers_from_compact_first_last(self, logits, first_lse, last_lse, num_pages, block_table):
+        """``page_selector.py:186-204``: logits [n_layers, B, n_heads, 2,
+        kv_stride], LSE [n_layers, B, n_heads]; returns
+        (selected [n_layers, B, k], valid_counts [B])."""
+        n_layers, batch = logits.shape[:2]
+        flat = logits.reshape(n_layers * batch, self.n_heads, 2, logits.shape[-1])
+        if flat.shape[-1] != self.max_seq_length:
+            flat = flat[..., :self.max_seq_length]
+        sel, counts = self._compact_launch(flat, first_lse.reshape(n_layers * batch, self.n_heads),
+                                           last_lse.reshape(n_layers * batch, self.n_heads),
+                                           num_pages.repeat(n_layers), block_table.repeat(n_layers, 1))
+        return sel.view(n_layers, batch, self.subset_cache_size), counts[:batch]

@@ -21,7 +21,10 @@
  *            (index 0 of dim 1 = K, 1 = V; "NHD" paged layout)
  *   out      bf16 [tokens, num_qo_heads, 128], strides given
  *   lse      fp32 [tokens, num_qo_heads], base-2 log-sum-exp of the scaled logits
- *   dump     fp16 [batch, dump_num_heads, 2, dump_kv_stride] first/last logits
+ *   dump     raw q.k logits of chosen queries (fp16, or fp32 holding the
+ *            fp16-rounded value): [batch, dump_num_heads, 2, dump_kv_stride]
+ *            first/last (ASPIRE_DUMP_FIRST_LAST) or [batch, dump_num_heads,
+ *            dump_kv_stride] last query only (ASPIRE_DUMP_LAST_TOKEN)
  *
  * Only page_size 16 and head_dim 128 are supported (every ASPIRE config).
  */
@@ -41,7 +44,7 @@
 extern "C" {
 #endif
 
-#define ASPIRE_B200_ABI_VERSION 4
+#define ASPIRE_B200_ABI_VERSION 5
 
 #define ASPIRE_OK 0
 #define ASPIRE_ERR_INVALID (-1)  /* bad argument (shape, size, alignment)       */
@@ -55,6 +58,15 @@ extern "C" {
 #define ASPIRE_STATUS_BAD_ROW 4u   /* attention row past q_rows, or selection
                                       row/argument out of range               */
 #define ASPIRE_STATUS_TIMEOUT 8u   /* a bounded device wait expired; the CTA stopped */
+
+/* Logit-dump variants (AspireAttnArgs.dump_kind, AspireSelectArgs.dump_kind),
+ * the dump kinds of aspire/backends/jit_kernels.py:180-193: */
+#define ASPIRE_DUMP_FIRST_LAST 0  /* "first_last_compact": query 0 -> slot 0, query
+                                     q_len-1 (q_len > 1) -> slot 1 (ASPIRE backend) */
+#define ASPIRE_DUMP_LAST_TOKEN 1  /* "last_token": query q_len-1 only, one slot
+                                     (LMBackendBase, base.py:208-214)              */
+#define ASPIRE_DUMP_F16 0         /* dump buffer element type: fp16                */
+#define ASPIRE_DUMP_F32 1         /* fp32, holding the fp16-rounded logit          */
 
 /* ------------------------------------------------------------------------ */
 /* Plan (host).                                                             */
@@ -139,7 +151,7 @@ typedef struct AspireAttnArgs {
   int64_t o_stride_n;
   int64_t o_stride_h;
   float* lse;               /* optional fp32 [tokens, num_qo_heads] (NULL = skip) */
-  void* dump;               /* optional fp16 first/last logit dump (NULL = skip)  */
+  void* dump;               /* optional logit dump (NULL = skip), see dump_kind   */
   int64_t dump_num_heads;   /* heads dimension of the dump buffer                 */
   int64_t dump_kv_stride;   /* last dimension of the dump buffer                  */
   float sm_scale;           /* <= 0 selects 1/sqrt(128)                           */
@@ -164,14 +176,25 @@ typedef struct AspireAttnArgs {
   int64_t draft_stride;
   const int32_t* block_table;
   int64_t block_table_stride;
+  /* Dump variant: ASPIRE_DUMP_FIRST_LAST or ASPIRE_DUMP_LAST_TOKEN, element
+   * type ASPIRE_DUMP_F16 or ASPIRE_DUMP_F32, and optional per-row enable
+   * flags (int32 [batch], NULL = every row): row b writes its dump only when
+   * dump_flags[b] != 0, the dump_enabled guard of the use_mode_flags variant
+   * (jit_kernels.py:196-203, :300-301).  A zero-initialised struct keeps the
+   * fp16 first/last dump of every row. */
+  int32_t dump_kind;
+  int32_t dump_dtype;
+  const int32_t* dump_flags;
 } AspireAttnArgs;
 
 /*
  * Runs the planned attention program on `stream`.  Replaces
  * HolisticAttentionWrapper.run (aspire/attention/holistic_wrapper.py:344-386)
  * and the persistent FlashInfer kernel with its split-KV merge; with `dump`
- * set it also replaces the first/last logit-dump variant
- * (aspire/backends/jit_kernels.py:188-193, :252-256).
+ * set it also replaces the logit-dump variants (first/last and last-token,
+ * with or without mode flags, fp16 or fp32 buffer:
+ * aspire/backends/jit_kernels.py:180-203, :240-256, :271-332;
+ * aspire/attention/holistic_wrapper.py:401-434).
  * Capturable in a CUDA graph; allocates nothing.
  */
 ASPIRE_API int aspire_mixed_attention(const AspireAttnArgs* args, const AspirePlanInfo* plan, void* stream);
@@ -264,7 +287,8 @@ ASPIRE_API int aspire_append_kv(const AspireAppendArgs* args, void* stream);
 /* ------------------------------------------------------------------------ */
 
 typedef struct AspireSelectArgs {
-  const uint16_t* dump;     /* fp16 [dump_batch, num_heads, 2, kv_stride]; NULL when scores_in set */
+  const void* dump;         /* [dump_batch, num_heads, 2 or 1, kv_stride] (dump_kind,
+                               dump_dtype); NULL when scores_in set                 */
   int64_t kv_stride;
   int64_t max_seq_len;      /* logits past this position are ignored              */
   const float* lse;         /* fp32 [lse_rows, num_heads]                         */
@@ -303,14 +327,19 @@ typedef struct AspireSelectArgs {
                                seeding of LMBackendBase._build_recent_draft_rows
                                (aspire/backends/base.py:1522-1537).  0: ascending
                                block ids, as the replan path stores them          */
+  int32_t dump_kind;        /* ASPIRE_DUMP_FIRST_LAST: PageSelectorFirstLastAvg's
+                               score (page_selector.py:163-181); ASPIRE_DUMP_LAST_TOKEN:
+                               PageSelector's (page_selector.py:110-130, 140-146)  */
+  int32_t dump_dtype;       /* ASPIRE_DUMP_F16 or ASPIRE_DUMP_F32                  */
 } AspireSelectArgs;
 
 /*
- * Scores pages from the first/last logit dump and the dump program's LSE,
- * selects the top pages (ties broken by the lower page index) and writes the
- * ascending page-id rows plus the valid counts in place.  Replaces
+ * Scores pages from the logit dump and the dump program's LSE, selects the
+ * top pages (ties broken by the lower page index) and writes the ascending
+ * page-id rows plus the valid counts in place.  Replaces
  * PageSelectorFirstLastAvg.select (aspire/backends/page_selector.py:206-214,
- * :163-181, :79-108) followed by LMBackendBase._store_draft_rows
+ * :163-181, :79-108), or with ASPIRE_DUMP_LAST_TOKEN PageSelector.select
+ * (:140-146, :110-130), followed by LMBackendBase._store_draft_rows
  * (aspire/backends/base.py:1421-1471).
  */
 ASPIRE_API int aspire_select_pages(const AspireSelectArgs* args, void* stream);

@@ -23,7 +23,12 @@ The first/last dump restates the ``first_last_compact`` logits transform
 (aspire/backends/jit_kernels.py:188-193 body, :252-256 offsets): for
 q_idx == 0 (slot 0) and q_idx == q_len - 1 (slot 1; only when q_len > 1) the
 raw fp32 q.k, before scaling and before the causal mask, is written rounded
-to fp16 at dump[b, h, slot, kv_idx] for every kv_idx < kv_len.
+to fp16 at dump[b, h, slot, kv_idx] for every kv_idx < kv_len.  The
+``last_token`` transform (:180-184 body, :240-243 offsets) writes only
+q_idx == q_len - 1, at dump[b, h, kv_idx].  With ``dump_flags`` (the
+use_mode_flags variant, :196-203, :300-301) row b writes nothing when its
+flag is 0.  An fp32 dump buffer receives the fp16-rounded value, as the
+transform's ``__float2half`` result assigned to a float element does.
 """
 
 from __future__ import annotations
@@ -50,6 +55,8 @@ def paged_attention(
     dump: Optional[torch.Tensor] = None,
     dump_num_heads: int = 0,
     dump_kv_stride: int = 0,
+    dump_kind: str = "first_last_compact",
+    dump_flags=None,
 ) -> Tuple[torch.Tensor, torch.Tensor]:
     """Returns (out fp32 [T, Hq, D], lse fp32 [T, Hq]); fills `dump` in place.
 
@@ -70,7 +77,13 @@ def paged_attention(
     lse = torch.full((T, Hq), float("-inf"), dtype=torch.float32)
     dump_view = None
     if dump is not None:
-        dump_view = dump.view(-1, dump_num_heads, 2, dump_kv_stride)
+        if dump_kind == "first_last_compact":
+            dump_view = dump.view(-1, dump_num_heads, 2, dump_kv_stride)
+        elif dump_kind == "last_token":
+            dump_view = dump.view(-1, dump_num_heads, dump_kv_stride)
+        else:
+            raise ValueError(f"unknown dump_kind {dump_kind!r}")
+    flags = None if dump_flags is None else [int(x) for x in torch.as_tensor(dump_flags).tolist()]
     for b in range(len(kvl)):
         q0, q1 = qo[b], qo[b + 1]
         ql = q1 - q0
@@ -86,10 +99,14 @@ def paged_attention(
         Kh = K.repeat_interleave(group, dim=1)  # [L, Hq, D]
         Vh = V.repeat_interleave(group, dim=1)
         s = torch.einsum("qhd,khd->hqk", q[q0:q1], Kh)  # raw logits [Hq, ql, L]
-        if dump_view is not None:
-            dump_view[b, :Hq, 0, :L] = s[:, 0, :].to(torch.float16)
-            if ql > 1:
-                dump_view[b, :Hq, 1, :L] = s[:, ql - 1, :].to(torch.float16)
+        if dump_view is not None and (flags is None or flags[b] != 0):
+            as_dump = lambda t: t.to(torch.float16).to(dump.dtype)  # noqa: E731
+            if dump_kind == "first_last_compact":
+                dump_view[b, :Hq, 0, :L] = as_dump(s[:, 0, :])
+                if ql > 1:
+                    dump_view[b, :Hq, 1, :L] = as_dump(s[:, ql - 1, :])
+            else:
+                dump_view[b, :Hq, :L] = as_dump(s[:, ql - 1, :])
         x = s * (scale * LOG2E)
         if causal:
             kv_idx = torch.arange(L).view(1, 1, L)

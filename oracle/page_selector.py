@@ -1,4 +1,4 @@
-"""CPU restatement of ASPIRE's first/last page selector (test infrastructure).
+"""CPU restatement of ASPIRE's page selectors (test infrastructure).
 
 Restates, as plain functions over torch CPU tensors:
 
@@ -11,6 +11,11 @@ Restates, as plain functions over torch CPU tensors:
                           exp2, max over heads, sum of the two slots, zero pad
                           to pages*16, sum of each page's 16 tokens, plus the
                           position bias -page*1e-7 (page_selector.py:34-36).
+* ``last_token_scores`` - PageSelector._select_impl up to the page-score
+                          buffer (page_selector.py:110-127): logit *
+                          (sm_scale*log2 e) in the dump's dtype, minus the
+                          fp32 LSE of the row's last query, NaN -> -inf, max
+                          over heads, exp2, zero pad, page sums, position bias.
 * ``finalize_scores``   - _finalize_scores (page_selector.py:79-108): last L
                           valid pages +inf, pages >= num_pages -inf, top-k,
                           gather block-table ids, keep the valid prefix by
@@ -20,6 +25,7 @@ Restates, as plain functions over torch CPU tensors:
                           (stable descending sort), the rule the GPU kernel
                           implements.
 * ``select``            - PageSelectorFirstLastAvg.select (page_selector.py:206-214).
+* ``select_last_token`` - PageSelector.select (page_selector.py:140-146).
 * ``store_draft_rows``  - LMBackendBase._store_draft_rows with full_prefix
                           (aspire/backends/base.py:1421-1471).
 """
@@ -67,6 +73,21 @@ def first_last_scores(logits: torch.Tensor, first_lse: torch.Tensor, last_lse: t
     return scores + position_bias(pages_per_slot)
 
 
+def last_token_scores(logits: torch.Tensor, lse: torch.Tensor, pages_per_slot: int, page_size: int,
+                      head_dim: int = 128) -> torch.Tensor:
+    """logits: fp16 or fp32 [B, H, S]; lse: fp32 [B, H] -> fp32 [B, pages]."""
+    B, _, S = logits.shape
+    c = (1.0 / math.sqrt(head_dim)) * math.log2(math.e)
+    norm = logits * c - lse[:, :, None]                  # fp16 product rounded to fp16, then fp32
+    norm = torch.nan_to_num(norm.float(), nan=float("-inf"))
+    per_token = torch.exp2(norm.amax(dim=1))             # [B, S]
+    pad = pages_per_slot * page_size - S
+    if pad > 0:
+        per_token = F.pad(per_token, (0, pad))
+    scores = per_token.view(B, pages_per_slot, page_size).sum(dim=-1)
+    return scores + position_bias(pages_per_slot)
+
+
 def finalize_scores(scores: torch.Tensor, num_pages: torch.Tensor, block_table: torch.Tensor, k: int,
                     L: int, draft_percent: Optional[float] = None,
                     min_draft_pages: Optional[int] = None) -> Tuple[torch.Tensor, torch.Tensor]:
@@ -102,6 +123,22 @@ def select(dump: torch.Tensor, lse_buffer: torch.Tensor, num_pages: torch.Tensor
     last = (qo_indptr[1: batch + 1].long() - 1).clamp(min=0, max=max_q)
     scores = first_last_scores(logits, lse_buffer[first], lse_buffer[last], pages_per_slot, page_size,
                                head_dim)
+    selected, valid = finalize_scores(scores, num_pages[:batch], block_table[:batch], k, L,
+                                      draft_percent, min_draft_pages)
+    if return_scores:
+        return selected, valid, scores
+    return selected, valid
+
+
+def select_last_token(dump: torch.Tensor, lse_buffer: torch.Tensor, num_pages: torch.Tensor,
+                      block_table: torch.Tensor, qo_indptr: torch.Tensor, *, batch: int, n_heads: int,
+                      kv_stride: int, max_seq_len: int, pages_per_slot: int, k: int, L: int, page_size: int = 16,
+                      head_dim: int = 128, draft_percent: Optional[float] = None,
+                      min_draft_pages: Optional[int] = None, return_scores: bool = False):
+    """Whole-batch selection from the flat last-token dump buffer and the LSE buffer."""
+    logits = dump.view(batch, n_heads, kv_stride)[..., :max_seq_len]
+    last = (qo_indptr[1: batch + 1].long() - 1).clamp(min=0)
+    scores = last_token_scores(logits, lse_buffer[last], pages_per_slot, page_size, head_dim)
     selected, valid = finalize_scores(scores, num_pages[:batch], block_table[:batch], k, L,
                                       draft_percent, min_draft_pages)
     if return_scores:

@@ -14,6 +14,7 @@ Needs a CUDA GPU (FlashInfer JIT-compiles its kernel on first use):
     python tests/golden/make_flashinfer_golden.py [out.pt]
     python tests/golden/make_flashinfer_golden.py --prefill [out.pt]
     python tests/golden/make_flashinfer_golden.py --dump [out.pt]
+    python tests/golden/make_flashinfer_golden.py --dump-last [out.pt]
 
 `--dump` runs the reference's first/last logit-dump transform inside
 FlashInfer (aspire/backends/jit_kernels.py:188-193, offsets :252-256): a
@@ -27,6 +28,12 @@ index is what the reference's patch adds), so it cannot place a per-request
 dump; the FA2 kernel passes the request index, and in both kernels the
 transform sees the raw q.k (sm_scale is applied afterwards, in the softmax
 update).
+
+`--dump-last` does the same for the last-token transform (jit_kernels.py:
+180-184, offsets :240-243) with the use_mode_flags guard (:196-203,
+:300-301): one variant writing an fp32 buffer whose rows are enabled by an
+int32 mode_flags tensor (every other row on), one writing fp16 with no flags,
+into flashinfer_dump_last.pt.
 
 `--prefill` runs FlashInfer's BatchPrefillWithPagedKVCacheWrapper, the
 library the reference runs its prefill chunks through
@@ -107,6 +114,92 @@ struct FirstLastDumpFA2 : AttentionVariantBase {
   })
 };
 """
+
+
+# The last-token transform: the logit of the last query of a row (q_len >= 1)
+# goes to dump[row, head, kv_idx] as __float2half(logit), converted to the
+# buffer's element type; with DUMP_FLAGS a row whose mode flag is 0 writes
+# nothing.  Written for this fixture from the transform's description.
+LAST_VARIANT = r"""
+struct LastTokenDumpFA2 : AttentionVariantBase {
+  static constexpr bool use_softmax = true;
+  uint32_t window_left, qo_len, kv_len, dump_on;
+  float sm_scale_log2;
+  DUMP_T* out_dump;
+  uint64_t head_stride, row_offset;
+
+  template <typename Params>
+  __device__ __host__ LastTokenDumpFA2(const Params& params, uint32_t batch_idx, uint8_t* smem_ptr) {
+    qo_len = params.get_qo_len(batch_idx);
+    kv_len = params.get_kv_len(batch_idx);
+    window_left = kv_len;
+    sm_scale_log2 = params.sm_scale * math::log2e;
+    out_dump = params.attention_weights;
+    head_stride = (uint64_t)params.jit_kv_stride;
+    row_offset = (uint64_t)batch_idx * (uint64_t)params.num_heads * head_stride;
+    dump_on = DUMP_ON;
+  }
+
+  REGISTER_LOGITS_TRANSFORM(params, logits, batch_idx, qo_idx, kv_idx, qo_head_idx, kv_head_idx, {
+    if (dump_on && qo_idx + 1u == qo_len) {
+      out_dump[row_offset + (uint64_t)qo_head_idx * head_stride + kv_idx] = __float2half(logits);
+    }
+    return logits;
+  })
+};
+"""
+
+
+def dump_last_main(out_path):
+    """Last-token dump fixtures: (fp32 buffer, mode flags) and (fp16, no flags)."""
+    import flashinfer
+
+    dev = torch.device("cuda:0")
+    result = {"flashinfer_version": flashinfer.__version__, "variant": LAST_VARIANT, "cases": {}}
+    variants = {
+        "f32_flags": ("float", torch.float32, "(params.mode_flags[batch_idx] != 0) ? 1u : 0u", True),
+        "f16": ("half", torch.float16, "1u", False),
+    }
+    for vname, (ctype, dtype, on, flagged) in variants.items():
+        src = LAST_VARIANT.replace("LastTokenDumpFA2", "LastTokenDumpFA2_" + vname) \
+            .replace("DUMP_T", ctype).replace("DUMP_ON", on)
+        names, types = ["attention_weights"], [ctype]
+        if flagged:
+            names.append("mode_flags")
+            types.append("int32_t")
+        jit_args = ["aspire_golden_last_dump_" + vname, torch.bfloat16, torch.bfloat16, torch.bfloat16, torch.int32,
+                    128, 128, names, types, ["sm_scale", "num_heads", "jit_kv_stride"],
+                    ["double", "int64_t", "int64_t"], "LastTokenDumpFA2_" + vname, src]
+        for name, lay, seed in dump_cases():
+            q, kv = fill_tensors(lay, device="cpu", dtype=torch.bfloat16, seed=seed)
+            q, kv = q.to(dev), kv.to(dev)
+            i32 = lambda a: torch.from_numpy(np.ascontiguousarray(a, dtype=np.int32)).to(dev)  # noqa: E731
+            stride = (lay.pages_per_row * 16 + 127) // 128 * 128
+            H = lay.num_qo_heads
+            dump = torch.full((lay.batch * H * stride,), float("-inf"), dtype=dtype, device=dev)
+            flags = (torch.arange(lay.batch, dtype=torch.int32, device=dev) + 1) % 2  # rows 0, 2, ... on
+            ws = torch.empty(128 * 1024 * 1024, dtype=torch.uint8, device=dev)
+            w = flashinfer.BatchPrefillWithPagedKVCacheWrapper(ws, "NHD", backend="fa2", jit_args=jit_args)
+            w.plan(i32(lay.qo_indptr), i32(lay.kv_indptr), i32(lay.kv_indices), i32(last_page_lens(lay)), H,
+                   lay.num_kv_heads, 128, 16, causal=True, q_data_type=torch.bfloat16, kv_data_type=torch.bfloat16,
+                   disable_split_kv=True)
+            sm_scale = 1.0 / 128 ** 0.5
+            run_args = [dump, flags] if flagged else [dump]
+            out, lse = w.run(q, kv, *run_args, sm_scale, H, stride, return_lse=True)
+            torch.cuda.synchronize()
+            result["cases"][f"{vname}/{name}"] = {
+                "seed": seed, "kv_stride": stride, "flags": flags.cpu() if flagged else None,
+                "layout": {k: getattr(lay, k) for k in ("num_qo_heads", "num_kv_heads", "modes", "q_lens", "kv_lens",
+                                                        "qo_indptr", "kv_indptr", "kv_indices", "block_table",
+                                                        "ctx_lens", "pages_per_row", "num_pages_total")},
+                "dump": dump.view(lay.batch, H, stride).cpu(),
+                "out": out.cpu(),
+                "lse": lse.float().cpu(),
+            }
+            print(vname, name, "dump", (lay.batch, H, stride), dtype, "finite", int(torch.isfinite(dump).sum()),
+                  flush=True)
+    torch.save(result, out_path)
+    print("saved", out_path)
 
 
 def dump_cases():
@@ -194,7 +287,10 @@ def prefill_main(out_path):
 def main():
     import flashinfer
 
-    args = [a for a in sys.argv[1:] if a not in ("--prefill", "--dump")]
+    args = [a for a in sys.argv[1:] if a not in ("--prefill", "--dump", "--dump-last")]
+    if "--dump-last" in sys.argv[1:]:
+        dump_last_main(Path(args[0]) if args else HERE / "flashinfer_dump_last.pt")
+        return
     if "--prefill" in sys.argv[1:]:
         prefill_main(Path(args[0]) if args else HERE / "flashinfer_prefill.pt")
         return

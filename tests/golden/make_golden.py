@@ -3,12 +3,14 @@
 Run where the reference tree is checked out, with $ASPIRE_REFERENCE naming
 its root:
 
-    ASPIRE_REFERENCE=<path to the ASPIRE checkout> python tests/golden/make_golden.py
+    ASPIRE_REFERENCE=<path to the ASPIRE checkout> python tests/golden/make_golden.py [group ...]
 
 * page_selector_*.pt : inputs and outputs of the reference's
   aspire.backends.page_selector.PageSelectorFirstLastAvg.select (imported
   unchanged from the reference tree, run on CPU), including its page-score
   buffer before the +/-inf forcing; tie cases run its _finalize_scores.
+  page_selector_last_*.pt: the same for the base PageSelector.select on a
+  last-token dump (fp16 and fp32 buffers).
 * recent_rows.pt : the reference's LMBackendBase._build_recent_draft_rows
   (recent-page seeding of the draft table) on CPU.
 * unified_indices.pt : the reference's build_unified_indices
@@ -102,6 +104,54 @@ def selector_case(name, *, B, H, max_seq_len, kv_stride, top_k_pages, L, draft_p
     }
     torch.save(out, HERE / f"page_selector_{name}.pt")
     print(f"page_selector_{name}: k={k} valid={valid.tolist()}")
+
+
+def last_token_case(name, *, B, H, max_seq_len, kv_stride, top_k_pages, L, draft_percent, seed, q_lens, lens,
+                    dump_dtype=torch.float16, lse_neg_inf_rows=()):
+    """The base PageSelector (last-token dump [B, H, kv_stride])."""
+    sys.path.insert(0, str(REF))
+    from aspire.backends.page_selector import PageSelector  # noqa: E402
+
+    gen = torch.Generator().manual_seed(seed)
+    page = 16
+    pps = (max_seq_len + page - 1) // page
+    k = max(top_k_pages, math.ceil(pps * draft_percent / 100)) if draft_percent is not None else top_k_pages
+    sel = PageSelector(max_batch_size=B, pages_per_slot=pps, subset_cache_size=k, L=L, n_heads=H, page_size=page,
+                       max_seq_length=max_seq_len, device="cpu", bsz=B, dec_len=9, head_dim=128,
+                       kv_stride=kv_stride, draft_percent=draft_percent, min_draft_pages=top_k_pages)
+    d = torch.full((B, H, kv_stride), float("-inf"), dtype=dump_dtype)
+    for b in range(B):
+        n = int(lens[b])
+        # fp16-representable logits in either buffer, as the dump kernels write them
+        d[b, :, :n] = (torch.randn(H, n, generator=gen) * 11.3).to(torch.float16).to(dump_dtype)
+    qo = torch.zeros(B + 1, dtype=torch.int32)
+    qo[1:] = torch.cumsum(torch.tensor(q_lens, dtype=torch.int32), 0)
+    T = int(qo[-1]) + 3
+    lse = (torch.randn(T, H, generator=gen) * 2.0 + 12.0).float()
+    for b in lse_neg_inf_rows:
+        # A last query that saw no keys: -inf LSE and -inf logits -> NaN -> -inf.
+        lse[int(qo[b + 1]) - 1] = float("-inf")
+        d[b] = float("-inf")
+    dump = d.reshape(-1)
+    num_pages = torch.tensor([(int(x) + page - 1) // page for x in lens], dtype=torch.int32)
+    block_table = torch.stack([b * pps + torch.randperm(pps, generator=gen) for b in range(B)]).to(torch.int32)
+    captured = {}
+    orig = sel._finalize_scores
+
+    def capture(scores, num_pages_, block_table_):
+        captured["scores_raw"] = scores.clone()
+        return orig(scores, num_pages_, block_table_)
+
+    sel._finalize_scores = capture
+    selected, valid = sel.select(dump, lse, num_pages, block_table, qo)
+    out = {
+        "params": dict(B=B, H=H, max_seq_len=max_seq_len, kv_stride=kv_stride, pps=pps, k=k, L=L,
+                       draft_percent=draft_percent, min_draft_pages=top_k_pages, page_size=page),
+        "dump": dump, "lse": lse, "num_pages": num_pages, "block_table": block_table, "qo_indptr": qo,
+        "scores_raw": captured["scores_raw"], "selected": selected.clone(), "valid": valid.clone(),
+    }
+    torch.save(out, HERE / f"page_selector_last_{name}.pt")
+    print(f"page_selector_last_{name}: k={k} valid={valid.tolist()}")
 
 
 def tie_case():
@@ -293,27 +343,44 @@ def spill_case():
     torch.save(out, HERE / "draft_spill.pt")
 
 
-def main():
+def main(groups=None):
+    """Writes every fixture, or only those of the named groups (selector,
+    last_token, ties, append, indices, recent, spill)."""
     if not os.environ.get("ASPIRE_REFERENCE") or not REF.exists():
         raise SystemExit("set ASPIRE_REFERENCE to the root of the reference (ASPIRE) checkout")
-    # BASELINE config 1 geometry: 16 heads, 1024-token cache, 8 selected pages.
-    selector_case("cfg1", B=4, H=16, max_seq_len=1024, kv_stride=1024, top_k_pages=8, L=2,
-                  draft_percent=None, seed=0, q_lens=[1, 1, 5, 5], lens=[1000, 1024, 1021, 1024],
-                  stale_rows=(0, 1))
-    # Engine defaults (top_k_pages 32, recent 8, draft_percent 7) on a long, padded-stride dump,
-    # with a tiny row (num_pages < L) and a row whose first-query LSE is -inf (NaN -> -inf path).
-    selector_case("pct", B=3, H=2, max_seq_len=16640, kv_stride=16768, top_k_pages=32, L=8,
-                  draft_percent=7.0, seed=1, q_lens=[5, 1, 9], lens=[16633, 70, 9001],
-                  stale_rows=(1,), lse_neg_inf_rows=(2,))
-    # Config-2-like (budget 128 pages, L 8, draft_percent unset), local heads of TP 4.
-    selector_case("budget", B=2, H=4, max_seq_len=16640, kv_stride=16640, top_k_pages=128, L=8,
-                  draft_percent=None, seed=2, q_lens=[5, 3], lens=[16500, 16001])
-    tie_case()
-    append_case()
-    indices_case()
-    recent_case()
-    spill_case()
+    want = lambda g: not groups or g in groups  # noqa: E731
+    if want("selector"):
+        # BASELINE config 1 geometry: 16 heads, 1024-token cache, 8 selected pages.
+        selector_case("cfg1", B=4, H=16, max_seq_len=1024, kv_stride=1024, top_k_pages=8, L=2,
+                      draft_percent=None, seed=0, q_lens=[1, 1, 5, 5], lens=[1000, 1024, 1021, 1024],
+                      stale_rows=(0, 1))
+        # Engine defaults (top_k_pages 32, recent 8, draft_percent 7) on a long, padded-stride dump,
+        # with a tiny row (num_pages < L) and a row whose first-query LSE is -inf (NaN -> -inf path).
+        selector_case("pct", B=3, H=2, max_seq_len=16640, kv_stride=16768, top_k_pages=32, L=8,
+                      draft_percent=7.0, seed=1, q_lens=[5, 1, 9], lens=[16633, 70, 9001],
+                      stale_rows=(1,), lse_neg_inf_rows=(2,))
+        # Config-2-like (budget 128 pages, L 8, draft_percent unset), local heads of TP 4.
+        selector_case("budget", B=2, H=4, max_seq_len=16640, kv_stride=16640, top_k_pages=128, L=8,
+                      draft_percent=None, seed=2, q_lens=[5, 3], lens=[16500, 16001])
+    if want("last_token"):
+        # The base backend's selector on its last-token dump: config-1 geometry in
+        # fp16, and a padded-stride fp32 dump with draft_percent and a -inf LSE row.
+        last_token_case("cfg1", B=4, H=16, max_seq_len=1024, kv_stride=1024, top_k_pages=8, L=2,
+                        draft_percent=None, seed=10, q_lens=[1, 1, 5, 5], lens=[1000, 1024, 1021, 1024])
+        last_token_case("f32", B=3, H=4, max_seq_len=4000, kv_stride=4096, top_k_pages=32, L=8,
+                        draft_percent=7.0, seed=11, q_lens=[5, 1, 9], lens=[3990, 70, 2500],
+                        dump_dtype=torch.float32, lse_neg_inf_rows=(2,))
+    if want("ties"):
+        tie_case()
+    if want("append"):
+        append_case()
+    if want("indices"):
+        indices_case()
+    if want("recent"):
+        recent_case()
+    if want("spill"):
+        spill_case()
 
 
 if __name__ == "__main__":
-    main()
+    main(sys.argv[1:])

@@ -5,7 +5,7 @@ from __future__ import annotations
 
 import torch
 
-from aspire_b200.attention import HolisticAttentionWrapper, first_last_dump_jit_args
+from aspire_b200.attention import HolisticAttentionWrapper, dump_jit_args
 from aspire_b200.workloads import MixedLayout, fill_tensors
 from oracle import attention as oracle_attn
 
@@ -15,12 +15,18 @@ MEAN_ABS = 2e-3
 LSE_ATOL = 2e-3
 
 
+def _slots(kind: str) -> int:
+    return 2 if kind == "first_last_compact" else 1
+
+
 def run_attention(layout: MixedLayout, q: torch.Tensor, kv: torch.Tensor, *, dump: bool = False,
-                  dump_stride: int = 0, wrapper: HolisticAttentionWrapper | None = None, causal: bool = True):
+                  dump_stride: int = 0, wrapper: HolisticAttentionWrapper | None = None, causal: bool = True,
+                  dump_kind: str = "first_last_compact", dump_dtype: torch.dtype = torch.float16,
+                  dump_flags: torch.Tensor | None = None):
     dev = q.device
     if wrapper is None:
-        wrapper = HolisticAttentionWrapper(torch.empty(1, device=dev),
-                                           jit_args=first_last_dump_jit_args() if dump else None)
+        jit = dump_jit_args(dump_kind, use_mode_flags=dump_flags is not None, dump_buffer_dtype=dump_dtype)
+        wrapper = HolisticAttentionWrapper(torch.empty(1, device=dev), jit_args=jit if dump else None)
     kv_indices = torch.from_numpy(layout.kv_indices).to(dev)
     wrapper.plan_host(torch.from_numpy(layout.qo_indptr), torch.from_numpy(layout.kv_indptr),
                       torch.from_numpy(layout.kv_lens), kv_indices, layout.num_qo_heads, layout.num_kv_heads,
@@ -28,22 +34,25 @@ def run_attention(layout: MixedLayout, q: torch.Tensor, kv: torch.Tensor, *, dum
     dump_buf = None
     args = []
     if dump:
-        dump_buf = torch.full((layout.batch * layout.num_qo_heads * 2 * dump_stride,), float("-inf"),
-                              dtype=torch.float16, device=dev)
-        args = [dump_buf, layout.num_qo_heads, dump_stride]
+        dump_buf = torch.full((layout.batch * layout.num_qo_heads * _slots(dump_kind) * dump_stride,),
+                              float("-inf"), dtype=dump_dtype, device=dev)
+        flags = [dump_flags.to(dev)] if dump_flags is not None else []
+        args = [dump_buf, *flags, layout.num_qo_heads, dump_stride]
     out, lse = wrapper.run(q, kv, *args, return_lse=True)
     return out, lse, dump_buf, wrapper
 
 
 def oracle_attention(layout: MixedLayout, q: torch.Tensor, kv: torch.Tensor, *, dump_stride: int = 0,
-                     causal: bool = True):
+                     causal: bool = True, dump_kind: str = "first_last_compact",
+                     dump_dtype: torch.dtype = torch.float16, dump_flags: torch.Tensor | None = None):
     dump = None
     if dump_stride:
-        dump = torch.full((layout.batch * layout.num_qo_heads * 2 * dump_stride,), float("-inf"),
-                          dtype=torch.float16)
+        dump = torch.full((layout.batch * layout.num_qo_heads * _slots(dump_kind) * dump_stride,), float("-inf"),
+                          dtype=dump_dtype)
     out, lse = oracle_attn.paged_attention(
         q.float().cpu(), kv.cpu(), layout.qo_indptr, layout.kv_indptr, layout.kv_indices, layout.kv_lens,
-        causal=causal, dump=dump, dump_num_heads=layout.num_qo_heads, dump_kv_stride=dump_stride)
+        causal=causal, dump=dump, dump_num_heads=layout.num_qo_heads, dump_kv_stride=dump_stride,
+        dump_kind=dump_kind, dump_flags=dump_flags)
     return out, lse, dump
 
 
@@ -63,20 +72,29 @@ def assert_attention_close(out, lse, ref_out, ref_lse, rows=None):
         assert d <= LSE_ATOL, f"lse max-abs {d:.3e}"
 
 
-def assert_dump_close(dump, ref_dump, layout: MixedLayout, stride: int):
-    """fp16 dumps agree to one fp16 rounding step on every written position."""
-    d = dump.cpu().view(layout.batch, layout.num_qo_heads, 2, stride).float()
-    r = ref_dump.view(layout.batch, layout.num_qo_heads, 2, stride).float()
+def assert_dump_close(dump, ref_dump, layout: MixedLayout, stride: int, *, dump_kind: str = "first_last_compact",
+                      dump_flags: torch.Tensor | None = None):
+    """Dumps agree to one fp16 rounding step on every written position (the
+    values are fp16-rounded in an fp32 buffer too); positions past kv_len,
+    unwritten slots and rows whose flag is 0 keep their -inf fill."""
+    S = _slots(dump_kind)
+    d = dump.cpu().view(layout.batch, layout.num_qo_heads, S, stride).float()
+    r = ref_dump.view(layout.batch, layout.num_qo_heads, S, stride).float()
+    if dump.dtype == torch.float32:
+        assert torch.equal(d, d.half().float()), "fp32 dump holds values that are not fp16-rounded"
     for b in range(layout.batch):
+        if dump_flags is not None and int(dump_flags[b]) == 0:
+            assert bool(torch.isinf(d[b]).all()), f"row {b} is flagged off but was written"
+            continue
         L = int(layout.kv_lens[b])
-        slots = [0] + ([1] if int(layout.q_lens[b]) > 1 else [])
-        for s in slots:
+        written = [0] + ([1] if S == 2 and int(layout.q_lens[b]) > 1 else [])
+        for s in written:
             a, e = d[b, :, s, :L], r[b, :, s, :L]
             tol = e.abs() * 2.0 ** -10 + 2.0 ** -14 + 2e-3
             assert bool(((a - e).abs() <= tol).all()), f"dump row {b} slot {s}"
         # Positions past kv_len and unwritten slots keep their previous contents.
         assert bool(torch.isinf(d[b, :, :, L:]).all())
-        if int(layout.q_lens[b]) == 1:
+        if S == 2 and int(layout.q_lens[b]) == 1:
             assert bool(torch.isinf(d[b, :, 1, :]).all())
 
 

@@ -5,7 +5,7 @@ import pytest
 import torch
 
 from aspire_b200.attention import HolisticAttentionWrapper
-from aspire_b200.workloads import MixedLayout, config1_layout, make_layout
+from aspire_b200.workloads import MixedLayout, config1_layout, full_context_layout, make_layout, rows_layout
 
 from gpu_helpers import (assert_attention_close, assert_dump_close, make_inputs, oracle_attention,
                          run_attention)
@@ -249,6 +249,69 @@ def test_matches_flashinfer_golden(cuda_device, golden_dir, case):
     assert (lse.cpu() - g["lse"]).abs().max().item() <= 2e-3
 
 
+DUMP_VARIANTS = [("last_token", torch.float16, False), ("last_token", torch.float32, True),
+                 ("first_last_compact", torch.float32, False), ("first_last_compact", torch.float16, True)]
+
+
+@pytest.mark.parametrize("kind,dtype,flagged", DUMP_VARIANTS,
+                         ids=["last_f16", "last_f32_flags", "first_last_f32", "first_last_f16_flags"])
+@pytest.mark.parametrize("shape", ["refresh", "prefill"])
+def test_dump_variants(cuda_device, kind, dtype, flagged, shape):
+    """The reference's other dump variants (jit_kernels.py:180-203,
+    holistic_wrapper.py:401-434): last-token (one slot, the last query of
+    every row, q_len 1 included), the use_mode_flags guard (rows 0, 2, 4, ...
+    on, the others untouched) and an fp32 buffer holding fp16-rounded logits,
+    against the oracle, on a refresh-layer program (draft rows with one query,
+    verify rows with 3-9) and on prefill chunks beside decode rows."""
+    if shape == "refresh":
+        lay = full_context_layout(make_layout(batch=6, ctx=2999, num_qo_heads=32, num_kv_heads=8,
+                                              draft_fraction=0.5, budget_pages=37, seed=31))
+    else:
+        lay = rows_layout([150, 1, 5, 64], [1000, 1500, 800, 64], 32, 8, seed=32)
+    q, kv = make_inputs(lay, cuda_device, seed=33)
+    stride = (int(lay.kv_lens.max()) + 127) // 128 * 128 + 16
+    flags = (torch.arange(lay.batch, dtype=torch.int32) + 1) % 2 if flagged else None
+    out, lse, dump, w = run_attention(lay, q, kv, dump=True, dump_stride=stride, dump_kind=kind, dump_dtype=dtype,
+                                      dump_flags=flags)
+    ref_out, ref_lse, ref_dump = oracle_attention(lay, q, kv, dump_stride=stride, dump_kind=kind, dump_dtype=dtype,
+                                                  dump_flags=flags)
+    assert dump.dtype == dtype
+    assert w.device_status() == 0
+    if shape == "prefill":
+        assert w.plan_info.num_items_prefill > 0 or not w.plan_info.tc_enabled
+    assert_attention_close(out, lse, ref_out, ref_lse)
+    assert_dump_close(dump, ref_dump, lay, stride, dump_kind=kind, dump_flags=flags)
+
+
+def test_dump_variant_arguments_are_checked(cuda_device):
+    """run() refuses a dump buffer of the wrong element type for the variant,
+    one too small for its slots, and missing mode flags."""
+    from aspire_b200.attention import dump_jit_args
+
+    lay = config1_layout(seed=2)
+    q, kv = make_inputs(lay, cuda_device, seed=2)
+    stride = 1024
+    w = HolisticAttentionWrapper(torch.empty(1, device=cuda_device),
+                                 jit_args=dump_jit_args("last_token", use_mode_flags=True,
+                                                        dump_buffer_dtype=torch.float32))
+    kvi = torch.from_numpy(lay.kv_indices).to(cuda_device)
+    w.plan_host(torch.from_numpy(lay.qo_indptr), torch.from_numpy(lay.kv_indptr), torch.from_numpy(lay.kv_lens),
+                kvi, lay.num_qo_heads, lay.num_kv_heads, 128, 16, causal=True)
+    H = lay.num_qo_heads
+    flags = torch.ones(lay.batch, dtype=torch.int32, device=cuda_device)
+    f16 = torch.full((lay.batch * H * stride,), float("-inf"), dtype=torch.float16, device=cuda_device)
+    f32 = torch.full((lay.batch * H * stride,), float("-inf"), dtype=torch.float32, device=cuda_device)
+    with pytest.raises(ValueError, match="dump variant writes"):
+        w.run(q, kv, f16, flags, H, stride)
+    with pytest.raises(ValueError, match="smaller than"):
+        w.run(q, kv, f32[:-1], flags, H, stride)
+    with pytest.raises(ValueError, match="mode_flags"):
+        w.run(q, kv, f32, H, stride)
+    w.run(q, kv, f32, flags, H, stride)
+    torch.cuda.synchronize()
+    assert bool(torch.isfinite(f32).any())
+
+
 @pytest.mark.parametrize("case", ["cfg1_full", "qwen8b_full"])
 def test_dump_matches_flashinfer_variant(cuda_device, golden_dir, case):
     """The refresh-layer dump of the sm_100a kernels against the reference's
@@ -270,6 +333,28 @@ def test_dump_matches_flashinfer_variant(cuda_device, golden_dir, case):
     out, lse, dump, _ = run_attention(lay, q.to(cuda_device), kv.to(cuda_device), dump=True, dump_stride=S)
     torch.cuda.synchronize()
     dump_positions_close(dump.cpu().view(lay.batch, lay.num_qo_heads, 2, S), g["dump"], lay)
+    err = (out.float().cpu() - g["out"].float()).abs()
+    assert err.max().item() <= 2e-2 and err.mean().item() <= 2e-3, err.max().item()
+    assert (lse.cpu() - g["lse"]).abs().max().item() <= 2e-3
+
+
+@pytest.mark.parametrize("case", ["f32_flags/cfg1_full", "f32_flags/qwen8b_full", "f16/cfg1_full",
+                                  "f16/qwen8b_full"])
+def test_last_token_dump_matches_flashinfer_variant(cuda_device, golden_dir, case):
+    """The last-token dump of the sm_100a kernels (fp32 buffer with mode
+    flags, fp16 without) against the reference's last_token transform run
+    inside FlashInfer (tests/golden/make_flashinfer_golden.py --dump-last)."""
+    from aspire_b200.workloads import fill_tensors
+    from test_oracle_golden import last_dump_positions_close
+
+    g = torch.load(golden_dir / "flashinfer_dump_last.pt", weights_only=False)["cases"][case]
+    lay = MixedLayout(**g["layout"])
+    S = g["kv_stride"]
+    q, kv = fill_tensors(lay, device="cpu", dtype=torch.bfloat16, seed=g["seed"])
+    out, lse, dump, _ = run_attention(lay, q.to(cuda_device), kv.to(cuda_device), dump=True, dump_stride=S,
+                                      dump_kind="last_token", dump_dtype=g["dump"].dtype, dump_flags=g["flags"])
+    torch.cuda.synchronize()
+    last_dump_positions_close(dump.cpu().view(lay.batch, lay.num_qo_heads, S), g["dump"], lay, g["flags"])
     err = (out.float().cpu() - g["out"].float()).abs()
     assert err.max().item() <= 2e-2 and err.mean().item() <= 2e-3, err.max().item()
     assert (lse.cpu() - g["lse"]).abs().max().item() <= 2e-3

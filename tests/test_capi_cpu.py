@@ -27,7 +27,7 @@ def test_library_exports_every_declared_symbol(built_library):
     for name in declared:
         assert hasattr(built_library, name), name
     assert set(declared) == set(_capi.exported_symbols())
-    assert built_library.aspire_abi_version() == _capi.EXPECTED_ABI_VERSION == 4
+    assert built_library.aspire_abi_version() == _capi.EXPECTED_ABI_VERSION == 5
     assert built_library.aspire_status_offset() == 256
 
 

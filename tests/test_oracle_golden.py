@@ -42,6 +42,26 @@ def test_selector_tables_match_reference(golden_dir, case):
     assert torch.equal(selected, g["selected"])
 
 
+LAST_CASES = ["cfg1", "f32"]
+
+
+@pytest.mark.parametrize("case", LAST_CASES)
+def test_last_token_selector_matches_reference(golden_dir, case):
+    """The base PageSelector on a last-token dump (fp16 and fp32 buffers):
+    the oracle's page scores are bit-identical and its tables equal."""
+    g = _load(golden_dir, f"page_selector_last_{case}.pt")
+    p = g["params"]
+    selected, valid, scores = oracle_sel.select_last_token(
+        g["dump"], g["lse"], g["num_pages"], g["block_table"], g["qo_indptr"], batch=p["B"], n_heads=p["H"],
+        kv_stride=p["kv_stride"], max_seq_len=p["max_seq_len"], pages_per_slot=p["pps"], k=p["k"], L=p["L"],
+        draft_percent=p["draft_percent"], min_draft_pages=p["min_draft_pages"], return_scores=True)
+    assert torch.equal(scores, g["scores_raw"])
+    assert torch.equal(valid, g["valid"])
+    assert torch.equal(selected, g["selected"])
+    if case == "f32":
+        assert g["dump"].dtype == torch.float32
+
+
 def _boundary_tied(scores_row, num_pages, L, valid):
     s = scores_row.clone()
     j = torch.arange(s.shape[0])
@@ -53,7 +73,7 @@ def _boundary_tied(scores_row, num_pages, L, valid):
 
 def test_golden_cases_have_untied_boundaries(golden_dir):
     """The fixtures exercise selection where the reference's result is tie-free."""
-    for case in CASES:
+    for case in CASES + ["last_" + c for c in LAST_CASES]:
         g = _load(golden_dir, f"page_selector_{case}.pt")
         p = g["params"]
         for b in range(p["B"]):
@@ -264,6 +284,50 @@ def test_dump_oracle_matches_flashinfer_variant(golden_dir, case):
                                            lay.kv_lens, dump=dump, dump_num_heads=lay.num_qo_heads,
                                            dump_kv_stride=S)
     dump_positions_close(dump.view(lay.batch, lay.num_qo_heads, 2, S), g["dump"], lay)
+    err = (out - g["out"].float()).abs()
+    assert err.max().item() <= 2e-2 and err.mean().item() <= 2e-3
+    assert (lse - g["lse"]).abs().max().item() <= 2e-3
+
+
+def last_dump_positions_close(got, ref, lay, flags):
+    """Last-token dumps [B, H, stride] agree within one fp16 step at keys
+    [0, kv_len) of every row whose flag is set (all rows without flags);
+    rows flagged off hold only the -inf fill in both."""
+    for b in range(lay.batch):
+        if flags is not None and int(flags[b]) == 0:
+            assert bool(torch.isinf(ref[b]).all()) and bool(torch.isinf(got[b]).all()), b
+            continue
+        L = int(lay.kv_lens[b])
+        a, e = got[b, :, :L].float(), ref[b, :, :L].float()
+        tol = e.abs() * 2.0 ** -10 + 2.0 ** -14 + 2e-3
+        assert bool(torch.isfinite(e).all()), b
+        assert bool(((a - e).abs() <= tol).all()), (b, float((a - e).abs().max()))
+
+
+LAST_DUMP_CASES = ["f32_flags/cfg1_full", "f32_flags/qwen8b_full", "f16/cfg1_full", "f16/qwen8b_full"]
+
+
+@pytest.mark.parametrize("case", LAST_DUMP_CASES)
+def test_last_dump_oracle_matches_flashinfer_variant(golden_dir, case):
+    """The oracle's last-token dump (with the mode-flag guard and an fp32
+    buffer) against the reference's last_token transform run inside
+    FlashInfer (fixture from tests/golden/make_flashinfer_golden.py
+    --dump-last): the raw q.k of each row's last query, fp16-rounded, at
+    dump[b, h, kv_idx]; rows whose flag is 0 untouched."""
+    from aspire_b200.workloads import MixedLayout, fill_tensors
+    from oracle import attention as oracle_attn
+
+    g = _load(golden_dir, "flashinfer_dump_last.pt")["cases"][case]
+    lay = MixedLayout(**g["layout"])
+    S = g["kv_stride"]
+    dtype = g["dump"].dtype
+    q, kv = fill_tensors(lay, device="cpu", dtype=torch.bfloat16, seed=g["seed"])
+    dump = torch.full((lay.batch * lay.num_qo_heads * S,), float("-inf"), dtype=dtype)
+    out, lse = oracle_attn.paged_attention(q.float(), kv, lay.qo_indptr, lay.kv_indptr, lay.kv_indices,
+                                           lay.kv_lens, dump=dump, dump_num_heads=lay.num_qo_heads,
+                                           dump_kv_stride=S, dump_kind="last_token", dump_flags=g["flags"])
+    assert dtype == (torch.float32 if case.startswith("f32") else torch.float16)
+    last_dump_positions_close(dump.view(lay.batch, lay.num_qo_heads, S), g["dump"], lay, g["flags"])
     err = (out - g["out"].float()).abs()
     assert err.max().item() <= 2e-2 and err.mean().item() <= 2e-3
     assert (lse - g["lse"]).abs().max().item() <= 2e-3

@@ -3,7 +3,7 @@
 import pytest
 import torch
 
-from aspire_b200.page_selector import PageSelectorFirstLastAvg
+from aspire_b200.page_selector import PageSelector, PageSelectorFirstLastAvg
 from oracle import page_selector as oracle_sel
 
 pytestmark = pytest.mark.gpu
@@ -127,3 +127,65 @@ def test_seed_recent_matches_reference_golden(cuda_device, golden_dir, case):
     torch.cuda.synchronize()
     assert torch.equal(valid.cpu(), c["valid"])
     assert torch.equal(rows.cpu(), c["rows"])
+
+
+LAST_CASES = ["cfg1", "f32"]
+
+
+def _last_selector(p, dev):
+    return PageSelector(max_batch_size=p["B"], pages_per_slot=p["pps"], subset_cache_size=p["k"], L=p["L"],
+                        n_heads=p["H"], page_size=16, max_seq_length=p["max_seq_len"], device=dev, bsz=p["B"],
+                        dec_len=9, head_dim=128, kv_stride=p["kv_stride"], draft_percent=p["draft_percent"],
+                        min_draft_pages=p["min_draft_pages"])
+
+
+@pytest.mark.parametrize("case", LAST_CASES)
+def test_last_token_select_matches_reference(cuda_device, golden_dir, case):
+    """The base PageSelector (last-token dump, fp16 and fp32 buffers) against
+    the reference's own PageSelector.select on the same inputs: page scores
+    within SCORE_RTOL, tables equal, and the oracle's top-k of the kernel's
+    scores bit-exact; select_subset picks the same rows."""
+    g = torch.load(golden_dir / f"page_selector_last_{case}.pt", weights_only=False)
+    p = g["params"]
+    dev = cuda_device
+    sel = _last_selector(p, dev)
+    scores = torch.empty(p["B"], p["pps"], dtype=torch.float32, device=dev)
+    selected, valid = sel.select(g["dump"].to(dev), g["lse"].to(dev), g["num_pages"].to(dev),
+                                 g["block_table"].to(dev), g["qo_indptr"].to(dev), scores_out=scores)
+    torch.cuda.synchronize()
+    _assert_scores_close(scores.cpu(), g["scores_raw"])
+    o_sel, o_valid = oracle_sel.finalize_scores(scores.cpu(), g["num_pages"], g["block_table"], p["k"], p["L"],
+                                                p["draft_percent"], p["min_draft_pages"])
+    assert torch.equal(valid.cpu(), o_valid) and torch.equal(selected.cpu(), o_sel)
+    assert torch.equal(valid.cpu(), g["valid"]) and torch.equal(selected.cpu(), g["selected"])
+    ids = torch.tensor([p["B"] - 1, 0], dtype=torch.long)
+    s_sel, s_valid = sel.select_subset(ids.to(dev), g["dump"].to(dev), g["lse"].to(dev), g["num_pages"].to(dev),
+                                       g["block_table"].to(dev), g["qo_indptr"].to(dev))
+    assert torch.equal(s_sel.cpu(), g["selected"][ids]) and torch.equal(s_valid.cpu(), g["valid"][ids])
+
+
+def test_compact_first_last_entry_points(cuda_device, golden_dir):
+    """select_from_compact_first_last / select_layers_from_compact_first_last
+    (explicit [B, H, 2, max_seq_len] logit views and first/last LSE) give the
+    tables of select() on the same dump."""
+    g = torch.load(golden_dir / "page_selector_pct.pt", weights_only=False)
+    p = g["params"]
+    dev = cuda_device
+    sel = _selector(p, dev)
+    dump = g["dump"].to(dev)
+    lse = g["lse"].to(dev)
+    qo = g["qo_indptr"].long()
+    max_q = lse.shape[0] - 1
+    first = lse[qo[:p["B"]].clamp(0, max_q).to(dev)]
+    last = lse[(qo[1:p["B"] + 1] - 1).clamp(0, max_q).to(dev)]
+    logits = dump.view(p["B"], p["H"], 2, p["kv_stride"])[..., :p["max_seq_len"]]
+    a_sel, a_valid = sel.select_from_compact_first_last(logits, first, last, g["num_pages"].to(dev),
+                                                        g["block_table"].to(dev))
+    assert torch.equal(a_sel.cpu(), g["selected"]) and torch.equal(a_valid.cpu(), g["valid"])
+    layers = torch.stack([dump.view(p["B"], p["H"], 2, p["kv_stride"])] * 2)
+    l_sel, l_valid = sel.select_layers_from_compact_first_last(layers, torch.stack([first] * 2),
+                                                               torch.stack([last] * 2), g["num_pages"].to(dev),
+                                                               g["block_table"].to(dev))
+    assert l_sel.shape == (2, p["B"], p["k"])
+    assert torch.equal(l_sel[0].cpu(), g["selected"]) and torch.equal(l_sel[1].cpu(), g["selected"])
+    assert torch.equal(l_valid.cpu(), g["valid"])
