@@ -136,7 +136,7 @@ constexpr int kIndicesThreads = 128;
 __global__ void aspire_build_indices_kernel(IndicesParams p);
 
 constexpr int kSelThreads = 512;
-constexpr int kScoreThreads = 256;
+constexpr int kScoreThreads = 128;
 __global__ void aspire_page_scores_kernel(SelectParams p);
 constexpr int kMaxSelHeads = 128;
 

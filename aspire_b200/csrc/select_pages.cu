@@ -139,8 +139,11 @@ __device__ __forceinline__ void page_token_scores(const SelectParams& p, const f
 // Phase 1 on its own grid (rows x page splits), one page per thread: the
 // scores go to p.scores_out, which the selection launch then reads as its
 // scores_in.
-__global__ void __launch_bounds__(kScoreThreads) aspire_page_scores_kernel(SelectParams p) {
-  pdl_begin();
+__global__ void __launch_bounds__(kScoreThreads, 8) aspire_page_scores_kernel(SelectParams p) {
+  // The selection launch that follows is released only after this CTA's
+  // scores are stored (or it has no page): released at the start, its
+  // waiting CTAs took SM slots from the scoring CTAs.
+  pdl_wait();
   __shared__ float lse_s[2][kMaxSelHeads];
   const int b = blockIdx.x;
   const int src_row = p.row_ids ? p.row_ids[b] : b;
@@ -176,6 +179,7 @@ __global__ void __launch_bounds__(kScoreThreads) aspire_page_scores_kernel(Selec
 #pragma unroll
     for (int i = 0; i < w; ++i) tok[i] = tok[i] + tok[i + w];
   p.scores_out[int64_t(b) * pps + pg] = tok[0] + (-(float(pg) * 1e-7f));
+  pdl_launch_dependents();
 }
 
 __global__ void __launch_bounds__(kSelThreads) aspire_select_pages_kernel(SelectParams p) {
@@ -187,7 +191,7 @@ __global__ void __launch_bounds__(kSelThreads) aspire_select_pages_kernel(Select
   __shared__ uint32_t hist[256];
   __shared__ uint32_t sh_prefix, sh_remaining;
   __shared__ int sh_count;
-  __shared__ int scan_buf[kSelThreads];
+  __shared__ int scan_buf[kSelThreads / 32];
 
   const int b = blockIdx.x;  // output row
   const int tid = threadIdx.x;
@@ -198,12 +202,25 @@ __global__ void __launch_bounds__(kSelThreads) aspire_select_pages_kernel(Select
   // Recent-page seeding (order_by_page) ranks pages by the given scores
   // alone: no forced trailing pages.
   const int last_start = p.order_by_page ? np : max(np - p.L, 0);
-  for (int pg = tid; pg < pps; pg += blockDim.x) {
-    float score = p.scores_in[int64_t(b) * pps + pg];
-    if (p.scores_out) p.scores_out[int64_t(b) * pps + pg] = score;
-    if (pg >= last_start && pg < np) score = INFINITY;
-    if (pg >= np) score = -INFINITY;
-    keys[pg] = order_key(score);
+  // Four scores per thread in flight at a time (one round trip instead of four).
+  constexpr int kLoadBatch = 4;
+  for (int pg0 = tid; pg0 < pps; pg0 += kLoadBatch * blockDim.x) {
+    float sc[kLoadBatch];
+#pragma unroll
+    for (int u = 0; u < kLoadBatch; ++u) {
+      const int pg = pg0 + u * blockDim.x;
+      sc[u] = pg < pps ? p.scores_in[int64_t(b) * pps + pg] : 0.f;
+    }
+#pragma unroll
+    for (int u = 0; u < kLoadBatch; ++u) {
+      const int pg = pg0 + u * blockDim.x;
+      if (pg >= pps) break;
+      float score = sc[u];
+      if (p.scores_out) p.scores_out[int64_t(b) * pps + pg] = score;
+      if (pg >= last_start && pg < np) score = INFINITY;
+      if (pg >= np) score = -INFINITY;
+      keys[pg] = order_key(score);
+    }
   }
   __syncthreads();
 
@@ -277,17 +294,30 @@ __global__ void __launch_bounds__(kSelThreads) aspire_select_pages_kernel(Select
   int eq_local = 0;
   if (valid > 0)
     for (int i = i0; i < i1; ++i) eq_local += (keys[i] == T);
-  scan_buf[tid] = eq_local;
   if (tid == 0) sh_count = 0;
-  __syncthreads();
-  // Exclusive scan of eq counts (Hillis-Steele over kSelThreads entries).
-  for (int off = 1; off < kSelThreads; off <<= 1) {
-    const int v = (tid >= off) ? scan_buf[tid - off] : 0;
-    __syncthreads();
-    scan_buf[tid] += v;
-    __syncthreads();
+  // Exclusive scan of eq counts: within each warp by shuffles, then over the
+  // warp totals.
+  const int lane = tid & 31, warp = tid >> 5;
+  int incl = eq_local;
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const int v = __shfl_up_sync(0xffffffffu, incl, off);
+    if (lane >= off) incl += v;
   }
-  int eq_before = scan_buf[tid] - eq_local;
+  if (lane == 31) scan_buf[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    constexpr int kWarps = kSelThreads / 32;
+    int w = lane < kWarps ? scan_buf[lane] : 0;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const int v = __shfl_up_sync(0xffffffffu, w, off);
+      if (lane >= off) w += v;
+    }
+    if (lane < kWarps) scan_buf[lane] = w;  // inclusive over warps
+  }
+  __syncthreads();
+  int eq_before = (warp > 0 ? scan_buf[warp - 1] : 0) + incl - eq_local;
   const int32_t* bt = p.block_table + int64_t(b) * p.block_table_stride;
   if (valid > 0) {
     for (int i = i0; i < i1; ++i) {
@@ -307,34 +337,22 @@ __global__ void __launch_bounds__(kSelThreads) aspire_select_pages_kernel(Select
   const int count = min(sh_count, valid);
   if (tid == 0 && sh_count != valid && p.status) atomicOr(p.status, ASPIRE_STATUS_BAD_ROW);
 
-  // ---------------- Phase 3: ascending sort of the selected ids ----------------
-  int n2 = 1;
-  while (n2 < count) n2 <<= 1;
-  for (int i = count + tid; i < n2; i += blockDim.x) sortbuf[i] = INT32_MAX;
-  __syncthreads();
-  for (int size = 2; size <= n2; size <<= 1) {
-    for (int stride = size >> 1; stride > 0; stride >>= 1) {
-      for (int i = tid; i < n2; i += blockDim.x) {
-        const int j = i ^ stride;
-        if (j > i) {
-          const bool up = (i & size) == 0;
-          const int a = sortbuf[i], c = sortbuf[j];
-          if ((a > c) == up) {
-            sortbuf[i] = c;
-            sortbuf[j] = a;
-          }
-        }
-      }
-      __syncthreads();
-    }
-  }
+  // ---------------- Phase 3: ascending order of the selected ids ----------------
+  // Each selected id goes straight to its rank (the ids below it plus the
+  // equal ids picked before it): one pass over at most k ids per id, no
+  // sorting network.  The tail of the row is zero.
   int32_t* row_out = p.table_out + int64_t(b) * p.table_stride;
-  for (int c = tid; c < p.table_width; c += blockDim.x) {
-    int32_t v = 0;
-    if (c < count && c < p.subset_cache_size)
-      v = p.order_by_page ? bt[min(sortbuf[c], p.block_table_cols - 1)] : sortbuf[c];
-    row_out[c] = v;
+  const int width = min(p.table_width, p.subset_cache_size);
+  for (int j = tid; j < count; j += blockDim.x) {
+    const int x = sortbuf[j];
+    int r = 0;
+    for (int i = 0; i < count; ++i) {
+      const int y = sortbuf[i];
+      r += (y < x) || (y == x && i < j);
+    }
+    if (r < width) row_out[r] = p.order_by_page ? bt[min(x, p.block_table_cols - 1)] : x;
   }
+  for (int c = count + tid; c < p.table_width; c += blockDim.x) row_out[c] = 0;
   if (tid == 0) p.counts_out[b] = reported;
 }
 
