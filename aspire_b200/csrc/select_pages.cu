@@ -83,12 +83,15 @@ __device__ __forceinline__ void load_page_logits(const float* src, bool vec, int
     for (int i = 0; i < kPageSize; ++i) v[i] = (t0 + i < max_seq_len) ? src[i] : -INFINITY;
   }
 }
-// logit * sm_scale*log2(e) in the dump's own type: an fp16 tensor times a
-// scalar is computed in fp32 and rounded back to fp16; an fp32 one stays fp32.
-__device__ __forceinline__ float scaled_logit(float f, float scale, const __half*) {
-  return __half2float(__float2half_rn(f * scale));
+// logit * sm_scale*log2(e) in the dump's own type, two at a time: an fp16
+// tensor times a scalar is computed in fp32 and rounded back to fp16; an fp32
+// one stays fp32.
+__device__ __forceinline__ float2 scaled_logits(float a, float b, float scale, const __half*) {
+  return __half22float2(__floats2half2_rn(a * scale, b * scale));
 }
-__device__ __forceinline__ float scaled_logit(float f, float scale, const float*) { return f * scale; }
+__device__ __forceinline__ float2 scaled_logits(float a, float b, float scale, const float*) {
+  return make_float2(a * scale, b * scale);
+}
 
 // Token scores of page pg of one row: tok[t] = sum over the dump's slots of
 // max_h exp2(norm), norm = scaled_logit - lse (NaN -> -inf); zero past
@@ -119,11 +122,13 @@ __device__ __forceinline__ void page_token_scores(const SelectParams& p, const f
       const float ls = lse_s[kSlots == 2 ? s : 1][h];
       float v[kPageSize];
       load_page_logits(src, vec, t0, p.max_seq_len, v);
+      // NaN (a -inf logit under a -inf LSE) counts as -inf: fmaxf returns
+      // its other operand for a NaN, and every maximum starts at -inf.
 #pragma unroll
-      for (int i = 0; i < kPageSize; ++i) {
-        float n = scaled_logit(v[i], p.scale_log2, src) - ls;
-        if (isnan(n)) n = -INFINITY;
-        mx[s][i] = fmaxf(mx[s][i], n);
+      for (int i = 0; i < kPageSize; i += 2) {
+        const float2 r = scaled_logits(v[i], v[i + 1], p.scale_log2, src);
+        mx[s][i] = fmaxf(mx[s][i], r.x - ls);
+        mx[s][i + 1] = fmaxf(mx[s][i + 1], r.y - ls);
       }
     }
   }
