@@ -112,28 +112,57 @@ def measured_peaks():
 
 
 class ClockSampler:
-    """Samples nvidia-smi clocks and throttle reasons while the timed region runs."""
+    """Samples the SM clock and the clock-event (throttle) reasons while the
+    timed region runs: through NVML every 20 ms (read-only queries on the
+    device with this CUDA device's PCI bus id), else nvidia-smi every 0.2 s."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, gpu_index: int):
-        self.gpu_index = gpu_index
+    def __init__(self, device):
+        self.device = torch.device(device)
+        self.gpu_index = self.device.index or 0
         self.rows = []
+        self.source = "nvidia-smi"
         self._stop = threading.Event()
         self._thread = None
+        self._nvml = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            props = torch.cuda.get_device_properties(self.device)
+            bus = f"{props.pci_domain_id:08x}:{props.pci_bus_id:02x}:{props.pci_device_id:02x}.0"
+            self._handle = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+            self._nvml = pynvml
+            self.source = "nvml"
+        except Exception:
+            self._nvml = None
+
+    def _sample_nvml(self):
+        nv = self._nvml
+        sm = nv.nvmlDeviceGetClockInfo(self._handle, nv.NVML_CLOCK_SM)
+        mx = nv.nvmlDeviceGetMaxClockInfo(self._handle, nv.NVML_CLOCK_SM)
+        bits = nv.nvmlDeviceGetCurrentClocksEventReasons(self._handle)
+        masks = (nv.nvmlClocksEventReasonHwSlowdown, nv.nvmlClocksEventReasonHwThermalSlowdown,
+                 nv.nvmlClocksEventReasonSwThermalSlowdown, nv.nvmlClocksEventReasonSwPowerCap)
+        flags = ["Active" if bits & m else "Not Active" for m in masks]
+        self.rows.append([str(self.gpu_index), str(sm), str(mx), "", hex(bits)] + flags)
 
     def _run(self):
         while not self._stop.is_set():
             try:
-                out = subprocess.run(["nvidia-smi", f"--id={self.gpu_index}", f"--query-gpu={self.FIELDS}",
-                                      "--format=csv,noheader,nounits"], capture_output=True, text=True, timeout=5)
-                for line in out.stdout.strip().splitlines():
-                    self.rows.append([x.strip() for x in line.split(",")])
+                if self._nvml is not None:
+                    self._sample_nvml()
+                else:
+                    out = subprocess.run(["nvidia-smi", f"--id={self.gpu_index}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits"], capture_output=True, text=True,
+                                         timeout=5)
+                    for line in out.stdout.strip().splitlines():
+                        self.rows.append([x.strip() for x in line.split(",")])
             except Exception:
                 pass
-            self._stop.wait(0.2)
+            self._stop.wait(0.02 if self._nvml is not None else 0.2)
 
     def __enter__(self):
         self._thread = threading.Thread(target=self._run, daemon=True)
@@ -157,7 +186,7 @@ class ClockSampler:
                 if val.strip().lower() == "active":
                     reasons.add(name)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": sorted(reasons), "samples": len(self.rows)}
+                "reasons": sorted(reasons), "samples": len(self.rows), "source": self.source}
 
 
 # ----------------------------------------------------------------------------- workload
@@ -329,8 +358,11 @@ def kernel_roofline(hp: HotPath, steps: int, peak: float, peak_kind: str):
     torch.cuda.synchronize()
     # A CUDA graph of back-to-back launches timed between two events on the
     # launching stream: device time only, under the sustained load of a step;
-    # the average over three replays (90+ launches).
-    ms = graph_time(lambda: hp.mixed.run(q, hp.kv, out=out), max(steps, 30), replays=3)
+    # the average over three replays (90+ launches), and the median of three
+    # such measurements (the first, right after the timed steps, can run a few
+    # per cent slow while the power cap settles).
+    ms = statistics.median(graph_time(lambda: hp.mixed.run(q, hp.kv, out=out), max(steps, 30), replays=3)
+                           for _ in range(3))
     bytes_ = hp.lay.algorithmic_bytes()
     achieved = bytes_ / (ms * 1e-3) / 1e9
     # DRAM bytes (read + write) per algorithmic byte of the mixed layer-call,
@@ -986,7 +1018,7 @@ def main():
     sb = step_bytes(lay, full, CFG["n_layer"], hp.kv_stride, hp.k_sel)
 
     peak, peak_kind = measured_peaks()
-    with ClockSampler(local_rank) as clocks:
+    with ClockSampler(device) as clocks:
         ms = time_device(hp.graph.replay, args.steps, args.warmup, dist_on)
     t = torch.tensor([ms], device=device)
     tot_bytes = torch.tensor([float(sb["total"])], device=device)
