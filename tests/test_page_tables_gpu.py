@@ -8,7 +8,7 @@ import numpy as np
 import pytest
 import torch
 
-from aspire_b200.attention import HolisticAttentionWrapper, first_last_dump_jit_args
+from aspire_b200.attention import HolisticAttentionWrapper, dump_jit_args, first_last_dump_jit_args
 from aspire_b200.kv_ops import append_kv
 from aspire_b200.workloads import fill_tensors, full_context_layout, last_page_lens, make_layout
 from gpu_helpers import assert_attention_close, assert_dump_close, oracle_attention
@@ -84,6 +84,58 @@ def test_refresh_dump_page_tables_match_flat_list(cuda_device):
     ref_out, ref_lse, ref_dump = oracle_attention(full, q, kv, dump_stride=stride)
     assert_attention_close(outs[1][0], outs[1][1], ref_out, ref_lse)
     assert_dump_close(outs[1][2], ref_dump, full, stride)
+
+
+def test_last_token_flagged_dump_device_plan_tables_graph(cuda_device):
+    """The last-token dump with per-row mode flags into an fp32 buffer (the
+    base backend's variant), planned on the device inside a CUDA graph with
+    the pages read from the tables: bit-identical to the host-planned
+    flat-list launch, rows flagged off untouched, and the oracle's dump."""
+    dev = cuda_device
+    lay = make_layout(batch=6, ctx=2000, num_qo_heads=32, num_kv_heads=8, draft_fraction=0.5, budget_pages=24,
+                      seed=41, block_table="random")
+    full = full_context_layout(lay)
+    q, kv = fill_tensors(full, device=dev, seed=42)
+    stride = lay.pages_per_row * 16
+    H = full.num_qo_heads
+    flags = torch.tensor([1, 0, 1, 1, 0, 1], dtype=torch.int32, device=dev)
+    jit = dump_jit_args("last_token", use_mode_flags=True, dump_buffer_dtype=torch.float32)
+    new_dump = lambda: torch.full((full.batch * H * stride,), float("-inf"), dtype=torch.float32, device=dev)  # noqa: E731
+
+    w1 = HolisticAttentionWrapper(torch.empty(1, device=dev), jit_args=jit)
+    _plan(w1, full, dev, torch.from_numpy(full.kv_indices).to(dev))
+    d1 = new_dump()
+    out1, lse1 = w1.run(q, kv, d1, flags, H, stride, return_lse=True)
+
+    w2 = HolisticAttentionWrapper(torch.empty(1, device=dev), jit_args=jit)
+    _, draft, bt = _tables(full, dev)
+    w2.set_page_tables(torch.ones(full.batch, dtype=torch.int32, device=dev), draft, bt)
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a, dtype=np.int32)).to(dev)  # noqa: E731
+    qo, kvp, lpl = t(full.qo_indptr), t(full.kv_indptr), t(last_page_lens(full))
+    d2 = new_dump()
+    out2 = torch.empty_like(q)
+    lse2 = torch.empty(q.shape[0], H, dtype=torch.float32, device=dev)
+
+    def step():
+        w2.plan_device(qo, kvp, lpl, H, full.num_kv_heads, 128, 16, causal=True)
+        w2.run(q, kv, d2, flags, H, stride, out=out2, lse=lse2)
+
+    step()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step()
+    d2.fill_(float("-inf"))
+    out2.zero_()
+    graph.replay()
+    torch.cuda.synchronize()
+    assert w2.device_status() == 0
+    assert torch.equal(d1, d2) and torch.equal(out1, out2) and torch.equal(lse1, lse2)
+    ref_out, ref_lse, ref_dump = oracle_attention(full, q, kv, dump_stride=stride, dump_kind="last_token",
+                                                  dump_dtype=torch.float32, dump_flags=flags.cpu())
+    assert_attention_close(out2, lse2, ref_out, ref_lse)
+    assert_dump_close(d2, ref_dump, full, stride, dump_kind="last_token", dump_flags=flags.cpu())
+    del graph
 
 
 def test_append_page_tables_match_flat_list(cuda_device):
