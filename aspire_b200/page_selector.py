@@ -92,6 +92,17 @@ class PageSelector:
                 or counts_out.shape[0] < batch:
             raise ValueError("block_table / num_pages / outputs have fewer rows than the batch")
         stride = self._kv_stride if kv_stride is None else int(kv_stride)
+        # The scores land in scores_out, or in a scratch buffer of `batch` rows:
+        # the selector's own holds max_batch_size rows, so larger batches (the
+        # layered entry point) take a temporary one, as the reference's
+        # _get_scores_buffer does (page_selector.py:64-67).
+        if scores_out is not None and (scores_out.dtype != torch.float32 or not scores_out.is_contiguous()
+                                       or scores_out.dim() != 2 or scores_out.shape[0] < batch
+                                       or scores_out.shape[1] != self.pages_per_slot):
+            raise ValueError("scores_out must be a contiguous fp32 [>= batch, pages_per_slot] tensor")
+        scores_ws = self._scores
+        if scores_in is None and scores_out is None and batch > self._scores.shape[0]:
+            scores_ws = torch.empty(batch, self.pages_per_slot, dtype=torch.float32, device=self.device)
         if dump is not None:
             if dump.dtype not in (torch.float16, torch.float32) or not dump.is_contiguous():
                 raise ValueError("dump buffer must be a contiguous float16 or float32 tensor")
@@ -132,7 +143,7 @@ class PageSelector:
         a.table_width = int(table_width)
         a.counts_out = counts_out.data_ptr()
         a.scores_out = ptr(scores_out)
-        a.scores_ws = self._scores.data_ptr()
+        a.scores_ws = scores_ws.data_ptr()
         a.status = ptr(status)
         a.order_by_page = 1 if order_by_page else 0
         stream = torch.cuda.current_stream(self.device).cuda_stream
