@@ -174,6 +174,7 @@ class AspireIndicesArgs(ctypes.Structure):
         ("indices_out", ctypes.c_void_p),
         ("indptr_out", ctypes.c_void_p),
         ("status", ctypes.c_void_p),
+        ("indices_capacity", ctypes.c_int64),
     ]
 
 

@@ -565,6 +565,8 @@ int aspire_build_unified_indices(const AspireIndicesArgs* a, void* stream) {
   if (a->draft_cols < 0 || a->verify_cols < 0 || a->draft_stride < a->draft_cols ||
       a->verify_stride < a->verify_cols)
     return set_error(ASPIRE_ERR_INVALID, "aspire_build_unified_indices: bad table geometry");
+  if (a->indices_capacity < 0)
+    return set_error(ASPIRE_ERR_INVALID, "aspire_build_unified_indices: negative indices_capacity");
   IndicesParams p;
   p.mode_flags = a->mode_flags;
   p.draft_indices = a->draft_indices;
@@ -578,6 +580,7 @@ int aspire_build_unified_indices(const AspireIndicesArgs* a, void* stream) {
   p.indices_out = a->indices_out;
   p.indptr_out = a->indptr_out;
   p.status = a->status;
+  p.indices_capacity = a->indices_capacity;
   return launch(aspire_build_indices_kernel, dim3(a->batch), dim3(kIndicesThreads), 0,
                 static_cast<cudaStream_t>(stream), "aspire_build_indices_kernel launch", p);
 }

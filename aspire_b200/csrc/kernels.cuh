@@ -114,6 +114,7 @@ struct IndicesParams {
   int32_t* indices_out;
   int32_t* indptr_out;
   uint32_t* status;
+  int64_t indices_capacity;
 };
 
 struct SpillParams {

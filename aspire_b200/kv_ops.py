@@ -156,6 +156,7 @@ def build_unified_indices(mode_flags: torch.Tensor, draft_indices: torch.Tensor,
     a.indices_out = paged_kv_indices.data_ptr()
     a.indptr_out = paged_kv_indptr.data_ptr()
     a.status = status.data_ptr() if status is not None else None
+    a.indices_capacity = paged_kv_indices.numel()
     stream = torch.cuda.current_stream(mode_flags.device).cuda_stream
     rc = _capi.load_library().aspire_build_unified_indices(ctypes.byref(a), ctypes.c_void_p(stream))
     _capi.check(rc, "aspire_build_unified_indices")

@@ -437,6 +437,8 @@ typedef struct AspireIndicesArgs {
   int32_t* indices_out;           /* int32 [sum of the rows' page counts]                 */
   int32_t* indptr_out;            /* int32 [batch + 1]: exclusive prefix sum              */
   uint32_t* status;               /* optional device status word                          */
+  int64_t indices_capacity;       /* entries of indices_out: pages that would land past
+                                     it are not written (ASPIRE_STATUS_BAD_ROW)          */
 } AspireIndicesArgs;
 
 /*
@@ -445,8 +447,10 @@ typedef struct AspireIndicesArgs {
  * in row order, with indptr the prefix sum of the counts.  Replaces
  * build_unified_indices (aspire/models/sparse_draft_runner.py:126-153) and
  * its Triton _copy_indices_kernel (:93-123).  A count larger than its table's
- * width copies the width and sets ASPIRE_STATUS_BAD_ROW.  With batch 0 only
- * indptr_out[0] = 0 is written, as the reference does.
+ * width copies the width, a negative count counts as 0, and a page that
+ * would land at or past indices_capacity is not written; each sets
+ * ASPIRE_STATUS_BAD_ROW.  With batch 0 only indptr_out[0] = 0 is written, as
+ * the reference does.
  */
 ASPIRE_API int aspire_build_unified_indices(const AspireIndicesArgs* args, void* stream);
 

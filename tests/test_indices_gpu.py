@@ -74,3 +74,33 @@ def test_indices_empty_batch_writes_only_indptr0(cuda_device):
     indptr = torch.full((2,), 4, dtype=torch.int32, device=cuda_device)
     build_unified_indices(e, e.view(0, 1), e.view(0, 1), e, e, e, indptr)
     assert indptr.tolist() == [0, 4]
+
+
+def test_indices_stop_at_the_output_capacity(cuda_device):
+    """Counts summing past the output buffer (a malformed step) write nothing
+    beyond it: the buffer handed over is a view of a larger one, whose guard
+    tail must keep its fill; a negative count counts as 0.  Both report
+    BAD_ROW; rows that fit are copied as usual."""
+    from aspire_b200._capi import STATUS_BAD_ROW
+
+    dev = cuda_device
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a, dtype=np.int32)).to(dev)  # noqa: E731
+    mode = np.array([1, 1, 0, 1], np.int32)
+    verify = (np.arange(4 * 16, dtype=np.int32).reshape(4, 16) + 1000)
+    draft = (np.arange(4 * 8, dtype=np.int32).reshape(4, 8) + 5000)
+    vn = np.array([6, -3, 0, 16], np.int32)
+    dn = np.array([0, 0, 8, 0], np.int32)
+    backing = torch.full((20 + 64,), -7, dtype=torch.int32, device=dev)
+    indices = backing[:20]
+    indptr = torch.zeros(5, dtype=torch.int32, device=dev)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    build_unified_indices(t(mode), t(draft), t(verify), t(dn), t(vn), indices, indptr, status=status)
+    torch.cuda.synchronize()
+    assert int(status.item()) & STATUS_BAD_ROW
+    # Row 1's -3 counts as 0; row 3 starts at 14 and has room for 6 of its 16.
+    assert indptr.tolist() == [0, 6, 6, 14, 30]
+    got = backing.cpu().numpy()
+    np.testing.assert_array_equal(got[:6], verify[0, :6])
+    np.testing.assert_array_equal(got[6:14], draft[2, :8])
+    np.testing.assert_array_equal(got[14:20], verify[3, :6])
+    assert (got[20:] == -7).all(), "wrote past the output buffer"
