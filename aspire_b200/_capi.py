@@ -91,6 +91,12 @@ class AspireAttnArgs(ctypes.Structure):
         ("dump_kind", ctypes.c_int32),
         ("dump_dtype", ctypes.c_int32),
         ("dump_flags", ctypes.c_void_p),
+        ("k_new", ctypes.c_void_p),
+        ("v_new", ctypes.c_void_p),
+        ("k_new_stride_n", ctypes.c_int64),
+        ("k_new_stride_h", ctypes.c_int64),
+        ("v_new_stride_n", ctypes.c_int64),
+        ("v_new_stride_h", ctypes.c_int64),
     ]
 
 

@@ -318,8 +318,14 @@ class HolisticAttentionWrapper:
         out: Optional[torch.Tensor] = None,
         return_lse: bool = False,
         lse: Optional[torch.Tensor] = None,
+        append: Optional[Tuple[torch.Tensor, torch.Tensor]] = None,
         **kwargs,
     ) -> Union[torch.Tensor, Tuple[torch.Tensor, torch.Tensor]]:
+        """Runs the planned program.  ``append=(k_new, v_new)`` (bf16
+        [tokens, num_kv_heads, 128], the queries' own keys and values) also
+        writes each row's new tokens into the cache before the row's keys are
+        read, as ``append_kv`` with the same qo_indptr and page source would
+        (one launch instead of two); host plans of tcgen05 decode rows only."""
         if self._plan_info is None:
             raise RuntimeError("run() before plan()/plan_host()")
         kv = _unpack_paged_kv_cache(paged_kv_cache, self._kv_layout)
@@ -401,6 +407,16 @@ class HolisticAttentionWrapper:
         a.dump = dump.data_ptr() if dump is not None else None
         a.dump_num_heads = dump_heads
         a.dump_kv_stride = dump_stride
+        if append is not None:
+            k_new, v_new = append
+            for name, t in (("k_new", k_new), ("v_new", v_new)):
+                if t.dtype != torch.bfloat16 or t.dim() != 3 or t.stride(2) != 1 or t.device != q.device:
+                    raise ValueError(f"{name} must be a bf16 [tokens, num_kv_heads, 128] tensor on q's device")
+                if t.shape[1] != self._num_kv_heads or t.shape[2] != q.shape[2] or t.shape[0] < q.shape[0]:
+                    raise ValueError(f"{name} shape {tuple(t.shape)} does not match the plan")
+            a.k_new, a.v_new = k_new.data_ptr(), v_new.data_ptr()
+            a.k_new_stride_n, a.k_new_stride_h = k_new.stride(0), k_new.stride(1)
+            a.v_new_stride_n, a.v_new_stride_h = v_new.stride(0), v_new.stride(1)
         a.dump_kind = _capi.DUMP_LAST_TOKEN if self._dump_kind == "last_token" else _capi.DUMP_FIRST_LAST
         a.dump_dtype = _capi.DUMP_F32 if dump is not None and dump.dtype == torch.float32 else _capi.DUMP_F16
         a.dump_flags = dump_flags.data_ptr() if dump_flags is not None else None

@@ -34,6 +34,11 @@ struct AttnParams {
   uint32_t* status;          // int workspace (first word)
   float* partial_o;          // float workspace
   uint64_t wait_ns;          // bound of one pipeline wait of the tcgen05 kernel (ns)
+  // Optional fused KV append (decode items of the tcgen05 kernel): the rows'
+  // new K / V tokens, bf16 [tokens, num_kv_heads, 128] with these strides.
+  const __nv_bfloat16* k_new;
+  const __nv_bfloat16* v_new;
+  int64_t k_new_stride_n, k_new_stride_h, v_new_stride_n, v_new_stride_h;
 };
 
 // Page id of logical page lp of a row: from the flat page list at the row's

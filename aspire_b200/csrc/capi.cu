@@ -204,6 +204,17 @@ int check_attention_args(const AspireAttnArgs* a, const AspirePlanInfo* plan, co
     return set_error(ASPIRE_ERR_INVALID, w + ": dump buffer not aligned to its element type");
   if (a->q_rows <= 0 || a->q_rows > INT32_MAX)
     return set_error(ASPIRE_ERR_INVALID, w + ": q_rows (rows of q) must be set");
+  if (a->k_new || a->v_new) {
+    if (!a->k_new || !a->v_new) return set_error(ASPIRE_ERR_INVALID, w + ": fused append needs k_new and v_new");
+    if (plan->on_device || plan->num_items_prefill > 0 || plan->num_items_gather > 0 || !plan->tc_enabled)
+      return set_error(ASPIRE_ERR_INVALID,
+                       w + ": fused append needs a host plan of tcgen05 decode items only (no prefill rows, "
+                           "no CUDA-core rows); append with aspire_append_kv first otherwise");
+    if ((reinterpret_cast<uintptr_t>(a->k_new) | reinterpret_cast<uintptr_t>(a->v_new)) & 15)
+      return set_error(ASPIRE_ERR_INVALID, w + ": k_new / v_new not 16-byte aligned");
+    if ((a->k_new_stride_n | a->k_new_stride_h | a->v_new_stride_n | a->v_new_stride_h) & 7)
+      return set_error(ASPIRE_ERR_INVALID, w + ": k_new / v_new strides must be multiples of 8 elements");
+  }
   const int group = a->num_qo_heads / a->num_kv_heads;
   const bool run_tc = plan->tc_enabled && group <= kTcQTile;
   if (run_tc && ((reinterpret_cast<uintptr_t>(a->out) & 15) || ((a->o_stride_n | a->o_stride_h) & 7)))
@@ -372,6 +383,12 @@ int aspire_mixed_attention(const AspireAttnArgs* a, const AspirePlanInfo* plan, 
   p.dump_kind = a->dump_kind;
   p.dump_f32 = a->dump_dtype == ASPIRE_DUMP_F32 ? 1 : 0;
   p.dump_flags = a->dump_flags;
+  p.k_new = static_cast<const __nv_bfloat16*>(a->k_new);
+  p.v_new = static_cast<const __nv_bfloat16*>(a->v_new);
+  p.k_new_stride_n = a->k_new_stride_n;
+  p.k_new_stride_h = a->k_new_stride_h;
+  p.v_new_stride_n = a->v_new_stride_n;
+  p.v_new_stride_h = a->v_new_stride_h;
   const float sm_scale = a->sm_scale > 0.f ? a->sm_scale : 1.0f / std::sqrt(float(kHeadDim));
   p.scale_log2 = sm_scale * 1.44269504088896340736f;
   p.num_qo_heads = a->num_qo_heads;

@@ -128,6 +128,45 @@ __device__ __forceinline__ int next_item_with_tiles(const AttnParams& p, Sh& sm,
   }
 }
 
+// ------------------------------------------------------------------ fused append
+// Writes the item's share of its row's new tokens (K for kv_sel 0, V for 1)
+// into the cache before the item's tiles are requested: the positions
+// kv_len - q_len + i (i < q_len) inside the item's key range, at the row's own
+// pages, as aspire_append_kv places them.  The chunks of a decode group
+// partition its key range, so every new token is written once, by the item
+// that reads it; half a warp copies one 256-byte token row.  The writes are
+// fenced into the async proxy before the warp's TMA loads.
+__device__ __forceinline__ void append_new_tokens(const AttnParams& p, const WorkItem& it, int kv_sel, int lane) {
+  const int64_t first_new = int64_t(it.kv_len) - it.q_len;
+  int64_t lo = first_new > it.tok_begin ? first_new : int64_t(it.tok_begin);
+  lo = lo > 0 ? lo : 0;
+  const int64_t hi = it.tok_end;
+  const __nv_bfloat16* src_base = kv_sel ? p.v_new : p.k_new;
+  const int64_t sn = kv_sel ? p.v_new_stride_n : p.k_new_stride_n;
+  const int64_t sh = kv_sel ? p.v_new_stride_h : p.k_new_stride_h;
+  __nv_bfloat16* cache = const_cast<__nv_bfloat16*>(p.kv);
+  const int col = (lane & 15) * 8;
+  for (int64_t pos = lo + (lane >> 4); pos < hi; pos += 2) {
+    const int64_t t = int64_t(it.q_start) + (pos - first_new);
+    if (t >= p.q_rows) {
+      record_status(p.status, ASPIRE_STATUS_BAD_ROW);
+      continue;
+    }
+    const int32_t page = row_page(p.kv_indices, it.kv_page_base, p.mode_flags, p.draft_table, p.draft_stride,
+                                  p.block_table, p.block_table_stride, it.row, int(pos / kPageSize));
+    if (page < 0 || int64_t(page) >= p.num_pages_total) {
+      record_status(p.status, ASPIRE_STATUS_BAD_PAGE);
+      continue;
+    }
+    const __nv_bfloat16* src = src_base + t * sn + int64_t(it.kv_head) * sh + col;
+    const int64_t dst = ((int64_t(page) * 2 + kv_sel) * kPageSize + pos % kPageSize) * int64_t(p.num_kv_heads) *
+                            kHeadDim + int64_t(it.kv_head) * kHeadDim + col;
+    *reinterpret_cast<uint4*>(cache + dst) = *reinterpret_cast<const uint4*>(src);
+  }
+  ptx::fence_proxy_async_global();
+  __syncwarp();
+}
+
 // ------------------------------------------------------------------ producers
 // Lane pg (< 8) owns page pg of every tile: it reads the page id one tile
 // ahead (the read overlaps the wait for a free slot) and issues the page's two
@@ -150,6 +189,11 @@ __device__ bool run_producer(const AttnParams& p, const CUtensorMap* tmap, Sh& s
     if (ii < 0) break;
     const WorkItem it = load_item(p.plan, ii);
     if (!item_valid(p, it, max_rows)) continue;
+    // The new tokens sit in the item's last tile or two: they are written just
+    // before the first tile that holds one is requested, while the earlier
+    // tiles stream (the writes overlap the wait for a free ring slot).
+    const int64_t first_new = (p.k_new != nullptr && it.kind == 1) ? int64_t(it.kv_len) - it.q_len : INT64_MAX;
+    bool appended = first_new >= it.tok_end;
     const int nt = n_tiles_of(it);
     const int first_page = it.tok_begin / kPageSize;
     const int end_page = (it.tok_end + kPageSize - 1) / kPageSize;
@@ -165,6 +209,10 @@ __device__ bool run_producer(const AttnParams& p, const CUtensorMap* tmap, Sh& s
       if (t + 1 < nt) next_id = page_id(t + 1);
       const int s = g % STAGES;
       const uint32_t ph = (g / STAGES) & 1;
+      if (!appended && int64_t(it.tok_begin) + int64_t(t + 1) * kTile > first_new) {
+        append_new_tokens(p, it, kv_sel, lane);
+        appended = true;
+      }
       if (!wait_bar(sm, empty[s], ph ^ 1, p.status)) {
         ok = false;
         break;

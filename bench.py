@@ -9,6 +9,8 @@ batch 64, 32k context, sparse budget 128 pages, refresh layer -2):
     q_len = U{2..8} + 1, causal);
   * the refresh layer: append + full-context attention of every row with the
     first/last logit dump;
+  (the append runs inside the attention launch, `run(..., append=(k, v))`;
+  `--separate-append` launches it as its own kernel before each attention)
   * page scoring + top-k re-selection written in place into the draft table.
 
 Every layer reads one resident single-layer KV cache (8.7 GB at TP 1, far
@@ -81,6 +83,8 @@ def parse_args():
                     help="arange: the reference engine's contiguous per-row pages; random: scattered pages")
     ap.add_argument("--workload", default="step", choices=["step", "prefill", "sweep", "decode"])
     ap.add_argument("--no-decode", action="store_true", help="skip the end-to-end decode leg of the step run")
+    ap.add_argument("--separate-append", action="store_true",
+                    help="launch each layer's KV append as its own kernel instead of inside the attention launch")
     ap.add_argument("--decode-config", type=int, default=2, choices=[2, 3, 4],
                     help="the reference's end-to-end config the decode leg runs (2 by default)")
     ap.add_argument("--decode-batch", type=int, default=None)
@@ -220,13 +224,14 @@ def step_bytes(lay, full, n_layer: int, kv_stride: int, k: int) -> dict:
 class HotPath:
     """All device state of the benchmark step, driven through the public API."""
 
-    def __init__(self, device, lay, full, lpl_mixed, lpl_full):
+    def __init__(self, device, lay, full, lpl_mixed, lpl_full, fused_append: bool = True):
         from aspire_b200.attention import HolisticAttentionWrapper, first_last_dump_jit_args
         from aspire_b200.kv_ops import append_kv
         from aspire_b200.page_selector import PageSelectorFirstLastAvg
         from aspire_b200.workloads import fill_tensors
 
         self.append_kv = append_kv
+        self.fused_append = fused_append
         self.device = device
         self.lay, self.full = lay, full
         n_layer = CFG["n_layer"]
@@ -287,16 +292,22 @@ class HotPath:
                                full.num_qo_heads, full.num_kv_heads, 128, 16, causal=True)
 
     def layer(self, layer: int):
-        """Append + attention of one layer (the refresh layer with the dump)."""
+        """Append + attention of one layer (the refresh layer with the dump):
+        one launch with the append inside the attention, or the append kernel
+        and then the attention."""
+        new = (self.k_new[layer], self.v_new[layer])
+        fused = new if self.fused_append else None
         if layer == CFG["refresh_layer"]:
-            self.append_kv(self.k_new[layer], self.v_new[layer], self.qo_indptr, self.kv, None,
-                           self.full_indptr, self.full_last, 16, page_tables=self.full_tables)
+            if not self.fused_append:
+                self.append_kv(*new, self.qo_indptr, self.kv, None, self.full_indptr, self.full_last, 16,
+                               page_tables=self.full_tables)
             self.refresh.run(self.q[layer], self.kv, self.dump, self.lay.num_qo_heads, self.kv_stride,
-                             out=self.out[layer], lse=self.lse)
+                             out=self.out[layer], lse=self.lse, append=fused)
         else:
-            self.append_kv(self.k_new[layer], self.v_new[layer], self.qo_indptr, self.kv, None,
-                           self.mixed_indptr, self.mixed_last, 16, page_tables=self.mixed_tables)
-            self.mixed.run(self.q[layer], self.kv, out=self.out[layer])
+            if not self.fused_append:
+                self.append_kv(*new, self.qo_indptr, self.kv, None, self.mixed_indptr, self.mixed_last, 16,
+                               page_tables=self.mixed_tables)
+            self.mixed.run(self.q[layer], self.kv, out=self.out[layer], append=fused)
 
     def select(self):
         self.selector.select_into(self.draft_table, self.draft_counts, self.dump, self.lse, self.num_pages,
@@ -328,7 +339,7 @@ class HotPath:
         tc = bool(self.mixed.plan_info.tc_enabled)
         all_tc = tc and int(os.environ.get("ASPIRE_B200_TC_MIN_ROWS", "1") or "1") <= 1
         per_attn = (1 if tc else 0) + (0 if all_tc else 1) + 1
-        return CFG["n_layer"] * (1 + per_attn) + 2
+        return CFG["n_layer"] * ((0 if self.fused_append else 1) + per_attn) + 2
 
 
 def time_device(fn, steps, warmup, dist_on):
@@ -471,6 +482,8 @@ def breakdown(hp: HotPath) -> dict:
         "append": (lambda: hp.append_kv(hp.k_new[0], hp.v_new[0], hp.qo_indptr, hp.kv, None,
                                         hp.mixed_indptr, hp.mixed_last, 16, page_tables=hp.mixed_tables), 200),
         "mixed_attention": (lambda: hp.mixed.run(hp.q[0], hp.kv, out=hp.out[0]), 30),
+        "mixed_attention_fused_append": (lambda: hp.mixed.run(hp.q[0], hp.kv, out=hp.out[0],
+                                                              append=(hp.k_new[0], hp.v_new[0])), 30),
         "refresh_attention": (lambda: hp.refresh.run(hp.q[L - 2], hp.kv, hp.dump, hp.lay.num_qo_heads,
                                                      hp.kv_stride, out=hp.out[L - 2], lse=hp.lse), 15),
         "refresh_nodump": (lambda: hp.refresh_nodump.run(hp.q[L - 2], hp.kv, out=hp.out[L - 2], lse=hp.lse), 15),
@@ -1012,7 +1025,7 @@ def main():
     from aspire_b200 import load_library
     load_library()
     lay, full, lpl_m, lpl_f = build_workload(device, rank, world)
-    hp = HotPath(device, lay, full, lpl_m, lpl_f)
+    hp = HotPath(device, lay, full, lpl_m, lpl_f, fused_append=not args.separate_append)
     hp.plan()
     hp.capture()
     sb = step_bytes(lay, full, CFG["n_layer"], hp.kv_stride, hp.k_sel)
@@ -1067,7 +1080,9 @@ def main():
                                    "attention) + refresh layer (append + full attention + first/last dump) + page "
                                    "selection; Qwen3-8B heads 32/8/128, 36 layers, B=64, 32k ctx, draft fraction 0.5, "
                                    "verify q_len U{3..9}, budget 128 pages, one resident layer cache; pages read "
-                                   "straight from the draft / block tables (page-list build absorbed)",
+                                   "straight from the draft / block tables (page-list build absorbed); "
+                                   + ("append as its own kernel" if args.separate_append
+                                      else "append inside the attention launch"),
                        "batch": CFG["batch"], "ctx": CFG["ctx"], "tp": world, "heads_per_rank": [lay.num_qo_heads, lay.num_kv_heads],
                        "l2": "inputs larger than L2 (8.7 GB cache at TP1)", "bytes_per_step": sb},
             "roofline": roof, "breakdown": parts, "clocks": clocks.summary(), "e2e": e2e, "check": check,

@@ -185,6 +185,21 @@ typedef struct AspireAttnArgs {
   int32_t dump_kind;
   int32_t dump_dtype;
   const int32_t* dump_flags;
+  /* Optional fused KV append (NULL = none): bf16 [>= q_rows, num_kv_heads, 128]
+   * rows of the step's new keys and values (the queries' own: new token i of
+   * row b at row qo_indptr[b] + i), head_dim contiguous, strides multiples of
+   * 8 elements.
+   * Before reading a row's keys the attention writes its new tokens into the
+   * cache at positions kv_len - q_len + i of the row's pages (the page list or
+   * the page tables), exactly as aspire_append_kv with the same qo_indptr and
+   * page source does, so the separate append launch before the attention
+   * (mylib::update_kv_padded, aspire/attention/kv_ops.py:127-187) goes away.
+   * Host plans whose rows all run as tcgen05 decode items only: a plan with
+   * prefill or CUDA-core items, or a device-side plan, is rejected. */
+  const void* k_new;
+  const void* v_new;
+  int64_t k_new_stride_n, k_new_stride_h;
+  int64_t v_new_stride_n, v_new_stride_h;
 } AspireAttnArgs;
 
 /*
