@@ -241,3 +241,45 @@ def test_plan_keeps_every_query0_tile_whole(built_library, monkeypatch):
         if it["pq_begin"] < 8:
             assert max(i["tok_end"] for i in items
                        if i["pq_begin"] == it["pq_begin"] and i["kv_head"] == it["kv_head"]) == 1000
+
+
+def _attn_args(**over):
+    """Attention args with plausible, 16-byte aligned (but never dereferenced)
+    addresses; the cases below are rejected before any CUDA call."""
+    a = _capi.AspireAttnArgs()
+    a.q, a.kv_cache, a.out, a.kv_indices = 0x10000, 0x20000, 0x30000, 0x40000
+    a.q_stride_n, a.q_stride_h, a.o_stride_n, a.o_stride_h = 32 * 128, 128, 32 * 128, 128
+    a.num_pages_total, a.q_rows = 100, 12
+    a.num_qo_heads, a.num_kv_heads, a.head_dim, a.page_size = 32, 8, 128, 16
+    for k, v in over.items():
+        setattr(a, k, v)
+    return a
+
+
+def _plan_info(**over):
+    info = _capi.AspirePlanInfo()
+    info.num_qo_heads, info.num_kv_heads, info.tc_enabled = 32, 8, 1
+    for k, v in over.items():
+        setattr(info, k, v)
+    return info
+
+
+@pytest.mark.parametrize("case,args,plan,msg", [
+    ("dump_kind", dict(dump=0x50000, dump_num_heads=32, dump_kv_stride=1024, dump_kind=7), {}, b"dump_kind"),
+    ("dump_dtype", dict(dump=0x50000, dump_num_heads=32, dump_kv_stride=1024, dump_dtype=3), {}, b"dump_dtype"),
+    ("dump_f32_align", dict(dump=0x50002, dump_num_heads=32, dump_kv_stride=1024, dump_dtype=1), {},
+     b"not aligned to its element type"),
+    ("append_half", dict(k_new=0x60000), {}, b"needs k_new and v_new"),
+    ("append_device_plan", dict(k_new=0x60000, v_new=0x70000), dict(on_device=1), b"fused append"),
+    ("append_prefill", dict(k_new=0x60000, v_new=0x70000), dict(num_items_prefill=3), b"fused append"),
+    ("append_gather", dict(k_new=0x60000, v_new=0x70000), dict(num_items_gather=3), b"fused append"),
+    ("append_stride", dict(k_new=0x60000, v_new=0x70000, k_new_stride_n=1028, k_new_stride_h=128,
+                           v_new_stride_n=1024, v_new_stride_h=128), {}, b"multiples of 8"),
+    ("append_align", dict(k_new=0x60008, v_new=0x70000), {}, b"16-byte aligned"),
+])
+def test_attention_rejects_bad_dump_and_append_args(built_library, case, args, plan, msg):
+    a = _attn_args(**args)
+    info = _plan_info(**plan)
+    rc = built_library.aspire_mixed_attention(ctypes.byref(a), ctypes.byref(info), None)
+    assert rc == _capi.ASPIRE_ERR_INVALID, (case, rc)
+    assert msg in built_library.aspire_last_error(), built_library.aspire_last_error()
