@@ -78,11 +78,12 @@ def _both_ways(lay, q, kv0, k_new, v_new, dev, *, tables=False, dump_stride=0):
     return res
 
 
+@pytest.mark.parametrize("hq,hkv", [(32, 8), (8, 8), (8, 1)])
 @pytest.mark.parametrize("tables", [False, True], ids=["page_list", "page_tables"])
-def test_fused_append_matches_separate_append(cuda_device, tables):
+def test_fused_append_matches_separate_append(cuda_device, tables, hq, hkv):
     dev = cuda_device
-    lay = make_layout(batch=12, ctx=3000, num_qo_heads=32, num_kv_heads=8, draft_fraction=0.5, budget_pages=40,
-                      seed=61, block_table="random")
+    lay = make_layout(batch=12, ctx=3000, num_qo_heads=hq, num_kv_heads=hkv, draft_fraction=0.5, budget_pages=40,
+                      seed=61 + hq + hkv, block_table="random")
     q, kv0 = fill_tensors(lay, device=dev, seed=62)
     k_new, v_new = _new_tokens(lay, dev, 63)
     (kv_a, out_a, lse_a, _), (kv_b, out_b, lse_b, _) = _both_ways(lay, q, kv0, k_new, v_new, dev, tables=tables)
