@@ -246,6 +246,26 @@ class AspireSpillArgs(ctypes.Structure):
     ]
 
 
+class AspireClearDumpArgs(ctypes.Structure):
+    _fields_ = [
+        ("dump", ctypes.c_void_p),
+        ("dump_dtype", ctypes.c_int32),
+        ("num_heads", ctypes.c_int32),
+        ("slots", ctypes.c_int32),
+        ("kv_stride", ctypes.c_int64),
+        ("dump_rows", ctypes.c_int64),
+        ("slot_ids", ctypes.c_void_p),
+        ("n_slots", ctypes.c_int32),
+        ("lse", ctypes.c_void_p),
+        ("lse_rows", ctypes.c_int64),
+        ("qo_indptr", ctypes.c_void_p),
+        ("qo_len", ctypes.c_int64),
+        ("mode_flags", ctypes.c_void_p),
+        ("mode_value", ctypes.c_int32),
+        ("status", ctypes.c_void_p),
+    ]
+
+
 # Exported symbols and their signatures (must match include/aspire_b200.h).
 _SIGNATURES = {
     "aspire_plan": (
@@ -276,6 +296,7 @@ _SIGNATURES = {
     "aspire_build_unified_indices": (ctypes.c_int, [ctypes.POINTER(AspireIndicesArgs), ctypes.c_void_p]),
     "aspire_qkv_prologue": (ctypes.c_int, [ctypes.POINTER(AspirePrologueArgs), ctypes.c_void_p]),
     "aspire_draft_page_spill": (ctypes.c_int, [ctypes.POINTER(AspireSpillArgs), ctypes.c_void_p]),
+    "aspire_clear_dump_slots": (ctypes.c_int, [ctypes.POINTER(AspireClearDumpArgs), ctypes.c_void_p]),
     "aspire_plan_device": (
         ctypes.c_int,
         [c_int32_p, c_int32_p, c_int32_p, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,

@@ -32,6 +32,7 @@ SOURCES = [
     "plan_device.cu",
     "noalloc.cu",
     "draft_spill.cu",
+    "dump_state.cu",
 ]
 
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]

@@ -245,7 +245,7 @@ int aspire_set_wait_limit_ns(uint64_t ns) {
 const char* aspire_kernel_names(void) {
   return "aspire_attn_gather_kernel\naspire_attn_tc_kernel\naspire_attn_merge_kernel\naspire_append_kv_kernel\n"
          "aspire_select_pages_kernel\naspire_page_scores_kernel\naspire_build_indices_kernel\naspire_qkv_prologue_kernel\naspire_plan_device_kernel\n"
-         "aspire_draft_spill_kernel\n";
+         "aspire_draft_spill_kernel\naspire_clear_dump_kernel\n";
 }
 
 int aspire_plan_host_only(const int32_t* qo_indptr, const int32_t* kv_indptr,

@@ -7,6 +7,9 @@
 // and _handle_draft_page_spill, :718-742).  The reference computes the mask
 // with several torch operations and synchronises the host on need_spill.any()
 // before the insert; here the check and the insert are one launch.
+//
+// The entry point of the cleared slots' dump-state reset (kernel in
+// dump_state.cu) sits here too, with the other slot-bookkeeping launch.
 #include "kernels.cuh"
 #include "errors.h"
 
@@ -75,4 +78,46 @@ extern "C" int aspire_draft_page_spill(const AspireSpillArgs* a, void* stream) {
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   return check_cuda(cudaLaunchKernelEx(&cfg, aspire_draft_spill_kernel, p), "aspire_draft_spill_kernel launch");
+}
+
+extern "C" int aspire_clear_dump_slots(const AspireClearDumpArgs* a, void* stream) {
+  clear_error();
+  if (!a) return set_error(ASPIRE_ERR_INVALID, "aspire_clear_dump_slots: null argument");
+  if (a->n_slots < 0) return set_error(ASPIRE_ERR_INVALID, "aspire_clear_dump_slots: negative n_slots");
+  if (a->n_slots == 0) return ASPIRE_OK;
+  if (!a->dump || !a->slot_ids) return set_error(ASPIRE_ERR_INVALID, "aspire_clear_dump_slots: null pointer");
+  if (a->dump_dtype != ASPIRE_DUMP_F16 && a->dump_dtype != ASPIRE_DUMP_F32)
+    return set_error(ASPIRE_ERR_INVALID, "aspire_clear_dump_slots: bad dump_dtype");
+  if (a->num_heads <= 0 || (a->slots != 1 && a->slots != 2) || a->kv_stride <= 0 || a->dump_rows <= 0)
+    return set_error(ASPIRE_ERR_INVALID, "aspire_clear_dump_slots: bad dump geometry");
+  if (reinterpret_cast<uintptr_t>(a->dump) & (a->dump_dtype == ASPIRE_DUMP_F32 ? 3 : 1))
+    return set_error(ASPIRE_ERR_INVALID, "aspire_clear_dump_slots: dump not aligned to its element type");
+  if (a->lse && (!a->qo_indptr || a->lse_rows <= 0 || a->qo_len <= 0))
+    return set_error(ASPIRE_ERR_INVALID, "aspire_clear_dump_slots: lse needs qo_indptr, lse_rows and qo_len");
+  ClearDumpParams p;
+  p.dump = a->dump;
+  p.dump_f32 = a->dump_dtype == ASPIRE_DUMP_F32 ? 1 : 0;
+  p.row_elems = int64_t(a->num_heads) * a->slots * a->kv_stride;
+  p.dump_rows = a->dump_rows;
+  p.slot_ids = a->slot_ids;
+  p.lse = a->lse;
+  p.lse_rows = a->lse_rows;
+  p.num_heads = a->num_heads;
+  p.qo_indptr = a->qo_indptr;
+  p.qo_len = a->qo_len;
+  p.mode_flags = a->mode_flags;
+  p.mode_value = a->mode_value;
+  p.status = a->status;
+  const int64_t pieces = (p.row_elems + kClearPieceElems - 1) / kClearPieceElems;
+  if (pieces > 65535) return set_error(ASPIRE_ERR_CAPACITY, "aspire_clear_dump_slots: dump rows too long");
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(a->n_slots), static_cast<unsigned>(pieces));
+  cfg.blockDim = dim3(kClearThreads);
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return check_cuda(cudaLaunchKernelEx(&cfg, aspire_clear_dump_kernel, p), "aspire_clear_dump_kernel launch");
 }

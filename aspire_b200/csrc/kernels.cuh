@@ -133,6 +133,26 @@ struct SpillParams {
 };
 __global__ void aspire_draft_spill_kernel(SpillParams p);
 
+// Slot-local dump state reset (dump_state.cu).
+struct ClearDumpParams {
+  void* dump;                 // fp16 or fp32 (dump_f32) [dump_rows, row_elems]
+  int32_t dump_f32;
+  int64_t row_elems;          // heads x slots x kv_stride
+  int64_t dump_rows;
+  const int32_t* slot_ids;
+  float* lse;                 // optional [lse_rows, num_heads]
+  int64_t lse_rows;
+  int32_t num_heads;
+  const int32_t* qo_indptr;   // required with lse
+  int64_t qo_len;
+  int32_t* mode_flags;        // optional [dump_rows]
+  int32_t mode_value;
+  uint32_t* status;
+};
+constexpr int kClearThreads = 256;
+constexpr int64_t kClearPieceElems = 32768;  // elements of a row one CTA fills
+__global__ void aspire_clear_dump_kernel(ClearDumpParams p);
+
 constexpr int kIndicesThreads = 128;
 __global__ void aspire_build_indices_kernel(IndicesParams p);
 

@@ -6,6 +6,10 @@ Tensor kv_page_indices, Tensor kv_page_indptr, Tensor kv_last_page_len,
 int page_size) -> ()``; non-contiguous k/v heads raise ``ValueError``.
 Registered as ``aspire_b200::update_kv_padded`` with a fake implementation
 so ``torch.compile(fullgraph=True)`` can trace it.
+
+The module also holds the step's other cache and slot bookkeeping:
+``build_unified_indices``, ``draft_page_spill``, ``qkv_prologue`` (norm +
+RoPE + append) and ``clear_dump_slots`` (dump-state reset of cleared slots).
 """
 
 from __future__ import annotations
@@ -292,3 +296,56 @@ def qkv_prologue(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, kv_append_in
     rc = _capi.load_library().aspire_qkv_prologue(ctypes.byref(a), ctypes.c_void_p(stream))
     _capi.check(rc, "aspire_qkv_prologue")
     return q_out
+
+
+def clear_dump_slots(attention_weights_buffer: torch.Tensor, slot_ids: torch.Tensor, num_heads: int,
+                     dump_slots: int, kv_stride: int, lse_buffer: torch.Tensor | None = None,
+                     qo_indptr: torch.Tensor | None = None, mode_flags: torch.Tensor | None = None,
+                     mode_value: int = 1, status: torch.Tensor | None = None) -> None:
+    """Dump-state reset of cleared slots in one launch (C ABI
+    ``aspire_clear_dump_slots``), replacing
+    LMBackendBase._clear_variant_slot_state (aspire/backends/base.py:1404-1419):
+    the slots' rows of the flat dump buffer ``[rows, num_heads, dump_slots,
+    kv_stride]`` (fp16 or fp32) become -inf, the LSE row of each slot's last
+    query (``qo_indptr[slot + 1] - 1``, clamped) becomes 0, and
+    ``mode_flags[slot]`` becomes ``mode_value`` (VERIFY_MODE = 1).  Slot ids
+    past the buffer's rows are skipped and reported in ``status``."""
+    dump = attention_weights_buffer
+    if dump.dtype not in (torch.float16, torch.float32) or not dump.is_contiguous() or dump.device.type != "cuda":
+        raise ValueError("attention_weights_buffer must be a contiguous fp16 or fp32 CUDA tensor")
+    row_elems = int(num_heads) * int(dump_slots) * int(kv_stride)
+    if row_elems <= 0 or dump.numel() % row_elems != 0:
+        raise ValueError("attention_weights_buffer is not a whole number of [num_heads, slots, kv_stride] rows")
+    ids = slot_ids.to(device=dump.device, dtype=torch.int32).contiguous()
+    for name, t in (("qo_indptr", qo_indptr), ("mode_flags", mode_flags)):
+        if t is not None and (t.dtype != torch.int32 or not t.is_contiguous() or t.device != dump.device):
+            raise ValueError(f"{name} must be a contiguous int32 tensor on the dump's device")
+    if lse_buffer is not None:
+        if (lse_buffer.dtype != torch.float32 or not lse_buffer.is_contiguous() or lse_buffer.dim() != 2
+                or lse_buffer.shape[1] != num_heads):
+            raise ValueError("lse_buffer must be a contiguous fp32 [tokens, num_heads] tensor")
+        if qo_indptr is None:
+            raise ValueError("lse_buffer needs qo_indptr")
+    a = _capi.AspireClearDumpArgs()
+    a.dump = dump.data_ptr()
+    a.dump_dtype = _capi.DUMP_F32 if dump.dtype == torch.float32 else _capi.DUMP_F16
+    a.num_heads = int(num_heads)
+    a.slots = int(dump_slots)
+    a.kv_stride = int(kv_stride)
+    a.dump_rows = dump.numel() // row_elems
+    a.slot_ids = ids.data_ptr()
+    a.n_slots = ids.numel()
+    if lse_buffer is not None:
+        a.lse = lse_buffer.data_ptr()
+        a.lse_rows = lse_buffer.shape[0]
+        a.qo_indptr = qo_indptr.data_ptr()
+        a.qo_len = qo_indptr.numel()
+    if mode_flags is not None:
+        if mode_flags.numel() < a.dump_rows:
+            raise ValueError("mode_flags needs an entry per dump row")
+        a.mode_flags = mode_flags.data_ptr()
+    a.mode_value = int(mode_value)
+    a.status = status.data_ptr() if status is not None else None
+    stream = torch.cuda.current_stream(dump.device).cuda_stream
+    _capi.check(_capi.load_library().aspire_clear_dump_slots(ctypes.byref(a), ctypes.c_void_p(stream)),
+                "aspire_clear_dump_slots")

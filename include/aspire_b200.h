@@ -506,6 +506,40 @@ typedef struct AspireSpillArgs {
 ASPIRE_API int aspire_draft_page_spill(const AspireSpillArgs* args, void* stream);
 
 /* ------------------------------------------------------------------------ */
+/* Dump-state reset of cleared slots (device).                              */
+/* ------------------------------------------------------------------------ */
+
+typedef struct AspireClearDumpArgs {
+  void* dump;               /* [dump_rows, num_heads, slots, kv_stride], dump_dtype  */
+  int32_t dump_dtype;       /* ASPIRE_DUMP_F16 or ASPIRE_DUMP_F32                    */
+  int32_t num_heads;
+  int32_t slots;            /* 2 (first/last dump) or 1 (last-token dump)            */
+  int64_t kv_stride;
+  int64_t dump_rows;        /* rows of the dump buffer (slot ids must be below it)   */
+  const int32_t* slot_ids;  /* int32 [n_slots], device                               */
+  int32_t n_slots;
+  float* lse;               /* optional fp32 [lse_rows, num_heads] (NULL = skip)     */
+  int64_t lse_rows;
+  const int32_t* qo_indptr; /* int32 [qo_len] of the dump program; required with lse */
+  int64_t qo_len;
+  int32_t* mode_flags;      /* optional int32 [dump_rows] dump enable flags (NULL = skip) */
+  int32_t mode_value;       /* value written to mode_flags[slot] (VERIFY_MODE = 1)   */
+  uint32_t* status;         /* optional device status word                           */
+} AspireClearDumpArgs;
+
+/*
+ * Resets the dump state of cleared slots in one launch: every element of the
+ * slots' dump rows becomes -inf, the LSE row of each slot's last query
+ * (qo_indptr[slot + 1] - 1, clamped to [0, lse_rows)) becomes 0 and
+ * mode_flags[slot] becomes mode_value.  Replaces
+ * LMBackendBase._clear_variant_slot_state (aspire/backends/base.py:1404-1419),
+ * three torch indexing ops.  A slot id outside [0, dump_rows) or whose
+ * qo_indptr entry is past qo_len is skipped and sets ASPIRE_STATUS_BAD_ROW.
+ * Capturable; allocates nothing.
+ */
+ASPIRE_API int aspire_clear_dump_slots(const AspireClearDumpArgs* args, void* stream);
+
+/* ------------------------------------------------------------------------ */
 /* Utilities.                                                               */
 /* ------------------------------------------------------------------------ */
 

@@ -13,6 +13,8 @@ its root:
   last-token dump (fp16 and fp32 buffers).
 * recent_rows.pt : the reference's LMBackendBase._build_recent_draft_rows
   (recent-page seeding of the draft table) on CPU.
+* dump_state.pt : the reference's LMBackendBase._clear_variant_slot_state
+  (dump-state reset of cleared slots) on CPU.
 * unified_indices.pt : the reference's build_unified_indices
   (aspire/models/sparse_draft_runner.py, with its Triton _copy_indices_kernel)
   under the Triton CPU interpreter.
@@ -281,6 +283,42 @@ def recent_case():
     torch.save(out, HERE / "recent_rows.pt")
 
 
+def dump_state_case():
+    """Dump-state reset of cleared slots: the reference's
+    LMBackendBase._clear_variant_slot_state (imported unchanged) on a bound
+    stand-in carrying the attributes it reads, for an fp16 first/last dump and
+    an fp32 last-token dump; the buffers before and after are saved."""
+    import types
+
+    sys.path.insert(0, str(REF))
+    from aspire.backends.base import LMBackendBase  # noqa: E402
+
+    out = {}
+    for name, (dtype, slots, H, stride) in {"f16_first_last": (torch.float16, 2, 16, 1040),
+                                            "f32_last_token": (torch.float32, 1, 4, 2053)}.items():
+        B = 6
+        g = torch.Generator().manual_seed(slots * 13)
+        dump = (torch.randn(B * H * slots * stride, generator=g) * 9).to(dtype)
+        q_lens = torch.randint(1, 10, (B,), generator=g)
+        qo = torch.zeros(B + 1, dtype=torch.int32)
+        qo[1:] = torch.cumsum(q_lens, 0).to(torch.int32)
+        lse = torch.randn(int(qo[-1]) + 3, H, generator=g).float()
+        flags = torch.zeros(B, dtype=torch.int32)
+        before = {"dump": dump.clone(), "lse": lse.clone(), "mode_flags": flags.clone(), "qo_indptr": qo.clone()}
+        fake = types.SimpleNamespace(
+            attention_weights_buffer=dump, batch_size=B,
+            model=types.SimpleNamespace(config=types.SimpleNamespace(n_head=H)),
+            _dump_query_slots=lambda slots=slots: slots, _kv_stride_alloc=stride,
+            attention_weights_buffer_neg_inf=torch.tensor(float("-inf"), dtype=dtype),
+            unified_full_qo_indptr=qo, _lse_buffer=lse, _dump_mode_flags=flags)
+        slot_ids = torch.tensor([1, 4, 5])
+        LMBackendBase._clear_variant_slot_state(fake, slot_ids)
+        out[name] = {"params": dict(B=B, H=H, slots=slots, kv_stride=stride), "slot_ids": slot_ids.to(torch.int32),
+                     "before": before, "after": {"dump": dump, "lse": lse, "mode_flags": flags}}
+        print("dump_state", name, int(torch.isinf(dump).sum()))
+    torch.save(out, HERE / "dump_state.pt")
+
+
 def spill_case():
     """Draft-page spill insert: the reference's LMBackendBase._handle_draft_page_spill
     (aspire/backends/base.py:718-742, imported unchanged) applied to the spill
@@ -345,7 +383,7 @@ def spill_case():
 
 def main(groups=None):
     """Writes every fixture, or only those of the named groups (selector,
-    last_token, ties, append, indices, recent, spill)."""
+    last_token, ties, append, indices, recent, spill, dump_state)."""
     if not os.environ.get("ASPIRE_REFERENCE") or not REF.exists():
         raise SystemExit("set ASPIRE_REFERENCE to the root of the reference (ASPIRE) checkout")
     want = lambda g: not groups or g in groups  # noqa: E731
@@ -380,6 +418,8 @@ def main(groups=None):
         recent_case()
     if want("spill"):
         spill_case()
+    if want("dump_state"):
+        dump_state_case()
 
 
 if __name__ == "__main__":

@@ -331,3 +331,19 @@ def test_last_dump_oracle_matches_flashinfer_variant(golden_dir, case):
     err = (out - g["out"].float()).abs()
     assert err.max().item() <= 2e-2 and err.mean().item() <= 2e-3
     assert (lse - g["lse"]).abs().max().item() <= 2e-3
+
+
+@pytest.mark.parametrize("case", ["f16_first_last", "f32_last_token"])
+def test_dump_state_oracle_matches_reference(golden_dir, case):
+    """The restatement of LMBackendBase._clear_variant_slot_state reproduces
+    the reference's own method (run on CPU by tests/golden/make_golden.py)."""
+    from oracle import dump_state as oracle_dump
+
+    g = _load(golden_dir, "dump_state.pt")[case]
+    p = g["params"]
+    dump, lse, flags = (g["before"][k].clone() for k in ("dump", "lse", "mode_flags"))
+    oracle_dump.clear_variant_slot_state(dump, lse, g["before"]["qo_indptr"], flags, g["slot_ids"],
+                                         num_heads=p["H"], dump_slots=p["slots"], kv_stride=p["kv_stride"])
+    assert torch.equal(dump, g["after"]["dump"])
+    assert torch.equal(lse, g["after"]["lse"])
+    assert torch.equal(flags, g["after"]["mode_flags"])
