@@ -4,11 +4,15 @@
  *
  *   1. paged mixed draft/verify attention (draft rows attend a sparse page
  *      list with q_len 1, verify rows attend the full cache with a causal
- *      multi-token query), optionally dumping first/last-query logits at the
- *      refresh layer;
+ *      multi-token query), optionally dumping the first/last-query or the
+ *      last-query logits at the refresh layer, and optionally appending the
+ *      step's new tokens inside the same launch;
  *   2. refresh-layer page scoring + top-k page re-selection, written in place
  *      into the draft page table;
- *   3. the paged KV append of the step's new tokens.
+ *   3. the paged KV append of the step's new tokens, the mixed page-list
+ *      build, the draft-page spill insert and the dump-state reset of cleared
+ *      slots;
+ *   4. planning: on the host, or on the device inside a CUDA graph.
  *
  * Every entry point takes plain pointers, sizes and a CUDA stream handle
  * (passed as void*); no framework types cross this boundary.  Every entry
