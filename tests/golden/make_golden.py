@@ -23,8 +23,8 @@ its root:
   FlashInfer's get_batch_indices_positions_kernel) executed by Triton's CPU
   interpreter (TRITON_INTERPRET=1) on a padded mixed batch.
 
-The fixtures are small (< 2 MB total) and committed; tests never read the
-reference tree.
+The fixtures are small (about 4 MB together) and committed; tests never
+read the reference tree.
 """
 
 from __future__ import annotations
