@@ -123,6 +123,35 @@ __host__ __device__ inline bool whole_groups_cheaper(int64_t n_groups, int64_t m
                         (n_chunk_items > n_groups ? kMergeCost10 : 0);
   return whole <= split;
 }
+// Mixed batches (long verify groups beside short draft groups) whose long
+// groups are few enough: cutting each long group (span > max_span / 2) into
+// k = SMs / n_long equal pieces gives every piece its own SM, and the short
+// groups fill the SMs left over.  The common rule's two items per SM leave a
+// partly filled second round there instead (a TP-8 share of the bench: 288
+// verify chunks + 32 draft items on 148 SMs).  Returns that chunk length when
+// the short groups' work (tenths of a tile, each group whole) fits into the
+// spare SMs' time, else 0.  Both planners use it.  Measured on the bench's
+// mixed layer-call: TP-8 share 0.108 -> 0.101 ms (chunk 3840 -> 8192), TP-4
+// 0.188 -> 0.181 ms (7552 -> 16384); TP 1 has more long groups than SMs.
+__host__ __device__ inline int64_t long_group_chunk(int64_t n_long, int64_t max_span, int64_t short_work10,
+                                                    int64_t num_sms) {
+  if (n_long <= 0 || num_sms <= 0) return 0;
+  const int64_t k = num_sms / n_long;
+  if (k < 1) return 0;
+  int64_t chunk = ((max_span + k - 1) / k + 127) / 128 * 128;
+  chunk = chunk < 512 ? 512 : chunk;
+  const int64_t pieces = n_long * ((max_span + chunk - 1) / chunk);
+  const int64_t spare = num_sms - pieces;
+  if (spare < 0 || short_work10 > spare * (chunk / 128 * 10 + kItemCost10)) return 0;
+  return chunk;
+}
+// A group counts as long for long_group_chunk when its span exceeds half the
+// longest; a short group's work is its tiles plus one item boundary.
+__host__ __device__ inline bool long_group(int64_t span, int64_t max_span) { return 2 * span > max_span; }
+__host__ __device__ inline int64_t short_group_work10(int64_t span) {
+  return (span + 127) / 128 * 10 + kItemCost10;
+}
+
 // The chunk length that keeps every group whole.
 __host__ __device__ inline int64_t whole_group_chunk(int64_t max_span) {
   const int64_t c = (max_span + 127) / 128 * 128;

@@ -133,6 +133,26 @@ __global__ void __launch_bounds__(kDevPlanThreads) aspire_plan_device_kernel(Dev
   block_exclusive_scan(tokens, warp_sums, &total_tokens);  // (its barriers publish max_span)
   const bool similar = 2 * int64_t(min_span) >= max_span;
   int64_t chunk = chunk_for(total_tokens, p.num_sms, similar ? kItemsPerCtaUniform : kItemsPerCtaMixed);
+  if (!similar) {
+    // Long groups cut into one piece per SM when that packs the grid (long_group_chunk).
+    int64_t my_long = 0, my_short = 0;
+    for (int b = r0; b < r1; ++b) {
+      const RowShape s = row_shape(p, b);
+      if (s.ql <= 0) continue;
+      for (int qt = 0; qt < s.ntq; ++qt) {
+        const int32_t span = tile_span(p, s, qt * s.tile, min(s.nq, (qt + 1) * s.tile));
+        if (long_group(span, max_span))
+          my_long += p.num_kv_heads;
+        else
+          my_short += int64_t(p.num_kv_heads) * short_group_work10(span);
+      }
+    }
+    int64_t n_long, short_work10;
+    block_exclusive_scan(my_long, warp_sums, &n_long);
+    block_exclusive_scan(my_short, warp_sums, &short_work10);
+    const int64_t c = long_group_chunk(n_long, max_span, short_work10, p.num_sms);
+    if (c > 0) chunk = c;
+  }
   {
     // Whole groups when they balance about as well (whole_groups_cheaper).
     int64_t my_groups = 0, my_chunk_items = 0;

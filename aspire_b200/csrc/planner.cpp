@@ -166,6 +166,17 @@ int plan_impl(const int32_t* qo_indptr, const int32_t* kv_indptr, const int32_t*
   }
   const bool similar = 2 * int64_t(min_span) >= max_span;
   int64_t chunk = chunk_for(total_tokens, num_sms, similar ? kItemsPerCtaUniform : kItemsPerCtaMixed);
+  if (!similar) {
+    int64_t n_long = 0, short_work10 = 0;
+    for (const GroupDesc& g : groups) {
+      if (long_group(g.span, max_span))
+        ++n_long;
+      else
+        short_work10 += short_group_work10(g.span);
+    }
+    const int64_t c = long_group_chunk(n_long, max_span, short_work10, num_sms);
+    if (c > 0) chunk = c;
+  }
   {
     int64_t n_chunk_items = 0;
     for (const GroupDesc& g : groups) n_chunk_items += g.span > 0 ? (g.span + chunk - 1) / chunk : 1;

@@ -122,7 +122,20 @@ def _expected_chunk(spans, hkv, num_sms):
         c = max(cdiv(total, target), 512)
         return cdiv(c, 128) * 128
 
-    chunk = chunk_for(4 if 2 * min(spans) >= max(spans) else 2)
+    similar = 2 * min(spans) >= max(spans)
+    chunk = chunk_for(4 if similar else 2)
+    if not similar:
+        # Long groups (span > max / 2) cut into k = SMs / n_long pieces each,
+        # when the short groups (tiles + 2.3 per group) fit the spare SMs.
+        mx = max(spans)
+        n_long = sum(2 * s > mx for s in spans) * hkv
+        short = sum(cdiv(s, 128) * 10 + 23 for s in spans if 2 * s <= mx) * hkv
+        k = num_sms // n_long if n_long else 0
+        if k >= 1:
+            c = max(512, cdiv(cdiv(mx, k), 128) * 128)
+            spare = num_sms - n_long * cdiv(mx, c)
+            if spare >= 0 and short <= spare * (c // 128 * 10 + 23):
+                chunk = c
     n_groups = len(spans) * hkv
     n_items = sum(cdiv(s, chunk) if s > 0 else 1 for s in spans) * hkv
     whole = cdiv(n_groups, num_sms) * (cdiv(max(spans), 128) * 10 + 23)
@@ -131,11 +144,14 @@ def _expected_chunk(spans, hkv, num_sms):
     return max(512, cdiv(max(spans), 128) * 128) if whole <= split else chunk
 
 
-@pytest.mark.parametrize("case", ["mixed", "full_context", "prefill_spread", "draft_b1", "draft_b16", "draft_b32"])
+@pytest.mark.parametrize("case", ["mixed", "mixed_tp4", "mixed_tp8", "full_context", "prefill_spread", "draft_b1",
+                                  "draft_b16", "draft_b32"])
 def test_plan_chunk_rule(built_library, case):
     """Decode batches (long verify rows beside short draft rows) get about two
     items per SM; whole-context rows of equal length, four; the spread-out
-    query tiles of a causal prefill chunk stay whole at two per SM.  Medium
+    query tiles of a causal prefill chunk stay whole at two per SM.  When the
+    long groups are fewer than the SMs (the TP-4 and TP-8 head shares of the
+    decode batch), each is cut into SMs / long groups pieces.  Medium
     draft-only batches keep every group whole (one item each, no merge): 16
     rows over 64 pages at 32 / 8 heads, 32 rows over 136 pages at 16 / 8; one
     row over 64 pages is still split (its 8 groups use 16 SMs)."""
@@ -155,8 +171,12 @@ def test_plan_chunk_rule(built_library, case):
             assert info.chunk_tokens == pages * 16
             assert info.num_merge == 0 and info.num_items_tc == B * hkv
         return
-    if case == "mixed":
-        lay = make_layout(batch=64, ctx=32768, num_qo_heads=32, num_kv_heads=8, draft_fraction=0.5,
+    hq, hkv = 32, 8
+    if case.startswith("mixed"):
+        # The bench's batch at TP 1 and at the TP-4 / TP-8 head shares (2 and 1
+        # KV heads): at the shares the verify groups are cut into one piece per SM.
+        hq, hkv = {"mixed": (32, 8), "mixed_tp4": (8, 2), "mixed_tp8": (4, 1)}[case]
+        lay = make_layout(batch=64, ctx=32768, num_qo_heads=hq, num_kv_heads=hkv, draft_fraction=0.5,
                           budget_pages=128, seed=0)
         qo, kvp, kvl = lay.qo_indptr, lay.kv_indptr, lay.kv_lens
         spans = [int(k) for k in kvl]
@@ -171,11 +191,13 @@ def test_plan_chunk_rule(built_library, case):
         qo = np.array([0, 8192], np.int32)
         kvp = np.array([0, 512], np.int32)
         spans = [8192] + [64 * (t + 1) for t in range(1, 128)]
-    rc, info, _ = _plan(built_library, qo, kvp, kvl, 32, 8, num_sms=num_sms)
+    rc, info, _ = _plan(built_library, qo, kvp, kvl, hq, hkv, num_sms=num_sms)
     assert rc == 0, built_library.aspire_last_error()
-    assert info.chunk_tokens == _expected_chunk(spans, 8, num_sms)
+    assert info.chunk_tokens == _expected_chunk(spans, hkv, num_sms)
     if case == "mixed":
         assert info.num_items_tc == 768  # verify rows in two chunks, draft rows whole
+    if case in ("mixed_tp4", "mixed_tp8"):
+        assert info.chunk_tokens == {"mixed_tp4": 16384, "mixed_tp8": 8192}[case]
     if case == "prefill_spread":
         assert info.num_merge == 0 and info.num_items_prefill == 128 * 8
 

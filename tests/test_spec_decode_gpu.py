@@ -93,8 +93,15 @@ def test_full_budget_drafts_are_accepted(model):
 def test_random_draft_lengths_mix_steps_and_stay_greedy(model):
     """Per-row draft lengths drawn from 2..6 after every verification (config
     3's asynchronous interleaving): the rows drift apart, so most steps hold
-    drafting and verifying rows together, and the output is still the plain
-    greedy decode of the same prompts."""
+    drafting and verifying rows together, and the output is still a greedy
+    decode of the same prompts.  It is compared with plain greedy decoding
+    token for token: the split-KV chunk of a row depends on the batch around
+    it (a mixed step cuts the verify rows into one piece per SM, a plain
+    step into 512-token chunks), so the two sum a row's attention in a
+    different order, and where the top two bf16 logits are that close the
+    argmax can differ.  Rows may therefore part only at such a near-tie:
+    at the first divergence both emitted tokens are within GAP_TOL of the
+    teacher-forced maximum of their common prefix."""
     prompts = synthetic_prompts(B, P, model.cfg.vocab, seed=2)
     dec = SpecDecoder(model, batch=B, prompt_len=P, max_new=G, draft_len=(2, 6), budget_pages=32, recent_pages=8,
                       draft_seed=3)
@@ -105,10 +112,17 @@ def test_random_draft_lengths_mix_steps_and_stay_greedy(model):
     dec.restart(g0)
     b = dec.generate()
     assert np.array_equal(a["tokens"], b["tokens"])
-    _check_greedy(dec, a["tokens"], "random lengths")
+    _, gaps_a = _check_greedy(dec, a["tokens"], "random lengths")
     ar = SpecDecoder(model, batch=B, prompt_len=P, max_new=G, draft_len=0, budget_pages=32, recent_pages=8)
     ar.prefill(prompts)
     r = ar.generate()
+    _, gaps_r = _check_greedy(ar, r["tokens"], "plain greedy")
     cmp = compare_sequences(a["tokens"], r["tokens"])
     print("random lengths vs plain greedy:", cmp)
-    assert cmp["rows_identical"] == B, cmp
+    for row, d in enumerate(cmp["first_divergence"]):
+        if d < 0:
+            continue
+        # gaps[:, j] belongs to token j + 1; the first token comes from the shared prefill
+        assert d >= 1, (row, d)
+        ga, gr = float(gaps_a[row, d - 1]), float(gaps_r[row, d - 1])
+        assert ga <= GAP_TOL and gr <= GAP_TOL, (row, d, ga, gr)
