@@ -4,9 +4,9 @@
 // HolisticAttentionWrapper.plan / plan_host (aspire/attention/
 // holistic_wrapper.py:253-265, :323-335).  The planner is a different
 // design: every (request row, KV head, packed-query tile) is cut into
-// split-KV chunks of a common length chosen so that the persistent grid
-// gets several items per CTA, and items are placed on CTAs longest-first
-// onto the least-loaded CTA (LPT).  By default every row goes to the
+// split-KV chunks of a common length (common.cuh: about two or four items
+// per CTA, one piece per SM for few long groups, or every group whole), and
+// items are placed on CTAs longest-first onto the least-loaded CTA (LPT).  By default every row goes to the
 // tcgen05 kernel (decode items, or prefill items for rows of at least 128
 // packed query rows); the CUDA-core gather kernel takes narrow rows only when
 // the routing thresholds (ASPIRE_B200_TC_MIN_ROWS / ASPIRE_B200_TC_MIN_KV)
