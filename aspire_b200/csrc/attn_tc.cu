@@ -106,20 +106,17 @@ static_assert(sizeof(TcShared) + 1024 <= 227 * 1024, "tcgen05 kernel shared memo
 static_assert(sizeof(pf::Buffers) <= offsetof(TcShared, red), "prefill buffers overlap decode state");
 static_assert(kNMax % 16 == 0 && kNMax <= 64, "N tile must be a multiple of 16 and fit a 64-column buffer");
 
-// Columns N of an item's products: its packed rows padded to 16, or kNMax for
-// every item of a launch with short items.  Each width has its own softmax
-// loop (consume_item<N / 2>), and a CTA alternates between widths from item
-// to item; with items of a few tiles (split-KV chunks of <= 4096 tokens, as in
-// a TP-4 or TP-8 rank's share of the heads) the switches, whose code must come
-// back into the instruction cache under full HBM load, cost more than the
-// padded columns, so such launches run one width.  Measured per mixed
-// layer-call (B=64, 32k, Qwen3-8B heads): -5 % at a TP-8 share with 1920-token
-// chunks, -2.5 % with 3840-token chunks; one width everywhere was +2 % at TP-2
-// (7680-token chunks).  Launches with the dump keep the exact widths (their
-// dump path is longer per column).
-constexpr int kUniformColumnsMaxChunk = 4096;
-__device__ __forceinline__ int item_columns(int nrows, bool uniform) {
-  return uniform ? kNMax : (nrows + 15) / 16 * 16;
+// Columns N of an item's products: its packed rows rounded up to 16, or the
+// wider width its plan gives it (WorkItem::cols: the planners give the long
+// groups' items one width when there are few items per CTA, so that those
+// CTAs stream at one rate).  Each width has its own softmax loop
+// (consume_item<N / 2>).  A value that is not a multiple of 16 between the
+// rows' own width and kNMax is ignored, so every role derives the same N.
+// Launches with the dump keep the exact widths (their dump path is longer
+// per column).
+__device__ __forceinline__ int item_columns(const WorkItem& it, bool use_cols) {
+  const int exact = (it.pq_end - it.pq_begin + 15) / 16 * 16;
+  return use_cols && it.cols > exact && it.cols <= kNMax && it.cols % 16 == 0 ? it.cols : exact;
 }
 
 // Barrier of one softmax warpgroup's 128 threads on an mbarrier (bounded, so that a thread
@@ -145,7 +142,7 @@ __device__ __forceinline__ bool group_sync(TcShared& sm, uint64_t& grp, uint32_t
 
 // QK^T of every tile, and the query-tile loads (warp 1).
 __device__ void run_qk(const AttnParams& p, const CUtensorMap* qmap, TcShared& sm, int lane, uint32_t& k,
-                       bool uniform) {
+                       bool use_cols) {
   const uint32_t tmem = sm.tmem_base;
   uint32_t g = 0, items_done = 0;
   bool ok = true;
@@ -163,8 +160,7 @@ __device__ void run_qk(const AttnParams& p, const CUtensorMap* qmap, TcShared& s
   while (ii >= 0 && ok) {
     const WorkItem it = load_item(p.plan, ii);
     const int nt = n_tiles_of(it);
-    const int nrows = it.pq_end - it.pq_begin;
-    const uint32_t N = uint32_t(item_columns(nrows, uniform));
+    const uint32_t N = uint32_t(item_columns(it, use_cols));
     const uint32_t idesc_qk = ptx::idesc_bf16(128, N, false, false);
     if (!wait_bar(sm, sm.q_full, items_done & 1, p.status)) {
       ok = false;
@@ -221,7 +217,7 @@ __device__ void run_qk(const AttnParams& p, const CUtensorMap* qmap, TcShared& s
 }
 
 // P.V of every tile into the O accumulator (warp 11).
-__device__ void run_pv(const AttnParams& p, TcShared& sm, int lane, uint32_t& k, bool uniform) {
+__device__ void run_pv(const AttnParams& p, TcShared& sm, int lane, uint32_t& k, bool use_cols) {
   const uint32_t tmem = sm.tmem_base;
   uint32_t g = 0, items_done = 0;
   bool ok = true;
@@ -232,8 +228,7 @@ __device__ void run_pv(const AttnParams& p, TcShared& sm, int lane, uint32_t& k,
   while (ii >= 0 && ok) {
     const WorkItem it = load_item(p.plan, ii);
     const int nt = n_tiles_of(it);
-    const int nrows = it.pq_end - it.pq_begin;
-    const uint32_t N = uint32_t(item_columns(nrows, uniform));
+    const uint32_t N = uint32_t(item_columns(it, use_cols));
     const uint32_t idesc_pv = ptx::idesc_bf16(128, N, true, true);
     for (int t = 0; t < nt && ok; ++t, ++g) {
       const uint32_t vs = g % kVStages, pb = g % 2;
@@ -656,7 +651,7 @@ __device__ bool consume_item(const AttnParams& p, TcShared& sm, const WorkItem& 
 }
 
 __device__ void consume_items(const AttnParams& p, TcShared& sm, bool causal, int warp, int lane, uint32_t& k,
-                              bool uniform) {
+                              bool use_cols) {
   const int wq = warp & 3;
   const int wg = (warp - kFirstSoftmaxWarp) / 4;  // softmax warpgroup 0 or 1
   const int r = wq * 32 + lane;                    // TMEM lane = S-tile token = O-tile dim
@@ -677,7 +672,7 @@ __device__ void consume_items(const AttnParams& p, TcShared& sm, bool causal, in
       for (int j = wg; j < nrows; j += 2) store_final(p, it, it.pq_begin + j, r, 0.f, -INFINITY);
       continue;
     }
-    const int N = item_columns(nrows, uniform);
+    const int N = item_columns(it, use_cols);
     // Items whose columns include dumped rows (query 0 or the last query, as
     // the dump kind and the row's flag have it) take the instantiation that
     // carries the dump path.
@@ -705,8 +700,8 @@ __device__ void consume_items(const AttnParams& p, TcShared& sm, bool causal, in
 }
 
 __device__ void run_consumer(const AttnParams& p, TcShared& sm, bool causal, int warp, int lane, uint32_t& k,
-                             bool uniform) {
-  consume_items(p, sm, causal, warp, lane, k, uniform);
+                             bool use_cols) {
+  consume_items(p, sm, causal, warp, lane, k, use_cols);
   // The bulk stores of each group's last item (issued by its thread 0) finish
   // before the CTA exits.
   if (lane == 0 && (warp - kFirstSoftmaxWarp) % 4 == 0) ptx::bulk_wait_all();
@@ -785,8 +780,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const int n_tc = live ? pf_first - tc_first : 0;
   const int n_pf = live ? plan[kHdrNumItems] - pf_first : 0;
   const bool causal = live && plan[kHdrCausal] != 0;
-  const int chunk_tokens = live ? plan[kHdrChunkTokens] : 0;
-  const bool uniform = p.dump == nullptr && chunk_tokens > 0 && chunk_tokens <= kUniformColumnsMaxChunk;
+  const bool use_cols = p.dump == nullptr;
 
   // Both phases read one item sequence (the ring of claimed item indices);
   // each warp keeps its position across the phase change.
@@ -800,11 +794,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       run_producer<kVStages>(p, &tmap, sm, sm.v, sm.v_full, sm.v_empty, 1, false, tc_first, n_tc, kHdrTcClaim,
                              kNMax, lane, k);
     } else if (warp == 1) {
-      run_qk(p, &qmap, sm, lane, k, uniform);
+      run_qk(p, &qmap, sm, lane, k, use_cols);
     } else if (warp == kPvWarp) {
-      run_pv(p, sm, lane, k, uniform);
+      run_pv(p, sm, lane, k, use_cols);
     } else {
-      run_consumer(p, sm, causal, warp, lane, k, uniform);
+      run_consumer(p, sm, causal, warp, lane, k, use_cols);
     }
   }
   // Phase 2: the prefill list, in the same shared memory and TMEM.  Every

@@ -60,7 +60,7 @@ struct WorkItem {
   int32_t partial_base;  // partial row of chunk 0 of the merge group
   int32_t merge_id;      // merge descriptor index, -1 when n_chunks == 1
   int32_t kind;          // 0 = CUDA-core gather kernel, 1 = tcgen05 decode kernel, 2 = prefill kernel
-  int32_t reserved;
+  int32_t cols;          // tcgen05 decode items: product columns, 0 = packed rows rounded up to 16
 };
 static_assert(sizeof(WorkItem) == 64, "WorkItem must stay 64 bytes");
 
@@ -161,6 +161,25 @@ __host__ __device__ inline int64_t whole_group_chunk(int64_t max_span) {
 // Resident CTAs per SM of each kernel class (sets the persistent grids).
 constexpr int kGatherCtasPerSm = 4;
 constexpr int kTcCtasPerSm = 1;
+
+// Product columns of the tcgen05 decode items.  Each item's products take
+// its packed rows rounded up to 16 columns, except that when the decode list
+// holds at most kPadMaxItemsPerCta items per CTA, the long groups' items
+// (long_group) all take the widest of their widths.  Then most CTAs run one
+// long item and nothing else, and the launch ends when the slowest of them
+// does; long items of different widths (verify rows with 3 to 9 queries: 16,
+// 32 and 48 columns) stream at different rates, and the fast CTAs idle.  At
+// one width they finish together.  Measured per mixed layer-call on the
+// bench's batch (B=64, 32k, verify q_len 3-9): TP-8 share 0.101 -> 0.097 ms,
+// TP-4 0.181 -> 0.175 ms; with one q_len for every verify row, or with more
+// items per CTA (TP 1), padding gains nothing, and padding the short
+// (draft) items too, as a launch-wide single width did, cost up to 15 %
+// (one draft row: 13.9 -> 16.3 us).  Both planners use it.
+constexpr int kPadMaxItemsPerCta = 2;
+__host__ __device__ inline int32_t tc_columns(int32_t rows) { return (rows + 15) / 16 * 16; }
+__host__ __device__ inline bool pad_long_items(int64_t n_decode_items, int64_t num_sms) {
+  return n_decode_items > 0 && n_decode_items <= int64_t(kPadMaxItemsPerCta) * num_sms * kTcCtasPerSm;
+}
 
 // Packed query rows handled by one gather-kernel item.
 constexpr int kGatherQTile = 4;

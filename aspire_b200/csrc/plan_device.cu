@@ -100,12 +100,13 @@ __global__ void __launch_bounds__(kDevPlanThreads) aspire_plan_device_kernel(Dev
   pdl_begin();
   __shared__ int64_t warp_sums[32];
   __shared__ int32_t bucket[2][kCostBuckets];  // per kernel list: decode (1), prefill (2)
-  __shared__ int bad, max_span, min_span;
+  __shared__ int bad, max_span, min_span, long_cols;
   const int tid = threadIdx.x, nthreads = blockDim.x;
   if (tid == 0) {
     bad = 0;
     max_span = 0;
     min_span = INT_MAX;
+    long_cols = 0;
   }
   for (int i = tid; i < 2 * kCostBuckets; i += nthreads) bucket[i / kCostBuckets][i % kCostBuckets] = 0;
   __syncthreads();
@@ -172,8 +173,10 @@ __global__ void __launch_bounds__(kDevPlanThreads) aspire_plan_device_kernel(Dev
       chunk = whole_group_chunk(max_span);
   }
 
-  // Per-thread counts; item lengths into the cost histogram.
+  // Per-thread counts; item lengths into the cost histogram; the widest long
+  // decode group (pad_long_items).
   int64_t n_items = 0, n_merge = 0, n_prow = 0, n_units = 0;
+  int my_long_cols = 0;
   for (int b = r0; b < r1; ++b) {
     const RowShape s = row_shape(p, b);
     if (s.ql <= 0) continue;
@@ -192,8 +195,10 @@ __global__ void __launch_bounds__(kDevPlanThreads) aspire_plan_device_kernel(Dev
       }
       const int64_t last_len = span - int64_t(nch - 1) * chunk;
       atomicAdd(&hist[cost_bucket(last_len)], heads);
+      if (s.kind == 1 && long_group(span, max_span)) my_long_cols = max(my_long_cols, int(tc_columns(rows)));
     }
   }
+  if (my_long_cols > 0) atomicMax(&long_cols, my_long_cols);
   int64_t tot_items, tot_merge, tot_prow, tot_units;
   int64_t off_item = block_exclusive_scan(n_items, warp_sums, &tot_items);
   (void)off_item;
@@ -234,6 +239,7 @@ __global__ void __launch_bounds__(kDevPlanThreads) aspire_plan_device_kernel(Dev
     return;
   }
 
+  const int32_t pad_cols = pad_long_items(n_decode, p.num_sms) ? long_cols : 0;
   WorkItem* items = reinterpret_cast<WorkItem*>(w + off_items);
   MergeDesc* merges = reinterpret_cast<MergeDesc*>(w + off_merges);
   int32_t* units = w + off_units;
@@ -278,6 +284,7 @@ __global__ void __launch_bounds__(kDevPlanThreads) aspire_plan_device_kernel(Dev
           it.partial_base = pbase;
           it.merge_id = merge_id;
           it.kind = s.kind;
+          it.cols = s.kind == 1 && long_group(span, max_span) ? pad_cols : 0;
           const int slot = atomicAdd(&slots[cost_bucket(it.tok_end - it.tok_begin)], 1);
           items[slot] = it;
         }

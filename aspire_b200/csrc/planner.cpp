@@ -184,6 +184,18 @@ int plan_impl(const int32_t* qo_indptr, const int32_t* kv_indptr, const int32_t*
       chunk = whole_group_chunk(max_span);
   }
 
+  // Few decode items per CTA: the long groups' items take one width (pad_long_items).
+  int32_t pad_cols = 0;
+  {
+    int64_t n_tc = 0;
+    for (const GroupDesc& g : groups) {
+      if (g.kind != 1) continue;
+      n_tc += g.span > 0 ? (g.span + chunk - 1) / chunk : 1;
+      if (long_group(g.span, max_span)) pad_cols = std::max(pad_cols, tc_columns(g.pq_end - g.pq_begin));
+    }
+    if (!pad_long_items(n_tc, num_sms)) pad_cols = 0;
+  }
+
   std::vector<WorkItem> gather_items, tc_items, pf_items;
   std::vector<MergeDesc> merges;
   std::vector<int32_t> merge_units;  // (merge index << 8) | packed row within the tile
@@ -227,6 +239,7 @@ int plan_impl(const int32_t* qo_indptr, const int32_t* kv_indptr, const int32_t*
       it.partial_base = partial_base;
       it.merge_id = merge_id;
       it.kind = g.kind;
+      it.cols = g.kind == 1 && long_group(g.span, max_span) ? pad_cols : 0;
       (g.kind == 2 ? pf_items : g.kind == 1 ? tc_items : gather_items).push_back(it);
     }
   }

@@ -13,7 +13,7 @@ from aspire_b200.workloads import make_layout
 
 HEADER = Path(__file__).resolve().parent.parent / "include" / "aspire_b200.h"
 ITEM_FIELDS = ["row", "kv_head", "q_start", "q_len", "kv_page_base", "kv_len", "tok_begin", "tok_end",
-               "pq_begin", "pq_end", "chunk", "n_chunks", "partial_base", "merge_id", "kind", "reserved"]
+               "pq_begin", "pq_end", "chunk", "n_chunks", "partial_base", "merge_id", "kind", "cols"]
 
 
 def header_functions():
@@ -58,7 +58,7 @@ def test_plan_covers_every_token_once(built_library, draft_fraction):
     assert rc == 0, built_library.aspire_last_error()
     w, items = _decode(buf, info)
     assert w[0] == 0x41535042
-    assert int(w[17]) == info.chunk_tokens  # the chunk length the kernel reads to pick its column widths
+    assert int(w[17]) == info.chunk_tokens  # the plan's common chunk length
     group = 4
     cover = {}
     for it in items:
@@ -144,6 +144,31 @@ def _expected_chunk(spans, hkv, num_sms):
     return max(512, cdiv(max(spans), 128) * 128) if whole <= split else chunk
 
 
+def _check_item_columns(items, info, num_sms):
+    """Product columns of the tcgen05 decode items (WorkItem.cols): when the
+    decode list has at most two items per SM, every item of a long group
+    (span above half the longest) takes the widest long group's width
+    (packed rows rounded up to 16), other items 0 (their own width); with
+    more items, all 0."""
+    tc = [it for it in items if it["kind"] == 1]
+    assert all(it["cols"] == 0 for it in items if it["kind"] != 1)
+    if not tc:
+        return
+    r16 = lambda n: -(-n // 16) * 16  # noqa: E731
+    span = {}
+    for it in tc:
+        key = (it["row"], it["kv_head"], it["pq_begin"])
+        span[key] = max(span.get(key, 0), it["tok_end"])
+    longest = max(span.values())
+    long_of = lambda it: 2 * span[(it["row"], it["kv_head"], it["pq_begin"])] > longest  # noqa: E731
+    if len(tc) <= 2 * num_sms:
+        width = max(r16(it["pq_end"] - it["pq_begin"]) for it in tc if long_of(it))
+        for it in tc:
+            assert it["cols"] == (width if long_of(it) else 0), it
+    else:
+        assert all(it["cols"] == 0 for it in tc)
+
+
 @pytest.mark.parametrize("case", ["mixed", "mixed_tp4", "mixed_tp8", "full_context", "prefill_spread", "draft_b1",
                                   "draft_b16", "draft_b32"])
 def test_plan_chunk_rule(built_library, case):
@@ -191,13 +216,19 @@ def test_plan_chunk_rule(built_library, case):
         qo = np.array([0, 8192], np.int32)
         kvp = np.array([0, 512], np.int32)
         spans = [8192] + [64 * (t + 1) for t in range(1, 128)]
-    rc, info, _ = _plan(built_library, qo, kvp, kvl, hq, hkv, num_sms=num_sms)
+    rc, info, buf = _plan(built_library, qo, kvp, kvl, hq, hkv, num_sms=num_sms)
     assert rc == 0, built_library.aspire_last_error()
     assert info.chunk_tokens == _expected_chunk(spans, hkv, num_sms)
+    _, items = _decode(buf, info)
+    _check_item_columns(items, info, num_sms)
     if case == "mixed":
         assert info.num_items_tc == 768  # verify rows in two chunks, draft rows whole
     if case in ("mixed_tp4", "mixed_tp8"):
         assert info.chunk_tokens == {"mixed_tp4": 16384, "mixed_tp8": 8192}[case]
+        # verify rows of 3-9 queries x 4 heads: all 48 columns
+        assert {it["cols"] for it in items if it["kind"] == 1 and it["q_len"] > 1} == {48}
+    if case == "mixed":
+        assert all(it["cols"] == 0 for it in items)
     if case == "prefill_spread":
         assert info.num_merge == 0 and info.num_items_prefill == 128 * 8
 

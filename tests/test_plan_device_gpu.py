@@ -16,7 +16,7 @@ from gpu_helpers import MAX_ABS, MEAN_ABS, assert_attention_close, oracle_attent
 pytestmark = pytest.mark.gpu
 
 ITEM = ["row", "kv_head", "q_start", "q_len", "kv_page_base", "kv_len", "tok_begin", "tok_end", "pq_begin",
-        "pq_end", "chunk", "n_chunks", "partial_base", "merge_id", "kind", "reserved"]
+        "pq_end", "chunk", "n_chunks", "partial_base", "merge_id", "kind", "cols"]
 
 
 def _decode(words):
