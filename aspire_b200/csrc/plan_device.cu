@@ -6,9 +6,11 @@
 //
 // It produces the same items as the host planner (planner.cpp): every
 // (row, KV head, packed-query tile) is cut into chunks of one common length
-// (chunk_for: a multiple of 128 tokens, at least 512, sized for about two
-// or four items per SM by the spread of the groups' spans), with
-// merge descriptors for the split groups.  Rows go to the tcgen05 decode
+// (a multiple of 128 tokens, at least 512: about two or four items per SM by
+// the spread of the groups' spans, one piece per SM for few long groups, or
+// every group whole; common.cuh), with merge descriptors for the split
+// groups, and the long groups' items take one product width when there are
+// few items per CTA (pad_long_items).  Rows go to the tcgen05 decode
 // kernel, or to the prefill kernel when their packed queries reach
 // kPfMinRows (the default routing); each list is stored longest first through
 // a counting sort on item length in 128-token tiles, the order in which the
