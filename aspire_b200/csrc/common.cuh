@@ -152,6 +152,22 @@ __host__ __device__ inline int64_t short_group_work10(int64_t span) {
   return (span + 127) / 128 * 10 + kItemCost10;
 }
 
+// Split plans at the 512-token minimum that keep at most a quarter of the
+// SMs busy (a drafting row over 64 pages: 8 groups of 1024 tokens, 16
+// items) take 256-token chunks: such a call is bound by the latency of its
+// first tiles, not by HBM, and each item's share of it halves.  Measured on
+// the config-5 sweep: one drafting row over 64 pages 13.9 -> 12.9-13.0 us at
+// every context.  Plans of 64 items doubled to 128 were 4-8.5 % slower (one
+// row of 4k context: the extra merge work and item boundaries outweigh the
+// shorter items) and four drafting rows only 1-2 % faster, so the rule stops
+// at a quarter; a 256-token minimum for every plan slowed the calls whose
+// items then outnumber the SMs (one row of 16k context: 32 -> 47 us).  Both
+// planners use it.
+__host__ __device__ inline int64_t small_plan_chunk(int64_t chunk, int64_t n_groups, int64_t n_items,
+                                                    int64_t num_sms) {
+  return chunk == 512 && n_items > n_groups && 4 * n_items <= num_sms ? 256 : chunk;
+}
+
 // The chunk length that keeps every group whole.
 __host__ __device__ inline int64_t whole_group_chunk(int64_t max_span) {
   const int64_t c = (max_span + 127) / 128 * 128;

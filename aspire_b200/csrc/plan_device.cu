@@ -6,9 +6,9 @@
 //
 // It produces the same items as the host planner (planner.cpp): every
 // (row, KV head, packed-query tile) is cut into chunks of one common length
-// (a multiple of 128 tokens, at least 512: about two or four items per SM by
-// the spread of the groups' spans, one piece per SM for few long groups, or
-// every group whole; common.cuh), with merge descriptors for the split
+// (a multiple of 128 tokens, at least 512, or 256 for small split plans:
+// about two or four items per SM by the spread of the groups' spans, one
+// piece per SM for few long groups, or every group whole; common.cuh), with merge descriptors for the split
 // groups, and the long groups' items take one product width when there are
 // few items per CTA (pad_long_items).  Rows go to the tcgen05 decode
 // kernel, or to the prefill kernel when their packed queries reach
@@ -157,7 +157,8 @@ __global__ void __launch_bounds__(kDevPlanThreads) aspire_plan_device_kernel(Dev
     if (c > 0) chunk = c;
   }
   {
-    // Whole groups when they balance about as well (whole_groups_cheaper).
+    // Whole groups when they balance about as well (whole_groups_cheaper),
+    // else 256-token chunks for small split plans (small_plan_chunk).
     int64_t my_groups = 0, my_chunk_items = 0;
     for (int b = r0; b < r1; ++b) {
       const RowShape s = row_shape(p, b);
@@ -173,6 +174,8 @@ __global__ void __launch_bounds__(kDevPlanThreads) aspire_plan_device_kernel(Dev
     block_exclusive_scan(my_chunk_items, warp_sums, &n_chunk_items);
     if (whole_groups_cheaper(n_groups, max_span, total_tokens, chunk, n_chunk_items, p.num_sms))
       chunk = whole_group_chunk(max_span);
+    else
+      chunk = small_plan_chunk(chunk, n_groups, n_chunk_items, p.num_sms);
   }
 
   // Per-thread counts; item lengths into the cost histogram; the widest long

@@ -157,8 +157,8 @@ int plan_impl(const int32_t* qo_indptr, const int32_t* kv_indptr, const int32_t*
   }
 
   // Common chunk length (chunk_for): a multiple of 128 tokens (one tcgen05 KV
-  // tile = 8 pages), never below 512; two or four items per CTA by the spread
-  // of the groups' spans.
+  // tile = 8 pages), at least 512 (256 for small split plans); two or four
+  // items per CTA by the spread of the groups' spans, then the rules below.
   int32_t max_span = 0, min_span = INT32_MAX;
   for (const GroupDesc& g : groups) {
     max_span = std::max(max_span, g.span);
@@ -182,6 +182,8 @@ int plan_impl(const int32_t* qo_indptr, const int32_t* kv_indptr, const int32_t*
     for (const GroupDesc& g : groups) n_chunk_items += g.span > 0 ? (g.span + chunk - 1) / chunk : 1;
     if (whole_groups_cheaper(int64_t(groups.size()), max_span, total_tokens, chunk, n_chunk_items, num_sms))
       chunk = whole_group_chunk(max_span);
+    else
+      chunk = small_plan_chunk(chunk, int64_t(groups.size()), n_chunk_items, num_sms);
   }
 
   // Few decode items per CTA: the long groups' items take one width (pad_long_items).

@@ -58,9 +58,9 @@ def test_mixed_ragged_split_kv(cuda_device, hq, hkv, draft_fraction):
 
 
 def test_exact_widths_with_long_chunks(cuda_device):
-    """A plan whose split-KV chunks exceed 4096 tokens: the kernel runs every
-    item at its own padded width (16/32/48 columns) instead of one common width
-    (the mode every smaller test above runs in)."""
+    """A plan with more than two items per SM and split-KV chunks above 4096
+    tokens: every item runs at its own width (16/32/48 columns), and a CTA
+    moves between widths from item to item."""
     lay = make_layout(batch=24, ctx=24000, num_qo_heads=32, num_kv_heads=8, draft_fraction=0.5, budget_pages=40,
                       seed=21)
     q, kv = make_inputs(lay, cuda_device, seed=21)
@@ -72,11 +72,52 @@ def test_exact_widths_with_long_chunks(cuda_device):
     assert_attention_close(out, lse, ref_out, ref_lse)
 
 
+def _tc_item_columns(lay, num_sms):
+    """(packed rows, planned columns) of every tcgen05 decode item, from the
+    library's host planner for this layout (WorkItem words 8, 9 and 15)."""
+    import ctypes
+
+    from aspire_b200 import _capi
+
+    lib = _capi.load_library()
+    buf = np.zeros(1 << 22, dtype=np.uint8)
+    info = _capi.AspirePlanInfo()
+    p = lambda a: np.ascontiguousarray(a, dtype=np.int32).ctypes.data_as(_capi.c_int32_p)  # noqa: E731
+    arrays = [np.ascontiguousarray(a, dtype=np.int32) for a in (lay.qo_indptr, lay.kv_indptr, lay.kv_lens)]
+    rc = lib.aspire_plan_host_only(p(arrays[0]), p(arrays[1]), p(arrays[2]), lay.batch, lay.num_qo_heads,
+                                   lay.num_kv_heads, 128, 16, 1, num_sms, buf.ctypes.data_as(ctypes.c_void_p),
+                                   buf.nbytes, 1 << 30, ctypes.byref(info))
+    assert rc == 0, lib.aspire_last_error()
+    w = buf.view(np.int32)
+    items = w[w[5]: w[5] + info.num_items * 16].reshape(-1, 16)
+    tc = items[items[:, 14] == 1]
+    return tc[:, 9] - tc[:, 8], tc[:, 15]
+
+
+def test_padded_long_items(cuda_device):
+    """Few items per SM (8 rows): the plan gives the verify rows' items (3 to
+    9 queries x 4 heads: 16, 32 and 48 columns of their own) one width, the
+    widest, while the drafting rows' items keep their 16 columns; the padded
+    columns hold no query and must not reach the output."""
+    lay = make_layout(batch=8, ctx=6000, num_qo_heads=32, num_kv_heads=8, draft_fraction=0.5, budget_pages=16,
+                      seed=31)
+    num_sms = torch.cuda.get_device_properties(cuda_device).multi_processor_count
+    rows, cols = _tc_item_columns(lay, num_sms)
+    exact = (rows + 15) // 16 * 16
+    padded = cols > exact
+    assert padded.any() and (cols[padded] == cols.max()).all(), "the case must pad some verify items"
+    assert (cols[~padded] == 0).any(), "the drafting rows' items keep their own width"
+    q, kv = make_inputs(lay, cuda_device, seed=31)
+    out, lse, _, _ = run_attention(lay, q, kv)
+    ref_out, ref_lse, _ = oracle_attention(lay, q, kv)
+    assert_attention_close(out, lse, ref_out, ref_lse)
+
+
 @pytest.mark.parametrize("hq,hkv", [(40, 8), (56, 8), (24, 1)])
 def test_common_width_groups_not_dividing_the_tile(cuda_device, hq, hkv):
-    """Short chunks (every item at the common 48-column width) with GQA groups
-    of 5, 7 and 24: the query tile holds 45, 42 and 48 rows, the rest of its
-    columns stay zero."""
+    """GQA groups of 5, 7 and 24: the query tile holds 45, 42 and 48 rows, so
+    the item's 48 columns include rows past its queries, which must not reach
+    the output."""
     lay = make_layout(batch=7, ctx=1900, num_qo_heads=hq, num_kv_heads=hkv, draft_fraction=0.4, budget_pages=23,
                       seed=hq)
     q, kv = make_inputs(lay, cuda_device, seed=hq)

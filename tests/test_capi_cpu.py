@@ -113,7 +113,9 @@ def _expected_chunk(spans, hkv, num_sms):
     groups' spans are within 2x of each other, else about two; but every
     group whole (chunk = longest span rounded up to 128, at least 512) when
     the whole-group makespan estimate is no worse than the split one (in
-    tenths of a 128-token tile: an item boundary 2.3 tiles, the merge 2.5)."""
+    tenths of a 128-token tile: an item boundary 2.3 tiles, the merge 2.5);
+    few long groups cut into one piece per SM; and 256-token chunks for a
+    split plan at 512 that keeps at most a quarter of the SMs busy."""
     total = sum(max(s, 1) for s in spans) * hkv
     cdiv = lambda a, b: -(-a // b)  # noqa: E731
 
@@ -141,7 +143,10 @@ def _expected_chunk(spans, hkv, num_sms):
     whole = cdiv(n_groups, num_sms) * (cdiv(max(spans), 128) * 10 + 23)
     split = (max(cdiv(total * 10, 128 * num_sms), chunk // 128 * 10) + cdiv(n_items, num_sms) * 23
              + (25 if n_items > n_groups else 0))
-    return max(512, cdiv(max(spans), 128) * 128) if whole <= split else chunk
+    if whole <= split:
+        return max(512, cdiv(max(spans), 128) * 128)
+    # A split plan at the 512 minimum on at most a quarter of the SMs: 256.
+    return 256 if chunk == 512 and n_items > n_groups and 4 * n_items <= num_sms else chunk
 
 
 def _check_item_columns(items, info, num_sms):
@@ -170,7 +175,7 @@ def _check_item_columns(items, info, num_sms):
 
 
 @pytest.mark.parametrize("case", ["mixed", "mixed_tp4", "mixed_tp8", "full_context", "prefill_spread", "draft_b1",
-                                  "draft_b16", "draft_b32"])
+                                  "draft_b4", "draft_b16", "draft_b32"])
 def test_plan_chunk_rule(built_library, case):
     """Decode batches (long verify rows beside short draft rows) get about two
     items per SM; whole-context rows of equal length, four; the spread-out
@@ -179,10 +184,11 @@ def test_plan_chunk_rule(built_library, case):
     decode batch), each is cut into SMs / long groups pieces.  Medium
     draft-only batches keep every group whole (one item each, no merge): 16
     rows over 64 pages at 32 / 8 heads, 32 rows over 136 pages at 16 / 8; one
-    row over 64 pages is still split (its 8 groups use 16 SMs)."""
+    row over 64 pages is still split, into 256-token chunks (its 8 groups
+    use 32 SMs), four rows into 512-token chunks."""
     num_sms = 148
     if case.startswith("draft_"):
-        B, pages, hq, hkv = {"draft_b1": (1, 64, 32, 8), "draft_b16": (16, 64, 32, 8),
+        B, pages, hq, hkv = {"draft_b1": (1, 64, 32, 8), "draft_b4": (4, 64, 32, 8), "draft_b16": (16, 64, 32, 8),
                              "draft_b32": (32, 136, 16, 8)}[case]
         kvl = np.full(B, pages * 16, np.int32)
         qo = np.arange(B + 1, dtype=np.int32)
@@ -190,7 +196,9 @@ def test_plan_chunk_rule(built_library, case):
         rc, info, _ = _plan(built_library, qo, kvp, kvl, hq, hkv, num_sms=num_sms)
         assert rc == 0, built_library.aspire_last_error()
         assert info.chunk_tokens == _expected_chunk([pages * 16] * B, hkv, num_sms)
-        if case == "draft_b1":
+        if case == "draft_b1":  # 16 items at 512 tokens on 148 SMs: cut at 256
+            assert info.chunk_tokens == 256 and info.num_merge == B * hkv
+        elif case == "draft_b4":  # 64 items at 512 tokens: more than a quarter of the SMs
             assert info.chunk_tokens == 512 and info.num_merge == B * hkv
         else:
             assert info.chunk_tokens == pages * 16
