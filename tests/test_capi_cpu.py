@@ -50,16 +50,13 @@ def _decode(buf, info):
     return w, [dict(zip(ITEM_FIELDS, map(int, r))) for r in items]
 
 
-@pytest.mark.parametrize("draft_fraction", [0.0, 0.5, 1.0])
-def test_plan_covers_every_token_once(built_library, draft_fraction):
-    lay = make_layout(batch=12, ctx=3000, num_qo_heads=32, num_kv_heads=8, draft_fraction=draft_fraction,
-                      budget_pages=40, seed=3)
-    rc, info, buf = _plan(built_library, lay.qo_indptr, lay.kv_indptr, lay.kv_lens, 32, 8)
-    assert rc == 0, built_library.aspire_last_error()
+def _check_coverage(lay, info, buf):
+    """Every (row, KV head, packed query) sees keys [0, kv_len) exactly once
+    over its items; merge descriptors, list order and CTA indptrs agree."""
     w, items = _decode(buf, info)
     assert w[0] == 0x41535042
     assert int(w[17]) == info.chunk_tokens  # the plan's common chunk length
-    group = 4
+    group = lay.num_qo_heads // lay.num_kv_heads
     cover = {}
     for it in items:
         for pq in range(it["pq_begin"], it["pq_end"]):
@@ -73,7 +70,7 @@ def test_plan_covers_every_token_once(built_library, draft_fraction):
             assert md[4] == it["partial_base"] and md[3] == it["kv_head"]
     for b in range(lay.batch):
         nq = int(lay.q_lens[b]) * group
-        for h in range(8):
+        for h in range(lay.num_kv_heads):
             for pq in range(nq):
                 ranges = sorted(cover[(b, h, pq)])
                 assert ranges[0][0] == 0 and ranges[-1][1] == int(lay.kv_lens[b])
@@ -93,6 +90,39 @@ def test_plan_covers_every_token_once(built_library, draft_fraction):
     g_indptr = w[w[3]: w[3] + g_ctas + 1]
     assert g_indptr[0] == 0 and np.all(np.diff(g_indptr) >= 0)
     assert g_indptr[-1] == info.num_items_gather
+    return items
+
+
+@pytest.mark.parametrize("draft_fraction", [0.0, 0.5, 1.0])
+def test_plan_covers_every_token_once(built_library, draft_fraction):
+    lay = make_layout(batch=12, ctx=3000, num_qo_heads=32, num_kv_heads=8, draft_fraction=draft_fraction,
+                      budget_pages=40, seed=3)
+    rc, info, buf = _plan(built_library, lay.qo_indptr, lay.kv_indptr, lay.kv_lens, 32, 8)
+    assert rc == 0, built_library.aspire_last_error()
+    _check_coverage(lay, info, buf)
+
+
+@pytest.mark.parametrize("batch,ctx,draft_fraction,hq,hkv", [(1, 2000, 0.0, 32, 8), (2, 1500, 0.5, 16, 8),
+                                                              (4, 900, 1.0, 32, 8), (3, 5000, 0.5, 8, 1)])
+def test_small_plans_cover_every_token_once(built_library, batch, ctx, draft_fraction, hq, hkv):
+    """Small batches on 148 SMs, the plans the small-plan and item-width rules
+    shape: 256-token chunks where the split plan keeps at most a quarter of
+    the SMs busy, long verify items padded to one width."""
+    lay = make_layout(batch=batch, ctx=ctx, num_qo_heads=hq, num_kv_heads=hkv, draft_fraction=draft_fraction,
+                      budget_pages=16, seed=batch)
+    rc, info, buf = _plan(built_library, lay.qo_indptr, lay.kv_indptr, lay.kv_lens, hq, hkv, num_sms=148)
+    assert rc == 0, built_library.aspire_last_error()
+    items = _check_coverage(lay, info, buf)
+    _check_item_columns(items, info, 148)
+    # Spans per (row, query tile of 48 packed rows), as the planner groups them:
+    # the tile with query 0 sees every key, a later one keys up to its last query.
+    group, spans = hq // hkv, []
+    for ql, kl in zip(lay.q_lens.tolist(), lay.kv_lens.tolist()):
+        tile = 48 // group * group
+        for p0 in range(0, ql * group, tile):
+            p1 = min(ql * group, p0 + tile)
+            spans.append(kl if p0 < group else min(kl, kl - ql + (p1 - 1) // group + 1))
+    assert info.chunk_tokens == _expected_chunk(spans, hkv, 148)
 
 
 def test_plan_balances_ctas(built_library):
